@@ -1,0 +1,162 @@
+/*
+ * mvdecode -- B200 (sm_100a) paged GQA decode attention and paged KV append.
+ *
+ * C ABI of libmvdecode.so. Every entry point takes plain device pointers,
+ * element strides and sizes, enqueues work on the caller's CUDA stream and
+ * returns an MV_* status code; on failure mv_last_error() names the problem
+ * (thread-local). Nothing here synchronises the device or reads device
+ * memory from the host. Call with the device that owns the pointers current.
+ *
+ * Layouts (the reference's own, so a micro-vllm cache drops in unchanged):
+ *   q, out        [batch, num_q_heads, head_dim]   head_dim stride 1, outer strides given
+ *   K/V pages     [num_blocks, num_kv_heads, block_size, head_dim]  contiguous
+ *   block_table   [batch, >= blocks_per_seq]       row stride given, int32 or int64
+ *   context_lens  [batch]                          tokens to attend, incl. this step's
+ * Query head j uses KV head j / (num_q_heads / num_kv_heads).
+ */
+#ifndef MVDECODE_H_
+#define MVDECODE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define MV_API __attribute__((visibility("default")))
+#else
+#define MV_API
+#endif
+
+#define MV_ABI_VERSION 1
+
+/* Element type of q, pages and outputs. */
+#define MV_DTYPE_F32 0
+#define MV_DTYPE_F16 1
+#define MV_DTYPE_BF16 2
+
+/* Integer type of block tables, context lengths and positions. */
+#define MV_INDEX_I32 0
+#define MV_INDEX_I64 1
+
+/* Meaning of a per-sequence position array given to mv_write_paged_kv. */
+#define MV_POSITIONS_START 0 /* logical slot of the first new token */
+#define MV_POSITIONS_END 1   /* length after the append; first slot = end - num_tokens */
+
+/* Flags for mv_paged_decode / mv_paged_decode_workspace_size. */
+#define MV_FLAG_FORCE_SIMT 1u /* use the CUDA-core kernel even where the tensor-core one applies */
+
+/* Status codes. */
+#define MV_OK 0
+#define MV_ERR_INVALID_ARGUMENT 1
+#define MV_ERR_UNSUPPORTED 2
+#define MV_ERR_WORKSPACE_TOO_SMALL 3
+#define MV_ERR_CUDA 4
+
+/* Device status bits (sticky, per device; see mv_device_status). */
+#define MV_DEVICE_STATUS_WAIT_TIMEOUT 1u
+
+/* Kernel paths reported by mv_paged_decode_plan. */
+#define MV_PATH_SIMT 0
+#define MV_PATH_TMA_MMA 1
+
+MV_API int mv_abi_version(void);
+
+/* Message for the last non-MV_OK status returned on this thread. */
+MV_API const char* mv_last_error(void);
+
+/*
+ * Workspace bytes mv_paged_decode needs for this geometry (0 when every
+ * sequence fits one split). max_context_len bounds every context length;
+ * pages_per_split 0 lets the library choose.
+ * Replaces no reference call: the reference kernel allocates an output-sized
+ * running buffer itself (src/micro_vllm/csrc/online_attention.cuh:154-156).
+ */
+MV_API int mv_paged_decode_workspace_size(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                                   int32_t head_dim, int32_t block_size, int64_t max_context_len,
+                                   int32_t pages_per_split, uint32_t flags, int32_t dtype,
+                                   size_t* bytes);
+
+/*
+ * Which kernel mv_paged_decode would run, and its split-KV shape. k_cache and
+ * v_cache are only inspected for alignment.
+ */
+MV_API int mv_paged_decode_plan(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                         int32_t head_dim, int32_t block_size, int64_t max_context_len,
+                         int32_t pages_per_split, uint32_t flags, int32_t dtype,
+                         const void* k_cache, const void* v_cache,
+                         int32_t* path, int32_t* chosen_pages_per_split, int32_t* max_splits);
+
+/*
+ * Paged GQA decode attention: for every sequence b and query head j,
+ *   out[b, j] = softmax(scale * K_b q[b, j]) V_b
+ * over the first context_lens[b] tokens of the pages block_table[b, :].
+ *
+ * Replaces the reference's _decode_attention_paged(query, key_pages,
+ * value_pages, table, length) (src/micro_vllm/csrc/decode_attention.cpp:147-152,
+ * launched at decode_attention_paged.cu:51-57): that call is batch 1, with
+ * context_lens == NULL, max_context_len == length, an int64 table and
+ * scale == head_dim ** -0.5.
+ *
+ * context_lens may be NULL: every sequence then attends max_context_len tokens.
+ * Device-side contract (the host cannot see device lengths or table contents):
+ *   - a used page whose ID is outside [0, num_blocks) makes that sequence's
+ *     whole GQA group NaN, with no out-of-bounds read (as the reference);
+ *   - a length of 0 gives zeros; a negative length, or one above
+ *     max_context_len or blocks_per_seq * block_size, gives NaN.
+ * workspace: mv_paged_decode_workspace_size bytes of device scratch (may be
+ * NULL when that size is 0), used only by this call while it runs.
+ * dtype: MV_DTYPE_* of q, pages and out; accumulation is fp32.
+ */
+MV_API int mv_paged_decode(const void* q, int64_t q_stride_seq, int64_t q_stride_head,
+                    const void* k_cache, const void* v_cache, int64_t num_blocks,
+                    int32_t num_kv_heads, int32_t block_size, int32_t head_dim,
+                    const void* block_table, int32_t block_table_type,
+                    int64_t block_table_stride, int64_t blocks_per_seq,
+                    const void* context_lens, int32_t context_lens_type,
+                    int64_t max_context_len, int32_t batch, int32_t num_q_heads, float scale,
+                    void* out, int64_t out_stride_seq, int64_t out_stride_head,
+                    void* workspace, size_t workspace_bytes, int32_t pages_per_split,
+                    uint32_t flags, int32_t dtype, void* stream);
+
+/*
+ * Paged KV append (reshape-and-cache): token t of sequence b goes to logical
+ * position start_b + t, i.e. page block_table[b, pos / block_size], slot
+ * pos % block_size. Copies are bit-exact (no conversion).
+ *
+ * Replaces the reference's write_paged_kv(key, value, key_pages, value_pages,
+ * page_table, start) (src/micro_vllm/csrc/paged_kv_cache.cpp:96-107, kernel
+ * paged_kv_cache.cu:44-62): that call is batch 1, positions == NULL and start
+ * the host-side start.
+ *
+ * key/value: [batch, num_kv_heads, num_tokens, head_dim] with the given element
+ * strides (feature stride 1; zero strides broadcast). positions: NULL (every
+ * sequence starts at `start`) or a device array read per positions_kind.
+ * A token whose position is negative, beyond blocks_per_seq pages, or whose
+ * physical page ID is outside [0, num_blocks) is skipped, never written out of
+ * bounds (as the reference kernel skips bad IDs).
+ */
+MV_API int mv_write_paged_kv(const void* key, int64_t key_stride_seq, int64_t key_stride_head,
+                      int64_t key_stride_token, const void* value, int64_t value_stride_seq,
+                      int64_t value_stride_head, int64_t value_stride_token, void* k_cache,
+                      void* v_cache, int64_t num_blocks, int32_t num_kv_heads,
+                      int32_t block_size, int32_t head_dim, const void* block_table,
+                      int32_t block_table_type, int64_t block_table_stride,
+                      int64_t blocks_per_seq, const void* positions, int32_t positions_type,
+                      int32_t positions_kind, int64_t start, int32_t batch, int32_t num_tokens,
+                      int32_t dtype, void* stream);
+
+/*
+ * Sticky MV_DEVICE_STATUS_* bits kernels have raised on `device` (a bounded
+ * wait that gave up). Reading synchronises with the device's legacy stream.
+ */
+MV_API int mv_device_status(int32_t device, uint32_t* status);
+MV_API int mv_clear_device_status(int32_t device);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MVDECODE_H_ */

@@ -1,0 +1,15 @@
+"""B200-native paged decode path for micro-vllm.
+
+Hand-written sm_100a CUDA kernels for paged GQA decode attention (split-KV,
+TMA page staging, tensor-core tiles) and the paged KV append, behind a C ABI
+(libmvdecode.so, include/mvdecode.h) and host wrappers that keep micro-vllm's
+own function names, arguments and errors:
+
+    cuda_attention.decode_attention_paged        <- micro_vllm.cuda_attention
+    cuda_paged_cache._write_paged_kv             <- micro_vllm.cuda_paged_cache
+    paged_kv_cache.PagedKVCache                  <- micro_vllm.paged_kv_cache
+
+plus batched forms (``paged_decode_attention``, ``write_paged_kv``) over one
+shared page pool, and KV-head sharding across GPUs (``sharding``).
+"""
+__version__ = '0.1.0'

@@ -1,0 +1,101 @@
+"""ctypes binding of libmvdecode.so (declared in include/mvdecode.h).
+
+The library is loaded on first use, never at import, and there is no fallback:
+if it is missing or fails to load, every entry point raises.
+"""
+import ctypes
+from functools import lru_cache
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / 'lib' / 'libmvdecode.so'
+
+MV_ABI_VERSION = 1
+DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
+INDEX_I32, INDEX_I64 = 0, 1
+POSITIONS_START, POSITIONS_END = 0, 1
+FLAG_FORCE_SIMT = 1
+PATH_SIMT, PATH_TMA_MMA = 0, 1
+DEVICE_STATUS_WAIT_TIMEOUT = 1
+
+MV_OK = 0
+STATUS_NAMES = {
+    1: 'invalid argument',
+    2: 'unsupported',
+    3: 'workspace too small',
+    4: 'CUDA error',
+}
+
+EXPORTED_SYMBOLS = (
+    'mv_abi_version', 'mv_last_error', 'mv_paged_decode_workspace_size',
+    'mv_paged_decode_plan', 'mv_paged_decode', 'mv_write_paged_kv',
+    'mv_device_status', 'mv_clear_device_status',
+)
+
+_i32, _i64, _u32, _vp, _sz, _f32 = (ctypes.c_int32, ctypes.c_int64, ctypes.c_uint32,
+                                    ctypes.c_void_p, ctypes.c_size_t, ctypes.c_float)
+
+_SIGNATURES = {
+    'mv_abi_version': (ctypes.c_int, []),
+    'mv_last_error': (ctypes.c_char_p, []),
+    'mv_paged_decode_workspace_size': (
+        ctypes.c_int, [_i32, _i32, _i32, _i32, _i32, _i64, _i32, _u32, _i32,
+                       ctypes.POINTER(_sz)]),
+    'mv_paged_decode_plan': (
+        ctypes.c_int, [_i32, _i32, _i32, _i32, _i32, _i64, _i32, _u32, _i32, _vp, _vp,
+                       ctypes.POINTER(_i32), ctypes.POINTER(_i32), ctypes.POINTER(_i32)]),
+    'mv_paged_decode': (
+        ctypes.c_int, [_vp, _i64, _i64,            # q, strides
+                       _vp, _vp, _i64,             # k_cache, v_cache, num_blocks
+                       _i32, _i32, _i32,           # kv heads, block size, head dim
+                       _vp, _i32, _i64, _i64,      # block table, type, stride, blocks/seq
+                       _vp, _i32, _i64,            # context lens, type, max context len
+                       _i32, _i32, _f32,           # batch, q heads, scale
+                       _vp, _i64, _i64,            # out, strides
+                       _vp, _sz, _i32, _u32, _i32, _vp]),  # workspace, bytes, pps, flags, dtype, stream
+    'mv_write_paged_kv': (
+        ctypes.c_int, [_vp, _i64, _i64, _i64,      # key, strides
+                       _vp, _i64, _i64, _i64,      # value, strides
+                       _vp, _vp, _i64,             # caches, num_blocks
+                       _i32, _i32, _i32,           # kv heads, block size, head dim
+                       _vp, _i32, _i64, _i64,      # block table, type, stride, blocks/seq
+                       _vp, _i32, _i32, _i64,      # positions, type, kind, start
+                       _i32, _i32, _i32, _vp]),    # batch, tokens, dtype, stream
+    'mv_device_status': (ctypes.c_int, [_i32, ctypes.POINTER(_u32)]),
+    'mv_clear_device_status': (ctypes.c_int, [_i32]),
+}
+
+
+class NativeError(RuntimeError):
+    """A libmvdecode entry point returned a non-OK status."""
+
+    def __init__(self, status, message):
+        super().__init__(f'{message} ({STATUS_NAMES.get(status, "status %d" % status)})')
+        self.status = status
+
+
+@lru_cache(maxsize=1)
+def library() -> ctypes.CDLL:
+    """Load libmvdecode.so once; raise if it is absent or incompatible."""
+    if not LIB_PATH.exists():
+        raise RuntimeError(
+            f'{LIB_PATH} is not built: run `python -m micro_vllm_b200.build` '
+            '(or __graft_entry__.build()) before using the CUDA kernels')
+    lib = ctypes.CDLL(str(LIB_PATH))
+    for name, (restype, argtypes) in _SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = restype
+        fn.argtypes = argtypes
+    version = lib.mv_abi_version()
+    if version != MV_ABI_VERSION:
+        raise RuntimeError(f'libmvdecode ABI {version}, expected {MV_ABI_VERSION}')
+    return lib
+
+
+def check(status: int) -> None:
+    if status != MV_OK:
+        message = library().mv_last_error().decode(errors='replace')
+        raise NativeError(status, message)
+
+
+def call(name: str, *args) -> None:
+    check(getattr(library(), name)(*args))

@@ -1,0 +1,531 @@
+// C ABI of libmvdecode.so: argument checks, split-KV planning, TMA tensor-map
+// construction and kernel dispatch for paged decode attention and paged KV
+// append. Declarations and the contract live in include/mvdecode.h.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <type_traits>
+
+#include "mvdecode.h"
+#include "paged_append.cuh"
+#include "paged_decode_merge.cuh"
+#include "paged_decode_mma.cuh"
+#include "paged_decode_simt.cuh"
+
+namespace {
+
+thread_local std::string g_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list args;
+    va_start(args, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, args);
+    va_end(args);
+    g_error = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t err, const char* what) {
+    return fail(MV_ERR_CUDA, "%s: %s", what, cudaGetErrorString(err));
+}
+
+// ------------------------------------------------------------ device facts
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+    int sms = 0;
+    int smem_optin = 0;
+};
+
+DeviceInfo g_devices[kMaxDevices];
+std::mutex g_device_mutex;
+
+int device_info(DeviceInfo* info) {
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaGetDevice");
+    if (dev < 0 || dev >= kMaxDevices) return fail(MV_ERR_UNSUPPORTED, "device index %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_device_mutex);
+    DeviceInfo& d = g_devices[dev];
+    if (d.sms == 0) {
+        err = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+        if (err == cudaSuccess)
+            err = cudaDeviceGetAttribute(&d.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        if (err != cudaSuccess) {
+            d.sms = 0;
+            return cuda_fail(err, "cudaDeviceGetAttribute");
+        }
+    }
+    *info = d;
+    return MV_OK;
+}
+
+// Opt a kernel into `bytes` of dynamic shared memory on the current device.
+template <typename Kernel>
+int ensure_smem(Kernel kernel, size_t bytes) {
+    if (bytes <= 48 * 1024) return MV_OK;
+    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           static_cast<int>(bytes));
+    return err == cudaSuccess ? MV_OK : cuda_fail(err, "cudaFuncSetAttribute");
+}
+
+// ---------------------------------------------------------------- planning
+
+constexpr int kMmaWarps = 4;
+constexpr int kMaxPagesPerSplit = 32 * kMmaWarps;
+
+struct Geometry {
+    int32_t batch, q_heads, kv_heads, head_dim, block_size;
+    int64_t max_context_len;
+    int32_t dtype;
+};
+
+int check_geometry(const Geometry& g) {
+    if (g.batch <= 0 || g.q_heads <= 0 || g.kv_heads <= 0 || g.head_dim <= 0 || g.block_size <= 0)
+        return fail(MV_ERR_INVALID_ARGUMENT,
+                    "batch, head counts, head dimension and block size must be positive");
+    if (g.q_heads % g.kv_heads)
+        return fail(MV_ERR_INVALID_ARGUMENT, "query head count must be divisible by KV head count");
+    if (g.max_context_len < 0) return fail(MV_ERR_INVALID_ARGUMENT, "max_context_len must be nonnegative");
+    if (g.dtype != MV_DTYPE_F32 && g.dtype != MV_DTYPE_F16 && g.dtype != MV_DTYPE_BF16)
+        return fail(MV_ERR_INVALID_ARGUMENT, "dtype must be MV_DTYPE_F32, MV_DTYPE_F16 or MV_DTYPE_BF16");
+    if (g.batch > 65535 || g.kv_heads > 65535)
+        return fail(MV_ERR_UNSUPPORTED, "batch and KV head count are limited to 65535");
+    return MV_OK;
+}
+
+struct Plan {
+    int path;
+    int pages_per_split;
+    int max_splits;
+    int nt;  // mma n-tiles (8 query heads each)
+    size_t workspace;
+};
+
+bool mma_shape_ok(const Geometry& g) {
+    const int group = g.q_heads / g.kv_heads;
+    return (g.dtype == MV_DTYPE_BF16 || g.dtype == MV_DTYPE_F16) && g.block_size == 16 &&
+           (g.head_dim == 64 || g.head_dim == 128 || g.head_dim == 256) && group <= 16;
+}
+
+int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool aligned_for_tma,
+              Plan* plan) {
+    int rc = check_geometry(g);
+    if (rc != MV_OK) return rc;
+    DeviceInfo dev;
+    rc = device_info(&dev);
+    if (rc != MV_OK) return rc;
+    const int group = g.q_heads / g.kv_heads;
+    plan->path = (!(flags & MV_FLAG_FORCE_SIMT) && aligned_for_tma && mma_shape_ok(g)) ? MV_PATH_TMA_MMA
+                                                                                       : MV_PATH_SIMT;
+    plan->nt = group <= 8 ? 1 : 2;
+    const int64_t max_pages = (g.max_context_len + g.block_size - 1) / g.block_size;
+    int64_t pps = pages_per_split;
+    if (pps < 0) return fail(MV_ERR_INVALID_ARGUMENT, "pages_per_split must be nonnegative");
+    if (pps == 0) {
+        // Enough splits that the page work of the whole batch spreads over
+        // ~16 CTAs per SM, but no split shorter than 8 pages.
+        const int64_t pages = static_cast<int64_t>(g.batch) * g.kv_heads * std::max<int64_t>(max_pages, 1);
+        const int64_t target = static_cast<int64_t>(dev.sms) * 16;
+        pps = (pages + target - 1) / target;
+        pps = std::max<int64_t>(8, std::min<int64_t>(pps, kMaxPagesPerSplit));
+        pps = (pps + kMmaWarps - 1) / kMmaWarps * kMmaWarps;
+    }
+    if (plan->path == MV_PATH_TMA_MMA && pps > kMaxPagesPerSplit)
+        return fail(MV_ERR_INVALID_ARGUMENT, "pages_per_split above %d for the tensor-core kernel",
+                    kMaxPagesPerSplit);
+    const int64_t splits = std::max<int64_t>(1, (max_pages + pps - 1) / pps);
+    if (splits > 8192) return fail(MV_ERR_UNSUPPORTED, "more than 8192 splits: raise pages_per_split");
+    plan->pages_per_split = static_cast<int>(pps);
+    plan->max_splits = static_cast<int>(splits);
+    if (splits > 1) {
+        const size_t rows = static_cast<size_t>(g.batch) * g.q_heads * splits;
+        const size_t o_bytes = (rows * g.head_dim * sizeof(float) + 255) / 256 * 256;
+        plan->workspace = o_bytes + (rows * sizeof(float) + 255) / 256 * 256;
+    } else {
+        plan->workspace = 0;
+    }
+    if (plan->path == MV_PATH_SIMT) {
+        const size_t smem = mv::simt_smem_bytes(group, g.head_dim);
+        if (smem > static_cast<size_t>(dev.smem_optin))
+            return fail(MV_ERR_UNSUPPORTED,
+                        "GQA group %d x head_dim %d needs %zu bytes of shared memory (device limit %d)",
+                        group, g.head_dim, smem, dev.smem_optin);
+    }
+    return MV_OK;
+}
+
+bool tma_aligned(const void* k_cache, const void* v_cache) {
+    return (reinterpret_cast<uintptr_t>(k_cache) % 16 == 0) && (reinterpret_cast<uintptr_t>(v_cache) % 16 == 0);
+}
+
+// ------------------------------------------------------------ tensor maps
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult status;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &status) ==
+                cudaSuccess &&
+            status == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    });
+    return fn;
+}
+
+struct MapKey {
+    const void* base;
+    int64_t num_blocks;
+    int32_t heads, dim, dtype;
+    bool operator==(const MapKey& o) const {
+        return base == o.base && num_blocks == o.num_blocks && heads == o.heads && dim == o.dim &&
+               dtype == o.dtype;
+    }
+};
+
+struct MapEntry {
+    MapKey key;
+    CUtensorMap map;
+    bool used;
+};
+
+constexpr int kMapCache = 64;
+MapEntry g_maps[kMapCache];
+int g_map_next = 0;
+std::mutex g_map_mutex;
+
+// Page pool [num_blocks, heads, 16, dim] viewed as 5-D (d % 64, slot, d / 64,
+// head, page) so one box = one page of one head, stored as dim/64 swizzled
+// [16 x 128 B] sub-tiles.
+int page_tensor_map(const void* base, int64_t num_blocks, int heads, int dim, int dtype, CUtensorMap* out) {
+    const MapKey key{base, num_blocks, heads, dim, dtype};
+    std::lock_guard<std::mutex> lock(g_map_mutex);
+    for (int i = 0; i < kMapCache; ++i) {
+        if (g_maps[i].used && g_maps[i].key == key) {
+            *out = g_maps[i].map;
+            return MV_OK;
+        }
+    }
+    auto encode = encode_fn();
+    if (!encode) return fail(MV_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+    const cuuint64_t row = static_cast<cuuint64_t>(dim) * 2;
+    cuuint64_t dims[5] = {64, 16, static_cast<cuuint64_t>(dim / 64), static_cast<cuuint64_t>(heads),
+                          static_cast<cuuint64_t>(num_blocks)};
+    cuuint64_t strides[4] = {row, 128, 16 * row, static_cast<cuuint64_t>(heads) * 16 * row};
+    cuuint32_t box[5] = {64, 16, static_cast<cuuint32_t>(dim / 64), 1, 1};
+    cuuint32_t elem_strides[5] = {1, 1, 1, 1, 1};
+    CUtensorMap map;
+    CUresult r = encode(&map, dtype == MV_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                        5, const_cast<void*>(base), dims, strides, box, elem_strides,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(MV_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
+    g_maps[g_map_next] = MapEntry{key, map, true};
+    g_map_next = (g_map_next + 1) % kMapCache;
+    *out = map;
+    return MV_OK;
+}
+
+// ----------------------------------------------------------------- launch
+
+template <typename T, int D, int NT>
+int launch_mma(const mv::DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap, dim3 grid,
+               cudaStream_t stream) {
+    constexpr int STAGES = D == 64 ? 6 : (D == 128 ? 3 : 2);
+    using Shape = mv::MmaDecodeShape<D, NT, kMmaWarps, STAGES>;
+    auto kernel = mv::paged_decode_mma_kernel<T, D, NT, kMmaWarps, STAGES>;
+    int rc = ensure_smem(kernel, Shape::kSmemBytes);
+    if (rc != MV_OK) return rc;
+    kernel<<<grid, kMmaWarps * 32, Shape::kSmemBytes, stream>>>(p, kmap, vmap);
+    return MV_OK;
+}
+
+template <typename T>
+int launch_mma_dispatch(const mv::DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap,
+                        dim3 grid, int nt, cudaStream_t stream) {
+    switch (p.head_dim * 4 + nt) {
+        case 64 * 4 + 1: return launch_mma<T, 64, 1>(p, kmap, vmap, grid, stream);
+        case 64 * 4 + 2: return launch_mma<T, 64, 2>(p, kmap, vmap, grid, stream);
+        case 128 * 4 + 1: return launch_mma<T, 128, 1>(p, kmap, vmap, grid, stream);
+        case 128 * 4 + 2: return launch_mma<T, 128, 2>(p, kmap, vmap, grid, stream);
+        case 256 * 4 + 1: return launch_mma<T, 256, 1>(p, kmap, vmap, grid, stream);
+        case 256 * 4 + 2: return launch_mma<T, 256, 2>(p, kmap, vmap, grid, stream);
+        default: return fail(MV_ERR_UNSUPPORTED, "no tensor-core kernel for head_dim %d", p.head_dim);
+    }
+}
+
+template <typename T>
+int launch_decode(const mv::DecodeParams& p, const Plan& plan, const CUtensorMap* kmap,
+                  const CUtensorMap* vmap, cudaStream_t stream) {
+    const dim3 grid(plan.max_splits, p.kv_heads, p.batch);
+    int rc;
+    if (plan.path == MV_PATH_TMA_MMA) {
+        if constexpr (std::is_same<T, float>::value) {
+            return fail(MV_ERR_UNSUPPORTED, "tensor-core kernel takes fp16/bf16 only");
+        } else {
+            rc = launch_mma_dispatch<T>(p, *kmap, *vmap, grid, plan.nt, stream);
+        }
+    } else {
+        const size_t smem = mv::simt_smem_bytes(p.group, p.head_dim);
+        auto kernel = mv::paged_decode_simt_kernel<T>;
+        rc = ensure_smem(kernel, smem);
+        if (rc == MV_OK) kernel<<<grid, mv::kSimtThreads, smem, stream>>>(p);
+    }
+    if (rc != MV_OK) return rc;
+    cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess) return cuda_fail(err, "decode kernel launch");
+    if (plan.max_splits > 1) {
+        const size_t smem = static_cast<size_t>(plan.max_splits) * sizeof(float);
+        auto merge = mv::paged_decode_merge_kernel<T>;
+        rc = ensure_smem(merge, smem);
+        if (rc != MV_OK) return rc;
+        merge<<<dim3(p.q_heads, p.batch), mv::kMergeThreads, smem, stream>>>(p);
+        err = cudaGetLastError();
+        if (err != cudaSuccess) return cuda_fail(err, "merge kernel launch");
+    }
+    return MV_OK;
+}
+
+int check_index_type(int32_t type, const char* what) {
+    if (type != MV_INDEX_I32 && type != MV_INDEX_I64)
+        return fail(MV_ERR_INVALID_ARGUMENT, "%s type must be MV_INDEX_I32 or MV_INDEX_I64", what);
+    return MV_OK;
+}
+
+size_t dtype_bytes(int32_t dtype) { return dtype == MV_DTYPE_F32 ? 4 : 2; }
+
+}  // namespace
+
+extern "C" {
+
+int mv_abi_version(void) { return MV_ABI_VERSION; }
+
+const char* mv_last_error(void) { return g_error.c_str(); }
+
+int mv_paged_decode_workspace_size(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                                   int32_t head_dim, int32_t block_size, int64_t max_context_len,
+                                   int32_t pages_per_split, uint32_t flags, int32_t dtype,
+                                   size_t* bytes) {
+    if (!bytes) return fail(MV_ERR_INVALID_ARGUMENT, "bytes must not be NULL");
+    const Geometry g{batch, num_q_heads, num_kv_heads, head_dim, block_size, max_context_len, dtype};
+    Plan plan;
+    // Alignment never changes the split shape, so plan as if aligned.
+    int rc = make_plan(g, pages_per_split, flags, true, &plan);
+    if (rc != MV_OK) return rc;
+    *bytes = plan.workspace;
+    return MV_OK;
+}
+
+int mv_paged_decode_plan(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads, int32_t head_dim,
+                         int32_t block_size, int64_t max_context_len, int32_t pages_per_split,
+                         uint32_t flags, int32_t dtype, const void* k_cache, const void* v_cache,
+                         int32_t* path, int32_t* chosen_pages_per_split, int32_t* max_splits) {
+    const Geometry g{batch, num_q_heads, num_kv_heads, head_dim, block_size, max_context_len, dtype};
+    Plan plan;
+    int rc = make_plan(g, pages_per_split, flags, tma_aligned(k_cache, v_cache), &plan);
+    if (rc != MV_OK) return rc;
+    if (path) *path = plan.path;
+    if (chosen_pages_per_split) *chosen_pages_per_split = plan.pages_per_split;
+    if (max_splits) *max_splits = plan.max_splits;
+    return MV_OK;
+}
+
+int mv_paged_decode(const void* q, int64_t q_stride_seq, int64_t q_stride_head, const void* k_cache,
+                    const void* v_cache, int64_t num_blocks, int32_t num_kv_heads, int32_t block_size,
+                    int32_t head_dim, const void* block_table, int32_t block_table_type,
+                    int64_t block_table_stride, int64_t blocks_per_seq, const void* context_lens,
+                    int32_t context_lens_type, int64_t max_context_len, int32_t batch,
+                    int32_t num_q_heads, float scale, void* out, int64_t out_stride_seq,
+                    int64_t out_stride_head, void* workspace, size_t workspace_bytes,
+                    int32_t pages_per_split, uint32_t flags, int32_t dtype, void* stream) {
+    if (!q || !k_cache || !v_cache || !block_table || !out)
+        return fail(MV_ERR_INVALID_ARGUMENT, "q, k_cache, v_cache, block_table and out must not be NULL");
+    if (num_blocks <= 0 || blocks_per_seq <= 0)
+        return fail(MV_ERR_INVALID_ARGUMENT, "num_blocks and blocks_per_seq must be positive");
+    if (num_blocks >= (int64_t(1) << 31)) return fail(MV_ERR_UNSUPPORTED, "num_blocks must be below 2^31");
+    if (q_stride_seq < 0 || q_stride_head < 0 || out_stride_seq < 0 || out_stride_head < 0 ||
+        block_table_stride < 0)
+        return fail(MV_ERR_INVALID_ARGUMENT, "strides must be nonnegative");
+    if (batch > 1 && block_table_stride < blocks_per_seq)
+        return fail(MV_ERR_INVALID_ARGUMENT, "block_table_stride is smaller than blocks_per_seq");
+    int rc = check_index_type(block_table_type, "block_table");
+    if (rc == MV_OK && context_lens) rc = check_index_type(context_lens_type, "context_lens");
+    if (rc != MV_OK) return rc;
+    if (!context_lens && max_context_len <= 0)
+        return fail(MV_ERR_INVALID_ARGUMENT, "context length must be positive");
+    if (!(scale == scale) || scale == INFINITY || scale == -INFINITY)
+        return fail(MV_ERR_INVALID_ARGUMENT, "scale must be finite");
+
+    const Geometry g{batch, num_q_heads, num_kv_heads, head_dim, block_size, max_context_len, dtype};
+    Plan plan;
+    rc = make_plan(g, pages_per_split, flags, tma_aligned(k_cache, v_cache), &plan);
+    if (rc != MV_OK) return rc;
+    if (plan.workspace > 0 && (!workspace || workspace_bytes < plan.workspace))
+        return fail(MV_ERR_WORKSPACE_TOO_SMALL, "workspace of %zu bytes needed, %zu given", plan.workspace,
+                    workspace ? workspace_bytes : static_cast<size_t>(0));
+    if (plan.workspace > 0 && reinterpret_cast<uintptr_t>(workspace) % 16)
+        return fail(MV_ERR_INVALID_ARGUMENT, "workspace must be 16-byte aligned");
+
+    mv::DecodeParams p;
+    p.q = q;
+    p.q_stride_seq = q_stride_seq;
+    p.q_stride_head = q_stride_head;
+    p.k_cache = k_cache;
+    p.v_cache = v_cache;
+    p.num_blocks = num_blocks;
+    p.kv_heads = num_kv_heads;
+    p.block_size = block_size;
+    p.head_dim = head_dim;
+    p.group = num_q_heads / num_kv_heads;
+    p.q_heads = num_q_heads;
+    p.batch = batch;
+    p.block_table = block_table;
+    p.table_i64 = block_table_type == MV_INDEX_I64;
+    p.table_stride = block_table_stride;
+    p.blocks_per_seq = blocks_per_seq;
+    p.context_lens = context_lens;
+    p.lens_i64 = context_lens_type == MV_INDEX_I64;
+    p.uniform_len = max_context_len;
+    p.max_context_len = max_context_len;
+    p.scale_log2 = scale * 1.4426950408889634f;
+    p.out = out;
+    p.out_stride_seq = out_stride_seq;
+    p.out_stride_head = out_stride_head;
+    p.pages_per_split = plan.pages_per_split;
+    p.max_splits = plan.max_splits;
+    if (plan.workspace > 0) {
+        const size_t rows = static_cast<size_t>(batch) * num_q_heads * plan.max_splits;
+        const size_t o_bytes = (rows * head_dim * sizeof(float) + 255) / 256 * 256;
+        p.part_o = static_cast<float*>(workspace);
+        p.part_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + o_bytes);
+    } else {
+        p.part_o = nullptr;
+        p.part_lse = nullptr;
+    }
+
+    CUtensorMap kmap, vmap;
+    if (plan.path == MV_PATH_TMA_MMA) {
+        rc = page_tensor_map(k_cache, num_blocks, num_kv_heads, head_dim, dtype, &kmap);
+        if (rc == MV_OK) rc = page_tensor_map(v_cache, num_blocks, num_kv_heads, head_dim, dtype, &vmap);
+        if (rc != MV_OK) return rc;
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    switch (dtype) {
+        case MV_DTYPE_F32: return launch_decode<float>(p, plan, &kmap, &vmap, s);
+        case MV_DTYPE_F16: return launch_decode<__half>(p, plan, &kmap, &vmap, s);
+        default: return launch_decode<__nv_bfloat16>(p, plan, &kmap, &vmap, s);
+    }
+}
+
+int mv_write_paged_kv(const void* key, int64_t key_stride_seq, int64_t key_stride_head,
+                      int64_t key_stride_token, const void* value, int64_t value_stride_seq,
+                      int64_t value_stride_head, int64_t value_stride_token, void* k_cache,
+                      void* v_cache, int64_t num_blocks, int32_t num_kv_heads, int32_t block_size,
+                      int32_t head_dim, const void* block_table, int32_t block_table_type,
+                      int64_t block_table_stride, int64_t blocks_per_seq, const void* positions,
+                      int32_t positions_type, int32_t positions_kind, int64_t start, int32_t batch,
+                      int32_t num_tokens, int32_t dtype, void* stream) {
+    if (!key || !value || !k_cache || !v_cache || !block_table)
+        return fail(MV_ERR_INVALID_ARGUMENT, "key, value, caches and block_table must not be NULL");
+    if (num_blocks <= 0 || num_kv_heads <= 0 || block_size <= 0 || head_dim <= 0 || blocks_per_seq <= 0 ||
+        batch <= 0 || num_tokens <= 0)
+        return fail(MV_ERR_INVALID_ARGUMENT, "sizes must be positive");
+    if (dtype != MV_DTYPE_F32 && dtype != MV_DTYPE_F16 && dtype != MV_DTYPE_BF16)
+        return fail(MV_ERR_INVALID_ARGUMENT, "dtype must be MV_DTYPE_F32, MV_DTYPE_F16 or MV_DTYPE_BF16");
+    const int64_t strides[6] = {key_stride_seq, key_stride_head, key_stride_token,
+                                value_stride_seq, value_stride_head, value_stride_token};
+    for (int64_t s : strides)
+        if (s < 0) return fail(MV_ERR_INVALID_ARGUMENT, "strides must be nonnegative");
+    if (block_table_stride < 0) return fail(MV_ERR_INVALID_ARGUMENT, "block_table_stride must be nonnegative");
+    if (batch > 1 && block_table_stride < blocks_per_seq)
+        return fail(MV_ERR_INVALID_ARGUMENT, "block_table_stride is smaller than blocks_per_seq");
+    int rc = check_index_type(block_table_type, "block_table");
+    if (rc == MV_OK && positions) rc = check_index_type(positions_type, "positions");
+    if (rc != MV_OK) return rc;
+    if (positions && positions_kind != MV_POSITIONS_START && positions_kind != MV_POSITIONS_END)
+        return fail(MV_ERR_INVALID_ARGUMENT, "positions_kind must be MV_POSITIONS_START or MV_POSITIONS_END");
+    DeviceInfo dev;
+    rc = device_info(&dev);
+    if (rc != MV_OK) return rc;
+
+    mv::AppendParams a;
+    a.key = key;
+    a.value = value;
+    a.key_stride[0] = key_stride_seq;
+    a.key_stride[1] = key_stride_head;
+    a.key_stride[2] = key_stride_token;
+    a.value_stride[0] = value_stride_seq;
+    a.value_stride[1] = value_stride_head;
+    a.value_stride[2] = value_stride_token;
+    a.k_cache = k_cache;
+    a.v_cache = v_cache;
+    a.num_blocks = num_blocks;
+    a.kv_heads = num_kv_heads;
+    a.block_size = block_size;
+    a.elem_bytes = static_cast<int>(dtype_bytes(dtype));
+    a.row_bytes = head_dim * a.elem_bytes;
+    a.block_table = block_table;
+    a.table_i64 = block_table_type == MV_INDEX_I64;
+    a.table_stride = block_table_stride;
+    a.blocks_per_seq = blocks_per_seq;
+    a.positions = positions;
+    a.positions_i64 = positions_type == MV_INDEX_I64;
+    a.positions_end = positions_kind == MV_POSITIONS_END;
+    a.start = start;
+    a.batch = batch;
+    a.num_tokens = num_tokens;
+
+    // Widest vector every address and stride allows.
+    uintptr_t bits = reinterpret_cast<uintptr_t>(key) | reinterpret_cast<uintptr_t>(value) |
+                     reinterpret_cast<uintptr_t>(k_cache) | reinterpret_cast<uintptr_t>(v_cache) |
+                     static_cast<uintptr_t>(a.row_bytes);
+    for (int64_t s : strides) bits |= static_cast<uintptr_t>(s * a.elem_bytes);
+    int vec = 16;
+    while (vec > 2 && (bits % vec)) vec >>= 1;
+    const int64_t total = static_cast<int64_t>(batch) * num_tokens * num_kv_heads * 2 * (a.row_bytes / vec);
+    const int64_t want = (total + mv::kAppendThreads - 1) / mv::kAppendThreads;
+    const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(dev.sms) * 16)));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    switch (vec) {
+        case 16: mv::write_paged_kv_kernel<16><<<blocks, mv::kAppendThreads, 0, s>>>(a, total); break;
+        case 8: mv::write_paged_kv_kernel<8><<<blocks, mv::kAppendThreads, 0, s>>>(a, total); break;
+        case 4: mv::write_paged_kv_kernel<4><<<blocks, mv::kAppendThreads, 0, s>>>(a, total); break;
+        default: mv::write_paged_kv_kernel<2><<<blocks, mv::kAppendThreads, 0, s>>>(a, total); break;
+    }
+    cudaError_t err = cudaGetLastError();
+    return err == cudaSuccess ? MV_OK : cuda_fail(err, "append kernel launch");
+}
+
+int mv_device_status(int32_t device, uint32_t* status) {
+    if (!status) return fail(MV_ERR_INVALID_ARGUMENT, "status must not be NULL");
+    int prev = 0;
+    cudaError_t err = cudaGetDevice(&prev);
+    if (err == cudaSuccess && prev != device) err = cudaSetDevice(device);
+    unsigned int value = 0;
+    if (err == cudaSuccess) err = cudaMemcpyFromSymbol(&value, mv::g_device_status, sizeof(value));
+    if (prev != device) cudaSetDevice(prev);
+    if (err != cudaSuccess) return cuda_fail(err, "reading device status");
+    *status = value;
+    return MV_OK;
+}
+
+int mv_clear_device_status(int32_t device) {
+    int prev = 0;
+    cudaError_t err = cudaGetDevice(&prev);
+    if (err == cudaSuccess && prev != device) err = cudaSetDevice(device);
+    const unsigned int zero = 0;
+    if (err == cudaSuccess) err = cudaMemcpyToSymbol(mv::g_device_status, &zero, sizeof(zero));
+    if (prev != device) cudaSetDevice(prev);
+    return err == cudaSuccess ? MV_OK : cuda_fail(err, "clearing device status");
+}
+
+}  // extern "C"

@@ -1,0 +1,291 @@
+// Device-side building blocks shared by the decode and append kernels:
+// launch parameters, index/length helpers, and thin inline-PTX wrappers for
+// mbarriers, TMA tensor loads, ldmatrix, mma.sync and movmatrix on sm_100a.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mv {
+
+// Sticky per-device error bits (MV_DEVICE_STATUS_*), raised by kernels whose
+// bounded waits gave up. Zero at module load; cleared only by the host.
+__device__ unsigned int g_device_status;
+
+constexpr unsigned kStatusWaitTimeout = 1u;
+// A bounded wait gives up after this long; nothing legitimate takes it.
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+
+struct DecodeParams {
+    const void* q;
+    int64_t q_stride_seq;
+    int64_t q_stride_head;
+    const void* k_cache;
+    const void* v_cache;
+    int64_t num_blocks;
+    int kv_heads;
+    int block_size;
+    int head_dim;
+    int group;              // query heads per KV head
+    int q_heads;
+    int batch;
+    const void* block_table;
+    int table_i64;
+    int64_t table_stride;
+    int64_t blocks_per_seq;
+    const void* context_lens;  // nullptr: every sequence has uniform_len tokens
+    int lens_i64;
+    int64_t uniform_len;
+    int64_t max_context_len;
+    float scale_log2;       // softmax scale * log2(e): scores live in the exp2 domain
+    void* out;
+    int64_t out_stride_seq;
+    int64_t out_stride_head;
+    float* part_o;          // [batch, q_heads, max_splits, head_dim]  normalised partial outputs
+    float* part_lse;        // [batch, q_heads, max_splits]            log2-sum-exp of each split
+    int pages_per_split;
+    int max_splits;
+};
+
+struct AppendParams {
+    const void* key;
+    const void* value;
+    int64_t key_stride[3];    // seq, head, token (elements)
+    int64_t value_stride[3];
+    void* k_cache;
+    void* v_cache;
+    int64_t num_blocks;
+    int kv_heads;
+    int block_size;
+    int row_bytes;            // head_dim * element size
+    const void* block_table;
+    int table_i64;
+    int64_t table_stride;
+    int64_t blocks_per_seq;
+    const void* positions;
+    int positions_i64;
+    int positions_end;        // positions hold the end of the sequence, not the start
+    int64_t start;
+    int batch;
+    int num_tokens;
+    int elem_bytes;
+};
+
+__device__ __forceinline__ int64_t load_index(const void* base, int is64, int64_t i) {
+    return is64 ? __ldg(static_cast<const long long*>(base) + i)
+                : static_cast<int64_t>(__ldg(static_cast<const int*>(base) + i));
+}
+
+// How one sequence is cut into split-KV chunks of pages_per_split pages.
+struct SeqSplit {
+    int64_t len;
+    int64_t pages;
+    int splits;
+    int state;  // 0 attend, 1 empty (zeros), 2 invalid (NaN)
+};
+
+__device__ __forceinline__ SeqSplit seq_split(const DecodeParams& p, int b) {
+    SeqSplit s;
+    s.len = p.context_lens ? load_index(p.context_lens, p.lens_i64, b) : p.uniform_len;
+    const bool in_range = s.len >= 0 && s.len <= p.max_context_len &&
+                          s.len <= p.blocks_per_seq * p.block_size;
+    if (!in_range) {
+        s.state = 2;
+    } else if (s.len == 0) {
+        s.state = 1;
+    } else {
+        s.state = 0;
+    }
+    s.pages = s.state == 0 ? (s.len + p.block_size - 1) / p.block_size : 0;
+    const int64_t splits = (s.pages + p.pages_per_split - 1) / p.pages_per_split;
+    s.splits = splits < 1 ? 1 : static_cast<int>(splits);
+    return s;
+}
+
+template <typename T> __device__ __forceinline__ float to_float(T v);
+template <> __device__ __forceinline__ float to_float<float>(float v) { return v; }
+template <> __device__ __forceinline__ float to_float<__half>(__half v) { return __half2float(v); }
+template <> __device__ __forceinline__ float to_float<__nv_bfloat16>(__nv_bfloat16 v) {
+    return __bfloat162float(v);
+}
+
+template <typename T> __device__ __forceinline__ T from_float(float v);
+template <> __device__ __forceinline__ float from_float<float>(float v) { return v; }
+template <> __device__ __forceinline__ __half from_float<__half>(float v) { return __float2half_rn(v); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_float<__nv_bfloat16>(float v) {
+    return __float2bfloat16_rn(v);
+}
+
+// Fill out[b, h*G + g, :] for every g of KV head h with one value (0 or NaN).
+template <typename T>
+__device__ void write_group_constant(const DecodeParams& p, int b, int h, float value) {
+    T* out = static_cast<T*>(p.out);
+    const int total = p.group * p.head_dim;
+    for (int idx = threadIdx.x; idx < total; idx += blockDim.x) {
+        const int g = idx / p.head_dim;
+        const int d = idx - g * p.head_dim;
+        out[b * p.out_stride_seq + (int64_t)(h * p.group + g) * p.out_stride_head + d] =
+            from_float<T>(value);
+    }
+}
+
+// Same for a split's partial result: NaN output and NaN log-sum-exp.
+__device__ inline void write_group_partial_nan(const DecodeParams& p, int b, int h, int split) {
+    const float nan = __int_as_float(0x7fffffff);
+    const int total = p.group * p.head_dim;
+    for (int idx = threadIdx.x; idx < total; idx += blockDim.x) {
+        const int g = idx / p.head_dim;
+        const int d = idx - g * p.head_dim;
+        const int64_t row = ((int64_t)b * p.q_heads + h * p.group + g) * p.max_splits + split;
+        p.part_o[row * p.head_dim + d] = nan;
+        if (d == 0) p.part_lse[row] = nan;
+    }
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
+__device__ __forceinline__ unsigned long long global_timer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// ---------------------------------------------------------------- mbarrier
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// Order this thread's earlier generic-proxy shared-memory accesses before
+// later async-proxy (TMA) writes to the same buffer.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return done != 0;
+}
+
+// Wait for the barrier phase with the given parity; give up after kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long start = global_timer_ns();
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (global_timer_ns() - start > kWaitLimitNs) return false;
+    }
+}
+
+// --------------------------------------------------------------------- TMA
+
+// 5-D tiled TMA load into this CTA's shared memory, completing on `bar`.
+__device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
+                                            int c2, int c3, int c4, uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4, %5, %6}], [%7];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4),
+        "r"(bar)
+        : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tensor_map(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// -------------------------------------------------------- warp-level MMA
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t a) {
+    uint32_t d;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+    return d;
+}
+
+template <typename T> struct MmaOp;
+
+template <> struct MmaOp<__nv_bfloat16> {
+    __device__ __forceinline__ static void run(float (&c)[4], const uint32_t (&a)[4],
+                                               uint32_t b0, uint32_t b1) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, "
+            "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    }
+    // Two fp32 values -> packed pair; `lo` lands in the low half.
+    __device__ __forceinline__ static uint32_t pack(float lo, float hi) {
+        uint32_t r;
+        asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+        return r;
+    }
+};
+
+template <> struct MmaOp<__half> {
+    __device__ __forceinline__ static void run(float (&c)[4], const uint32_t (&a)[4],
+                                               uint32_t b0, uint32_t b1) {
+        asm volatile(
+            "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, "
+            "{%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+            : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    }
+    __device__ __forceinline__ static uint32_t pack(float lo, float hi) {
+        uint32_t r;
+        asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+        return r;
+    }
+};
+
+}  // namespace mv

@@ -1,0 +1,175 @@
+// Paged GQA decode on CUDA cores, for every shape the tensor-core kernel does
+// not take: fp32, odd head_dim (33, 257, ...), page sizes other than 16, GQA
+// groups above 16, unaligned caches.
+//
+// Same work split as the tensor-core kernel -- one CTA per (split, KV head,
+// sequence), so each K/V element is read from HBM once for the whole GQA
+// group -- and the same partial-output format for the merge kernel. Tokens
+// are processed in 32-token tiles staged in shared memory (fp32), with coalesced
+// row loads that follow the page table. The online softmax keeps the
+// normalised running output u/l exactly as the reference kernel does
+// (online_attention.cuh:47-89): each tile rescales the old output by
+// old_mass / new_denominator and adds its weights already divided by the new
+// denominator, so large finite V (+-2e38 in fp32) cannot overflow the state.
+#pragma once
+
+#include "mv_device.cuh"
+
+namespace mv {
+
+constexpr int kSimtThreads = 128;
+constexpr int kSimtTile = 32;  // tokens per tile == warp width (one lane per token)
+
+// Shared-memory floats the SIMT kernel needs (+ token offsets as int64).
+__host__ __device__ inline size_t simt_smem_bytes(int group, int head_dim) {
+    const size_t row = static_cast<size_t>(head_dim) + 1;  // padded: conflict-free column reads
+    const size_t floats = group * row                      // q
+                          + 2 * kSimtTile * row            // K and V tile
+                          + group * kSimtTile              // scores, then weights
+                          + static_cast<size_t>(group) * head_dim  // running output
+                          + 3 * static_cast<size_t>(group);         // m, l, rescale
+    return ((floats * 4 + 15) / 16) * 16 + kSimtTile * sizeof(int64_t);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kSimtThreads) paged_decode_simt_kernel(const DecodeParams p) {
+    extern __shared__ __align__(16) float sm[];
+    __shared__ int cta_bad;
+    const int G = p.group;
+    const int D = p.head_dim;
+    const int DP = D + 1;
+    const int bs = p.block_size;
+    float* q_s = sm;
+    float* k_s = q_s + G * DP;
+    float* v_s = k_s + kSimtTile * DP;
+    float* p_s = v_s + kSimtTile * DP;
+    float* acc = p_s + G * kSimtTile;
+    float* m_s = acc + G * D;
+    float* l_s = m_s + G;
+    float* r_s = l_s + G;
+    int64_t* off_s = reinterpret_cast<int64_t*>(
+        reinterpret_cast<uint8_t*>(sm) + simt_smem_bytes(G, D) - kSimtTile * sizeof(int64_t));
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    const int split = blockIdx.x;
+    const int h = blockIdx.y;
+    const int b = blockIdx.z;
+
+    const SeqSplit seq = seq_split(p, b);
+    if (split >= seq.splits) return;
+    if (seq.state != 0) {
+        write_group_constant<T>(p, b, h, seq.state == 1 ? 0.0f : __int_as_float(0x7fffffff));
+        return;
+    }
+    const bool single = seq.splits == 1;
+    const int64_t page_begin = static_cast<int64_t>(split) * p.pages_per_split;
+    const int64_t page_end_raw = page_begin + p.pages_per_split;
+    const int64_t page_end = page_end_raw < seq.pages ? page_end_raw : seq.pages;
+
+    if (tid == 0) cta_bad = 0;
+    __syncthreads();
+    for (int64_t pg = page_begin + tid; pg < page_end; pg += blockDim.x) {
+        const int64_t id = load_index(p.block_table, p.table_i64, b * p.table_stride + pg);
+        if (id < 0 || id >= p.num_blocks) atomicOr(&cta_bad, 1);
+    }
+    __syncthreads();
+    if (cta_bad) {
+        if (single) write_group_constant<T>(p, b, h, __int_as_float(0x7fffffff));
+        else write_group_partial_nan(p, b, h, split);
+        return;
+    }
+
+    const T* q = static_cast<const T*>(p.q) + b * p.q_stride_seq;
+    for (int idx = tid; idx < G * D; idx += blockDim.x) {
+        const int g = idx / D;
+        const int d = idx - g * D;
+        q_s[g * DP + d] = to_float<T>(q[static_cast<int64_t>(h * G + g) * p.q_stride_head + d]);
+        acc[idx] = 0.0f;
+    }
+    for (int g = tid; g < G; g += blockDim.x) {
+        m_s[g] = -INFINITY;
+        l_s[g] = 0.0f;
+    }
+
+    const T* kc = static_cast<const T*>(p.k_cache);
+    const T* vc = static_cast<const T*>(p.v_cache);
+    const int64_t tok_begin = page_begin * bs;
+    const int64_t tok_end_raw = page_end * bs;
+    const int64_t tok_end = tok_end_raw < seq.len ? tok_end_raw : seq.len;
+
+    for (int64_t t0 = tok_begin; t0 < tok_end; t0 += kSimtTile) {
+        const int count = static_cast<int>(tok_end - t0 < kSimtTile ? tok_end - t0 : kSimtTile);
+        if (tid < count) {
+            const int64_t tok = t0 + tid;
+            const int64_t pg = tok / bs;
+            const int64_t id = load_index(p.block_table, p.table_i64, b * p.table_stride + pg);
+            off_s[tid] = ((id * p.kv_heads + h) * bs + (tok - pg * bs)) * D;
+        }
+        __syncthreads();
+        for (int idx = tid; idx < count * D; idx += blockDim.x) {
+            const int t = idx / D;
+            const int d = idx - t * D;
+            k_s[t * DP + d] = to_float<T>(kc[off_s[t] + d]);
+            v_s[t * DP + d] = to_float<T>(vc[off_s[t] + d]);
+        }
+        __syncthreads();
+        for (int idx = tid; idx < G * kSimtTile; idx += blockDim.x) {
+            const int g = idx / kSimtTile;
+            const int t = idx - g * kSimtTile;
+            float s = -INFINITY;
+            if (t < count) {
+                const float* qr = q_s + g * DP;
+                const float* kr = k_s + t * DP;
+                float dot = 0.0f;
+                for (int d = 0; d < D; ++d) dot = fmaf(qr[d], kr[d], dot);
+                s = dot * p.scale_log2;
+            }
+            p_s[idx] = s;
+        }
+        __syncthreads();
+        for (int g = warp; g < G; g += kSimtThreads / 32) {
+            const float s = p_s[g * kSimtTile + lane];
+            const float m_old = m_s[g];
+            const float m_new = fmaxf(m_old, warp_max(s));
+            const float e = fast_exp2(s - m_new);
+            const float tile_mass = warp_sum(e);
+            const float old_mass = m_old == -INFINITY ? 0.0f : fast_exp2(m_old - m_new) * l_s[g];
+            const float l_new = old_mass + tile_mass;
+            p_s[g * kSimtTile + lane] = e / l_new;
+            __syncwarp();
+            if (lane == 0) {
+                m_s[g] = m_new;
+                l_s[g] = l_new;
+                r_s[g] = old_mass / l_new;
+            }
+        }
+        __syncthreads();
+        for (int idx = tid; idx < G * D; idx += blockDim.x) {
+            const int g = idx / D;
+            const int d = idx - g * D;
+            const float* w = p_s + g * kSimtTile;
+            float a = acc[idx] * r_s[g];
+            for (int t = 0; t < count; ++t) a = fmaf(w[t], v_s[t * DP + d], a);
+            acc[idx] = a;
+        }
+        __syncthreads();
+    }
+
+    T* out = static_cast<T*>(p.out);
+    for (int idx = tid; idx < G * D; idx += blockDim.x) {
+        const int g = idx / D;
+        const int d = idx - g * D;
+        if (single) {
+            out[b * p.out_stride_seq + static_cast<int64_t>(h * G + g) * p.out_stride_head + d] =
+                from_float<T>(acc[idx]);
+        } else {
+            const int64_t row = (static_cast<int64_t>(b) * p.q_heads + h * G + g) * p.max_splits + split;
+            p.part_o[row * D + d] = acc[idx];
+            if (d == 0) p.part_lse[row] = m_s[g] + log2f(l_s[g]);
+        }
+    }
+}
+
+}  // namespace mv

@@ -1,0 +1,282 @@
+"""Paged GQA decode attention: drop-in for the paged path of ``micro_vllm.cuda_attention``.
+
+Reference-shaped API (same names, arguments, error types and messages):
+
+* ``decode_attention_paged(query, cache, *, layer_idx)`` --
+  src/micro_vllm/cuda_attention.py:116-135 with ``_checked_paged_query``
+  (:86-113). Accepts the reference's ``PagedKVCache`` (or this package's
+  mirror of it) and reads its pages in place.
+* ``_load_extension()._decode_attention_paged(query, key_pages, value_pages,
+  table, length)`` -- the native entry point and its metadata checks
+  (src/micro_vllm/csrc/decode_attention.cpp:17-124, 147-152).
+
+Batched API (new surface; the reference is batch 1):
+
+* ``paged_decode_attention(query, key_cache, value_cache, block_table,
+  context_lens, scale)`` over one shared page pool, with bf16 support.
+
+All of them run libmvdecode.so's sm_100a kernels through the C ABI
+(``mv_paged_decode``): the TMA + tensor-core split-KV kernel for fp16/bf16
+with block size 16 and head_dim 64/128/256, the CUDA-core split-KV kernel for
+every other shape (fp32, odd head_dim or page size). Importing this module
+loads nothing; there is no CPU path.
+"""
+import ctypes
+from functools import lru_cache
+
+import torch
+
+from . import _native
+from ._tensors import DTYPE_CODES, INDEX_CODES, current_stream_handle
+
+_INT64_MAX = 2 ** 63 - 1
+
+
+def _check(condition, message):
+    if not condition:
+        raise RuntimeError(message)
+
+
+def _validate_storage(tensor):
+    _check(tensor.is_cuda, 'decode_attention requires CUDA tensors')
+    _check(tensor.layout == torch.strided, 'decode_attention requires strided tensors')
+    _check(not tensor.requires_grad, 'decode_attention does not support gradients')
+    _check(not tensor.is_neg(), 'decode_attention does not support lazy negative views')
+
+
+def _validate_gqa_tensor(tensor):
+    _validate_storage(tensor)
+    _check(tensor.dtype in (torch.float32, torch.float16), 'GQA requires float32 or float16 tensors')
+
+
+def _validate_gqa_strides(tensor):
+    _check(tensor.stride(3) == 1, 'GQA requires feature stride 1')
+    _check(all(tensor.stride(d) >= 0 for d in range(3)), 'GQA requires nonnegative outer strides')
+
+
+def _validate_paged_table(table, key, query, length):
+    _validate_storage(table)
+    _check(table.dtype == torch.int64, 'page table requires int64')
+    _check(table.dim() == 1, 'page table must be one-dimensional')
+    _check(table.is_contiguous(), 'page table must be contiguous')
+    _check(table.device == query.device, 'Q, K/V pages and table must use the same device')
+    _check(table.shape[0] > 0, 'page table length must be positive')
+    _check(table.shape[0] <= key.shape[0], 'page table length exceeds physical pages')
+    _check(table.shape[0] <= _INT64_MAX // key.shape[2], 'page table capacity exceeds int64 bounds')
+    _check(length > 0, 'context length must be positive')
+    _check(length <= table.shape[0] * key.shape[2], 'context length exceeds page table capacity')
+
+
+def _validate_paged_inputs(query, key, value, table, length):
+    for tensor in (query, key, value):
+        _validate_gqa_tensor(tensor)
+    _check(query.dtype == key.dtype == value.dtype, 'Q and K/V pages must use the same dtype')
+    _check(query.device == key.device == value.device, 'Q and K/V pages must use the same device')
+    _check(query.dim() == 4 and key.dim() == 4 and value.dim() == 4,
+           'Q must have shape [1,Hq,1,D] and K/V pages shape [P,Hkv,B,D]')
+    _validate_gqa_strides(query)
+    _check(key.is_contiguous() and value.is_contiguous(), 'K/V pages must be contiguous')
+    _check(query.shape[0] == 1, 'paged attention requires batch size 1')
+    _check(query.numel() > 0 and key.numel() > 0 and value.numel() > 0,
+           'page dimensions, head counts, and head dimension must be positive')
+    _check(query.shape[2] == 1, 'paged decode requires exactly one query token')
+    _check(key.shape == value.shape, 'K and V pages must have the same shape')
+    _check(query.shape[3] == key.shape[3], 'Q and K/V pages must share the head dimension')
+    _check(query.shape[1] % key.shape[1] == 0, 'query head count must be divisible by KV head count')
+    _validate_paged_table(table, key, query, length)
+
+
+def _run(query3, q_strides, key_cache, value_cache, block_table, table_stride, blocks_per_seq,
+         context_lens, max_context_len, scale, out, out_strides, pages_per_split=0, flags=0):
+    """Plan, allocate the split-KV workspace, and launch ``mv_paged_decode``."""
+    lib = _native.library()
+    batch, q_heads, dim = query3
+    num_blocks, kv_heads, block_size, _ = key_cache.shape
+    dtype = DTYPE_CODES[key_cache.dtype]
+    device = key_cache.device
+    with torch.cuda.device(device):
+        size = ctypes.c_size_t(0)
+        _native.check(lib.mv_paged_decode_workspace_size(
+            batch, q_heads, kv_heads, dim, block_size, max_context_len, pages_per_split, flags,
+            dtype, ctypes.byref(size)))
+        workspace = (torch.empty(size.value, dtype=torch.uint8, device=device)
+                     if size.value else None)
+        _native.check(lib.mv_paged_decode(
+            out.q_ptr, q_strides[0], q_strides[1],
+            key_cache.data_ptr(), value_cache.data_ptr(), num_blocks,
+            kv_heads, block_size, dim,
+            block_table.data_ptr(), INDEX_CODES[block_table.dtype], table_stride, blocks_per_seq,
+            context_lens.data_ptr() if context_lens is not None else None,
+            INDEX_CODES[context_lens.dtype] if context_lens is not None else 0,
+            max_context_len, batch, q_heads, float(scale),
+            out.out_ptr, out_strides[0], out_strides[1],
+            workspace.data_ptr() if workspace is not None else None, size.value,
+            pages_per_split, flags, dtype, current_stream_handle(device)))
+
+
+class _Pointers:
+    __slots__ = ('q_ptr', 'out_ptr')
+
+    def __init__(self, q_ptr, out_ptr):
+        self.q_ptr = q_ptr
+        self.out_ptr = out_ptr
+
+
+class _DecodeAttentionExtension:
+    """The object ``_load_extension()`` returns, shaped like the reference's pybind module."""
+
+    def _decode_attention_paged(self, query, key_pages, value_pages, table, length):
+        """Internal paged decode for Q [1,Hq,1,D] over pages [P,Hkv,B,D]; fresh output."""
+        _validate_paged_inputs(query, key_pages, value_pages, table, length)
+        output = torch.empty(query.shape, dtype=query.dtype, device=query.device)
+        _run((1, query.shape[1], query.shape[3]), (0, query.stride(1)), key_pages, value_pages,
+             table, table.numel(), table.numel(), None, int(length),
+             query.shape[3] ** -0.5, _Pointers(query.data_ptr(), output.data_ptr()),
+             (0, output.stride(1)))
+        return output
+
+
+@lru_cache(maxsize=1)
+def _load_extension() -> _DecodeAttentionExtension:
+    _native.library()
+    return _DecodeAttentionExtension()
+
+
+def _is_paged_cache(cache) -> bool:
+    """The reference's PagedKVCache, this package's mirror, or the same shape of object."""
+    from .paged_kv_cache import PagedKVCache
+
+    if isinstance(cache, PagedKVCache):
+        return True
+    return all(hasattr(cache, name) for name in
+               ('_keys', '_values', '_device_page_table', 'length', 'num_kv_heads', 'head_dim',
+                'dtype', 'device')) and type(cache).__name__ == 'PagedKVCache'
+
+
+def _checked_paged_query(query, cache, layer_idx):
+    if not _is_paged_cache(cache):
+        raise ValueError('paged decode requires an owned PagedKVCache')
+    length = cache.length(layer_idx)
+    if length <= 0:
+        raise ValueError('paged decode requires a nonempty cache layer')
+    if not isinstance(query, torch.Tensor):
+        raise ValueError('query must be a tensor')
+    if query.layout != torch.strided or query.is_nested:
+        raise ValueError('query must use dense strided storage')
+    if (query.ndim != 4 or query.shape[0] != 1 or query.shape[1] <= 0
+            or query.shape[2] != 1 or query.shape[3] != cache.head_dim):
+        raise ValueError('query shape must be [1, query_heads, 1, cache.head_dim]')
+    if query.shape[1] % cache.num_kv_heads:
+        raise ValueError('query head count must be divisible by KV head count')
+    if cache.dtype not in (torch.float16, torch.float32) or query.dtype != cache.dtype:
+        raise ValueError('query and cache require matching float16 or float32 dtype')
+    if query.requires_grad:
+        raise ValueError('paged decode does not support gradients')
+    if query.is_neg():
+        raise ValueError('paged decode does not support lazy negative views')
+    if query.stride(-1) != 1 or any(stride < 0 for stride in query.stride()[:-1]):
+        raise ValueError('query requires feature stride 1 and nonnegative outer strides')
+    if cache.device.type != 'cuda' or query.device != cache.device:
+        raise ValueError('paged decode requires a CUDA cache and query on the same device')
+    return length
+
+
+@torch.inference_mode()
+def decode_attention_paged(query: torch.Tensor, cache, *, layer_idx: int) -> torch.Tensor:
+    """Attend the latest query directly over one owned PagedKVCache layer.
+
+    Q is [1,Hq,1,D]; Hq is divisible by the cache's KV head count; every
+    cached token including the current one is visible; fp16/fp32 I/O with fp32
+    accumulation. No gather, KV repetition, host table read-back or
+    context-sized score buffer. Output is fresh contiguous storage with the
+    query's shape, device and dtype; inputs are unchanged.
+    """
+    length = _checked_paged_query(query, cache, layer_idx)
+    return _load_extension()._decode_attention_paged(
+        query, cache._keys[layer_idx], cache._values[layer_idx],
+        cache._device_page_table, length)
+
+
+def paged_decode_plan(query_heads, key_cache, context_bound, *, batch, pages_per_split=0,
+                      force_simt=False):
+    """(path, pages_per_split, max_splits) that ``paged_decode_attention`` would use."""
+    lib = _native.library()
+    num_blocks, kv_heads, block_size, dim = key_cache.shape
+    path, pps, splits = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
+    with torch.cuda.device(key_cache.device):
+        _native.check(lib.mv_paged_decode_plan(
+            batch, query_heads, kv_heads, dim, block_size, context_bound, pages_per_split,
+            _native.FLAG_FORCE_SIMT if force_simt else 0, DTYPE_CODES[key_cache.dtype],
+            key_cache.data_ptr(), key_cache.data_ptr(), ctypes.byref(path), ctypes.byref(pps),
+            ctypes.byref(splits)))
+    return ('tma_mma' if path.value == _native.PATH_TMA_MMA else 'simt'), pps.value, splits.value
+
+
+def paged_decode_attention(query: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
+                           block_table: torch.Tensor, context_lens: torch.Tensor,
+                           scale: float | None = None, *, max_context_len: int | None = None,
+                           out: torch.Tensor | None = None, pages_per_split: int = 0,
+                           force_simt: bool = False) -> torch.Tensor:
+    """Batched paged GQA decode over one shared page pool.
+
+    query: [B, Hq, D] (or [B, Hq, 1, D]) CUDA fp32/fp16/bf16, feature stride 1.
+    key_cache/value_cache: [P, Hkv, bs, D] contiguous, same dtype.
+    block_table: [B, max_blocks] int32/int64, contiguous rows.
+    context_lens: [B] int32/int64 device tensor; tokens attended per sequence,
+    including this step's appended token.
+    scale: softmax scale (default head_dim ** -0.5, the reference's).
+    max_context_len: host-side upper bound on context_lens; defaults to the
+    table capacity max_blocks * bs, so no device read-back is needed. Lengths
+    above it produce NaN (the split plan cannot cover them).
+    out: optional [B, Hq, D] destination (feature stride 1).
+    Returns out, or a fresh [B, Hq, D] tensor of the query's dtype.
+    """
+    squeeze = query.dim() == 4
+    q = query[:, :, 0, :] if squeeze else query
+    _check(isinstance(q, torch.Tensor) and q.dim() == 3, 'query must be [B, Hq, D] or [B, Hq, 1, D]')
+    if squeeze:
+        _check(query.shape[2] == 1, 'paged decode requires exactly one query token')
+    for tensor in (q, key_cache, value_cache, block_table, context_lens):
+        _validate_storage(tensor)
+    _check(q.dtype in DTYPE_CODES, 'query must be float32, float16 or bfloat16')
+    _check(q.dtype == key_cache.dtype == value_cache.dtype, 'Q and K/V pages must use the same dtype')
+    _check(q.device == key_cache.device == value_cache.device == block_table.device
+           == context_lens.device, 'Q, K/V pages, table and lengths must use the same device')
+    _check(key_cache.dim() == 4 and key_cache.shape == value_cache.shape,
+           'K/V pages must both have shape [P,Hkv,B,D]')
+    _check(key_cache.is_contiguous() and value_cache.is_contiguous(), 'K/V pages must be contiguous')
+    batch, q_heads, dim = q.shape
+    num_blocks, kv_heads, block_size, kdim = key_cache.shape
+    _check(batch > 0 and q_heads > 0 and dim > 0 and key_cache.numel() > 0,
+           'page dimensions, head counts, and head dimension must be positive')
+    _check(dim == kdim, 'Q and K/V pages must share the head dimension')
+    _check(q_heads % kv_heads == 0, 'query head count must be divisible by KV head count')
+    _check(q.stride(2) == 1 and q.stride(0) >= 0 and q.stride(1) >= 0,
+           'query requires feature stride 1 and nonnegative outer strides')
+    _check(block_table.dtype in INDEX_CODES and context_lens.dtype in INDEX_CODES,
+           'block table and context lengths must be int32 or int64')
+    _check(block_table.dim() == 2 and block_table.shape[0] == batch and block_table.shape[1] > 0,
+           'block table must have shape [B, max_blocks]')
+    _check(block_table.stride(1) == 1 and (batch == 1 or block_table.stride(0) >= block_table.shape[1]),
+           'block table rows must be contiguous')
+    _check(context_lens.shape == (batch,) and context_lens.is_contiguous(),
+           'context lengths must be a contiguous [B] tensor')
+    capacity = block_table.shape[1] * block_size
+    if max_context_len is None:
+        max_context_len = capacity
+    _check(0 <= max_context_len, 'max_context_len must be nonnegative')
+    if scale is None:
+        scale = dim ** -0.5
+    if out is None:
+        out = torch.empty((batch, q_heads, dim), dtype=q.dtype, device=q.device)
+    else:
+        _validate_storage(out)
+        _check(out.shape == (batch, q_heads, dim) and out.dtype == q.dtype and out.device == q.device,
+               'out must be a [B, Hq, D] tensor of the query dtype and device')
+        _check(out.stride(2) == 1, 'out requires feature stride 1')
+    _run((batch, q_heads, dim), (q.stride(0), q.stride(1)), key_cache, value_cache, block_table,
+         block_table.stride(0), block_table.shape[1], context_lens, int(max_context_len), scale,
+         _Pointers(q.data_ptr(), out.data_ptr()), (out.stride(0), out.stride(1)),
+         pages_per_split=int(pages_per_split),
+         flags=_native.FLAG_FORCE_SIMT if force_simt else 0)
+    return out

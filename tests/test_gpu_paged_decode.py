@@ -1,0 +1,312 @@
+"""GPU parity: append + paged decode through the C ABI against the CPU oracle.
+
+Every case regenerates the seeded inputs, appends the step's token with the
+batched append kernel, checks the pools bit-for-bit against the digests the
+reference's own code produced (tests/golden/), then checks attention against
+the oracle at the parity bar (fp32 1e-5 relative, fp16 2e-3, bf16 2e-2 max-abs
+of the fp32 math), on both kernels and with forced split-KV.
+"""
+import numpy as np
+import pytest
+import torch
+
+from oracle import decode_float, decode_fp64_per_head, to_float32
+from tests.golden.cases import array_digest, make_inputs
+from tests.golden.make_golden import GOLDEN_CASES
+from tests.helpers import as_float, assert_attention_close, to_numpy, to_torch, workload_tensors
+
+pytestmark = pytest.mark.gpu
+
+
+def _native():
+    from micro_vllm_b200 import cuda_attention, cuda_paged_cache
+    return cuda_attention, cuda_paged_cache
+
+
+def _fixture(name):
+    from pathlib import Path
+    with np.load(Path(__file__).resolve().parent / 'golden' / f'{name}.npz') as data:
+        return {key: data[key] for key in data.files}
+
+
+def _append_and_decode(inputs, *, force_simt=False, pages_per_split=0):
+    attention, cache = _native()
+    t = workload_tensors(inputs)
+    cache.write_paged_kv(t['key_new'], t['value_new'], t['key_pool'], t['value_pool'],
+                         t['block_table'], positions=t['context_lens'], positions_are_end=True)
+    out = attention.paged_decode_attention(
+        t['q'], t['key_pool'], t['value_pool'], t['block_table'], t['context_lens'],
+        force_simt=force_simt, pages_per_split=pages_per_split)
+    torch.cuda.synchronize()
+    return t, out
+
+
+def _oracle(inputs, key_pool, value_pool):
+    dim = inputs['q'].shape[-1]
+    return decode_float(inputs['q'], key_pool, value_pool, inputs['block_table'],
+                        inputs['context_lens'], dim ** -0.5, inputs['spec']['dtype'])
+
+
+@pytest.mark.parametrize('name', GOLDEN_CASES)
+@pytest.mark.parametrize('mode', ['auto', 'simt', 'split4'])
+def test_golden_workloads(name, mode):
+    inputs = make_inputs(name)
+    dtype = inputs['spec']['dtype']
+    t, out = _append_and_decode(inputs, force_simt=mode == 'simt',
+                                pages_per_split=4 if mode == 'split4' else 0)
+    fixture = _fixture(name)
+    key_pool = to_numpy(t['key_pool'])
+    value_pool = to_numpy(t['value_pool'])
+    # The append is bit-exact against the pools the reference's own append produced.
+    assert array_digest(key_pool) == str(fixture['key_pool_digest'])
+    assert array_digest(value_pool) == str(fixture['value_pool_digest'])
+    expected = _oracle(inputs, key_pool, value_pool)
+    assert_attention_close(as_float(out), expected, dtype)
+    # And close to the reference's own output within its own dtype rounding.
+    reference = to_float32(fixture['out'], dtype)
+    bound = {'float32': 2e-5, 'float16': 4e-3, 'bfloat16': 0.15}[dtype]
+    assert np.max(np.abs(as_float(out) - reference)) <= bound
+
+
+def test_tensor_core_path_is_selected_for_qwen_geometry():
+    attention, _ = _native()
+    inputs = make_inputs('qwen7b_bf16_small')
+    t = workload_tensors(inputs)
+    path, pps, splits = attention.paged_decode_plan(28, t['key_pool'], 4096, batch=64)
+    assert path == 'tma_mma'
+    assert splits >= 2
+
+
+@pytest.mark.parametrize('pages_per_split', [1, 4, 8, 12, 128])
+def test_split_counts_agree(pages_per_split):
+    inputs = make_inputs('qwen7b_bf16_small')
+    _, reference_out = _append_and_decode(inputs, pages_per_split=128)
+    inputs = make_inputs('qwen7b_bf16_small')
+    t, out = _append_and_decode(inputs, pages_per_split=pages_per_split)
+    expected = _oracle(inputs, to_numpy(t['key_pool']), to_numpy(t['value_pool']))
+    assert_attention_close(as_float(out), expected, 'bfloat16')
+    assert np.max(np.abs(as_float(out) - as_float(reference_out))) <= 1e-2
+
+
+@pytest.mark.parametrize('name', ['qwen7b_bf16_small', 'qwen05b_fp32', 'edge_bs4_d257_fp16'])
+def test_invalid_page_id_poisons_only_that_sequence(name):
+    attention, _ = _native()
+    inputs = make_inputs(name)
+    spec = inputs['spec']
+    t = workload_tensors(inputs)
+    lens = inputs['context_lens']
+    victim = int(np.argmax(lens))
+    used = -(-int(lens[victim]) // spec['block_size'])
+    for bad in (-1, t['key_pool'].shape[0], 2 ** 31 - 1):
+        table = t['block_table'].clone()
+        table[victim, used - 1] = bad
+        for force_simt in (False, True):
+            out = attention.paged_decode_attention(t['q'], t['key_pool'], t['value_pool'], table,
+                                                   t['context_lens'], force_simt=force_simt,
+                                                   pages_per_split=4)
+            values = as_float(out)
+            assert np.isnan(values[victim]).all()
+            others = np.delete(values, victim, axis=0)
+            assert np.isfinite(others).all()
+
+
+def test_zero_and_out_of_range_lengths():
+    attention, _ = _native()
+    inputs = make_inputs('qwen7b_bf16_small')
+    t = workload_tensors(inputs)
+    capacity = t['block_table'].shape[1] * 16
+    lens = t['context_lens'].clone()
+    lens[0] = 0
+    lens[1] = capacity + 1
+    lens[2] = -5
+    for force_simt in (False, True):
+        out = as_float(attention.paged_decode_attention(
+            t['q'], t['key_pool'], t['value_pool'], t['block_table'], lens, force_simt=force_simt))
+        assert (out[0] == 0).all()
+        assert np.isnan(out[1]).all() and np.isnan(out[2]).all()
+
+
+def test_lengths_above_the_planned_bound_are_nan_not_out_of_bounds():
+    attention, _ = _native()
+    inputs = make_inputs('qwen7b_bf16_small')
+    t = workload_tensors(inputs)
+    out = as_float(attention.paged_decode_attention(
+        t['q'], t['key_pool'], t['value_pool'], t['block_table'], t['context_lens'],
+        max_context_len=100))
+    lens = inputs['context_lens']
+    assert np.isnan(out[lens > 100]).all()
+    assert np.isfinite(out[lens <= 100]).all()
+
+
+@pytest.mark.parametrize('dtype', ['bfloat16', 'float16', 'float32'])
+def test_nan_in_unused_slots_does_not_leak(dtype):
+    """Slots past the context in the last page are NaN; P*V must not see them."""
+    attention, _ = _native()
+    spec = dict(make_inputs('qwen7b_bf16_small')['spec'])
+    spec.update(dtype=dtype, lens=('fixed', [5, 33, 47]), seed=77)
+    inputs = make_inputs(spec)
+    t = workload_tensors(inputs)
+    bs = spec['block_size']
+    lens = inputs['context_lens']
+    for b in range(spec['batch']):
+        last = int(inputs['block_table'][b, (lens[b] - 1) // bs])
+        slot = int(lens[b] % bs)
+        if slot:
+            t['key_pool'][last, :, slot:] = float('nan')
+            t['value_pool'][last, :, slot:] = float('nan')
+    for force_simt in (False, True):
+        out = attention.paged_decode_attention(t['q'], t['key_pool'], t['value_pool'],
+                                               t['block_table'], t['context_lens'],
+                                               force_simt=force_simt)
+        expected = _oracle(inputs, to_numpy(t['key_pool']), to_numpy(t['value_pool']))
+        assert np.isfinite(as_float(out)).all()
+        assert_attention_close(as_float(out), expected, dtype)
+
+
+@pytest.mark.parametrize('dtype', [torch.float16, torch.bfloat16])
+def test_large_logits_pick_the_argmax_value_exactly(dtype):
+    """test/test_cuda_gqa_precision.py:92-102 on pages: a one-hot softmax returns V exactly."""
+    attention, _ = _native()
+    big, up, down = (500, 501, 499) if dtype == torch.float16 else (8, 9, 7)
+    length = 65
+    pages = (length + 15) // 16
+    q = torch.full((1, 14, 64), big, dtype=dtype, device='cuda')
+    q[:, 1::2].neg_()
+    logical_k = torch.full((2, pages * 16, 64), big, dtype=dtype, device='cuda')
+    logical_k[:, 0] = up
+    logical_k[:, length - 1] = down
+    k = logical_k.reshape(2, pages, 16, 64).permute(1, 0, 2, 3).contiguous()
+    v = torch.randn(pages, 2, 16, 64, device='cuda').to(dtype)
+    table = torch.arange(pages, device='cuda', dtype=torch.int32)[None]
+    lens = torch.tensor([length], device='cuda', dtype=torch.int32)
+    vflat = v.permute(1, 0, 2, 3).reshape(2, pages * 16, 64)
+    for force_simt in (False, True):
+        out = attention.paged_decode_attention(q, k, v, table, lens, force_simt=force_simt)
+        # even heads (q > 0) pick the largest key (token 0), odd heads the smallest (last token)
+        for head in range(14):
+            token = 0 if head % 2 == 0 else length - 1
+            assert torch.equal(out[0, head], vflat[head // 7, token])
+
+
+def test_online_state_is_not_rounded_per_page():
+    """Mean of 32 ones and 4065 copies of 1 + 2^-10 is exactly 1 + 2^-10 in fp16
+    (test/test_cuda_gqa_precision.py:69-79); rounding the running state to fp16
+    per tile would lose the small updates."""
+    attention, _ = _native()
+    length = 4097
+    pages = (length + 15) // 16
+    q = torch.zeros(1, 14, 64, dtype=torch.float16, device='cuda')
+    k = torch.zeros(pages, 2, 16, 64, dtype=torch.float16, device='cuda')
+    v = torch.full((pages, 2, 16, 64), 1 + 2 ** -10, dtype=torch.float16, device='cuda')
+    v[:2] = 1  # tokens 0..31
+    table = torch.arange(pages, device='cuda', dtype=torch.int32)[None]
+    lens = torch.tensor([length], device='cuda', dtype=torch.int32)
+    for force_simt in (False, True):
+        for pps in (0, 4, 128):
+            out = attention.paged_decode_attention(q, k, v, table, lens, force_simt=force_simt,
+                                                   pages_per_split=pps)
+            assert torch.equal(out, torch.full_like(out, 1 + 2 ** -10))
+
+
+def test_fp32_large_values_stay_finite():
+    """+-2e38 V with uniform weights: the normalised running state cannot overflow
+    (test/test_cuda_paged_attention.py:102-112)."""
+    attention, _ = _native()
+    length = 65
+    pages = (length + 3) // 4
+    q = torch.zeros(1, 6, 33, device='cuda')
+    k = torch.zeros(pages, 2, 4, 33, device='cuda')
+    v = torch.empty(pages, 2, 4, 33, device='cuda')
+    v[:, 0] = 2e38
+    v[:, 1] = -2e38
+    table = torch.arange(pages, device='cuda', dtype=torch.int64)[None]
+    lens = torch.tensor([length], device='cuda', dtype=torch.int64)
+    for pps in (0, 2):
+        out = attention.paged_decode_attention(q, k, v, table, lens, pages_per_split=pps)
+        assert torch.isfinite(out).all()
+        expected = torch.empty_like(out)
+        expected[0, :3] = 2e38
+        expected[0, 3:] = -2e38
+        torch.testing.assert_close(out, expected, rtol=5e-6, atol=0)
+
+
+@pytest.mark.parametrize('heads,dim,dtype', [
+    ((1, 1), 33, 'float32'), ((4, 4), 64, 'bfloat16'), ((14, 2), 64, 'float16'),
+    ((14, 1), 64, 'bfloat16'), ((16, 1), 128, 'bfloat16'), ((24, 1), 128, 'bfloat16'),
+    ((6, 2), 257, 'float16'), ((8, 8), 256, 'bfloat16'), ((32, 4), 256, 'float16'),
+])
+def test_head_ratios_and_dims(heads, dim, dtype):
+    spec = dict(batch=3, q_heads=heads[0], kv_heads=heads[1], head_dim=dim, block_size=16,
+                pool=('factor', 1.5), lens=('fixed', [1, 40, 250]), dtype=dtype,
+                value_scale=1.0, seed=900 + dim + heads[0])
+    inputs = make_inputs(spec)
+    t, out = _append_and_decode(inputs)
+    expected = _oracle(inputs, to_numpy(t['key_pool']), to_numpy(t['value_pool']))
+    assert_attention_close(as_float(out), expected, dtype)
+
+
+def test_fp64_per_head_restatement_agrees_on_fp32():
+    """Cross-check against the reference tests' fp64 per-head loop (test_cuda_gqa.py:14-23)."""
+    inputs = make_inputs('edge_bs3_d33_fp32')
+    t, out = _append_and_decode(inputs)
+    key_pool, value_pool = to_numpy(t['key_pool']), to_numpy(t['value_pool'])
+    from oracle import gather_sequence
+    bs = inputs['spec']['block_size']
+    for b, length in enumerate(inputs['context_lens']):
+        k = gather_sequence(key_pool, inputs['block_table'][b], int(length))
+        v = gather_sequence(value_pool, inputs['block_table'][b], int(length))
+        expected = decode_fp64_per_head(inputs['q'][b], k, v)
+        np.testing.assert_allclose(as_float(out)[b], expected, rtol=2e-4, atol=2e-5)
+
+
+def test_strided_and_broadcast_queries_and_out():
+    attention, _ = _native()
+    inputs = make_inputs('qwen7b_bf16_small')
+    t = workload_tensors(inputs)
+    q = t['q']
+    base = attention.paged_decode_attention(q, t['key_pool'], t['value_pool'], t['block_table'],
+                                            t['context_lens'])
+    storage = torch.zeros(3, 60, 140, dtype=q.dtype, device='cuda')
+    strided = storage[:, 1:57:2, 5:133]
+    strided.copy_(q)
+    out_storage = torch.zeros(3, 30, 150, dtype=q.dtype, device='cuda')
+    out = out_storage[:, 1:29, 3:131]
+    result = attention.paged_decode_attention(strided, t['key_pool'], t['value_pool'],
+                                              t['block_table'], t['context_lens'], out=out)
+    assert result.data_ptr() == out.data_ptr()
+    assert torch.equal(out, base)
+    assert (out_storage[:, 0] == 0).all() and (out_storage[:, :, :3] == 0).all()
+    broadcast = q[:, :1].expand_as(q)
+    assert broadcast.stride(1) == 0
+    got = attention.paged_decode_attention(broadcast, t['key_pool'], t['value_pool'],
+                                           t['block_table'], t['context_lens'])
+    again = attention.paged_decode_attention(broadcast.contiguous(), t['key_pool'],
+                                             t['value_pool'], t['block_table'], t['context_lens'])
+    assert torch.equal(got, again)
+
+
+def test_int64_tables_and_lengths_match_int32():
+    attention, _ = _native()
+    inputs = make_inputs('qwen72b_bf16_small')
+    t = workload_tensors(inputs)
+    a = attention.paged_decode_attention(t['q'], t['key_pool'], t['value_pool'], t['block_table'],
+                                         t['context_lens'])
+    b = attention.paged_decode_attention(t['q'], t['key_pool'], t['value_pool'],
+                                         t['block_table'].long(), t['context_lens'].long())
+    assert torch.equal(a, b)
+
+
+def test_inputs_unchanged_and_repeatable():
+    attention, _ = _native()
+    inputs = make_inputs('qwen3_8b_bf16_small')
+    t = workload_tensors(inputs)
+    before = {k: v.clone() for k, v in t.items()}
+    first = attention.paged_decode_attention(t['q'], t['key_pool'], t['value_pool'],
+                                             t['block_table'], t['context_lens'])
+    second = attention.paged_decode_attention(t['q'], t['key_pool'], t['value_pool'],
+                                              t['block_table'], t['context_lens'])
+    assert torch.equal(first, second)
+    assert first.data_ptr() != second.data_ptr()
+    for key, tensor in t.items():
+        assert torch.equal(tensor.view(torch.uint8) if tensor.dtype.is_floating_point else tensor,
+                           before[key].view(torch.uint8) if tensor.dtype.is_floating_point else before[key])
