@@ -1,0 +1,602 @@
+#!/usr/bin/env python
+"""Benchmark: one decode step of one paged GQA attention layer on B200.
+
+A step is the hot path over one batch: append this step's K/V token for every
+sequence into its page (write_paged_kv) and run paged decode attention over
+the whole context (paged_decode_attention). Workload: Qwen2.5-7B decode
+geometry -- batch 64, 28 query / 4 KV heads, head_dim 128, bf16, context
+lengths uniform in [1024, 4096], 16-token pages in a randomly permuted pool
+1.25x the pages in use, q/K/V ~ 0.5 N(0,1), scale 128^-1/2. Seeded synthetic
+data; the KV pool (~0.42 GB per GPU) is larger than the 126 MB L2.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...
+
+Prints ONE JSON line on rank 0. ``value`` is whole-job achieved HBM GB/s by
+the path's algorithmic bytes (K and V read once, q and out, page indices,
+lengths, and the append's read+write), measured with CUDA events around K
+CUDA-graph replays of the step, max over ranks. ``e2e`` is the same metric
+through the public Python API with this step's inputs copied from pinned host
+memory and the output copied back inside the timed region.
+
+Multi-GPU (weak scaling, no collective on the data path): KV-head sharding,
+every rank owns a 4-KV-head (7-query-head-group) slice of an N x wider layer
+over the same batch, i.e. one config-sized shard per GPU. ``--scaling strong``
+instead splits the fixed single-layer workload by KV head (and by batch once
+ranks outnumber KV heads).
+
+``--impl reference`` times the reference's CPU path for the same workload
+(gather + causal attention + append, restated by the oracle) on the host cores.
+"""
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _path in (ROOT, ROOT / 'micro-vllm_b200'):
+    if str(_path) not in sys.path:
+        sys.path.insert(0, str(_path))
+
+METRIC = 'paged decode attn achieved HBM GB/s (% of B200 peak); decode tokens/s'
+DEFAULT_WORKLOAD = 'qwen7b_bf16'
+FALLBACK_HBM_GBS = 6650.0
+# dram__bytes_read.sum + dram__bytes_write.sum per launch of paged_decode_mma_kernel on this
+# workload, from ncu (profiles/paged_decode_mma_qwen7b_bf16.md); None until captured.
+NCU_TRAFFIC_BYTES = {}
+L2_BYTES = 126 * 1024 * 1024
+
+
+def parse_args(argv=None):
+    parser = argparse.ArgumentParser(description=__doc__.split('\n')[0])
+    parser.add_argument('--gpus', type=int, default=1)
+    parser.add_argument('--steps', type=int, default=2000)
+    parser.add_argument('--warmup', type=int, default=20)
+    parser.add_argument('--impl', choices=('ours', 'reference'), default='ours')
+    parser.add_argument('--workload', default=DEFAULT_WORKLOAD)
+    parser.add_argument('--scaling', choices=('weak', 'strong'), default='weak')
+    parser.add_argument('--cpu-seconds', type=float, default=12.0,
+                        help='wall-clock budget of the CPU baseline sample')
+    parser.add_argument('--no-cpu-baseline', action='store_true')
+    parser.add_argument('--pages-per-split', type=int, default=0)
+    return parser.parse_args(argv)
+
+
+# ----------------------------------------------------------------- setup
+
+def init_distributed(args):
+    import torch
+    world = int(os.environ.get('WORLD_SIZE', '1'))
+    rank = int(os.environ.get('RANK', '0'))
+    local_rank = int(os.environ.get('LOCAL_RANK', '0'))
+    if world != args.gpus:
+        if world == 1 and args.gpus > 1:
+            raise SystemExit('--gpus N > 1 needs torchrun --nproc-per-node N')
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group('nccl', timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device('cuda', local_rank))
+    return rank, world, local_rank
+
+
+def peak_hbm():
+    path = ROOT / 'MEASURED_PEAKS.json'
+    try:
+        data = json.loads(path.read_text())
+        return float(data['hbm_gbs']), 'measured'
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, 'fallback'
+
+
+def local_geometry(spec, rank, world, scaling):
+    """(q_heads, kv_heads, batch slice) this rank computes."""
+    from micro_vllm_b200.sharding import kv_head_shard
+    if world == 1 or scaling == 'weak':
+        return spec['q_heads'], spec['kv_heads'], (0, spec['batch'])
+    shard = kv_head_shard(rank, world, q_heads=spec['q_heads'], kv_heads=spec['kv_heads'],
+                          batch=spec['batch'])
+    return shard.num_q_heads, shard.num_kv_heads, shard.batch
+
+
+def draw_lengths(spec, generator):
+    import torch
+    batch = spec['batch']
+    kind = spec['lens'][0]
+    if kind == 'uniform':
+        _, lo, hi = spec['lens']
+        return torch.randint(lo, hi + 1, (batch,), generator=generator, dtype=torch.int64)
+    if kind == 'lognormal':
+        _, median, sigma, lo, hi = spec['lens']
+        raw = torch.empty(batch, dtype=torch.float64).log_normal_(math.log(median), sigma,
+                                                                   generator=generator)
+        return raw.round().clamp(lo, hi).to(torch.int64)
+    return torch.tensor(spec['lens'][1], dtype=torch.int64)
+
+
+def make_workload(spec, q_heads, kv_heads, batch_slice, seed, device):
+    """Seeded synthetic inputs of the workload's shapes, built on the device."""
+    import torch
+    dtype = {'bfloat16': torch.bfloat16, 'float16': torch.float16, 'float32': torch.float32}[spec['dtype']]
+    cpu = torch.Generator().manual_seed(seed)
+    lens = draw_lengths(spec, cpu)[batch_slice[0]:batch_slice[1]]
+    bs, dim = spec['block_size'], spec['head_dim']
+    pages = (lens + bs - 1) // bs
+    total = int(pages.sum())
+    kind, amount = spec['pool']
+    num_pages = max(total, int(amount) if kind == 'fixed_pages' else int(math.ceil(total * amount)))
+    perm = torch.randperm(num_pages, generator=cpu).to(torch.int32)
+    table = torch.full((len(lens), int(pages.max())), -1, dtype=torch.int32)
+    offset = 0
+    for b, n in enumerate(pages.tolist()):
+        table[b, :n] = perm[offset:offset + n]
+        offset += n
+    gen = torch.Generator(device=device).manual_seed(seed + 1)
+    scale = spec['value_scale']
+
+    def normal(shape):
+        out = torch.empty(shape, dtype=dtype, device=device)
+        chunk = 1 << 26
+        flat = out.view(-1)
+        for start in range(0, flat.numel(), chunk):
+            piece = torch.randn(min(chunk, flat.numel() - start), generator=gen, device=device)
+            flat[start:start + piece.numel()] = piece.mul_(scale)
+        return out
+
+    pool_shape = (num_pages, kv_heads, bs, dim)
+    k_pool = normal(pool_shape)
+    v_pool = normal(pool_shape)
+    if 'k_outlier' in spec:
+        frac, factor = spec['k_outlier']
+        mask = torch.rand((num_pages, kv_heads, bs), generator=gen, device=device) < frac
+        k_pool[mask] *= factor
+    return dict(
+        q=normal((len(lens), q_heads, dim)),
+        k_pool=k_pool, v_pool=v_pool,
+        k_new=normal((len(lens), kv_heads, 1, dim)),
+        v_new=normal((len(lens), kv_heads, 1, dim)),
+        block_table=table.to(device), context_lens=lens.to(torch.int32).to(device),
+        host_lens=lens.clone(), host_table=table.clone(), dtype=dtype)
+
+
+def step_bytes(spec, lens, q_heads, kv_heads):
+    """Algorithmic bytes of one step (decode + append) for this rank's slice."""
+    elem = 4 if spec['dtype'] == 'float32' else 2
+    lens = [int(x) for x in lens]
+    dim, bs = spec['head_dim'], spec['block_size']
+    b = len(lens)
+    kv = sum(2 * kv_heads * length * dim * elem for length in lens)
+    qo = b * q_heads * dim * 2 * elem
+    idx = sum(-(-length // bs) for length in lens) * 4
+    attention = kv + qo + idx + 4 * b
+    append = 4 * b * kv_heads * dim * elem
+    return attention + append, attention
+
+
+# ------------------------------------------------------------------ clocks
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ('clocks.sm', 'clocks.max.sm', 'power.draw', 'utilization.gpu',
+              'clocks_event_reasons.hw_slowdown', 'clocks_event_reasons.hw_thermal_slowdown',
+              'clocks_event_reasons.sw_thermal_slowdown', 'clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, device_index, interval_ms=50):
+        self.device_index = device_index
+        self.interval_ms = interval_ms
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        self.file = tempfile.NamedTemporaryFile('w+', suffix='.csv', delete=False)
+        try:
+            self.proc = subprocess.Popen(
+                ['nvidia-smi', f'--query-gpu={",".join(self.FIELDS)}', '--format=csv,noheader,nounits',
+                 '-i', str(self.device_index), '-lms', str(self.interval_ms)],
+                stdout=self.file, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.1)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        self.file.close()
+
+    def summary(self):
+        rows = []
+        try:
+            for line in Path(self.file.name).read_text().splitlines():
+                parts = [p.strip() for p in line.split(',')]
+                if len(parts) == len(self.FIELDS):
+                    rows.append(parts)
+        finally:
+            os.unlink(self.file.name)
+        if not rows:
+            return {'sm_mhz': None, 'sm_max_mhz': None, 'reasons': ['unsampled'], 'samples': 0}
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        loaded = [r for r in rows if (num(r[3]) or 0) >= 50] or rows
+        sm = [num(r[0]) for r in loaded if num(r[0]) is not None]
+        names = ('hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap')
+        reasons = sorted({name for r in loaded for name, flag in zip(names, r[4:8])
+                          if flag.lower() == 'active'})
+        return {'sm_mhz': statistics.median(sm) if sm else None,
+                'sm_max_mhz': num(rows[0][1]),
+                'reasons': reasons, 'samples': len(loaded),
+                'power_w_max': max((num(r[2]) or 0) for r in rows)}
+
+
+# ------------------------------------------------------------ CPU baseline
+
+def prepare_cpu_sample(spec, data, sequences):
+    """Host copy of the first ``sequences`` sequences of the workload (their pages only).
+
+    bf16 inputs are widened to fp32: the reference's CPU path is timed in fp32.
+    """
+    import numpy as np
+    import torch
+
+    sample = min(sequences, data['q'].shape[0])
+    lens = data['host_lens'][:sample].numpy()
+    table = data['host_table'][:sample].numpy()
+    bs = spec['block_size']
+    used = sorted({int(p) for b in range(sample) for p in table[b, :-(-int(lens[b]) // bs)]})
+    remap = {p: i for i, p in enumerate(used)}
+    local_table = np.full_like(table, -1)
+    for b in range(sample):
+        for j in range(-(-int(lens[b]) // bs)):
+            local_table[b, j] = remap[int(table[b, j])]
+    idx = torch.tensor(used, device=data['k_pool'].device)
+    return dict(
+        lens=lens, table=local_table, batch=data['q'].shape[0],
+        k_pool=data['k_pool'].index_select(0, idx).float().cpu().numpy(),
+        v_pool=data['v_pool'].index_select(0, idx).float().cpu().numpy(),
+        q=data['q'][:sample].float().cpu().numpy(),
+        k_new=data['k_new'][:sample].float().cpu().numpy(),
+        v_new=data['v_new'][:sample].float().cpu().numpy())
+
+
+def run_cpu_sample(spec, sample):
+    """One pass of the oracle (append, then gather + causal attention per sequence)."""
+    import numpy as np
+
+    from oracle import append_tokens, decode_float
+
+    append_tokens(sample['k_pool'], sample['v_pool'], sample['k_new'], sample['v_new'],
+                  sample['table'], sample['lens'] - 1)
+    decode_float(sample['q'], sample['k_pool'], sample['v_pool'], sample['table'], sample['lens'],
+                 spec['head_dim'] ** -0.5, 'float32', accum=np.float32)
+
+
+def blas_threads():
+    from threadpoolctl import threadpool_info
+    return int(max((info.get('num_threads', 1) for info in threadpool_info()), default=1))
+
+
+def describe_sample(sample, runs, elapsed):
+    return (f'{len(sample["lens"])} of {sample["batch"]} sequences (lens {sample["lens"].tolist()}): '
+            f'append + gather + causal attention per sequence, fp32 numpy oracle of the '
+            f'reference CPU path, {runs} runs in {elapsed:.1f} s; host has {os.cpu_count()} CPUs')
+
+
+def cpu_baseline(spec, data, q_heads, kv_heads, seconds):
+    """Time the oracle on a sample of this workload for ``seconds``; GB/s on the
+    same algorithmic-bytes basis as the GPU number."""
+    sample = prepare_cpu_sample(spec, data, 4)
+    step, _ = step_bytes(spec, sample['lens'], q_heads, kv_heads)
+    runs = 0
+    start = time.perf_counter()
+    while True:
+        run_cpu_sample(spec, sample)
+        runs += 1
+        elapsed = time.perf_counter() - start
+        if elapsed >= seconds:
+            break
+    return {'value': round(step * runs / elapsed / 1e9, 3), 'unit': 'GB/s',
+            'cores': blas_threads(), 'kind': 'port',
+            'sample': describe_sample(sample, runs, elapsed)}
+
+
+# ------------------------------------------------------------------- ours
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    from micro_vllm_b200 import cuda_attention, cuda_paged_cache
+    from tests.golden.cases import WORKLOADS
+
+    rank, world, local_rank = init_distributed(args)
+    device = torch.device('cuda', local_rank)
+    torch.cuda.set_device(device)
+    spec = WORKLOADS[args.workload]
+    q_heads, kv_heads, batch_slice = local_geometry(spec, rank, world, args.scaling)
+    seed = spec['seed'] + (rank * 7919 if args.scaling == 'weak' else 0)
+    data = make_workload(spec, q_heads, kv_heads, batch_slice, seed, device)
+    lens_host = data['host_lens'].tolist()
+    max_len = max(lens_host)
+    step_total, attn_bytes = step_bytes(spec, lens_host, q_heads, kv_heads)
+    out = torch.empty_like(data['q'])
+    pps = args.pages_per_split
+
+    def step():
+        cuda_paged_cache.write_paged_kv(data['k_new'], data['v_new'], data['k_pool'], data['v_pool'],
+                                        data['block_table'], positions=data['context_lens'],
+                                        positions_are_end=True)
+        cuda_attention.paged_decode_attention(data['q'], data['k_pool'], data['v_pool'],
+                                              data['block_table'], data['context_lens'],
+                                              max_context_len=max_len, out=out,
+                                              pages_per_split=pps)
+
+    def attention_only():
+        cuda_attention.paged_decode_attention(data['q'], data['k_pool'], data['v_pool'],
+                                              data['block_table'], data['context_lens'],
+                                              max_context_len=max_len, out=out,
+                                              pages_per_split=pps)
+
+    path, chosen_pps, splits = cuda_attention.paged_decode_plan(
+        q_heads, data['k_pool'], max_len, batch=len(lens_host), pages_per_split=pps)
+    launches_per_step = 1 + 1 + (1 if splits > 1 else 0)
+
+    stream = torch.cuda.Stream(device)
+    stream.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            step()
+            attention_only()
+    torch.cuda.synchronize(device)
+    step_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(step_graph, stream=stream):
+        step()
+    attn_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(attn_graph, stream=stream):
+        attention_only()
+    torch.cuda.synchronize(device)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    visible = os.environ.get('CUDA_VISIBLE_DEVICES')
+    smi_index = visible.split(',')[local_rank] if visible else str(local_rank)
+    with ClockSampler(smi_index) as clocks:
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                step_graph.replay()
+        torch.cuda.synchronize(device)
+        barrier()
+        torch.cuda.synchronize(device)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for _ in range(args.steps):
+                step_graph.replay()
+            end.record(stream)
+        torch.cuda.synchronize(device)
+        barrier()
+        elapsed_ms = start.elapsed_time(end)
+
+        # Attention alone, per launch (decode kernel + split merge), for the roofline.
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                attn_graph.replay()
+        torch.cuda.synchronize(device)
+        reps = min(args.steps, 500)
+        events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(reps)]
+        with torch.cuda.stream(stream):
+            for s, e in events:
+                s.record(stream)
+                attn_graph.replay()
+                e.record(stream)
+        torch.cuda.synchronize(device)
+        attn_ms = statistics.mean(s.elapsed_time(e) for s, e in events)
+
+        # End to end through the public API: pinned host inputs in, output back out.
+        e2e = run_e2e(args, data, max_len, pps, stream, device, barrier)
+    clock_summary = clocks.summary()
+
+    times = torch.tensor([elapsed_ms, attn_ms, e2e['ms']], dtype=torch.float64, device=device)
+    totals = torch.tensor([float(step_total), float(attn_bytes)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(times, op=dist.ReduceOp.MAX)
+        dist.all_reduce(totals, op=dist.ReduceOp.SUM)
+    elapsed_ms, attn_ms, e2e_ms = times.tolist()
+    job_step_bytes, job_attn_bytes = totals.tolist()
+    ms_per_step = elapsed_ms / args.steps
+    value = job_step_bytes * args.steps / (elapsed_ms / 1e3) / 1e9
+    e2e_value = job_step_bytes * args.steps / (e2e_ms / 1e3) / 1e9
+
+    result = None
+    if rank == 0:
+        peak, peak_kind = peak_hbm()
+        achieved = attn_bytes / (attn_ms / 1e3) / 1e9
+        traffic = NCU_TRAFFIC_BYTES.get(args.workload)
+        batch = len(lens_host)
+        result = {
+            'metric': METRIC,
+            'value': round(value, 1),
+            'unit': 'GB/s',
+            'n_gpus': world,
+            'steps': args.steps,
+            'warmup': args.warmup,
+            'ms_per_step': round(ms_per_step, 6),
+            'higher_is_better': True,
+            'scaling': args.scaling if world > 1 else 'weak',
+            'vs_baseline': None,
+            'dtype': {'bfloat16': 'bf16', 'float16': 'fp16', 'float32': 'fp32'}[spec['dtype']],
+            'data': 'synthetic (seeded, on device)',
+            'config': {
+                'workload': (f'{args.workload}: paged GQA decode layer, batch {spec["batch"]}, '
+                             f'{spec["q_heads"]} q / {spec["kv_heads"]} kv heads, head_dim '
+                             f'{spec["head_dim"]}, block {spec["block_size"]}, lens {spec["lens"]}'),
+                'per_rank': {'batch': batch, 'q_heads': q_heads, 'kv_heads': kv_heads},
+                'step': 'append 1 token/sequence + paged decode attention (1 layer)',
+                'l2': f'inputs larger than L2: KV pool {2 * data["k_pool"].numel() * data["k_pool"].element_size() / 1e9:.2f} GB per GPU',
+                'parallelism': f'kv-head sharded x{world}, {args.scaling}' if world > 1 else 'single GPU',
+                'timing': 'CUDA events around K CUDA-graph replays, max over ranks',
+                'kernel_path': path, 'pages_per_split': chosen_pps, 'max_splits': splits,
+            },
+            'us_per_layer': round(ms_per_step * 1e3, 3),
+            'decode_tokens_per_s': round(spec['batch'] / (ms_per_step / 1e3), 1),
+            'pct_of_hbm_peak': round(100 * value / world / peak, 2),
+            'roofline': {
+                'bound': 'hbm',
+                'kernel': 'paged decode attention (paged_decode_mma_kernel + split merge)',
+                'achieved': round(achieved, 1),
+                'peak': peak,
+                'peak_kind': f'{peak_kind} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)'
+                             if peak_kind == 'measured' else 'fallback 6.65 TB/s',
+                'unit': 'GB/s',
+                'frac': round(achieved / peak, 4),
+                'us_per_launch': round(attn_ms * 1e3, 3),
+                'algorithmic_bytes_per_launch': attn_bytes,
+                'traffic': traffic,
+            },
+            'e2e': {'value': round(e2e_value, 1), 'unit': 'GB/s',
+                    'h2d_bytes_per_step': e2e['h2d'], 'd2h_bytes_per_step': e2e['d2h'],
+                    'us_per_step': round(e2e_ms / args.steps * 1e3, 3)},
+            'clocks': clock_summary,
+            'gpu_launches': launches_per_step * args.steps,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            result['cpu_baseline'] = cpu_baseline(spec, data, q_heads, kv_heads, args.cpu_seconds)
+    del step_graph, attn_graph
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+    return result
+
+
+def run_e2e(args, data, max_len, pps, stream, device, barrier):
+    """Same step through the public API with host inputs and a host result."""
+    import torch
+
+    from micro_vllm_b200 import cuda_attention, cuda_paged_cache
+
+    host = {name: data[name].cpu().pin_memory() for name in ('q', 'k_new', 'v_new', 'context_lens')}
+    dev = {name: torch.empty_like(data[name]) for name in host}
+    out_dev = torch.empty_like(data['q'])
+    out_host = torch.empty(out_dev.shape, dtype=out_dev.dtype).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = out_host.numel() * out_host.element_size()
+
+    def step():
+        for name in host:
+            dev[name].copy_(host[name], non_blocking=True)
+        cuda_paged_cache.write_paged_kv(dev['k_new'], dev['v_new'], data['k_pool'], data['v_pool'],
+                                        data['block_table'], positions=dev['context_lens'],
+                                        positions_are_end=True)
+        cuda_attention.paged_decode_attention(dev['q'], data['k_pool'], data['v_pool'],
+                                              data['block_table'], dev['context_lens'],
+                                              max_context_len=max_len, out=out_dev,
+                                              pages_per_split=pps)
+        out_host.copy_(out_dev, non_blocking=True)
+
+    steps = min(args.steps, 1000)
+    with torch.cuda.stream(stream):
+        for _ in range(max(args.warmup, 3)):
+            step()
+    torch.cuda.synchronize(device)
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(steps):
+            step()
+        end.record(stream)
+    torch.cuda.synchronize(device)
+    barrier()
+    # Scale to the main loop's step count so value and e2e share one unit basis.
+    return {'ms': start.elapsed_time(end) * args.steps / steps, 'h2d': h2d, 'd2h': d2h}
+
+
+# -------------------------------------------------------------- reference
+
+def run_reference(args):
+    """The reference CPU path (oracle restatement) on this host's cores.
+
+    Each step is one pass over a bounded sample of the workload (the first
+    sequences; fewer when K + W steps would take more than ~2 minutes), timed
+    with the wall clock; value is the median GB/s over the K timed steps.
+    """
+    rank = int(os.environ.get('RANK', '0'))
+    if rank != 0:
+        return None
+    import torch
+
+    from tests.golden.cases import WORKLOADS
+
+    spec = WORKLOADS[args.workload]
+    torch.manual_seed(0)
+    # Only the sampled sequences are built; their lengths match the GPU run's first four.
+    data = make_workload(spec, spec['q_heads'], spec['kv_heads'], (0, 4), spec['seed'], 'cpu')
+    sample = prepare_cpu_sample(spec, data, 4)
+    sample['batch'] = spec['batch']
+    start = time.perf_counter()
+    run_cpu_sample(spec, sample)
+    one = time.perf_counter() - start
+    budget = 120.0
+    while len(sample['lens']) > 1 and one * (args.steps + args.warmup) > budget:
+        sample = prepare_cpu_sample(spec, data, len(sample['lens']) // 2)
+        sample['batch'] = spec['batch']
+        start = time.perf_counter()
+        run_cpu_sample(spec, sample)
+        one = time.perf_counter() - start
+    step, _ = step_bytes(spec, sample['lens'], spec['q_heads'], spec['kv_heads'])
+    values = []
+    total_elapsed = 0.0
+    for i in range(args.warmup + args.steps):
+        start = time.perf_counter()
+        run_cpu_sample(spec, sample)
+        elapsed = time.perf_counter() - start
+        if i >= args.warmup:
+            values.append(step / elapsed / 1e9)
+            total_elapsed += elapsed
+    value = round(statistics.median(values), 3)
+    description = describe_sample(sample, args.steps, total_elapsed)
+    return {
+        'impl': 'reference',
+        'metric': METRIC, 'value': value, 'unit': 'GB/s', 'n_gpus': args.gpus,
+        'steps': args.steps, 'warmup': args.warmup,
+        'ms_per_step': round(total_elapsed / args.steps * 1e3, 6),
+        'higher_is_better': True, 'scaling': args.scaling, 'vs_baseline': None,
+        'dtype': 'fp32 (bf16 inputs widened)', 'data': 'synthetic (seeded)',
+        'config': {'workload': args.workload, 'sample': description},
+        'cpu_baseline': {'value': value, 'unit': 'GB/s', 'cores': blas_threads(), 'kind': 'port',
+                         'sample': description},
+        'e2e': {'value': value, 'unit': 'GB/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
+    }
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    if args.impl == 'reference':
+        result = run_reference(args)
+    else:
+        result = run_ours(args)
+    if result is not None:
+        print(json.dumps(result), flush=True)
+
+
+if __name__ == '__main__':
+    main()
