@@ -47,6 +47,7 @@ extern "C" {
 
 /* Flags for mv_paged_decode / mv_paged_decode_workspace_size. */
 #define MV_FLAG_FORCE_SIMT 1u /* use the CUDA-core kernel even where the tensor-core one applies */
+#define MV_FLAG_SPLIT_GRID 2u /* tensor-core kernel with a fixed split grid instead of the persistent one */
 
 /* Status codes. */
 #define MV_OK 0
@@ -59,8 +60,9 @@ extern "C" {
 #define MV_DEVICE_STATUS_WAIT_TIMEOUT 1u
 
 /* Kernel paths reported by mv_paged_decode_plan. */
-#define MV_PATH_SIMT 0
-#define MV_PATH_TMA_MMA 1
+#define MV_PATH_SIMT 0            /* CUDA cores, one CTA per (split, KV head, sequence) */
+#define MV_PATH_TMA_MMA 1         /* TMA + tensor cores, one CTA per (split, KV head, sequence) */
+#define MV_PATH_TMA_MMA_PERSISTENT 2 /* TMA + tensor cores, persistent, equal page ranges per warp */
 
 MV_API int mv_abi_version(void);
 
@@ -68,9 +70,10 @@ MV_API int mv_abi_version(void);
 MV_API const char* mv_last_error(void);
 
 /*
- * Workspace bytes mv_paged_decode needs for this geometry (0 when every
- * sequence fits one split). max_context_len bounds every context length;
- * pages_per_split 0 lets the library choose.
+ * Workspace bytes mv_paged_decode needs for this geometry on the current
+ * device (0 when no split-KV pass is needed). max_context_len bounds every
+ * context length; pages_per_split 0 lets the library choose (a nonzero value
+ * selects a fixed split grid).
  * Replaces no reference call: the reference kernel allocates an output-sized
  * running buffer itself (src/micro_vllm/csrc/online_attention.cuh:154-156).
  */

@@ -105,14 +105,69 @@ struct Plan {
     int path;
     int pages_per_split;
     int max_splits;
-    int nt;  // mma n-tiles (8 query heads each)
+    int nt;          // mma n-tiles (8 query heads each)
+    int ctas;        // persistent grid size
+    int warps;       // persistent warps in the grid
     size_t workspace;
+    size_t part_o_bytes;
+    size_t part_lse_bytes;
 };
 
 bool mma_shape_ok(const Geometry& g) {
     const int group = g.q_heads / g.kv_heads;
     return (g.dtype == MV_DTYPE_BF16 || g.dtype == MV_DTYPE_F16) && g.block_size == 16 &&
            (g.head_dim == 64 || g.head_dim == 128 || g.head_dim == 256) && group <= 16;
+}
+
+size_t round256(size_t bytes) { return (bytes + 255) / 256 * 256; }
+
+// Persistent kernel: stages per warp for each head_dim (~96 KiB of stages per CTA
+// so two CTAs share an SM; one at head_dim 256), and the batch its prefix array fits.
+template <int D> struct PersistentStages { static constexpr int value = D == 64 ? 6 : (D == 128 ? 3 : 2); };
+constexpr int kPersistentMaxBatch = 1023;
+
+template <typename T, int D, int NT>
+auto persistent_kernel() {
+    return mv::paged_decode_persistent_kernel<T, D, NT, kMmaWarps, PersistentStages<D>::value>;
+}
+
+template <int D>
+constexpr int persistent_smem() {
+    return mv::PersistentShape<D, kMmaWarps, PersistentStages<D>::value>::smem_bytes(kPersistentMaxBatch);
+}
+
+// Resident CTAs per SM of the persistent kernel instance, cached per device.
+template <typename T, int D, int NT>
+int persistent_occupancy(int device, int* ctas_per_sm) {
+    static int cache[kMaxDevices] = {0};
+    static std::mutex mutex;
+    std::lock_guard<std::mutex> lock(mutex);
+    if (cache[device] == 0) {
+        auto kernel = persistent_kernel<T, D, NT>();
+        int rc = ensure_smem(kernel, persistent_smem<D>());
+        if (rc != MV_OK) return rc;
+        int blocks = 0;
+        cudaError_t err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel, kMmaWarps * 32,
+                                                                        persistent_smem<D>());
+        if (err != cudaSuccess) return cuda_fail(err, "cudaOccupancyMaxActiveBlocksPerMultiprocessor");
+        if (blocks < 1) return fail(MV_ERR_UNSUPPORTED, "persistent decode kernel does not fit an SM");
+        cache[device] = blocks;
+    }
+    *ctas_per_sm = cache[device];
+    return MV_OK;
+}
+
+template <typename T>
+int persistent_occupancy_dispatch(int device, int dim, int nt, int* ctas_per_sm) {
+    switch (dim * 4 + nt) {
+        case 64 * 4 + 1: return persistent_occupancy<T, 64, 1>(device, ctas_per_sm);
+        case 64 * 4 + 2: return persistent_occupancy<T, 64, 2>(device, ctas_per_sm);
+        case 128 * 4 + 1: return persistent_occupancy<T, 128, 1>(device, ctas_per_sm);
+        case 128 * 4 + 2: return persistent_occupancy<T, 128, 2>(device, ctas_per_sm);
+        case 256 * 4 + 1: return persistent_occupancy<T, 256, 1>(device, ctas_per_sm);
+        case 256 * 4 + 2: return persistent_occupancy<T, 256, 2>(device, ctas_per_sm);
+        default: return fail(MV_ERR_UNSUPPORTED, "no tensor-core kernel for head_dim %d", dim);
+    }
 }
 
 int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool aligned_for_tma,
@@ -122,13 +177,38 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
     DeviceInfo dev;
     rc = device_info(&dev);
     if (rc != MV_OK) return rc;
+    int device = 0;
+    cudaGetDevice(&device);
     const int group = g.q_heads / g.kv_heads;
-    plan->path = (!(flags & MV_FLAG_FORCE_SIMT) && aligned_for_tma && mma_shape_ok(g)) ? MV_PATH_TMA_MMA
-                                                                                       : MV_PATH_SIMT;
+    if (pages_per_split < 0) return fail(MV_ERR_INVALID_ARGUMENT, "pages_per_split must be nonnegative");
+    const bool mma = !(flags & MV_FLAG_FORCE_SIMT) && aligned_for_tma && mma_shape_ok(g);
+    const bool persistent = mma && pages_per_split == 0 && !(flags & MV_FLAG_SPLIT_GRID) &&
+                            g.batch <= kPersistentMaxBatch &&
+                            static_cast<int64_t>(g.batch) * g.kv_heads < (int64_t(1) << 31);
+    plan->path = persistent ? MV_PATH_TMA_MMA_PERSISTENT : (mma ? MV_PATH_TMA_MMA : MV_PATH_SIMT);
     plan->nt = group <= 8 ? 1 : 2;
+    plan->ctas = plan->warps = 0;
+    plan->part_o_bytes = plan->part_lse_bytes = 0;
     const int64_t max_pages = (g.max_context_len + g.block_size - 1) / g.block_size;
+
+    if (persistent) {
+        int per_sm = 0;
+        rc = g.dtype == MV_DTYPE_BF16 ? persistent_occupancy_dispatch<__nv_bfloat16>(device, g.head_dim, plan->nt, &per_sm)
+                                      : persistent_occupancy_dispatch<__half>(device, g.head_dim, plan->nt, &per_sm);
+        if (rc != MV_OK) return rc;
+        plan->ctas = dev.sms * per_sm;
+        plan->warps = plan->ctas * kMmaWarps;
+        plan->pages_per_split = 0;
+        plan->max_splits = 1;
+        const size_t rows = static_cast<size_t>(plan->warps) * 2 * 8 * plan->nt;  // 2 partial slots per warp
+        plan->part_o_bytes = round256(rows * g.head_dim * sizeof(float));
+        plan->part_lse_bytes = round256(rows * sizeof(float));
+        plan->workspace = plan->part_o_bytes + plan->part_lse_bytes +
+                          round256((static_cast<size_t>(g.batch) + 1) * sizeof(int64_t));
+        return MV_OK;
+    }
+
     int64_t pps = pages_per_split;
-    if (pps < 0) return fail(MV_ERR_INVALID_ARGUMENT, "pages_per_split must be nonnegative");
     if (pps == 0) {
         // Enough splits that the page work of the whole batch spreads over
         // ~16 CTAs per SM, but no split shorter than 8 pages.
@@ -147,11 +227,10 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
     plan->max_splits = static_cast<int>(splits);
     if (splits > 1) {
         const size_t rows = static_cast<size_t>(g.batch) * g.q_heads * splits;
-        const size_t o_bytes = (rows * g.head_dim * sizeof(float) + 255) / 256 * 256;
-        plan->workspace = o_bytes + (rows * sizeof(float) + 255) / 256 * 256;
-    } else {
-        plan->workspace = 0;
+        plan->part_o_bytes = round256(rows * g.head_dim * sizeof(float));
+        plan->part_lse_bytes = round256(rows * sizeof(float));
     }
+    plan->workspace = plan->part_o_bytes + plan->part_lse_bytes;
     if (plan->path == MV_PATH_SIMT) {
         const size_t smem = mv::simt_smem_bytes(group, g.head_dim);
         if (smem > static_cast<size_t>(dev.smem_optin))
@@ -263,9 +342,45 @@ int launch_mma_dispatch(const mv::DecodeParams& p, const CUtensorMap& kmap, cons
     }
 }
 
+template <typename T, int D, int NT>
+int launch_persistent(const mv::DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap,
+                      int ctas, cudaStream_t stream) {
+    auto kernel = persistent_kernel<T, D, NT>();
+    int rc = ensure_smem(kernel, persistent_smem<D>());
+    if (rc != MV_OK) return rc;
+    kernel<<<ctas, kMmaWarps * 32, persistent_smem<D>(), stream>>>(p, kmap, vmap);
+    cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess) return cuda_fail(err, "persistent decode kernel launch");
+    mv::paged_decode_persistent_merge_kernel<T, 8 * NT>
+        <<<dim3(p.kv_heads, p.batch), mv::kMergeThreads, 0, stream>>>(p);
+    err = cudaGetLastError();
+    return err == cudaSuccess ? MV_OK : cuda_fail(err, "merge kernel launch");
+}
+
+template <typename T>
+int launch_persistent_dispatch(const mv::DecodeParams& p, const CUtensorMap& kmap,
+                               const CUtensorMap& vmap, int ctas, int nt, cudaStream_t stream) {
+    switch (p.head_dim * 4 + nt) {
+        case 64 * 4 + 1: return launch_persistent<T, 64, 1>(p, kmap, vmap, ctas, stream);
+        case 64 * 4 + 2: return launch_persistent<T, 64, 2>(p, kmap, vmap, ctas, stream);
+        case 128 * 4 + 1: return launch_persistent<T, 128, 1>(p, kmap, vmap, ctas, stream);
+        case 128 * 4 + 2: return launch_persistent<T, 128, 2>(p, kmap, vmap, ctas, stream);
+        case 256 * 4 + 1: return launch_persistent<T, 256, 1>(p, kmap, vmap, ctas, stream);
+        case 256 * 4 + 2: return launch_persistent<T, 256, 2>(p, kmap, vmap, ctas, stream);
+        default: return fail(MV_ERR_UNSUPPORTED, "no tensor-core kernel for head_dim %d", p.head_dim);
+    }
+}
+
 template <typename T>
 int launch_decode(const mv::DecodeParams& p, const Plan& plan, const CUtensorMap* kmap,
                   const CUtensorMap* vmap, cudaStream_t stream) {
+    if (plan.path == MV_PATH_TMA_MMA_PERSISTENT) {
+        if constexpr (std::is_same<T, float>::value) {
+            return fail(MV_ERR_UNSUPPORTED, "tensor-core kernel takes fp16/bf16 only");
+        } else {
+            return launch_persistent_dispatch<T>(p, *kmap, *vmap, plan.ctas, plan.nt, stream);
+        }
+    }
     const dim3 grid(plan.max_splits, p.kv_heads, p.batch);
     int rc;
     if (plan.path == MV_PATH_TMA_MMA) {
@@ -402,18 +517,20 @@ int mv_paged_decode(const void* q, int64_t q_stride_seq, int64_t q_stride_head, 
     p.out_stride_head = out_stride_head;
     p.pages_per_split = plan.pages_per_split;
     p.max_splits = plan.max_splits;
+    p.part_o = nullptr;
+    p.part_lse = nullptr;
+    p.prefix_out = nullptr;
+    p.persistent_warps = plan.warps;
     if (plan.workspace > 0) {
-        const size_t rows = static_cast<size_t>(batch) * num_q_heads * plan.max_splits;
-        const size_t o_bytes = (rows * head_dim * sizeof(float) + 255) / 256 * 256;
-        p.part_o = static_cast<float*>(workspace);
-        p.part_lse = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + o_bytes);
-    } else {
-        p.part_o = nullptr;
-        p.part_lse = nullptr;
+        uint8_t* base = static_cast<uint8_t*>(workspace);
+        p.part_o = reinterpret_cast<float*>(base);
+        p.part_lse = reinterpret_cast<float*>(base + plan.part_o_bytes);
+        if (plan.path == MV_PATH_TMA_MMA_PERSISTENT)
+            p.prefix_out = reinterpret_cast<int64_t*>(base + plan.part_o_bytes + plan.part_lse_bytes);
     }
 
     CUtensorMap kmap, vmap;
-    if (plan.path == MV_PATH_TMA_MMA) {
+    if (plan.path == MV_PATH_TMA_MMA || plan.path == MV_PATH_TMA_MMA_PERSISTENT) {
         rc = page_tensor_map(k_cache, num_blocks, num_kv_heads, head_dim, dtype, &kmap);
         if (rc == MV_OK) rc = page_tensor_map(v_cache, num_blocks, num_kv_heads, head_dim, dtype, &vmap);
         if (rc != MV_OK) return rc;

@@ -48,6 +48,8 @@ struct DecodeParams {
     float* part_lse;        // [batch, q_heads, max_splits]            log2-sum-exp of each split
     int pages_per_split;
     int max_splits;
+    int64_t* prefix_out;    // persistent schedule: per-sequence page prefix sums [batch + 1]
+    int64_t persistent_warps;  // persistent schedule: warps in the grid
 };
 
 struct AppendParams {

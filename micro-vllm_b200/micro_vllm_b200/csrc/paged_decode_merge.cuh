@@ -73,4 +73,64 @@ __global__ void __launch_bounds__(kMergeThreads) paged_decode_merge_kernel(const
     }
 }
 
+// Merge pass of the persistent schedule. One CTA per (KV head h, sequence b):
+// writes the constant result of sequences with no pages (zeros or NaN), and
+// for a (b, h) segment cut across warps w0..w1 combines their partials. The
+// segment's piece is partial slot 1 of w0 when the segment starts inside w0's
+// range after w0's first piece, slot 0 otherwise. Segments inside one warp
+// were written by that warp and are skipped.
+template <typename T, int GP>
+__global__ void __launch_bounds__(kMergeThreads) paged_decode_persistent_merge_kernel(const DecodeParams p) {
+    const int h = blockIdx.x;
+    const int b = blockIdx.y;
+    const SeqSplit seq = seq_split(p, b);
+    if (seq.state != 0) {
+        write_group_constant<T>(p, b, h, seq.state == 1 ? 0.0f : __int_as_float(0x7fffffff));
+        return;
+    }
+    const int64_t* prefix = p.prefix_out;
+    const int64_t warps = p.persistent_warps;
+    const int64_t total = static_cast<int64_t>(p.kv_heads) * prefix[p.batch];
+    const int64_t pages = prefix[b + 1] - prefix[b];
+    const int64_t start = static_cast<int64_t>(p.kv_heads) * prefix[b] + h * pages;
+    const int64_t end = start + pages;
+    const int64_t w0 = ((start + 1) * warps - 1) / total;  // warp owning page `start`
+    const int64_t w1 = (end * warps - 1) / total;          // warp owning page end - 1
+    if (w0 == w1) return;
+    const int n = static_cast<int>(w1 - w0 + 1);
+    const int slot0 = (w0 * total / warps == start) ? 0 : 1;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    T* out = static_cast<T*>(p.out) + b * p.out_stride_seq;
+    auto row_of = [&](int j) -> int64_t { return ((w0 + j) * 2 + (j == 0 ? slot0 : 0)) * GP; };
+    for (int g = warp; g < p.group; g += kMergeThreads / 32) {
+        float mx = -INFINITY;
+        bool nan = false;
+        for (int j = lane; j < n; j += 32) {
+            const float v = p.part_lse[row_of(j) + g];
+            nan |= isnan(v);
+            mx = fmaxf(mx, v);
+        }
+        mx = warp_max(mx);
+        nan = __any_sync(0xffffffffu, nan);
+        T* row = out + static_cast<int64_t>(h * p.group + g) * p.out_stride_head;
+        if (nan) {
+            for (int d = lane; d < p.head_dim; d += 32) row[d] = from_float<T>(__int_as_float(0x7fffffff));
+            continue;
+        }
+        float sum = 0.0f;
+        for (int j = lane; j < n; j += 32) sum += fast_exp2(p.part_lse[row_of(j) + g] - mx);
+        const float inv = 1.0f / warp_sum(sum);
+        for (int d = lane; d < p.head_dim; d += 32) {
+            float acc = 0.0f;
+            for (int j = 0; j < n; ++j) {
+                const int64_t r = row_of(j) + g;
+                const float wgt = fast_exp2(p.part_lse[r] - mx) * inv;
+                acc = fmaf(wgt, p.part_o[r * p.head_dim + d], acc);
+            }
+            row[d] = from_float<T>(acc);
+        }
+    }
+}
+
 }  // namespace mv

@@ -1,38 +1,240 @@
 // Paged GQA decode on sm_100a: TMA page staging + tensor-core (mma.sync) tiles.
 //
-// One CTA owns (split, KV head h, sequence b): a run of pages_per_split pages
-// of one sequence. Every query head of h's GQA group shares each K/V page
-// read, so K/V bytes cross HBM once (the reference kernel re-reads them once
-// per query head: online_attention.cuh:112-115).
+// The unit of work is one 16-token page of one KV head h of one sequence b.
+// All query heads of h's GQA group are processed together, so each K/V page
+// crosses HBM once (the reference kernel re-reads it once per query head:
+// online_attention.cuh:112-115).
 //
-// Inside the CTA each warp owns every NWARPS-th page of the run and runs its
-// own STAGES-deep TMA ring: one elected lane issues two 5-D tiled bulk tensor
-// loads per page (the K page and the V page of head h, each block_size x D,
-// 128-byte swizzled) that complete on the stage's mbarrier; the warp waits,
-// computes, and refills the stage. Page IDs for the warp's whole run are read
-// once, coalesced, one per lane, validated, and broadcast by shuffle.
-//
-// Per 16-token page (block_size 16 = the mma M dimension):
+// Per page, one warp computes (WarpPageAttention below):
 //   S^T[16 tok, 8 q] = K_page[16 x D] . Q^T         mma m16n8k16, A = K via ldmatrix
 //   online softmax on the fragment (exp2 domain, quad shuffles for the max)
 //   P^T fragment from S's accumulator by movmatrix.trans (no shared memory)
 //   O^T[D, 8 q] += V_page^T[D x 16 tok] . P^T       mma m16n8k16, A = V via ldmatrix.trans
-// The GQA group (<= 8 per n-tile) is the mma N dimension, so a group of 7
-// wastes one column of eight; D is the M dimension of the P.V product.
+// The GQA group (<= 8 per n-tile, two n-tiles for groups up to 16) is the mma
+// N dimension, so a group of 7 wastes one column of eight; D is the M dimension
+// of the P.V product.
 //
-// Warps merge through shared memory at the end; a CTA that covers the whole
-// sequence writes the final output, otherwise a normalised partial and its
-// log2-sum-exp for the merge kernel.
+// Pages reach shared memory through each warp's own STAGES-deep ring: one lane
+// issues two 5-D tiled TMA loads per page (the K page and the V page of head h,
+// each block_size x D, 128-byte swizzled) that complete on the stage's mbarrier.
+//
+// Two schedules share that per-page code:
+//  * paged_decode_mma_kernel -- one CTA per (split, KV head, sequence); warps
+//    interleave the split's pages and merge through shared memory; a separate
+//    merge pass combines splits.
+//  * paged_decode_persistent_kernel -- one resident grid; the pages of the whole
+//    batch, laid out (sequence, KV head, page), are cut into equal contiguous
+//    ranges, one per warp (stream-K style), so every warp streams the same
+//    number of bytes whatever the length mix. A warp's range covers whole
+//    (sequence, head) segments, written as final output, plus at most two cut
+//    segments at its ends, written as partials for the merge pass.
 #pragma once
 
 #include "mv_device.cuh"
 
 namespace mv {
 
+constexpr int kPageTokens = 16;  // block_size of the tensor-core kernels (the mma M)
+
+template <int D>
+struct PageTile {
+    static constexpr int kBytes = kPageTokens * D * 2;  // one K (or V) page of one head
+    static_assert(D % 64 == 0, "pages are staged as 64-column (128-byte) swizzled boxes");
+};
+
+// One warp's online-softmax state over the pages of one (sequence, KV head).
+template <typename T, int D, int NT>
+struct WarpPageAttention {
+    using Op = MmaOp<T>;
+    static constexpr int KS = D / 16;
+
+    uint32_t qf[KS][NT][2];  // Q as the mma B operand
+    float m[NT][2];          // running max (exp2 domain) of queries nt*8 + 2*(lane%4) + {0,1}
+    float l[NT][2];          // running denominators (this lane's tokens only until reduce_l)
+    float o[KS][NT][4];      // O^T accumulator fragments
+
+    __device__ __forceinline__ void reset() {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            m[nt][0] = m[nt][1] = -INFINITY;
+            l[nt][0] = l[nt][1] = 0.0f;
+#pragma unroll
+            for (int mt = 0; mt < KS; ++mt) o[mt][nt][0] = o[mt][nt][1] = o[mt][nt][2] = o[mt][nt][3] = 0.0f;
+        }
+    }
+
+    // Lane holds q[g][16 ks + 2(lane%4) + {0,1,8,9}] for g = nt*8 + lane/4 (0 beyond the group).
+    __device__ __forceinline__ void load_q(const DecodeParams& p, int b, int h, int lane) {
+        const uint16_t* qbase = static_cast<const uint16_t*>(p.q) + b * p.q_stride_seq;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const int g = nt * 8 + (lane >> 2);
+            const bool has = g < p.group;
+            const uint16_t* qrow =
+                qbase + static_cast<int64_t>(h * p.group + (has ? g : 0)) * p.q_stride_head;
+#pragma unroll
+            for (int ks = 0; ks < KS; ++ks) {
+                const int d0 = ks * 16 + 2 * (lane & 3);
+                qf[ks][nt][0] = has ? (static_cast<uint32_t>(qrow[d0]) |
+                                       (static_cast<uint32_t>(qrow[d0 + 1]) << 16))
+                                    : 0u;
+                qf[ks][nt][1] = has ? (static_cast<uint32_t>(qrow[d0 + 8]) |
+                                       (static_cast<uint32_t>(qrow[d0 + 9]) << 16))
+                                    : 0u;
+            }
+        }
+    }
+
+    // Attend one staged page: K tile at shared address kt, V tile at vt (vgen is
+    // the V tile's generic pointer), `valid` tokens of 16 in use.
+    __device__ __forceinline__ void attend(uint32_t kt, uint32_t vt, uint8_t* vgen, int valid,
+                                           float scale_log2, int lane) {
+        if (valid < kPageTokens) {
+            // Slots past the context may hold anything (NaN included); P is 0 there,
+            // but 0 * NaN is NaN, so clear those V rows before P.V.
+            const int rows = kPageTokens - valid;
+            for (int idx = lane; idx < (D / 64) * rows * 8; idx += 32) {
+                const int chunk = idx & 7;
+                const int rr = idx >> 3;
+                const int half = rr / rows;
+                const int slot = valid + (rr - half * rows);
+                *reinterpret_cast<uint4*>(vgen + (half * 16 + slot) * 128 + chunk * 16) =
+                    make_uint4(0u, 0u, 0u, 0u);
+            }
+            __syncwarp();
+        }
+        float sc[NT][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.0f;
+        const int k_slot = (lane & 7) + ((lane >> 3) & 1) * 8;  // A = K: matrices (rows, cols) 00,10,01,11
+        const int k_chunk = lane >> 4;
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+            const int r = (ks >> 2) * 16 + k_slot;
+            const int c = ((ks & 3) << 1) + k_chunk;
+            uint32_t a[4];
+            ldmatrix_x4(a, kt + r * 128 + ((c ^ (r & 7)) << 4));
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) Op::run(sc[nt], a, qf[ks][nt][0], qf[ks][nt][1]);
+        }
+        const int row0 = lane >> 2;  // token of accumulator rows c0/c1 (+8 for c2/c3)
+        const bool v0 = row0 < valid;
+        const bool v1 = row0 + 8 < valid;
+        uint32_t pb[NT][2];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const float x0 = v0 ? sc[nt][0] * scale_log2 : -INFINITY;
+            const float x1 = v0 ? sc[nt][1] * scale_log2 : -INFINITY;
+            const float x2 = v1 ? sc[nt][2] * scale_log2 : -INFINITY;
+            const float x3 = v1 ? sc[nt][3] * scale_log2 : -INFINITY;
+            float mx0 = fmaxf(x0, x2);
+            float mx1 = fmaxf(x1, x3);
+#pragma unroll
+            for (int off = 4; off < 32; off <<= 1) {
+                mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
+                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
+            }
+            const float mn0 = fmaxf(m[nt][0], mx0);
+            const float mn1 = fmaxf(m[nt][1], mx1);
+            const float a0 = fast_exp2(m[nt][0] - mn0);
+            const float a1 = fast_exp2(m[nt][1] - mn1);
+            m[nt][0] = mn0;
+            m[nt][1] = mn1;
+            const float p0 = fast_exp2(x0 - mn0);
+            const float p1 = fast_exp2(x1 - mn1);
+            const float p2 = fast_exp2(x2 - mn0);
+            const float p3 = fast_exp2(x3 - mn1);
+            l[nt][0] = l[nt][0] * a0 + (p0 + p2);
+            l[nt][1] = l[nt][1] * a1 + (p1 + p3);
+#pragma unroll
+            for (int mt = 0; mt < KS; ++mt) {
+                o[mt][nt][0] *= a0;
+                o[mt][nt][1] *= a1;
+                o[mt][nt][2] *= a0;
+                o[mt][nt][3] *= a1;
+            }
+            pb[nt][0] = movmatrix_trans(Op::pack(p0, p1));
+            pb[nt][1] = movmatrix_trans(Op::pack(p2, p3));
+        }
+        const int v_tok = (lane & 7) + ((lane >> 4) & 1) * 8;  // A = V^T via .trans
+        const int v_chunk = (lane >> 3) & 1;
+#pragma unroll
+        for (int mt = 0; mt < KS; ++mt) {
+            const int r = (mt >> 2) * 16 + v_tok;
+            const int c = ((mt & 3) << 1) + v_chunk;
+            uint32_t a[4];
+            ldmatrix_x4_trans(a, vt + r * 128 + ((c ^ (r & 7)) << 4));
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) Op::run(o[mt][nt], a, pb[nt][0], pb[nt][1]);
+        }
+    }
+
+    // Sum the denominators over the eight lanes that share a query pair.
+    __device__ __forceinline__ void reduce_l() {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+#pragma unroll
+                for (int off = 4; off < 32; off <<= 1) l[nt][j] += __shfl_xor_sync(0xffffffffu, l[nt][j], off);
+            }
+        }
+    }
+
+    // out[b, h*G + q, :] = O / l for q < group (after reduce_l).
+    __device__ __forceinline__ void store_final(const DecodeParams& p, int b, int h, int lane) const {
+        T* out = static_cast<T*>(p.out) + b * p.out_stride_seq;
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const int q = nt * 8 + 2 * (lane & 3) + j;
+                if (q >= p.group) continue;
+                const float inv = 1.0f / l[nt][j];
+                T* row = out + static_cast<int64_t>(h * p.group + q) * p.out_stride_head;
+#pragma unroll
+                for (int mt = 0; mt < KS; ++mt) {
+                    const int d = mt * 16 + (lane >> 2);
+                    row[d] = from_float<T>(o[mt][nt][j] * inv);
+                    row[d + 8] = from_float<T>(o[mt][nt][j + 2] * inv);
+                }
+            }
+        }
+    }
+
+    // Normalised partial [8*NT][D] and its log2-sum-exp [8*NT] (after reduce_l).
+    __device__ __forceinline__ void store_partial(float* po, float* plse, int group, int lane) const {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const int q = nt * 8 + 2 * (lane & 3) + j;
+                if (q >= group) continue;
+                const float inv = 1.0f / l[nt][j];
+                float* row = po + q * D;
+#pragma unroll
+                for (int mt = 0; mt < KS; ++mt) {
+                    const int d = mt * 16 + (lane >> 2);
+                    row[d] = o[mt][nt][j] * inv;
+                    row[d + 8] = o[mt][nt][j + 2] * inv;
+                }
+                if ((lane >> 2) == 0) plse[q] = m[nt][j] + log2f(l[nt][j]);
+            }
+        }
+    }
+
+    __device__ __forceinline__ void store_partial_nan(float* po, float* plse, int group, int lane) const {
+        const float nan = __int_as_float(0x7fffffff);
+        for (int idx = lane; idx < group * D; idx += 32) po[idx] = nan;
+        if (lane < group) plse[lane] = nan;
+    }
+};
+
+// ------------------------------------------------------- split-grid kernel
+
 template <int D, int NT, int NWARPS, int STAGES>
 struct MmaDecodeShape {
-    static constexpr int kBlock = 16;                      // tokens per page
-    static constexpr int kTileBytes = kBlock * D * 2;      // one K (or V) page of one head
+    static constexpr int kTileBytes = PageTile<D>::kBytes;
     static constexpr int kStageBytes = 2 * kTileBytes;
     static constexpr int kWarpBytes = STAGES * kStageBytes;
     static constexpr int kSmemBytes = NWARPS * kWarpBytes + 1024;  // + 1 KiB for alignment
@@ -40,7 +242,6 @@ struct MmaDecodeShape {
     static constexpr int kRedStride = D + 4;
     static constexpr int kRedBytes = (kQRows * kRedStride + 2 * kQRows) * 4;
     static constexpr int kMaxPagesPerSplit = 32 * NWARPS;  // one page ID per lane per warp
-    static_assert(D % 64 == 0, "pages are staged as 64-column (128-byte) swizzled boxes");
     static_assert(kRedBytes <= kWarpBytes, "warp merge buffer must fit the warp's stages");
 };
 
@@ -49,8 +250,7 @@ __global__ void __launch_bounds__(NWARPS * 32)
 paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap) {
     using Shape = MmaDecodeShape<D, NT, NWARPS, STAGES>;
-    using Op = MmaOp<T>;
-    constexpr int KS = D / 16;  // k-steps of S = K q, and m-tiles of O^T = V^T P^T
+    using Warp = WarpPageAttention<T, D, NT>;
 
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t bars[NWARPS][STAGES];
@@ -106,7 +306,6 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
     uint8_t* wsm = smem + warp * Shape::kWarpBytes;
     const uint32_t wsm_addr = smem_addr(wsm);
 
-    // Prologue: fill the ring.
     const int prologue = n_my < STAGES ? n_my : STAGES;
     for (int i = 0; i < prologue; ++i) {
         const long long id = __shfl_sync(0xffffffffu, my_id, i);
@@ -119,46 +318,9 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
         }
     }
 
-    // Q as the B operand of S^T = K Q^T: lane holds q[g][16 ks + 2(lane%4) + {0,1,8,9}].
-    uint32_t qf[KS][NT][2];
-    {
-        const uint16_t* qbase = static_cast<const uint16_t*>(p.q) + b * p.q_stride_seq;
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-            const int g = nt * 8 + (lane >> 2);
-            const bool has = g < p.group;
-            const uint16_t* qrow =
-                qbase + static_cast<int64_t>(h * p.group + (has ? g : 0)) * p.q_stride_head;
-#pragma unroll
-            for (int ks = 0; ks < KS; ++ks) {
-                const int d0 = ks * 16 + 2 * (lane & 3);
-                qf[ks][nt][0] = has ? (static_cast<uint32_t>(qrow[d0]) |
-                                       (static_cast<uint32_t>(qrow[d0 + 1]) << 16))
-                                    : 0u;
-                qf[ks][nt][1] = has ? (static_cast<uint32_t>(qrow[d0 + 8]) |
-                                       (static_cast<uint32_t>(qrow[d0 + 9]) << 16))
-                                    : 0u;
-            }
-        }
-    }
-
-    float m_run[NT][2];
-    float l_run[NT][2];
-    float o[KS][NT][4];
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-        m_run[nt][0] = m_run[nt][1] = -INFINITY;
-        l_run[nt][0] = l_run[nt][1] = 0.0f;
-#pragma unroll
-        for (int mt = 0; mt < KS; ++mt) o[mt][nt][0] = o[mt][nt][1] = o[mt][nt][2] = o[mt][nt][3] = 0.0f;
-    }
-
-    // Lane-constant parts of the ldmatrix row addresses (see the file comment).
-    const int k_slot = (lane & 7) + ((lane >> 3) & 1) * 8;  // A = K: matrices (rows, cols) 00,10,01,11
-    const int k_chunk = lane >> 4;
-    const int v_tok = (lane & 7) + ((lane >> 4) & 1) * 8;   // A = V^T via .trans
-    const int v_chunk = (lane >> 3) & 1;
-    const int row0 = lane >> 2;                             // token of accumulator rows c0/c1
+    Warp w;
+    w.load_q(p, b, h, lane);
+    w.reset();
 
     bool failed = false;
     int i = 0;
@@ -173,89 +335,12 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
         const uint32_t kt = wsm_addr + st * Shape::kStageBytes;
         const uint32_t vt = kt + Shape::kTileBytes;
         const int64_t page = page_begin + warp + static_cast<int64_t>(i) * NWARPS;
-        const int64_t left = seq.len - page * 16;
-        const int valid = left < 16 ? static_cast<int>(left) : 16;
-        if (valid < 16) {
-            // Slots past the context in the last page may hold anything (NaN included);
-            // P is 0 there, but 0 * NaN is NaN, so clear those V rows before P.V.
-            uint8_t* vgen = wsm + st * Shape::kStageBytes + Shape::kTileBytes;
-            const int rows = 16 - valid;
-            for (int idx = lane; idx < (D / 64) * rows * 8; idx += 32) {
-                const int chunk = idx & 7;
-                const int rr = idx >> 3;
-                const int half = rr / rows;
-                const int slot = valid + (rr - half * rows);
-                *reinterpret_cast<uint4*>(vgen + (half * 16 + slot) * 128 + chunk * 16) =
-                    make_uint4(0u, 0u, 0u, 0u);
-            }
-            __syncwarp();
-        }
+        const int64_t left = seq.len - page * kPageTokens;
+        const int valid = left < kPageTokens ? static_cast<int>(left) : kPageTokens;
+        w.attend(kt, vt, wsm + st * Shape::kStageBytes + Shape::kTileBytes, valid, p.scale_log2, lane);
 
-        float sc[NT][4];
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.0f;
-#pragma unroll
-        for (int ks = 0; ks < KS; ++ks) {
-            const int r = (ks >> 2) * 16 + k_slot;
-            const int c = ((ks & 3) << 1) + k_chunk;
-            uint32_t a[4];
-            ldmatrix_x4(a, kt + r * 128 + ((c ^ (r & 7)) << 4));
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) Op::run(sc[nt], a, qf[ks][nt][0], qf[ks][nt][1]);
-        }
-
-        const bool v0 = row0 < valid;
-        const bool v1 = row0 + 8 < valid;
-        uint32_t pb[NT][2];
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-            const float x0 = v0 ? sc[nt][0] * p.scale_log2 : -INFINITY;
-            const float x1 = v0 ? sc[nt][1] * p.scale_log2 : -INFINITY;
-            const float x2 = v1 ? sc[nt][2] * p.scale_log2 : -INFINITY;
-            const float x3 = v1 ? sc[nt][3] * p.scale_log2 : -INFINITY;
-            float mx0 = fmaxf(x0, x2);
-            float mx1 = fmaxf(x1, x3);
-#pragma unroll
-            for (int off = 4; off < 32; off <<= 1) {
-                mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, off));
-                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, off));
-            }
-            const float mn0 = fmaxf(m_run[nt][0], mx0);
-            const float mn1 = fmaxf(m_run[nt][1], mx1);
-            const float a0 = fast_exp2(m_run[nt][0] - mn0);
-            const float a1 = fast_exp2(m_run[nt][1] - mn1);
-            m_run[nt][0] = mn0;
-            m_run[nt][1] = mn1;
-            const float p0 = fast_exp2(x0 - mn0);
-            const float p1 = fast_exp2(x1 - mn1);
-            const float p2 = fast_exp2(x2 - mn0);
-            const float p3 = fast_exp2(x3 - mn1);
-            l_run[nt][0] = l_run[nt][0] * a0 + (p0 + p2);
-            l_run[nt][1] = l_run[nt][1] * a1 + (p1 + p3);
-#pragma unroll
-            for (int mt = 0; mt < KS; ++mt) {
-                o[mt][nt][0] *= a0;
-                o[mt][nt][1] *= a1;
-                o[mt][nt][2] *= a0;
-                o[mt][nt][3] *= a1;
-            }
-            pb[nt][0] = movmatrix_trans(Op::pack(p0, p1));
-            pb[nt][1] = movmatrix_trans(Op::pack(p2, p3));
-        }
-
-#pragma unroll
-        for (int mt = 0; mt < KS; ++mt) {
-            const int r = (mt >> 2) * 16 + v_tok;
-            const int c = ((mt & 3) << 1) + v_chunk;
-            uint32_t a[4];
-            ldmatrix_x4_trans(a, vt + r * 128 + ((c ^ (r & 7)) << 4));
-#pragma unroll
-            for (int nt = 0; nt < NT; ++nt) Op::run(o[mt][nt], a, pb[nt][0], pb[nt][1]);
-        }
-
-        // Refill this stage with the page STAGES ahead.
         if (i + STAGES < n_my) {
-            if (valid < 16) fence_proxy_async_smem();  // generic writes above, TMA write next
+            if (valid < kPageTokens) fence_proxy_async_smem();  // generic writes above, TMA write next
             __syncwarp();
             const long long id = __shfl_sync(0xffffffffu, my_id, i + STAGES);
             if (lane == 0) {
@@ -277,41 +362,32 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
             atomicOr(&cta_bad, 2);
         }
     }
-
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt) {
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-#pragma unroll
-            for (int off = 4; off < 32; off <<= 1)
-                l_run[nt][j] += __shfl_xor_sync(0xffffffffu, l_run[nt][j], off);
-        }
-    }
+    w.reduce_l();
 
     __syncthreads();  // every warp is done with its stages: reuse them for the merge
     float* red = reinterpret_cast<float*>(wsm);
     float* red_m = red + Shape::kQRows * Shape::kRedStride;
     float* red_l = red_m + Shape::kQRows;
 #pragma unroll
-    for (int mt = 0; mt < KS; ++mt) {
+    for (int mt = 0; mt < Warp::KS; ++mt) {
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
             const int d = mt * 16 + (lane >> 2);
             const int q = nt * 8 + 2 * (lane & 3);
-            red[q * Shape::kRedStride + d] = o[mt][nt][0];
-            red[(q + 1) * Shape::kRedStride + d] = o[mt][nt][1];
-            red[q * Shape::kRedStride + d + 8] = o[mt][nt][2];
-            red[(q + 1) * Shape::kRedStride + d + 8] = o[mt][nt][3];
+            red[q * Shape::kRedStride + d] = w.o[mt][nt][0];
+            red[(q + 1) * Shape::kRedStride + d] = w.o[mt][nt][1];
+            red[q * Shape::kRedStride + d + 8] = w.o[mt][nt][2];
+            red[(q + 1) * Shape::kRedStride + d + 8] = w.o[mt][nt][3];
         }
     }
     if (lane < 4) {
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
             const int q = nt * 8 + 2 * lane;
-            red_m[q] = m_run[nt][0];
-            red_m[q + 1] = m_run[nt][1];
-            red_l[q] = l_run[nt][0];
-            red_l[q + 1] = l_run[nt][1];
+            red_m[q] = w.m[nt][0];
+            red_m[q + 1] = w.m[nt][1];
+            red_l[q] = w.l[nt][0];
+            red_l[q + 1] = w.l[nt][1];
         }
     }
     __syncthreads();
@@ -328,16 +404,16 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
         const int d = idx - g * D;
         float mx = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < NWARPS; ++w) {
-            const float* wm = reinterpret_cast<const float*>(smem + w * Shape::kWarpBytes) +
+        for (int v = 0; v < NWARPS; ++v) {
+            const float* wm = reinterpret_cast<const float*>(smem + v * Shape::kWarpBytes) +
                               Shape::kQRows * Shape::kRedStride;
             mx = fmaxf(mx, wm[g]);
         }
         float den = 0.0f;
         float num = 0.0f;
 #pragma unroll
-        for (int w = 0; w < NWARPS; ++w) {
-            const float* wr = reinterpret_cast<const float*>(smem + w * Shape::kWarpBytes);
+        for (int v = 0; v < NWARPS; ++v) {
+            const float* wr = reinterpret_cast<const float*>(smem + v * Shape::kWarpBytes);
             const float* wm = wr + Shape::kQRows * Shape::kRedStride;
             const float f = fast_exp2(wm[g] - mx);
             den += f * wm[Shape::kQRows + g];
@@ -351,6 +427,272 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
             const int64_t row = (static_cast<int64_t>(b) * p.q_heads + h * p.group + g) * p.max_splits + split;
             p.part_o[row * D + d] = value;
             if (d == 0) p.part_lse[row] = mx + log2f(den);
+        }
+    }
+}
+
+// --------------------------------------------------------- persistent kernel
+
+template <int D, int NWARPS, int STAGES>
+struct PersistentShape {
+    static constexpr int kTileBytes = PageTile<D>::kBytes;
+    static constexpr int kStageBytes = 2 * kTileBytes;
+    static constexpr int kWarpBytes = STAGES * kStageBytes;
+    static constexpr int kStageRegion = NWARPS * kWarpBytes;
+    // + prefix array of (batch + 1) int64, + 1 KiB for alignment
+    static __host__ __device__ constexpr int smem_bytes(int batch) {
+        return kStageRegion + (batch + 1) * 8 + 1024;
+    }
+};
+
+// Global page index -> (sequence, head, page). Segments are laid out
+// sequence-major, then KV head: segment (b, h) holds pages
+// [Hkv*prefix[b] + h*pages_b, + pages_b) of the batch's page space.
+struct PageRef {
+    int seg;      // b * kv_heads + h, or -1 past the warp's range
+    int page;     // page index within the sequence
+    int id;       // physical page, -1 if the table entry is outside the pool
+    int meta;     // valid tokens (bits 0..7) | last page of its segment (bit 8)
+};
+
+__device__ __forceinline__ PageRef locate_page(const DecodeParams& p, const int64_t* prefix,
+                                               int64_t g) {
+    // Largest b with kv_heads * prefix[b] <= g.
+    int lo = 0;
+    int hi = p.batch;  // prefix[batch] * kv_heads > g always
+    while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (p.kv_heads * prefix[mid] <= g) lo = mid;
+        else hi = mid;
+    }
+    const int b = lo;
+    const int64_t pages_b = prefix[b + 1] - prefix[b];
+    const int64_t r = g - p.kv_heads * prefix[b];
+    const int h = static_cast<int>(r / pages_b);
+    const int64_t page = r - h * pages_b;
+    PageRef ref;
+    ref.seg = b * p.kv_heads + h;
+    ref.page = static_cast<int>(page);
+    const int64_t id = load_index(p.block_table, p.table_i64, b * p.table_stride + page);
+    ref.id = (id < 0 || id >= p.num_blocks) ? -1 : static_cast<int>(id);
+    const int64_t len = p.context_lens ? load_index(p.context_lens, p.lens_i64, b) : p.uniform_len;
+    const int64_t left = len - page * kPageTokens;
+    ref.meta = static_cast<int>(left < kPageTokens ? left : kPageTokens) |
+               ((page == pages_b - 1) ? 0x100 : 0);
+    return ref;
+}
+
+template <typename T, int D, int NT, int NWARPS, int STAGES>
+__global__ void __launch_bounds__(NWARPS * 32)
+paged_decode_persistent_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap kmap,
+                               const __grid_constant__ CUtensorMap vmap) {
+    using Shape = PersistentShape<D, NWARPS, STAGES>;
+    using Warp = WarpPageAttention<T, D, NT>;
+    constexpr int kGP = 8 * NT;
+
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t bars[NWARPS][STAGES];
+    __shared__ long long warp_sums[NWARPS];
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    int64_t* prefix = reinterpret_cast<int64_t*>(smem + Shape::kStageRegion);
+
+    // Pages per sequence and their prefix sums (sequences with no work count 0 pages).
+    const int per_thread = (p.batch + blockDim.x - 1) / blockDim.x;
+    const int first = threadIdx.x * per_thread;
+    long long local = 0;
+    for (int k = 0; k < per_thread; ++k) {
+        const int b = first + k;
+        if (b < p.batch) {
+            const SeqSplit s = seq_split(p, b);
+            local += s.pages;
+        }
+    }
+    long long incl = local;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const long long v = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += v;
+    }
+    if (lane == 31) warp_sums[warp] = incl;
+    __syncthreads();
+    long long base = 0;
+    for (int v = 0; v < warp; ++v) base += warp_sums[v];
+    long long run = base + incl - local;
+    for (int k = 0; k < per_thread; ++k) {
+        const int b = first + k;
+        if (b < p.batch) {
+            prefix[b] = run;
+            run += seq_split(p, b).pages;
+        }
+    }
+    if (threadIdx.x == blockDim.x - 1) prefix[p.batch] = run;
+    const uint32_t bar0 = smem_addr(&bars[warp][0]);
+    if (lane == 0) {
+#pragma unroll
+        for (int st = 0; st < STAGES; ++st) mbar_init(bar0 + 8 * st, 1);
+    }
+    fence_mbar_init();
+    __syncthreads();
+    if (blockIdx.x == 0) {
+        // The merge pass reads the layout back from the workspace.
+        for (int b = threadIdx.x; b <= p.batch; b += blockDim.x) p.prefix_out[b] = prefix[b];
+    }
+
+    const int64_t total = static_cast<int64_t>(p.kv_heads) * prefix[p.batch];
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * NWARPS;
+    const int64_t wid = static_cast<int64_t>(blockIdx.x) * NWARPS + warp;
+    const int64_t lo = wid * total / warps;
+    const int64_t hi = (wid + 1) * total / warps;
+    const int n = static_cast<int>(hi - lo);
+    if (n <= 0) return;
+
+    uint8_t* wsm = smem + warp * Shape::kWarpBytes;
+    const uint32_t wsm_addr = smem_addr(wsm);
+
+    // Lane j of `cur` describes page 32k + j of the range, `nxt` the next 32.
+    PageRef cur, nxt;
+    cur.seg = nxt.seg = -1;
+    cur.id = nxt.id = -1;
+    cur.page = nxt.page = 0;
+    cur.meta = nxt.meta = 0;
+    if (lane < n) cur = locate_page(p, prefix, lo + lane);
+    if (32 + lane < n) nxt = locate_page(p, prefix, lo + 32 + lane);
+
+    auto issue = [&](int i, const PageRef& ref_batch) {
+        // Every lane calls this (warp-uniform i): broadcast page i's entry, lane 0 issues.
+        const int src = i & 31;
+        const int id = __shfl_sync(0xffffffffu, ref_batch.id, src);
+        const int seg = __shfl_sync(0xffffffffu, ref_batch.seg, src);
+        if (lane == 0) {
+            const uint32_t bar = bar0 + 8 * (i % STAGES);
+            const uint32_t dst = wsm_addr + (i % STAGES) * Shape::kStageBytes;
+            if (id >= 0) {
+                const int h = seg % p.kv_heads;
+                mbar_arrive_expect_tx(bar, Shape::kStageBytes);
+                tma_load_5d(dst, &kmap, 0, 0, 0, h, id, bar);
+                tma_load_5d(dst + Shape::kTileBytes, &vmap, 0, 0, 0, h, id, bar);
+            } else {
+                // No load for a corrupted ID; complete the phase so the ring stays in step.
+                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+            }
+        }
+    };
+
+    const int prologue = n < STAGES ? n : STAGES;
+    for (int i = 0; i < prologue; ++i) issue(i, i < 32 ? cur : nxt);
+
+    Warp w;
+    int piece_seg = -1;
+    int piece_first_page = 0;
+    bool piece_bad = false;
+    bool first_piece = true;
+    bool failed = false;
+    float* part_o = p.part_o + wid * 2 * kGP * D;
+    float* part_lse = p.part_lse + wid * 2 * kGP;
+
+    for (int i = 0; i < n; ++i) {
+        if (i > 0 && (i & 31) == 0) {
+            cur = nxt;
+            nxt.seg = -1;
+            nxt.id = -1;
+            if (i + 32 + lane < n) nxt = locate_page(p, prefix, lo + i + 32 + lane);
+        }
+        const int src = i & 31;
+        const int seg = __shfl_sync(0xffffffffu, cur.seg, src);
+        const int id = __shfl_sync(0xffffffffu, cur.id, src);
+        const int page = __shfl_sync(0xffffffffu, cur.page, src);
+        const int meta = __shfl_sync(0xffffffffu, cur.meta, src);
+        const int b = seg / p.kv_heads;
+        const int h = seg - b * p.kv_heads;
+        if (seg != piece_seg) {
+            piece_seg = seg;
+            piece_first_page = page;
+            piece_bad = false;
+            w.load_q(p, b, h, lane);
+            w.reset();
+        }
+        const int st = i % STAGES;
+        const bool ok = mbar_wait_bounded(bar0 + 8 * st, (i / STAGES) & 1);
+        if (!__all_sync(0xffffffffu, ok)) {
+            failed = true;
+            // Drain loads still in flight (bounded), then stop this warp.
+            const int last = i + STAGES < n ? i + STAGES : n;
+            for (int j = i + 1; j < last; ++j) mbar_wait_bounded(bar0 + 8 * (j % STAGES), (j / STAGES) & 1);
+            if (lane == 0) atomicOr(&g_device_status, kStatusWaitTimeout);
+            break;
+        }
+        const int valid = meta & 0xff;
+        if (id >= 0) {
+            const uint32_t kt = wsm_addr + st * Shape::kStageBytes;
+            w.attend(kt, kt + Shape::kTileBytes, wsm + st * Shape::kStageBytes + Shape::kTileBytes,
+                     valid, p.scale_log2, lane);
+        } else {
+            piece_bad = true;
+        }
+
+        if (i + STAGES < n) {
+            if (valid < kPageTokens) fence_proxy_async_smem();  // generic writes above, TMA write next
+            __syncwarp();
+            if (lane == 0) fence_proxy_async_smem();
+            const int j = i + STAGES;
+            issue(j, (j >> 5) == (i >> 5) ? cur : nxt);
+        }
+
+        // End of a piece: the next page belongs to another segment, or the range ends.
+        int next_seg = -1;
+        if (i + 1 < n) {
+            const int nsrc = (i + 1) & 31;
+            next_seg = __shfl_sync(0xffffffffu, ((i + 1) >> 5) == (i >> 5) ? cur.seg : nxt.seg, nsrc);
+        }
+        if (next_seg != seg) {
+            const bool whole = piece_first_page == 0 && (meta & 0x100);
+            const int slot = first_piece ? 0 : 1;
+            w.reduce_l();
+            if (whole) {
+                if (piece_bad) {
+                    const float nan = __int_as_float(0x7fffffff);
+                    T* out = static_cast<T*>(p.out) + b * p.out_stride_seq;
+                    for (int idx = lane; idx < p.group * D; idx += 32) {
+                        const int g = idx / D;
+                        out[static_cast<int64_t>(h * p.group + g) * p.out_stride_head + (idx - g * D)] =
+                            from_float<T>(nan);
+                    }
+                } else {
+                    w.store_final(p, b, h, lane);
+                }
+            } else if (piece_bad) {
+                w.store_partial_nan(part_o + slot * kGP * D, part_lse + slot * kGP, p.group, lane);
+            } else {
+                w.store_partial(part_o + slot * kGP * D, part_lse + slot * kGP, p.group, lane);
+            }
+            first_piece = false;
+        }
+    }
+    if (failed) {
+        // Everything this warp had not finished becomes NaN: cut pieces through
+        // both partial slots, whole segments through the output directly.
+        const float nan = __int_as_float(0x7fffffff);
+        w.store_partial_nan(part_o, part_lse, p.group, lane);
+        w.store_partial_nan(part_o + kGP * D, part_lse + kGP, p.group, lane);
+        for (int64_t g = lo; g < hi; g += 32) {
+            const int64_t mine = g + lane;
+            const int seg = mine < hi ? locate_page(p, prefix, mine).seg : -1;
+            for (int src = 0; src < 32; ++src) {
+                const int s = __shfl_sync(0xffffffffu, seg, src);
+                if (s < 0) continue;
+                const int b = s / p.kv_heads;
+                const int h = s - b * p.kv_heads;
+                T* out = static_cast<T*>(p.out) + b * p.out_stride_seq;
+                for (int idx = lane; idx < p.group * D; idx += 32) {
+                    const int q = idx / D;
+                    out[static_cast<int64_t>(h * p.group + q) * p.out_stride_head + (idx - q * D)] =
+                        from_float<T>(nan);
+                }
+            }
         }
     }
 }

@@ -197,26 +197,35 @@ def decode_attention_paged(query: torch.Tensor, cache, *, layer_idx: int) -> tor
         cache._device_page_table, length)
 
 
+def _flags(force_simt, split_grid):
+    return (_native.FLAG_FORCE_SIMT if force_simt else 0) | (_native.FLAG_SPLIT_GRID if split_grid else 0)
+
+
 def paged_decode_plan(query_heads, key_cache, context_bound, *, batch, pages_per_split=0,
-                      force_simt=False):
-    """(path, pages_per_split, max_splits) that ``paged_decode_attention`` would use."""
+                      force_simt=False, split_grid=False):
+    """(path, pages_per_split, max_splits) that ``paged_decode_attention`` would use.
+
+    path is 'tma_mma_persistent' (TMA + tensor cores, persistent grid with equal
+    page ranges per warp), 'tma_mma' (TMA + tensor cores, one CTA per split) or
+    'simt' (CUDA cores, one CTA per split).
+    """
     lib = _native.library()
     num_blocks, kv_heads, block_size, dim = key_cache.shape
     path, pps, splits = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
     with torch.cuda.device(key_cache.device):
         _native.check(lib.mv_paged_decode_plan(
             batch, query_heads, kv_heads, dim, block_size, context_bound, pages_per_split,
-            _native.FLAG_FORCE_SIMT if force_simt else 0, DTYPE_CODES[key_cache.dtype],
+            _flags(force_simt, split_grid), DTYPE_CODES[key_cache.dtype],
             key_cache.data_ptr(), key_cache.data_ptr(), ctypes.byref(path), ctypes.byref(pps),
             ctypes.byref(splits)))
-    return ('tma_mma' if path.value == _native.PATH_TMA_MMA else 'simt'), pps.value, splits.value
+    return _native.PATH_NAMES[path.value], pps.value, splits.value
 
 
 def paged_decode_attention(query: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
                            block_table: torch.Tensor, context_lens: torch.Tensor,
                            scale: float | None = None, *, max_context_len: int | None = None,
                            out: torch.Tensor | None = None, pages_per_split: int = 0,
-                           force_simt: bool = False) -> torch.Tensor:
+                           force_simt: bool = False, split_grid: bool = False) -> torch.Tensor:
     """Batched paged GQA decode over one shared page pool.
 
     query: [B, Hq, D] (or [B, Hq, 1, D]) CUDA fp32/fp16/bf16, feature stride 1.
@@ -229,6 +238,10 @@ def paged_decode_attention(query: torch.Tensor, key_cache: torch.Tensor, value_c
     table capacity max_blocks * bs, so no device read-back is needed. Lengths
     above it produce NaN (the split plan cannot cover them).
     out: optional [B, Hq, D] destination (feature stride 1).
+    pages_per_split / split_grid / force_simt: kernel selection for tests and
+    tuning (a fixed split-KV grid of that many pages per CTA; the CUDA-core
+    kernel); by default the library picks the persistent tensor-core kernel
+    where the shape allows.
     Returns out, or a fresh [B, Hq, D] tensor of the query's dtype.
     """
     squeeze = query.dim() == 4
@@ -277,6 +290,5 @@ def paged_decode_attention(query: torch.Tensor, key_cache: torch.Tensor, value_c
     _run((batch, q_heads, dim), (q.stride(0), q.stride(1)), key_cache, value_cache, block_table,
          block_table.stride(0), block_table.shape[1], context_lens, int(max_context_len), scale,
          _Pointers(q.data_ptr(), out.data_ptr()), (out.stride(0), out.stride(1)),
-         pages_per_split=int(pages_per_split),
-         flags=_native.FLAG_FORCE_SIMT if force_simt else 0)
+         pages_per_split=int(pages_per_split), flags=_flags(force_simt, split_grid))
     return out

@@ -29,14 +29,14 @@ def _fixture(name):
         return {key: data[key] for key in data.files}
 
 
-def _append_and_decode(inputs, *, force_simt=False, pages_per_split=0):
+def _append_and_decode(inputs, *, force_simt=False, pages_per_split=0, split_grid=False):
     attention, cache = _native()
     t = workload_tensors(inputs)
     cache.write_paged_kv(t['key_new'], t['value_new'], t['key_pool'], t['value_pool'],
                          t['block_table'], positions=t['context_lens'], positions_are_end=True)
     out = attention.paged_decode_attention(
         t['q'], t['key_pool'], t['value_pool'], t['block_table'], t['context_lens'],
-        force_simt=force_simt, pages_per_split=pages_per_split)
+        force_simt=force_simt, pages_per_split=pages_per_split, split_grid=split_grid)
     torch.cuda.synchronize()
     return t, out
 
@@ -47,13 +47,20 @@ def _oracle(inputs, key_pool, value_pool):
                         inputs['context_lens'], dim ** -0.5, inputs['spec']['dtype'])
 
 
+MODES = {
+    'auto': {},                               # persistent tensor-core kernel where the shape allows
+    'grid': dict(split_grid=True),            # tensor-core kernel, fixed split grid
+    'split4': dict(pages_per_split=4),        # fixed split grid, 4 pages per split
+    'simt': dict(force_simt=True),            # CUDA-core kernel
+}
+
+
 @pytest.mark.parametrize('name', GOLDEN_CASES)
-@pytest.mark.parametrize('mode', ['auto', 'simt', 'split4'])
+@pytest.mark.parametrize('mode', list(MODES))
 def test_golden_workloads(name, mode):
     inputs = make_inputs(name)
     dtype = inputs['spec']['dtype']
-    t, out = _append_and_decode(inputs, force_simt=mode == 'simt',
-                                pages_per_split=4 if mode == 'split4' else 0)
+    t, out = _append_and_decode(inputs, **MODES[mode])
     fixture = _fixture(name)
     key_pool = to_numpy(t['key_pool'])
     value_pool = to_numpy(t['value_pool'])
@@ -68,13 +75,28 @@ def test_golden_workloads(name, mode):
     assert np.max(np.abs(as_float(out) - reference)) <= bound
 
 
-def test_tensor_core_path_is_selected_for_qwen_geometry():
+def test_tensor_core_paths_are_selected_for_qwen_geometry():
     attention, _ = _native()
     inputs = make_inputs('qwen7b_bf16_small')
     t = workload_tensors(inputs)
-    path, pps, splits = attention.paged_decode_plan(28, t['key_pool'], 4096, batch=64)
-    assert path == 'tma_mma'
-    assert splits >= 2
+    assert attention.paged_decode_plan(28, t['key_pool'], 4096, batch=64)[0] == 'tma_mma_persistent'
+    path, pps, splits = attention.paged_decode_plan(28, t['key_pool'], 4096, batch=64, split_grid=True)
+    assert path == 'tma_mma' and splits >= 2
+    assert attention.paged_decode_plan(28, t['key_pool'], 4096, batch=64, force_simt=True)[0] == 'simt'
+    assert attention.paged_decode_plan(28, t['key_pool'].float(), 4096, batch=64)[0] == 'simt'
+
+
+@pytest.mark.parametrize('lens', [[1], [16], [17], [1, 1, 1], [4096, 1, 33], [5000, 40, 7, 0, 3000],
+                                  [16] * 37, [1029, 700, 1] * 5])
+def test_persistent_ranges_cover_every_length_mix(lens):
+    """Equal page ranges per warp cut segments anywhere; check many length mixes."""
+    spec = dict(batch=len(lens), q_heads=28, kv_heads=4, head_dim=128, block_size=16,
+                pool=('factor', 1.3), lens=('fixed', lens), dtype='bfloat16', value_scale=0.5,
+                seed=31 + len(lens))
+    inputs = make_inputs(spec)
+    t, out = _append_and_decode(inputs)
+    expected = _oracle(inputs, to_numpy(t['key_pool']), to_numpy(t['value_pool']))
+    assert_attention_close(as_float(out), expected, 'bfloat16')
 
 
 @pytest.mark.parametrize('pages_per_split', [1, 4, 8, 12, 128])
@@ -100,10 +122,9 @@ def test_invalid_page_id_poisons_only_that_sequence(name):
     for bad in (-1, t['key_pool'].shape[0], 2 ** 31 - 1):
         table = t['block_table'].clone()
         table[victim, used - 1] = bad
-        for force_simt in (False, True):
+        for mode in MODES.values():
             out = attention.paged_decode_attention(t['q'], t['key_pool'], t['value_pool'], table,
-                                                   t['context_lens'], force_simt=force_simt,
-                                                   pages_per_split=4)
+                                                   t['context_lens'], **mode)
             values = as_float(out)
             assert np.isnan(values[victim]).all()
             others = np.delete(values, victim, axis=0)
@@ -119,9 +140,9 @@ def test_zero_and_out_of_range_lengths():
     lens[0] = 0
     lens[1] = capacity + 1
     lens[2] = -5
-    for force_simt in (False, True):
+    for mode in MODES.values():
         out = as_float(attention.paged_decode_attention(
-            t['q'], t['key_pool'], t['value_pool'], t['block_table'], lens, force_simt=force_simt))
+            t['q'], t['key_pool'], t['value_pool'], t['block_table'], lens, **mode))
         assert (out[0] == 0).all()
         assert np.isnan(out[1]).all() and np.isnan(out[2]).all()
 
@@ -154,10 +175,9 @@ def test_nan_in_unused_slots_does_not_leak(dtype):
         if slot:
             t['key_pool'][last, :, slot:] = float('nan')
             t['value_pool'][last, :, slot:] = float('nan')
-    for force_simt in (False, True):
+    for mode in MODES.values():
         out = attention.paged_decode_attention(t['q'], t['key_pool'], t['value_pool'],
-                                               t['block_table'], t['context_lens'],
-                                               force_simt=force_simt)
+                                               t['block_table'], t['context_lens'], **mode)
         expected = _oracle(inputs, to_numpy(t['key_pool']), to_numpy(t['value_pool']))
         assert np.isfinite(as_float(out)).all()
         assert_attention_close(as_float(out), expected, dtype)
@@ -180,8 +200,8 @@ def test_large_logits_pick_the_argmax_value_exactly(dtype):
     table = torch.arange(pages, device='cuda', dtype=torch.int32)[None]
     lens = torch.tensor([length], device='cuda', dtype=torch.int32)
     vflat = v.permute(1, 0, 2, 3).reshape(2, pages * 16, 64)
-    for force_simt in (False, True):
-        out = attention.paged_decode_attention(q, k, v, table, lens, force_simt=force_simt)
+    for mode in MODES.values():
+        out = attention.paged_decode_attention(q, k, v, table, lens, **mode)
         # even heads (q > 0) pick the largest key (token 0), odd heads the smallest (last token)
         for head in range(14):
             token = 0 if head % 2 == 0 else length - 1
@@ -201,10 +221,9 @@ def test_online_state_is_not_rounded_per_page():
     v[:2] = 1  # tokens 0..31
     table = torch.arange(pages, device='cuda', dtype=torch.int32)[None]
     lens = torch.tensor([length], device='cuda', dtype=torch.int32)
-    for force_simt in (False, True):
+    for mode in MODES.values():
         for pps in (0, 4, 128):
-            out = attention.paged_decode_attention(q, k, v, table, lens, force_simt=force_simt,
-                                                   pages_per_split=pps)
+            out = attention.paged_decode_attention(q, k, v, table, lens, **{'pages_per_split': pps, **mode})
             assert torch.equal(out, torch.full_like(out, 1 + 2 ** -10))
 
 
