@@ -10,6 +10,7 @@
 #include <mutex>
 #include <string>
 #include <type_traits>
+#include <utility>
 
 #include "mvdecode.h"
 #include "paged_append.cuh"
@@ -65,6 +66,25 @@ int device_info(DeviceInfo* info) {
     }
     *info = d;
     return MV_OK;
+}
+
+// Launch with programmatic stream serialization: the grid may start while the
+// previous grid in the stream drains; the kernels wait (griddepcontrol.wait)
+// before touching any input.
+template <typename... Params, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t stream, Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
 // Opt a kernel into `bytes` of dynamic shared memory on the current device.
@@ -324,8 +344,8 @@ int launch_mma(const mv::DecodeParams& p, const CUtensorMap& kmap, const CUtenso
     auto kernel = mv::paged_decode_mma_kernel<T, D, NT, kMmaWarps, STAGES>;
     int rc = ensure_smem(kernel, Shape::kSmemBytes);
     if (rc != MV_OK) return rc;
-    kernel<<<grid, kMmaWarps * 32, Shape::kSmemBytes, stream>>>(p, kmap, vmap);
-    return MV_OK;
+    cudaError_t err = launch_pdl(kernel, grid, dim3(kMmaWarps * 32), Shape::kSmemBytes, stream, p, kmap, vmap);
+    return err == cudaSuccess ? MV_OK : cuda_fail(err, "decode kernel launch");
 }
 
 template <typename T>
@@ -348,12 +368,11 @@ int launch_persistent(const mv::DecodeParams& p, const CUtensorMap& kmap, const 
     auto kernel = persistent_kernel<T, D, NT>();
     int rc = ensure_smem(kernel, persistent_smem<D>());
     if (rc != MV_OK) return rc;
-    kernel<<<ctas, kMmaWarps * 32, persistent_smem<D>(), stream>>>(p, kmap, vmap);
-    cudaError_t err = cudaGetLastError();
+    cudaError_t err = launch_pdl(kernel, dim3(ctas), dim3(kMmaWarps * 32), persistent_smem<D>(), stream,
+                                 p, kmap, vmap);
     if (err != cudaSuccess) return cuda_fail(err, "persistent decode kernel launch");
-    mv::paged_decode_persistent_merge_kernel<T, 8 * NT>
-        <<<dim3(p.kv_heads, p.batch), mv::kMergeThreads, 0, stream>>>(p);
-    err = cudaGetLastError();
+    err = launch_pdl(mv::paged_decode_persistent_merge_kernel<T, 8 * NT>, dim3(p.kv_heads, p.batch),
+                     dim3(mv::kMergeThreads), 0, stream, p);
     return err == cudaSuccess ? MV_OK : cuda_fail(err, "merge kernel launch");
 }
 
@@ -393,7 +412,10 @@ int launch_decode(const mv::DecodeParams& p, const Plan& plan, const CUtensorMap
         const size_t smem = mv::simt_smem_bytes(p.group, p.head_dim);
         auto kernel = mv::paged_decode_simt_kernel<T>;
         rc = ensure_smem(kernel, smem);
-        if (rc == MV_OK) kernel<<<grid, mv::kSimtThreads, smem, stream>>>(p);
+        if (rc == MV_OK) {
+            cudaError_t err = launch_pdl(kernel, grid, dim3(mv::kSimtThreads), smem, stream, p);
+            if (err != cudaSuccess) return cuda_fail(err, "decode kernel launch");
+        }
     }
     if (rc != MV_OK) return rc;
     cudaError_t err = cudaGetLastError();
@@ -403,8 +425,7 @@ int launch_decode(const mv::DecodeParams& p, const Plan& plan, const CUtensorMap
         auto merge = mv::paged_decode_merge_kernel<T>;
         rc = ensure_smem(merge, smem);
         if (rc != MV_OK) return rc;
-        merge<<<dim3(p.q_heads, p.batch), mv::kMergeThreads, smem, stream>>>(p);
-        err = cudaGetLastError();
+        err = launch_pdl(merge, dim3(p.q_heads, p.batch), dim3(mv::kMergeThreads), smem, stream, p);
         if (err != cudaSuccess) return cuda_fail(err, "merge kernel launch");
     }
     return MV_OK;
@@ -612,13 +633,14 @@ int mv_write_paged_kv(const void* key, int64_t key_stride_seq, int64_t key_strid
     const int64_t want = (total + mv::kAppendThreads - 1) / mv::kAppendThreads;
     const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(dev.sms) * 16)));
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaError_t err;
+    const dim3 grid(blocks), block(mv::kAppendThreads);
     switch (vec) {
-        case 16: mv::write_paged_kv_kernel<16><<<blocks, mv::kAppendThreads, 0, s>>>(a, total); break;
-        case 8: mv::write_paged_kv_kernel<8><<<blocks, mv::kAppendThreads, 0, s>>>(a, total); break;
-        case 4: mv::write_paged_kv_kernel<4><<<blocks, mv::kAppendThreads, 0, s>>>(a, total); break;
-        default: mv::write_paged_kv_kernel<2><<<blocks, mv::kAppendThreads, 0, s>>>(a, total); break;
+        case 16: err = launch_pdl(mv::write_paged_kv_kernel<16>, grid, block, 0, s, a, total); break;
+        case 8: err = launch_pdl(mv::write_paged_kv_kernel<8>, grid, block, 0, s, a, total); break;
+        case 4: err = launch_pdl(mv::write_paged_kv_kernel<4>, grid, block, 0, s, a, total); break;
+        default: err = launch_pdl(mv::write_paged_kv_kernel<2>, grid, block, 0, s, a, total); break;
     }
-    cudaError_t err = cudaGetLastError();
     return err == cudaSuccess ? MV_OK : cuda_fail(err, "append kernel launch");
 }
 

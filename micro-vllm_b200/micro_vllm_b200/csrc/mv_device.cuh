@@ -165,6 +165,13 @@ __device__ __forceinline__ float fast_exp2(float x) {
     return y;
 }
 
+// Programmatic dependent launch: every kernel here waits for the grid before
+// it in the stream to finish (and flush) before reading any input, so it may
+// be launched early, overlapping its launch and setup with that grid's tail;
+// and it lets the next grid launch once it has finished its own setup.
+__device__ __forceinline__ void wait_for_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void allow_next_grid() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 __device__ __forceinline__ unsigned long long global_timer_ns() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -27,6 +27,8 @@ template <> struct VecType<2> { using type = uint16_t; };
 template <int VEC>
 __global__ void __launch_bounds__(kAppendThreads) write_paged_kv_kernel(const AppendParams a, int64_t total) {
     using V = typename VecType<VEC>::type;
+    wait_for_prior_grid();
+    allow_next_grid();
     const int chunks = a.row_bytes / VEC;
     const int64_t stride = static_cast<int64_t>(blockDim.x) * gridDim.x;
     for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total;

@@ -19,6 +19,8 @@ __global__ void __launch_bounds__(kMergeThreads) paged_decode_merge_kernel(const
     __shared__ int any_nan;
     const int hq = blockIdx.x;
     const int b = blockIdx.y;
+    wait_for_prior_grid();
+    allow_next_grid();
     const SeqSplit seq = seq_split(p, b);
     if (seq.splits <= 1) return;
     const int n = seq.splits;
@@ -83,14 +85,16 @@ template <typename T, int GP>
 __global__ void __launch_bounds__(kMergeThreads) paged_decode_persistent_merge_kernel(const DecodeParams p) {
     const int h = blockIdx.x;
     const int b = blockIdx.y;
+    wait_for_prior_grid();
+    allow_next_grid();
     const SeqSplit seq = seq_split(p, b);
     if (seq.state != 0) {
         write_group_constant<T>(p, b, h, seq.state == 1 ? 0.0f : __int_as_float(0x7fffffff));
         return;
     }
     const int64_t* prefix = p.prefix_out;
-    const int64_t warps = p.persistent_warps;
     const int64_t total = static_cast<int64_t>(p.kv_heads) * prefix[p.batch];
+    const int64_t warps = p.persistent_warps < total ? p.persistent_warps : total;
     const int64_t pages = prefix[b + 1] - prefix[b];
     const int64_t start = static_cast<int64_t>(p.kv_heads) * prefix[b] + h * pages;
     const int64_t end = start + pages;

@@ -262,6 +262,8 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
     const int h = blockIdx.y;
     const int b = blockIdx.z;
 
+    wait_for_prior_grid();
+    allow_next_grid();
     const SeqSplit seq = seq_split(p, b);
     if (split >= seq.splits) return;
     if (seq.state != 0) {
@@ -499,6 +501,13 @@ paged_decode_persistent_kernel(const DecodeParams p, const __grid_constant__ CUt
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
     int64_t* prefix = reinterpret_cast<int64_t*>(smem + Shape::kStageRegion);
+    const uint32_t bar0 = smem_addr(&bars[warp][0]);
+    if (lane == 0) {
+#pragma unroll
+        for (int st = 0; st < STAGES; ++st) mbar_init(bar0 + 8 * st, 1);
+    }
+    fence_mbar_init();
+    wait_for_prior_grid();
 
     // Pages per sequence and their prefix sums (sequences with no work count 0 pages).
     const int per_thread = (p.batch + blockDim.x - 1) / blockDim.x;
@@ -530,21 +539,18 @@ paged_decode_persistent_kernel(const DecodeParams p, const __grid_constant__ CUt
         }
     }
     if (threadIdx.x == blockDim.x - 1) prefix[p.batch] = run;
-    const uint32_t bar0 = smem_addr(&bars[warp][0]);
-    if (lane == 0) {
-#pragma unroll
-        for (int st = 0; st < STAGES; ++st) mbar_init(bar0 + 8 * st, 1);
-    }
-    fence_mbar_init();
     __syncthreads();
+    allow_next_grid();
     if (blockIdx.x == 0) {
         // The merge pass reads the layout back from the workspace.
         for (int b = threadIdx.x; b <= p.batch; b += blockDim.x) p.prefix_out[b] = prefix[b];
     }
 
     const int64_t total = static_cast<int64_t>(p.kv_heads) * prefix[p.batch];
-    const int64_t warps = static_cast<int64_t>(gridDim.x) * NWARPS;
+    // Never more ranges than pages, so every range in use holds at least one page.
+    const int64_t warps = min(static_cast<int64_t>(gridDim.x) * NWARPS, total);
     const int64_t wid = static_cast<int64_t>(blockIdx.x) * NWARPS + warp;
+    if (wid >= warps) return;
     const int64_t lo = wid * total / warps;
     const int64_t hi = (wid + 1) * total / warps;
     const int n = static_cast<int>(hi - lo);

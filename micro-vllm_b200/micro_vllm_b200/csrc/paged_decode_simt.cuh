@@ -57,6 +57,8 @@ __global__ void __launch_bounds__(kSimtThreads) paged_decode_simt_kernel(const D
     const int h = blockIdx.y;
     const int b = blockIdx.z;
 
+    wait_for_prior_grid();
+    allow_next_grid();
     const SeqSplit seq = seq_split(p, b);
     if (split >= seq.splits) return;
     if (seq.state != 0) {
