@@ -362,6 +362,12 @@ int launch_mma_dispatch(const mv::DecodeParams& p, const CUtensorMap& kmap, cons
     }
 }
 
+// One warp per output row (sequence, query head).
+dim3 merge_grid(const mv::DecodeParams& p) {
+    const int64_t rows = static_cast<int64_t>(p.batch) * p.q_heads;
+    return dim3(static_cast<unsigned>((rows + mv::kMergeRowsPerCta - 1) / mv::kMergeRowsPerCta));
+}
+
 template <typename T, int D, int NT>
 int launch_persistent(const mv::DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap,
                       int ctas, cudaStream_t stream) {
@@ -371,7 +377,7 @@ int launch_persistent(const mv::DecodeParams& p, const CUtensorMap& kmap, const 
     cudaError_t err = launch_pdl(kernel, dim3(ctas), dim3(kMmaWarps * 32), persistent_smem<D>(), stream,
                                  p, kmap, vmap);
     if (err != cudaSuccess) return cuda_fail(err, "persistent decode kernel launch");
-    err = launch_pdl(mv::paged_decode_persistent_merge_kernel<T, 8 * NT>, dim3(p.kv_heads, p.batch),
+    err = launch_pdl(mv::paged_decode_persistent_merge_kernel<T, 8 * NT>, merge_grid(p),
                      dim3(mv::kMergeThreads), 0, stream, p);
     return err == cudaSuccess ? MV_OK : cuda_fail(err, "merge kernel launch");
 }
@@ -421,11 +427,8 @@ int launch_decode(const mv::DecodeParams& p, const Plan& plan, const CUtensorMap
     cudaError_t err = cudaGetLastError();
     if (err != cudaSuccess) return cuda_fail(err, "decode kernel launch");
     if (plan.max_splits > 1) {
-        const size_t smem = static_cast<size_t>(plan.max_splits) * sizeof(float);
-        auto merge = mv::paged_decode_merge_kernel<T>;
-        rc = ensure_smem(merge, smem);
-        if (rc != MV_OK) return rc;
-        err = launch_pdl(merge, dim3(p.q_heads, p.batch), dim3(mv::kMergeThreads), smem, stream, p);
+        err = launch_pdl(mv::paged_decode_merge_kernel<T>, merge_grid(p), dim3(mv::kMergeThreads), 0,
+                         stream, p);
         if (err != cudaSuccess) return cuda_fail(err, "merge kernel launch");
     }
     return MV_OK;

@@ -35,6 +35,10 @@
 namespace mv {
 
 constexpr int kPageTokens = 16;  // block_size of the tensor-core kernels (the mma M)
+// Pages each warp keeps requested into L2 beyond its shared-memory ring: the
+// ring (a few pages) alone holds too few bytes in flight per SM to cover HBM
+// latency under load; L2 prefetches raise that without using shared memory.
+constexpr int kPrefetchPages = 8;
 
 template <int D>
 struct PageTile {
@@ -319,6 +323,13 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
             tma_load_5d(dst + Shape::kTileBytes, &vmap, 0, 0, 0, h, static_cast<int>(id), bar);
         }
     }
+    for (int i = prologue; i < n_my && i < STAGES + kPrefetchPages; ++i) {
+        const long long id = __shfl_sync(0xffffffffu, my_id, i);
+        if (lane == 0) {
+            tma_prefetch_l2_5d(&kmap, 0, 0, 0, h, static_cast<int>(id));
+            tma_prefetch_l2_5d(&vmap, 0, 0, 0, h, static_cast<int>(id));
+        }
+    }
 
     Warp w;
     w.load_q(p, b, h, lane);
@@ -345,12 +356,18 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
             if (valid < kPageTokens) fence_proxy_async_smem();  // generic writes above, TMA write next
             __syncwarp();
             const long long id = __shfl_sync(0xffffffffu, my_id, i + STAGES);
+            const int ahead = i + STAGES + kPrefetchPages;
+            const long long pf = __shfl_sync(0xffffffffu, my_id, ahead & 31);
             if (lane == 0) {
                 fence_proxy_async_smem();
                 const uint32_t bar = bar0 + 8 * st;
                 mbar_arrive_expect_tx(bar, Shape::kStageBytes);
                 tma_load_5d(kt, &kmap, 0, 0, 0, h, static_cast<int>(id), bar);
                 tma_load_5d(vt, &vmap, 0, 0, 0, h, static_cast<int>(id), bar);
+                if (ahead < n_my) {
+                    tma_prefetch_l2_5d(&kmap, 0, 0, 0, h, static_cast<int>(pf));
+                    tma_prefetch_l2_5d(&vmap, 0, 0, 0, h, static_cast<int>(pf));
+                }
             }
         }
     }
@@ -588,8 +605,21 @@ paged_decode_persistent_kernel(const DecodeParams p, const __grid_constant__ CUt
         }
     };
 
+    // L2 prefetch of page j (every lane calls; j within the cur/nxt window).
+    auto prefetch = [&](int j, const PageRef& ref_batch) {
+        const int src = j & 31;
+        const int id = __shfl_sync(0xffffffffu, ref_batch.id, src);
+        const int seg = __shfl_sync(0xffffffffu, ref_batch.seg, src);
+        if (lane == 0 && id >= 0) {
+            const int h = seg % p.kv_heads;
+            tma_prefetch_l2_5d(&kmap, 0, 0, 0, h, id);
+            tma_prefetch_l2_5d(&vmap, 0, 0, 0, h, id);
+        }
+    };
+
     const int prologue = n < STAGES ? n : STAGES;
     for (int i = 0; i < prologue; ++i) issue(i, i < 32 ? cur : nxt);
+    for (int i = prologue; i < n && i < STAGES + kPrefetchPages; ++i) prefetch(i, i < 32 ? cur : nxt);
 
     Warp w;
     int piece_seg = -1;
@@ -646,6 +676,8 @@ paged_decode_persistent_kernel(const DecodeParams p, const __grid_constant__ CUt
             if (lane == 0) fence_proxy_async_smem();
             const int j = i + STAGES;
             issue(j, (j >> 5) == (i >> 5) ? cur : nxt);
+            const int ahead = j + kPrefetchPages;
+            if (ahead < n) prefetch(ahead, (ahead >> 5) == (i >> 5) ? cur : nxt);
         }
 
         // End of a piece: the next page belongs to another segment, or the range ends.
