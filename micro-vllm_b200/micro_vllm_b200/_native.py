@@ -7,7 +7,11 @@ import ctypes
 from functools import lru_cache
 from pathlib import Path
 
-LIB_PATH = Path(__file__).resolve().parent / 'lib' / 'libmvdecode.so'
+import os
+
+# MVDECODE_LIBRARY may name another build of the same library (e.g. a tuning variant).
+LIB_PATH = Path(os.environ.get('MVDECODE_LIBRARY',
+                               Path(__file__).resolve().parent / 'lib' / 'libmvdecode.so'))
 
 MV_ABI_VERSION = 1
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2

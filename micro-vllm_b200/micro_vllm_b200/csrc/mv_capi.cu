@@ -98,7 +98,21 @@ int ensure_smem(Kernel kernel, size_t bytes) {
 
 // ---------------------------------------------------------------- planning
 
-constexpr int kMmaWarps = 4;
+// Tensor-core kernel shape: warps per CTA and TMA stages per warp by head_dim
+// (overridable at build time for tuning sweeps).
+#ifndef MV_MMA_WARPS
+#define MV_MMA_WARPS 4
+#endif
+#ifndef MV_STAGES_D64
+#define MV_STAGES_D64 6
+#endif
+#ifndef MV_STAGES_D128
+#define MV_STAGES_D128 3
+#endif
+#ifndef MV_STAGES_D256
+#define MV_STAGES_D256 2
+#endif
+constexpr int kMmaWarps = MV_MMA_WARPS;
 constexpr int kMaxPagesPerSplit = 32 * kMmaWarps;
 
 struct Geometry {
@@ -143,7 +157,9 @@ size_t round256(size_t bytes) { return (bytes + 255) / 256 * 256; }
 
 // Persistent kernel: stages per warp for each head_dim (~96 KiB of stages per CTA
 // so two CTAs share an SM; one at head_dim 256), and the batch its prefix array fits.
-template <int D> struct PersistentStages { static constexpr int value = D == 64 ? 6 : (D == 128 ? 3 : 2); };
+template <int D> struct PersistentStages {
+    static constexpr int value = D == 64 ? MV_STAGES_D64 : (D == 128 ? MV_STAGES_D128 : MV_STAGES_D256);
+};
 constexpr int kPersistentMaxBatch = 1023;
 
 template <typename T, int D, int NT>
@@ -339,7 +355,7 @@ int page_tensor_map(const void* base, int64_t num_blocks, int heads, int dim, in
 template <typename T, int D, int NT>
 int launch_mma(const mv::DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap, dim3 grid,
                cudaStream_t stream) {
-    constexpr int STAGES = D == 64 ? 6 : (D == 128 ? 3 : 2);
+    constexpr int STAGES = D == 64 ? MV_STAGES_D64 : (D == 128 ? MV_STAGES_D128 : MV_STAGES_D256);
     using Shape = mv::MmaDecodeShape<D, NT, kMmaWarps, STAGES>;
     auto kernel = mv::paged_decode_mma_kernel<T, D, NT, kMmaWarps, STAGES>;
     int rc = ensure_smem(kernel, Shape::kSmemBytes);

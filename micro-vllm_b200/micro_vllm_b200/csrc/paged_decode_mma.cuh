@@ -35,10 +35,14 @@
 namespace mv {
 
 constexpr int kPageTokens = 16;  // block_size of the tensor-core kernels (the mma M)
-// Pages each warp keeps requested into L2 beyond its shared-memory ring: the
-// ring (a few pages) alone holds too few bytes in flight per SM to cover HBM
-// latency under load; L2 prefetches raise that without using shared memory.
-constexpr int kPrefetchPages = 8;
+// Pages each warp requests into L2 (bulk tensor prefetch, no shared memory)
+// beyond its shared-memory ring. 0 disables it: measured on B200 with one
+// resident page stream per warp, prefetching 8 pages ahead thrashed L2 and
+// cost 20-45% of bandwidth.
+#ifndef MV_PREFETCH_PAGES
+#define MV_PREFETCH_PAGES 0
+#endif
+constexpr int kPrefetchPages = MV_PREFETCH_PAGES;
 
 template <int D>
 struct PageTile {
@@ -323,7 +327,7 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
             tma_load_5d(dst + Shape::kTileBytes, &vmap, 0, 0, 0, h, static_cast<int>(id), bar);
         }
     }
-    for (int i = prologue; i < n_my && i < STAGES + kPrefetchPages; ++i) {
+    for (int i = prologue; kPrefetchPages > 0 && i < n_my && i < STAGES + kPrefetchPages; ++i) {
         const long long id = __shfl_sync(0xffffffffu, my_id, i);
         if (lane == 0) {
             tma_prefetch_l2_5d(&kmap, 0, 0, 0, h, static_cast<int>(id));
@@ -364,7 +368,7 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
                 mbar_arrive_expect_tx(bar, Shape::kStageBytes);
                 tma_load_5d(kt, &kmap, 0, 0, 0, h, static_cast<int>(id), bar);
                 tma_load_5d(vt, &vmap, 0, 0, 0, h, static_cast<int>(id), bar);
-                if (ahead < n_my) {
+                if (kPrefetchPages > 0 && ahead < n_my) {
                     tma_prefetch_l2_5d(&kmap, 0, 0, 0, h, static_cast<int>(pf));
                     tma_prefetch_l2_5d(&vmap, 0, 0, 0, h, static_cast<int>(pf));
                 }
@@ -619,7 +623,8 @@ paged_decode_persistent_kernel(const DecodeParams p, const __grid_constant__ CUt
 
     const int prologue = n < STAGES ? n : STAGES;
     for (int i = 0; i < prologue; ++i) issue(i, i < 32 ? cur : nxt);
-    for (int i = prologue; i < n && i < STAGES + kPrefetchPages; ++i) prefetch(i, i < 32 ? cur : nxt);
+    for (int i = prologue; kPrefetchPages > 0 && i < n && i < STAGES + kPrefetchPages; ++i)
+        prefetch(i, i < 32 ? cur : nxt);
 
     Warp w;
     int piece_seg = -1;
@@ -677,7 +682,7 @@ paged_decode_persistent_kernel(const DecodeParams p, const __grid_constant__ CUt
             const int j = i + STAGES;
             issue(j, (j >> 5) == (i >> 5) ? cur : nxt);
             const int ahead = j + kPrefetchPages;
-            if (ahead < n) prefetch(ahead, (ahead >> 5) == (i >> 5) ? cur : nxt);
+            if (kPrefetchPages > 0 && ahead < n) prefetch(ahead, (ahead >> 5) == (i >> 5) ? cur : nxt);
         }
 
         // End of a piece: the next page belongs to another segment, or the range ends.
