@@ -93,10 +93,18 @@ struct WarpPageAttention {
         }
     }
 
-    // Attend one staged page: K tile at shared address kt, V tile at vt (vgen is
-    // the V tile's generic pointer), `valid` tokens of 16 in use.
-    __device__ __forceinline__ void attend(uint32_t kt, uint32_t vt, uint8_t* vgen, int valid,
-                                           float scale_log2, int lane) {
+    // The staged page as mma A fragments: K for S^T = K Q^T, V^T (via .trans)
+    // for O^T += V^T P^T. Loading them first frees the stage for the next TMA
+    // load before any of the page's arithmetic runs.
+    struct PageFrags {
+        uint32_t k[KS][4];
+        uint32_t v[KS][4];
+    };
+
+    // K tile at shared address kt, V tile at vt (vgen: its generic pointer);
+    // `valid` tokens of 16 in use.
+    __device__ __forceinline__ static void load_page(PageFrags& f, uint32_t kt, uint32_t vt, uint8_t* vgen,
+                                                     int valid, int lane) {
         if (valid < kPageTokens) {
             // Slots past the context may hold anything (NaN included); P is 0 there,
             // but 0 * NaN is NaN, so clear those V rows before P.V.
@@ -111,19 +119,36 @@ struct WarpPageAttention {
             }
             __syncwarp();
         }
-        float sc[NT][4];
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.0f;
         const int k_slot = (lane & 7) + ((lane >> 3) & 1) * 8;  // A = K: matrices (rows, cols) 00,10,01,11
         const int k_chunk = lane >> 4;
+        const int v_tok = (lane & 7) + ((lane >> 4) & 1) * 8;   // A = V^T via .trans
+        const int v_chunk = (lane >> 3) & 1;
 #pragma unroll
         for (int ks = 0; ks < KS; ++ks) {
             const int r = (ks >> 2) * 16 + k_slot;
             const int c = ((ks & 3) << 1) + k_chunk;
-            uint32_t a[4];
-            ldmatrix_x4(a, kt + r * 128 + ((c ^ (r & 7)) << 4));
+            ldmatrix_x4(f.k[ks], kt + r * 128 + ((c ^ (r & 7)) << 4));
+        }
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) Op::run(sc[nt], a, qf[ks][nt][0], qf[ks][nt][1]);
+        for (int mt = 0; mt < KS; ++mt) {
+            const int r = (mt >> 2) * 16 + v_tok;
+            const int c = ((mt & 3) << 1) + v_chunk;
+            ldmatrix_x4_trans(f.v[mt], vt + r * 128 + ((c ^ (r & 7)) << 4));
+        }
+    }
+
+    // Online-softmax update with one page held in registers.
+    __device__ __forceinline__ void attend(const PageFrags& f, int valid, float scale_log2, int lane) {
+        // Two accumulator chains (even and odd k-steps) halve the dependent mma chain.
+        float sc[NT][2][4];
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int c = 0; c < 2; ++c) sc[nt][c][0] = sc[nt][c][1] = sc[nt][c][2] = sc[nt][c][3] = 0.0f;
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) Op::run(sc[nt][ks & 1], f.k[ks], qf[ks][nt][0], qf[ks][nt][1]);
         }
         const int row0 = lane >> 2;  // token of accumulator rows c0/c1 (+8 for c2/c3)
         const bool v0 = row0 < valid;
@@ -131,10 +156,10 @@ struct WarpPageAttention {
         uint32_t pb[NT][2];
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-            const float x0 = v0 ? sc[nt][0] * scale_log2 : -INFINITY;
-            const float x1 = v0 ? sc[nt][1] * scale_log2 : -INFINITY;
-            const float x2 = v1 ? sc[nt][2] * scale_log2 : -INFINITY;
-            const float x3 = v1 ? sc[nt][3] * scale_log2 : -INFINITY;
+            const float x0 = v0 ? (sc[nt][0][0] + sc[nt][1][0]) * scale_log2 : -INFINITY;
+            const float x1 = v0 ? (sc[nt][0][1] + sc[nt][1][1]) * scale_log2 : -INFINITY;
+            const float x2 = v1 ? (sc[nt][0][2] + sc[nt][1][2]) * scale_log2 : -INFINITY;
+            const float x3 = v1 ? (sc[nt][0][3] + sc[nt][1][3]) * scale_log2 : -INFINITY;
             float mx0 = fmaxf(x0, x2);
             float mx1 = fmaxf(x1, x3);
 #pragma unroll
@@ -164,16 +189,10 @@ struct WarpPageAttention {
             pb[nt][0] = movmatrix_trans(Op::pack(p0, p1));
             pb[nt][1] = movmatrix_trans(Op::pack(p2, p3));
         }
-        const int v_tok = (lane & 7) + ((lane >> 4) & 1) * 8;  // A = V^T via .trans
-        const int v_chunk = (lane >> 3) & 1;
 #pragma unroll
         for (int mt = 0; mt < KS; ++mt) {
-            const int r = (mt >> 2) * 16 + v_tok;
-            const int c = ((mt & 3) << 1) + v_chunk;
-            uint32_t a[4];
-            ldmatrix_x4_trans(a, vt + r * 128 + ((c ^ (r & 7)) << 4));
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) Op::run(o[mt][nt], a, pb[nt][0], pb[nt][1]);
+            for (int nt = 0; nt < NT; ++nt) Op::run(o[mt][nt], f.v[mt], pb[nt][0], pb[nt][1]);
         }
     }
 
@@ -354,16 +373,17 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
         const int64_t page = page_begin + warp + static_cast<int64_t>(i) * NWARPS;
         const int64_t left = seq.len - page * kPageTokens;
         const int valid = left < kPageTokens ? static_cast<int>(left) : kPageTokens;
-        w.attend(kt, vt, wsm + st * Shape::kStageBytes + Shape::kTileBytes, valid, p.scale_log2, lane);
+        typename Warp::PageFrags frags;
+        Warp::load_page(frags, kt, vt, wsm + st * Shape::kStageBytes + Shape::kTileBytes, valid, lane);
 
+        // The page is in registers: refill its stage before the arithmetic.
         if (i + STAGES < n_my) {
-            if (valid < kPageTokens) fence_proxy_async_smem();  // generic writes above, TMA write next
+            fence_proxy_async_smem();  // this lane's shared reads/writes before the TMA write
             __syncwarp();
             const long long id = __shfl_sync(0xffffffffu, my_id, i + STAGES);
             const int ahead = i + STAGES + kPrefetchPages;
             const long long pf = __shfl_sync(0xffffffffu, my_id, ahead & 31);
             if (lane == 0) {
-                fence_proxy_async_smem();
                 const uint32_t bar = bar0 + 8 * st;
                 mbar_arrive_expect_tx(bar, Shape::kStageBytes);
                 tma_load_5d(kt, &kmap, 0, 0, 0, h, static_cast<int>(id), bar);
@@ -374,6 +394,7 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
                 }
             }
         }
+        w.attend(frags, valid, p.scale_log2, lane);
     }
 
     if (failed) {
@@ -667,23 +688,25 @@ paged_decode_persistent_kernel(const DecodeParams p, const __grid_constant__ CUt
             break;
         }
         const int valid = meta & 0xff;
+        typename Warp::PageFrags frags;
         if (id >= 0) {
             const uint32_t kt = wsm_addr + st * Shape::kStageBytes;
-            w.attend(kt, kt + Shape::kTileBytes, wsm + st * Shape::kStageBytes + Shape::kTileBytes,
-                     valid, p.scale_log2, lane);
+            Warp::load_page(frags, kt, kt + Shape::kTileBytes,
+                            wsm + st * Shape::kStageBytes + Shape::kTileBytes, valid, lane);
         } else {
             piece_bad = true;
         }
 
+        // The page is in registers: refill its stage before the arithmetic.
         if (i + STAGES < n) {
-            if (valid < kPageTokens) fence_proxy_async_smem();  // generic writes above, TMA write next
+            fence_proxy_async_smem();  // this lane's shared reads/writes before the TMA write
             __syncwarp();
-            if (lane == 0) fence_proxy_async_smem();
             const int j = i + STAGES;
             issue(j, (j >> 5) == (i >> 5) ? cur : nxt);
             const int ahead = j + kPrefetchPages;
             if (kPrefetchPages > 0 && ahead < n) prefetch(ahead, (ahead >> 5) == (i >> 5) ? cur : nxt);
         }
+        if (id >= 0) w.attend(frags, valid, p.scale_log2, lane);
 
         // End of a piece: the next page belongs to another segment, or the range ends.
         int next_seg = -1;
