@@ -378,11 +378,8 @@ int launch_mma_dispatch(const mv::DecodeParams& p, const CUtensorMap& kmap, cons
     }
 }
 
-// One warp per output row (sequence, query head).
-dim3 merge_grid(const mv::DecodeParams& p) {
-    const int64_t rows = static_cast<int64_t>(p.batch) * p.q_heads;
-    return dim3(static_cast<unsigned>((rows + mv::kMergeRowsPerCta - 1) / mv::kMergeRowsPerCta));
-}
+// One CTA per output row (query head, sequence).
+dim3 merge_grid(const mv::DecodeParams& p) { return dim3(p.q_heads, p.batch); }
 
 template <typename T, int D, int NT>
 int launch_persistent(const mv::DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap,

@@ -6,10 +6,10 @@
 // (no overflow for large finite partials). A NaN partial (corrupted page ID,
 // or a wait that gave up) poisons the row, as in the reference.
 //
-// One warp per output row, four rows per CTA: the lanes read the pieces'
-// log-sum-exps in parallel, then stream the partial rows with lanes over the
-// head dimension and the pieces' weights broadcast by shuffle, so every load
-// of the second phase is independent of the others.
+// One CTA per output row: the threads read the pieces' log-sum-exps in
+// parallel, reduce them through shared memory, then each thread owns output
+// columns and streams the pieces' partial rows with the weights read from
+// shared memory, so the loads of every piece are independent and coalesced.
 #pragma once
 
 #include "mv_device.cuh"
@@ -17,53 +17,60 @@
 namespace mv {
 
 constexpr int kMergeThreads = 128;
-constexpr int kMergeRowsPerCta = kMergeThreads / 32;
+constexpr int kMergeChunk = 256;  // pieces whose weights are staged at a time
 
 template <typename T, typename RowOf>
-__device__ __forceinline__ void merge_row(const DecodeParams& p, T* out, RowOf row_of, int n, int lane) {
+__device__ __forceinline__ void merge_row(const DecodeParams& p, T* out, RowOf row_of, int n) {
+    __shared__ float weights[kMergeChunk];
+    __shared__ float red[kMergeThreads / 32];
+    __shared__ int any_nan;
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    if (tid == 0) any_nan = 0;
     float mx = -INFINITY;
-    bool nan = false;
-    for (int j = lane; j < n; j += 32) {
+    for (int j = tid; j < n; j += kMergeThreads) {
         const float v = p.part_lse[row_of(j)];
-        nan |= isnan(v);
+        if (isnan(v)) any_nan = 1;
         mx = fmaxf(mx, v);
     }
     mx = warp_max(mx);
-    if (__any_sync(0xffffffffu, nan)) {
-        for (int d = lane; d < p.head_dim; d += 32) out[d] = from_float<T>(__int_as_float(0x7fffffff));
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    mx = red[0];
+#pragma unroll
+    for (int w = 1; w < kMergeThreads / 32; ++w) mx = fmaxf(mx, red[w]);
+    if (any_nan) {
+        for (int d = tid; d < p.head_dim; d += kMergeThreads) out[d] = from_float<T>(__int_as_float(0x7fffffff));
         return;
     }
     float sum = 0.0f;
-    for (int j = lane; j < n; j += 32) sum += fast_exp2(p.part_lse[row_of(j)] - mx);
-    const float inv = 1.0f / warp_sum(sum);
+    for (int j = tid; j < n; j += kMergeThreads) sum += fast_exp2(p.part_lse[row_of(j)] - mx);
+    sum = warp_sum(sum);
+    __syncthreads();  // red[] reads above are done
+    if (lane == 0) red[warp] = sum;
+    __syncthreads();
+    float total = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kMergeThreads / 32; ++w) total += red[w];
+    const float inv = 1.0f / total;
 
-    constexpr int kCols = 4;  // columns per lane per pass: 128 columns per pass
-    for (int d0 = 0; d0 < p.head_dim; d0 += 32 * kCols) {
-        float acc[kCols];
-#pragma unroll
-        for (int c = 0; c < kCols; ++c) acc[c] = 0.0f;
-        for (int j0 = 0; j0 < n; j0 += 32) {
-            const int j = j0 + lane;
-            const float wj = j < n ? fast_exp2(p.part_lse[row_of(j)] - mx) * inv : 0.0f;
-            const long long rj = j < n ? row_of(j) : 0;
-            const int count = n - j0 < 32 ? n - j0 : 32;
-#pragma unroll 4
-            for (int k = 0; k < count; ++k) {
-                const float w = __shfl_sync(0xffffffffu, wj, k);
-                const long long r = __shfl_sync(0xffffffffu, rj, k);
-                const float* src = p.part_o + r * p.head_dim;
-#pragma unroll
-                for (int c = 0; c < kCols; ++c) {
-                    const int d = d0 + c * 32 + lane;
-                    if (d < p.head_dim) acc[c] = fmaf(w, src[d], acc[c]);
-                }
+    for (int d0 = 0; d0 < p.head_dim; d0 += kMergeThreads) {
+        const int d = d0 + tid;
+        float acc = 0.0f;
+        for (int j0 = 0; j0 < n; j0 += kMergeChunk) {
+            const int count = n - j0 < kMergeChunk ? n - j0 : kMergeChunk;
+            __syncthreads();  // previous chunk's weights are consumed
+            for (int j = tid; j < count; j += kMergeThreads)
+                weights[j] = fast_exp2(p.part_lse[row_of(j0 + j)] - mx) * inv;
+            __syncthreads();
+            if (d < p.head_dim) {
+#pragma unroll 8
+                for (int j = 0; j < count; ++j)
+                    acc = fmaf(weights[j], p.part_o[static_cast<int64_t>(row_of(j0 + j)) * p.head_dim + d], acc);
             }
         }
-#pragma unroll
-        for (int c = 0; c < kCols; ++c) {
-            const int d = d0 + c * 32 + lane;
-            if (d < p.head_dim) out[d] = from_float<T>(acc[c]);
-        }
+        if (d < p.head_dim) out[d] = from_float<T>(acc);
     }
 }
 
@@ -74,16 +81,13 @@ template <typename T>
 __global__ void __launch_bounds__(kMergeThreads) paged_decode_merge_kernel(const DecodeParams p) {
     wait_for_prior_grid();
     allow_next_grid();
-    const int lane = threadIdx.x & 31;
-    const int64_t row = static_cast<int64_t>(blockIdx.x) * kMergeRowsPerCta + (threadIdx.x >> 5);
-    if (row >= static_cast<int64_t>(p.batch) * p.q_heads) return;
-    const int b = static_cast<int>(row / p.q_heads);
-    const int hq = static_cast<int>(row - static_cast<int64_t>(b) * p.q_heads);
+    const int hq = blockIdx.x;
+    const int b = blockIdx.y;
     const SeqSplit seq = seq_split(p, b);
     if (seq.splits <= 1) return;
     T* out = static_cast<T*>(p.out) + b * p.out_stride_seq + static_cast<int64_t>(hq) * p.out_stride_head;
-    const int64_t base = row * p.max_splits;
-    merge_row<T>(p, out, [&](int j) -> long long { return base + j; }, seq.splits, lane);
+    const int64_t base = (static_cast<int64_t>(b) * p.q_heads + hq) * p.max_splits;
+    merge_row<T>(p, out, [&](int j) -> long long { return base + j; }, seq.splits);
 }
 
 // Merge of the persistent schedule. Row (b, hq) belongs to segment (b, h =
@@ -96,18 +100,15 @@ template <typename T, int GP>
 __global__ void __launch_bounds__(kMergeThreads) paged_decode_persistent_merge_kernel(const DecodeParams p) {
     wait_for_prior_grid();
     allow_next_grid();
-    const int lane = threadIdx.x & 31;
-    const int64_t row = static_cast<int64_t>(blockIdx.x) * kMergeRowsPerCta + (threadIdx.x >> 5);
-    if (row >= static_cast<int64_t>(p.batch) * p.q_heads) return;
-    const int b = static_cast<int>(row / p.q_heads);
-    const int hq = static_cast<int>(row - static_cast<int64_t>(b) * p.q_heads);
+    const int hq = blockIdx.x;
+    const int b = blockIdx.y;
     const int h = hq / p.group;
     const int g = hq - h * p.group;
     T* out = static_cast<T*>(p.out) + b * p.out_stride_seq + static_cast<int64_t>(hq) * p.out_stride_head;
     const SeqSplit seq = seq_split(p, b);
     if (seq.state != 0) {
         const float value = seq.state == 1 ? 0.0f : __int_as_float(0x7fffffff);
-        for (int d = lane; d < p.head_dim; d += 32) out[d] = from_float<T>(value);
+        for (int d = threadIdx.x; d < p.head_dim; d += blockDim.x) out[d] = from_float<T>(value);
         return;
     }
     const int64_t* prefix = p.prefix_out;
@@ -122,7 +123,7 @@ __global__ void __launch_bounds__(kMergeThreads) paged_decode_persistent_merge_k
     const int slot0 = (w0 * total / warps == start) ? 0 : 1;
     merge_row<T>(p, out,
                  [&](int j) -> long long { return ((w0 + j) * 2 + (j == 0 ? slot0 : 0)) * GP + g; },
-                 static_cast<int>(w1 - w0 + 1), lane);
+                 static_cast<int>(w1 - w0 + 1));
 }
 
 }  // namespace mv
