@@ -47,7 +47,7 @@ extern "C" {
 
 /* Flags for mv_paged_decode / mv_paged_decode_workspace_size. */
 #define MV_FLAG_FORCE_SIMT 1u /* use the CUDA-core kernel even where the tensor-core one applies */
-#define MV_FLAG_SPLIT_GRID 2u /* tensor-core kernel with a fixed split grid instead of the persistent one */
+#define MV_FLAG_PERSISTENT 2u /* tensor-core kernel on the persistent schedule instead of the split grid */
 
 /* Status codes. */
 #define MV_OK 0
@@ -72,8 +72,7 @@ MV_API const char* mv_last_error(void);
 /*
  * Workspace bytes mv_paged_decode needs for this geometry on the current
  * device (0 when no split-KV pass is needed). max_context_len bounds every
- * context length; pages_per_split 0 lets the library choose (a nonzero value
- * selects a fixed split grid).
+ * context length; pages_per_split 0 lets the library choose.
  * Replaces no reference call: the reference kernel allocates an output-sized
  * running buffer itself (src/micro_vllm/csrc/online_attention.cuh:154-156).
  */
@@ -110,7 +109,11 @@ MV_API int mv_paged_decode_plan(int32_t batch, int32_t num_q_heads, int32_t num_
  *   - a length of 0 gives zeros; a negative length, or one above
  *     max_context_len or blocks_per_seq * block_size, gives NaN.
  * workspace: mv_paged_decode_workspace_size bytes of device scratch (may be
- * NULL when that size is 0), used only by this call while it runs.
+ * NULL when that size is 0). Its first 256 KiB hold split arrival counters:
+ * zero-fill the buffer before its first use; every completed call leaves those
+ * counters at zero again (nothing else is written there), so a buffer is
+ * zeroed once and reused by later calls of any shape. Calls that share a
+ * workspace must not overlap on the GPU (order them on one stream).
  * dtype: MV_DTYPE_* of q, pages and out; accumulation is fp32.
  */
 MV_API int mv_paged_decode(const void* q, int64_t q_stride_seq, int64_t q_stride_head,

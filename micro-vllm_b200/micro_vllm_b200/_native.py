@@ -18,7 +18,7 @@ DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
 INDEX_I32, INDEX_I64 = 0, 1
 POSITIONS_START, POSITIONS_END = 0, 1
 FLAG_FORCE_SIMT = 1
-FLAG_SPLIT_GRID = 2
+FLAG_PERSISTENT = 2
 PATH_SIMT, PATH_TMA_MMA, PATH_TMA_MMA_PERSISTENT = 0, 1, 2
 PATH_NAMES = {0: 'simt', 1: 'tma_mma', 2: 'tma_mma_persistent'}
 DEVICE_STATUS_WAIT_TIMEOUT = 1

@@ -143,8 +143,10 @@ struct Plan {
     int ctas;        // persistent grid size
     int warps;       // persistent warps in the grid
     size_t workspace;
+    size_t counter_bytes;  // zero-initialised arrival counters at the start of the workspace
     size_t part_o_bytes;
     size_t part_lse_bytes;
+    bool fused_merge;
 };
 
 bool mma_shape_ok(const Geometry& g) {
@@ -154,6 +156,12 @@ bool mma_shape_ok(const Geometry& g) {
 }
 
 size_t round256(size_t bytes) { return (bytes + 255) / 256 * 256; }
+
+// Every non-empty workspace starts with this many bytes of arrival counters
+// (one per sequence x KV head). No path writes anything else there, so once a
+// workspace is zero-filled its counters stay zero between completed calls.
+constexpr size_t kCounterRegion = 256 * 1024;
+constexpr int64_t kMaxCounters = kCounterRegion / sizeof(unsigned);
 
 // Persistent kernel: stages per warp for each head_dim (~96 KiB of stages per CTA
 // so two CTAs share an SM; one at head_dim 256), and the batch its prefix array fits.
@@ -206,6 +214,12 @@ int persistent_occupancy_dispatch(int device, int dim, int nt, int* ctas_per_sm)
     }
 }
 
+// Shared memory of the split-grid kernel's TMA stages (reused for the fused merge).
+size_t grid_stage_bytes(int dim) {
+    const int stages = dim == 64 ? MV_STAGES_D64 : (dim == 128 ? MV_STAGES_D128 : MV_STAGES_D256);
+    return static_cast<size_t>(kMmaWarps) * stages * 2 * (16 * static_cast<size_t>(dim) * 2);
+}
+
 int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool aligned_for_tma,
               Plan* plan) {
     int rc = check_geometry(g);
@@ -218,13 +232,14 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
     const int group = g.q_heads / g.kv_heads;
     if (pages_per_split < 0) return fail(MV_ERR_INVALID_ARGUMENT, "pages_per_split must be nonnegative");
     const bool mma = !(flags & MV_FLAG_FORCE_SIMT) && aligned_for_tma && mma_shape_ok(g);
-    const bool persistent = mma && pages_per_split == 0 && !(flags & MV_FLAG_SPLIT_GRID) &&
+    const bool persistent = mma && pages_per_split == 0 && (flags & MV_FLAG_PERSISTENT) &&
                             g.batch <= kPersistentMaxBatch &&
                             static_cast<int64_t>(g.batch) * g.kv_heads < (int64_t(1) << 31);
     plan->path = persistent ? MV_PATH_TMA_MMA_PERSISTENT : (mma ? MV_PATH_TMA_MMA : MV_PATH_SIMT);
     plan->nt = group <= 8 ? 1 : 2;
     plan->ctas = plan->warps = 0;
-    plan->part_o_bytes = plan->part_lse_bytes = 0;
+    plan->counter_bytes = plan->part_o_bytes = plan->part_lse_bytes = 0;
+    plan->fused_merge = false;
     const int64_t max_pages = (g.max_context_len + g.block_size - 1) / g.block_size;
 
     if (persistent) {
@@ -239,7 +254,8 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
         const size_t rows = static_cast<size_t>(plan->warps) * 2 * 8 * plan->nt;  // 2 partial slots per warp
         plan->part_o_bytes = round256(rows * g.head_dim * sizeof(float));
         plan->part_lse_bytes = round256(rows * sizeof(float));
-        plan->workspace = plan->part_o_bytes + plan->part_lse_bytes +
+        plan->counter_bytes = kCounterRegion;
+        plan->workspace = plan->counter_bytes + plan->part_o_bytes + plan->part_lse_bytes +
                           round256((static_cast<size_t>(g.batch) + 1) * sizeof(int64_t));
         return MV_OK;
     }
@@ -265,8 +281,14 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
         const size_t rows = static_cast<size_t>(g.batch) * g.q_heads * splits;
         plan->part_o_bytes = round256(rows * g.head_dim * sizeof(float));
         plan->part_lse_bytes = round256(rows * sizeof(float));
+        // The tensor-core split grid merges in its last CTA per segment when the
+        // segment's G x splits weights fit the CTA's stage memory.
+        plan->fused_merge = plan->path == MV_PATH_TMA_MMA &&
+                            static_cast<size_t>(group) * splits * sizeof(float) <= grid_stage_bytes(g.head_dim) &&
+                            static_cast<int64_t>(g.batch) * g.kv_heads <= kMaxCounters;
+        plan->counter_bytes = kCounterRegion;
     }
-    plan->workspace = plan->part_o_bytes + plan->part_lse_bytes;
+    plan->workspace = plan->counter_bytes + plan->part_o_bytes + plan->part_lse_bytes;
     if (plan->path == MV_PATH_SIMT) {
         const size_t smem = mv::simt_smem_bytes(group, g.head_dim);
         if (smem > static_cast<size_t>(dev.smem_optin))
@@ -439,7 +461,7 @@ int launch_decode(const mv::DecodeParams& p, const Plan& plan, const CUtensorMap
     if (rc != MV_OK) return rc;
     cudaError_t err = cudaGetLastError();
     if (err != cudaSuccess) return cuda_fail(err, "decode kernel launch");
-    if (plan.max_splits > 1) {
+    if (plan.max_splits > 1 && !plan.fused_merge) {
         err = launch_pdl(mv::paged_decode_merge_kernel<T>, merge_grid(p), dim3(mv::kMergeThreads), 0,
                          stream, p);
         if (err != cudaSuccess) return cuda_fail(err, "merge kernel launch");
@@ -557,9 +579,13 @@ int mv_paged_decode(const void* q, int64_t q_stride_seq, int64_t q_stride_head, 
     p.part_o = nullptr;
     p.part_lse = nullptr;
     p.prefix_out = nullptr;
+    p.counters = nullptr;
     p.persistent_warps = plan.warps;
+    p.fused_merge = plan.fused_merge ? 1 : 0;
     if (plan.workspace > 0) {
         uint8_t* base = static_cast<uint8_t*>(workspace);
+        if (plan.fused_merge) p.counters = reinterpret_cast<unsigned*>(base);
+        base += plan.counter_bytes;
         p.part_o = reinterpret_cast<float*>(base);
         p.part_lse = reinterpret_cast<float*>(base + plan.part_o_bytes);
         if (plan.path == MV_PATH_TMA_MMA_PERSISTENT)

@@ -50,6 +50,8 @@ struct DecodeParams {
     int max_splits;
     int64_t* prefix_out;    // persistent schedule: per-sequence page prefix sums [batch + 1]
     int64_t persistent_warps;  // persistent schedule: warps in the grid
+    unsigned int* counters; // split grid: per-(sequence, KV head) arrival counters, zero between calls
+    int fused_merge;        // split grid: the last split CTA of a segment merges it
 };
 
 struct AppendParams {

@@ -259,6 +259,66 @@ struct WarpPageAttention {
 
 // ------------------------------------------------------- split-grid kernel
 
+// Merge one (sequence, KV head) segment's n split partials into its G output
+// rows, by the whole CTA; `weights` holds G * n floats of shared memory.
+// Partials were written by other CTAs: read them through L2 (ld.cg).
+template <typename T>
+__device__ void merge_segment(const DecodeParams& p, int b, int h, int n, float* weights) {
+    const int G = p.group;
+    const int D = p.head_dim;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int nwarps = blockDim.x >> 5;
+    const int64_t row0 = (static_cast<int64_t>(b) * p.q_heads + h * G) * p.max_splits;
+    for (int g = warp; g < G; g += nwarps) {
+        const float* lse = p.part_lse + row0 + static_cast<int64_t>(g) * p.max_splits;
+        float mx = -INFINITY;
+        bool nan = false;
+        for (int j = lane; j < n; j += 32) {
+            const float v = __ldcg(lse + j);
+            nan |= isnan(v);
+            mx = fmaxf(mx, v);
+        }
+        mx = warp_max(mx);
+        nan = __any_sync(0xffffffffu, nan);
+        float sum = 0.0f;
+        for (int j = lane; j < n; j += 32) sum += fast_exp2(__ldcg(lse + j) - mx);
+        const float inv = nan ? __int_as_float(0x7fffffff) : 1.0f / warp_sum(sum);
+        for (int j = lane; j < n; j += 32) weights[g * n + j] = fast_exp2(__ldcg(lse + j) - mx) * inv;
+    }
+    __syncthreads();
+    T* out = static_cast<T*>(p.out) + b * p.out_stride_seq;
+    for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
+        const int g = idx / D;
+        const int d = idx - g * D;
+        const float* src = p.part_o + (row0 + static_cast<int64_t>(g) * p.max_splits) * D + d;
+        const float* w = weights + g * n;
+        float acc = 0.0f;
+#pragma unroll 8
+        for (int j = 0; j < n; ++j) acc = fmaf(w[j], __ldcg(src + static_cast<int64_t>(j) * D), acc);
+        out[static_cast<int64_t>(h * G + g) * p.out_stride_head + d] = from_float<T>(acc);
+    }
+}
+
+// After a CTA wrote its split's partial: count it in, and if it is the
+// segment's last split, merge the segment. The counter wraps back to 0 at the
+// last arrival (atomicInc), so it is zero again for the next call.
+template <typename T>
+__device__ void arrive_and_merge(const DecodeParams& p, int b, int h, int splits, float* weights,
+                                 int* flag) {
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned old = atomicInc(p.counters + b * p.kv_heads + h, static_cast<unsigned>(splits - 1));
+        *flag = old == static_cast<unsigned>(splits - 1);
+    }
+    __syncthreads();
+    if (*flag) {
+        __threadfence();
+        merge_segment<T>(p, b, h, splits, weights);
+    }
+}
+
 template <int D, int NT, int NWARPS, int STAGES>
 struct MmaDecodeShape {
     static constexpr int kTileBytes = PageTile<D>::kBytes;
@@ -282,6 +342,7 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t bars[NWARPS][STAGES];
     __shared__ int cta_bad;
+    __shared__ int cta_last;
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -327,8 +388,12 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
     __syncthreads();
     if (cta_bad) {
         // A corrupted table entry: never read that page, poison the group.
-        if (single) write_group_constant<T>(p, b, h, __int_as_float(0x7fffffff));
-        else write_group_partial_nan(p, b, h, split);
+        if (single) {
+            write_group_constant<T>(p, b, h, __int_as_float(0x7fffffff));
+        } else {
+            write_group_partial_nan(p, b, h, split);
+            if (p.fused_merge) arrive_and_merge<T>(p, b, h, seq.splits, reinterpret_cast<float*>(smem), &cta_last);
+        }
         return;
     }
 
@@ -436,8 +501,12 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
     }
     __syncthreads();
     if (cta_bad) {
-        if (single) write_group_constant<T>(p, b, h, __int_as_float(0x7fffffff));
-        else write_group_partial_nan(p, b, h, split);
+        if (single) {
+            write_group_constant<T>(p, b, h, __int_as_float(0x7fffffff));
+        } else {
+            write_group_partial_nan(p, b, h, split);
+            if (p.fused_merge) arrive_and_merge<T>(p, b, h, seq.splits, reinterpret_cast<float*>(smem), &cta_last);
+        }
         return;
     }
 
@@ -472,6 +541,10 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
             p.part_o[row * D + d] = value;
             if (d == 0) p.part_lse[row] = mx + log2f(den);
         }
+    }
+    if (!single && p.fused_merge) {
+        __syncthreads();  // the warps' merge buffers are read: reuse shared memory for weights
+        arrive_and_merge<T>(p, b, h, seq.splits, reinterpret_cast<float*>(smem), &cta_last);
     }
 }
 

@@ -86,6 +86,23 @@ def _validate_paged_inputs(query, key, value, table, length):
     _validate_paged_table(table, key, query, length)
 
 
+# Split-KV scratch per (device, stream): its arrival counters must be zero before
+# first use and every completed call leaves them zero, so buffers are zeroed once
+# and reused by the calls ordered on that stream.
+_WORKSPACES = {}
+
+
+def _workspace(device, stream, nbytes):
+    key = (device.index, stream)
+    cached = _WORKSPACES.get(key)
+    if cached is not None and cached.numel() >= nbytes:
+        return cached
+    buffer = torch.zeros(nbytes, dtype=torch.uint8, device=device)
+    if not torch.cuda.is_current_stream_capturing():
+        _WORKSPACES[key] = buffer
+    return buffer
+
+
 def _run(query3, q_strides, key_cache, value_cache, block_table, table_stride, blocks_per_seq,
          context_lens, max_context_len, scale, out, out_strides, pages_per_split=0, flags=0):
     """Plan, allocate the split-KV workspace, and launch ``mv_paged_decode``."""
@@ -99,8 +116,8 @@ def _run(query3, q_strides, key_cache, value_cache, block_table, table_stride, b
         _native.check(lib.mv_paged_decode_workspace_size(
             batch, q_heads, kv_heads, dim, block_size, max_context_len, pages_per_split, flags,
             dtype, ctypes.byref(size)))
-        workspace = (torch.empty(size.value, dtype=torch.uint8, device=device)
-                     if size.value else None)
+        stream = current_stream_handle(device)
+        workspace = _workspace(device, stream, size.value) if size.value else None
         _native.check(lib.mv_paged_decode(
             out.q_ptr, q_strides[0], q_strides[1],
             key_cache.data_ptr(), value_cache.data_ptr(), num_blocks,
@@ -110,8 +127,9 @@ def _run(query3, q_strides, key_cache, value_cache, block_table, table_stride, b
             INDEX_CODES[context_lens.dtype] if context_lens is not None else 0,
             max_context_len, batch, q_heads, float(scale),
             out.out_ptr, out_strides[0], out_strides[1],
-            workspace.data_ptr() if workspace is not None else None, size.value,
-            pages_per_split, flags, dtype, current_stream_handle(device)))
+            workspace.data_ptr() if workspace is not None else None,
+            workspace.numel() if workspace is not None else 0,
+            pages_per_split, flags, dtype, stream))
 
 
 class _Pointers:
@@ -197,17 +215,18 @@ def decode_attention_paged(query: torch.Tensor, cache, *, layer_idx: int) -> tor
         cache._device_page_table, length)
 
 
-def _flags(force_simt, split_grid):
-    return (_native.FLAG_FORCE_SIMT if force_simt else 0) | (_native.FLAG_SPLIT_GRID if split_grid else 0)
+def _flags(force_simt, persistent):
+    return (_native.FLAG_FORCE_SIMT if force_simt else 0) | (_native.FLAG_PERSISTENT if persistent else 0)
 
 
 def paged_decode_plan(query_heads, key_cache, context_bound, *, batch, pages_per_split=0,
-                      force_simt=False, split_grid=False):
+                      force_simt=False, persistent=False):
     """(path, pages_per_split, max_splits) that ``paged_decode_attention`` would use.
 
-    path is 'tma_mma_persistent' (TMA + tensor cores, persistent grid with equal
-    page ranges per warp), 'tma_mma' (TMA + tensor cores, one CTA per split) or
-    'simt' (CUDA cores, one CTA per split).
+    path is 'tma_mma' (TMA + tensor cores, one CTA per split of pages, the last
+    split of each sequence/head merging them), 'tma_mma_persistent' (TMA +
+    tensor cores, a resident grid with equal page ranges per warp and a merge
+    pass) or 'simt' (CUDA cores, one CTA per split, merge pass).
     """
     lib = _native.library()
     num_blocks, kv_heads, block_size, dim = key_cache.shape
@@ -215,7 +234,7 @@ def paged_decode_plan(query_heads, key_cache, context_bound, *, batch, pages_per
     with torch.cuda.device(key_cache.device):
         _native.check(lib.mv_paged_decode_plan(
             batch, query_heads, kv_heads, dim, block_size, context_bound, pages_per_split,
-            _flags(force_simt, split_grid), DTYPE_CODES[key_cache.dtype],
+            _flags(force_simt, persistent), DTYPE_CODES[key_cache.dtype],
             key_cache.data_ptr(), key_cache.data_ptr(), ctypes.byref(path), ctypes.byref(pps),
             ctypes.byref(splits)))
     return _native.PATH_NAMES[path.value], pps.value, splits.value
@@ -225,7 +244,7 @@ def paged_decode_attention(query: torch.Tensor, key_cache: torch.Tensor, value_c
                            block_table: torch.Tensor, context_lens: torch.Tensor,
                            scale: float | None = None, *, max_context_len: int | None = None,
                            out: torch.Tensor | None = None, pages_per_split: int = 0,
-                           force_simt: bool = False, split_grid: bool = False) -> torch.Tensor:
+                           force_simt: bool = False, persistent: bool = False) -> torch.Tensor:
     """Batched paged GQA decode over one shared page pool.
 
     query: [B, Hq, D] (or [B, Hq, 1, D]) CUDA fp32/fp16/bf16, feature stride 1.
@@ -238,10 +257,10 @@ def paged_decode_attention(query: torch.Tensor, key_cache: torch.Tensor, value_c
     table capacity max_blocks * bs, so no device read-back is needed. Lengths
     above it produce NaN (the split plan cannot cover them).
     out: optional [B, Hq, D] destination (feature stride 1).
-    pages_per_split / split_grid / force_simt: kernel selection for tests and
-    tuning (a fixed split-KV grid of that many pages per CTA; the CUDA-core
-    kernel); by default the library picks the persistent tensor-core kernel
-    where the shape allows.
+    pages_per_split / persistent / force_simt: kernel selection for tests and
+    tuning (that many pages per split-KV CTA; the persistent tensor-core
+    schedule; the CUDA-core kernel). By default the library picks the
+    tensor-core split grid where the shape allows, else the CUDA-core kernel.
     Returns out, or a fresh [B, Hq, D] tensor of the query's dtype.
     """
     squeeze = query.dim() == 4
@@ -290,5 +309,5 @@ def paged_decode_attention(query: torch.Tensor, key_cache: torch.Tensor, value_c
     _run((batch, q_heads, dim), (q.stride(0), q.stride(1)), key_cache, value_cache, block_table,
          block_table.stride(0), block_table.shape[1], context_lens, int(max_context_len), scale,
          _Pointers(q.data_ptr(), out.data_ptr()), (out.stride(0), out.stride(1)),
-         pages_per_split=int(pages_per_split), flags=_flags(force_simt, split_grid))
+         pages_per_split=int(pages_per_split), flags=_flags(force_simt, persistent))
     return out

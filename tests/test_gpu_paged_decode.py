@@ -29,14 +29,14 @@ def _fixture(name):
         return {key: data[key] for key in data.files}
 
 
-def _append_and_decode(inputs, *, force_simt=False, pages_per_split=0, split_grid=False):
+def _append_and_decode(inputs, *, force_simt=False, pages_per_split=0, persistent=False):
     attention, cache = _native()
     t = workload_tensors(inputs)
     cache.write_paged_kv(t['key_new'], t['value_new'], t['key_pool'], t['value_pool'],
                          t['block_table'], positions=t['context_lens'], positions_are_end=True)
     out = attention.paged_decode_attention(
         t['q'], t['key_pool'], t['value_pool'], t['block_table'], t['context_lens'],
-        force_simt=force_simt, pages_per_split=pages_per_split, split_grid=split_grid)
+        force_simt=force_simt, pages_per_split=pages_per_split, persistent=persistent)
     torch.cuda.synchronize()
     return t, out
 
@@ -48,9 +48,9 @@ def _oracle(inputs, key_pool, value_pool):
 
 
 MODES = {
-    'auto': {},                               # persistent tensor-core kernel where the shape allows
-    'grid': dict(split_grid=True),            # tensor-core kernel, fixed split grid
-    'split4': dict(pages_per_split=4),        # fixed split grid, 4 pages per split
+    'auto': {},                               # tensor-core split grid (fused merge) where the shape allows
+    'persistent': dict(persistent=True),      # tensor-core persistent schedule + merge pass
+    'split4': dict(pages_per_split=4),        # split grid, 4 pages per split
     'simt': dict(force_simt=True),            # CUDA-core kernel
 }
 
@@ -79,9 +79,10 @@ def test_tensor_core_paths_are_selected_for_qwen_geometry():
     attention, _ = _native()
     inputs = make_inputs('qwen7b_bf16_small')
     t = workload_tensors(inputs)
-    assert attention.paged_decode_plan(28, t['key_pool'], 4096, batch=64)[0] == 'tma_mma_persistent'
-    path, pps, splits = attention.paged_decode_plan(28, t['key_pool'], 4096, batch=64, split_grid=True)
+    path, pps, splits = attention.paged_decode_plan(28, t['key_pool'], 4096, batch=64)
     assert path == 'tma_mma' and splits >= 2
+    assert attention.paged_decode_plan(28, t['key_pool'], 4096, batch=64, persistent=True)[0] == \
+        'tma_mma_persistent'
     assert attention.paged_decode_plan(28, t['key_pool'], 4096, batch=64, force_simt=True)[0] == 'simt'
     assert attention.paged_decode_plan(28, t['key_pool'].float(), 4096, batch=64)[0] == 'simt'
 
@@ -94,9 +95,30 @@ def test_persistent_ranges_cover_every_length_mix(lens):
                 pool=('factor', 1.3), lens=('fixed', lens), dtype='bfloat16', value_scale=0.5,
                 seed=31 + len(lens))
     inputs = make_inputs(spec)
-    t, out = _append_and_decode(inputs)
-    expected = _oracle(inputs, to_numpy(t['key_pool']), to_numpy(t['value_pool']))
-    assert_attention_close(as_float(out), expected, 'bfloat16')
+    for mode in ('auto', 'persistent'):
+        t, out = _append_and_decode(inputs, **MODES[mode])
+        expected = _oracle(inputs, to_numpy(t['key_pool']), to_numpy(t['value_pool']))
+        assert_attention_close(as_float(out), expected, 'bfloat16')
+
+
+def test_workspace_counters_reset_across_calls_and_paths():
+    """The fused split merge counts arrivals in the shared workspace; alternating
+    kernels and shapes on one stream must keep giving identical results."""
+    attention, _ = _native()
+    small = workload_tensors(make_inputs('qwen7b_bf16_small'))
+    big = workload_tensors(make_inputs('qwen72b_bf16_small'))
+    runs = []
+    for _ in range(3):
+        row = []
+        for t in (small, big):
+            for mode in MODES.values():
+                row.append(attention.paged_decode_attention(
+                    t['q'], t['key_pool'], t['value_pool'], t['block_table'], t['context_lens'],
+                    **mode).clone())
+        runs.append(row)
+    for row in runs[1:]:
+        for a, b in zip(runs[0], row):
+            assert torch.equal(a, b)
 
 
 @pytest.mark.parametrize('pages_per_split', [1, 4, 8, 12, 128])
