@@ -48,6 +48,7 @@ extern "C" {
 /* Flags for mv_paged_decode / mv_paged_decode_workspace_size. */
 #define MV_FLAG_FORCE_SIMT 1u /* use the CUDA-core kernel even where the tensor-core one applies */
 #define MV_FLAG_PERSISTENT 2u /* tensor-core kernel on the persistent schedule instead of the split grid */
+#define MV_FLAG_FUSED_MERGE 4u /* split grid: the last split CTA of each sequence/head merges it */
 
 /* Status codes. */
 #define MV_OK 0

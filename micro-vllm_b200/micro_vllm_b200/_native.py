@@ -19,6 +19,7 @@ INDEX_I32, INDEX_I64 = 0, 1
 POSITIONS_START, POSITIONS_END = 0, 1
 FLAG_FORCE_SIMT = 1
 FLAG_PERSISTENT = 2
+FLAG_FUSED_MERGE = 4
 PATH_SIMT, PATH_TMA_MMA, PATH_TMA_MMA_PERSISTENT = 0, 1, 2
 PATH_NAMES = {0: 'simt', 1: 'tma_mma', 2: 'tma_mma_persistent'}
 DEVICE_STATUS_WAIT_TIMEOUT = 1

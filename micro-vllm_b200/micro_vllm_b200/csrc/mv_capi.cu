@@ -283,7 +283,10 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
         plan->part_lse_bytes = round256(rows * sizeof(float));
         // The tensor-core split grid merges in its last CTA per segment when the
         // segment's G x splits weights fit the CTA's stage memory.
-        plan->fused_merge = plan->path == MV_PATH_TMA_MMA &&
+        // Merging in the last split CTA of each segment holds that CTA's SM slot
+        // through a latency-bound merge; measured on B200 it cost more than the
+        // separate merge pass (launched early with PDL), so it is opt-in.
+        plan->fused_merge = (flags & MV_FLAG_FUSED_MERGE) && plan->path == MV_PATH_TMA_MMA &&
                             static_cast<size_t>(group) * splits * sizeof(float) <= grid_stage_bytes(g.head_dim) &&
                             static_cast<int64_t>(g.batch) * g.kv_heads <= kMaxCounters;
         plan->counter_bytes = kCounterRegion;

@@ -215,8 +215,9 @@ def decode_attention_paged(query: torch.Tensor, cache, *, layer_idx: int) -> tor
         cache._device_page_table, length)
 
 
-def _flags(force_simt, persistent):
-    return (_native.FLAG_FORCE_SIMT if force_simt else 0) | (_native.FLAG_PERSISTENT if persistent else 0)
+def _flags(force_simt, persistent, fused_merge=False):
+    return ((_native.FLAG_FORCE_SIMT if force_simt else 0) | (_native.FLAG_PERSISTENT if persistent else 0)
+            | (_native.FLAG_FUSED_MERGE if fused_merge else 0))
 
 
 def paged_decode_plan(query_heads, key_cache, context_bound, *, batch, pages_per_split=0,
@@ -244,7 +245,8 @@ def paged_decode_attention(query: torch.Tensor, key_cache: torch.Tensor, value_c
                            block_table: torch.Tensor, context_lens: torch.Tensor,
                            scale: float | None = None, *, max_context_len: int | None = None,
                            out: torch.Tensor | None = None, pages_per_split: int = 0,
-                           force_simt: bool = False, persistent: bool = False) -> torch.Tensor:
+                           force_simt: bool = False, persistent: bool = False,
+                           fused_merge: bool = False) -> torch.Tensor:
     """Batched paged GQA decode over one shared page pool.
 
     query: [B, Hq, D] (or [B, Hq, 1, D]) CUDA fp32/fp16/bf16, feature stride 1.
@@ -257,9 +259,10 @@ def paged_decode_attention(query: torch.Tensor, key_cache: torch.Tensor, value_c
     table capacity max_blocks * bs, so no device read-back is needed. Lengths
     above it produce NaN (the split plan cannot cover them).
     out: optional [B, Hq, D] destination (feature stride 1).
-    pages_per_split / persistent / force_simt: kernel selection for tests and
-    tuning (that many pages per split-KV CTA; the persistent tensor-core
-    schedule; the CUDA-core kernel). By default the library picks the
+    pages_per_split / persistent / fused_merge / force_simt: kernel selection
+    for tests and tuning (that many pages per split-KV CTA; the persistent
+    tensor-core schedule; merging splits in the last split CTA; the CUDA-core
+    kernel). By default the library picks the
     tensor-core split grid where the shape allows, else the CUDA-core kernel.
     Returns out, or a fresh [B, Hq, D] tensor of the query's dtype.
     """
@@ -309,5 +312,5 @@ def paged_decode_attention(query: torch.Tensor, key_cache: torch.Tensor, value_c
     _run((batch, q_heads, dim), (q.stride(0), q.stride(1)), key_cache, value_cache, block_table,
          block_table.stride(0), block_table.shape[1], context_lens, int(max_context_len), scale,
          _Pointers(q.data_ptr(), out.data_ptr()), (out.stride(0), out.stride(1)),
-         pages_per_split=int(pages_per_split), flags=_flags(force_simt, persistent))
+         pages_per_split=int(pages_per_split), flags=_flags(force_simt, persistent, fused_merge))
     return out

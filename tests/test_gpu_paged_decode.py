@@ -50,6 +50,7 @@ def _oracle(inputs, key_pool, value_pool):
 MODES = {
     'auto': {},                               # tensor-core split grid (fused merge) where the shape allows
     'persistent': dict(persistent=True),      # tensor-core persistent schedule + merge pass
+    'fused': dict(fused_merge=True),          # split grid, last split CTA merges
     'split4': dict(pages_per_split=4),        # split grid, 4 pages per split
     'simt': dict(force_simt=True),            # CUDA-core kernel
 }
