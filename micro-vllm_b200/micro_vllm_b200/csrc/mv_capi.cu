@@ -107,7 +107,7 @@ int ensure_smem(Kernel kernel, size_t bytes) {
 #define MV_STAGES_D64 6
 #endif
 #ifndef MV_STAGES_D128
-#define MV_STAGES_D128 3
+#define MV_STAGES_D128 2
 #endif
 #ifndef MV_STAGES_D256
 #define MV_STAGES_D256 2
@@ -262,13 +262,18 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
 
     int64_t pps = pages_per_split;
     if (pps == 0) {
-        // Enough splits that the page work of the whole batch spreads over
-        // ~16 CTAs per SM, but no split shorter than 8 pages.
-        const int64_t pages = static_cast<int64_t>(g.batch) * g.kv_heads * std::max<int64_t>(max_pages, 1);
-        const int64_t target = static_cast<int64_t>(dev.sms) * 16;
-        pps = (pages + target - 1) / target;
-        pps = std::max<int64_t>(8, std::min<int64_t>(pps, kMaxPagesPerSplit));
-        pps = (pps + kMmaWarps - 1) / kMmaWarps * kMmaWarps;
+        // Splits of 16..128 pages, sized so the batch's pages -- estimated as half
+        // the max_context_len bound per sequence -- fill about one wave of
+        // resident CTAs (three per SM). Measured on B200: longer splits lose to
+        // the tail of the last wave, shorter ones to per-CTA start-up and the
+        // merge; 64 pages at batch 64 x 4 KV heads x ~2.5k tokens, 128 at long
+        // contexts.
+        const int64_t pages = static_cast<int64_t>(g.batch) * g.kv_heads * std::max<int64_t>(max_pages, 1) / 2;
+        const int64_t target = static_cast<int64_t>(dev.sms) * 3;
+        const int64_t want = (pages + target - 1) / target;
+        pps = 16;
+        while (pps * 2 <= want && pps < kMaxPagesPerSplit) pps *= 2;
+        pps = std::min<int64_t>(pps, kMaxPagesPerSplit);
     }
     if (plan->path == MV_PATH_TMA_MMA && pps > kMaxPagesPerSplit)
         return fail(MV_ERR_INVALID_ARGUMENT, "pages_per_split above %d for the tensor-core kernel",

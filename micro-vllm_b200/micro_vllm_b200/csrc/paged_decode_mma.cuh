@@ -341,7 +341,7 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
 
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t bars[NWARPS][STAGES];
-    __shared__ int cta_bad;
+    __shared__ int warp_flags[NWARPS];  // 1: corrupted page ID, 2: a wait gave up
     __shared__ int cta_last;
 
     const int warp = threadIdx.x >> 5;
@@ -369,6 +369,7 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
     const int n_my = warp < cta_pages ? (cta_pages - warp + NWARPS - 1) / NWARPS : 0;
 
     // Page IDs of this warp's pages: lane i holds page warp + i * NWARPS of the run.
+    // A corrupted ID (outside the pool) is never loaded; the group becomes NaN.
     long long my_id = 0;
     bool bad = false;
     if (lane < n_my) {
@@ -376,44 +377,42 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
                            b * p.table_stride + page_begin + warp + lane * NWARPS);
         bad = my_id < 0 || my_id >= p.num_blocks;
     }
-    if (threadIdx.x == 0) cta_bad = 0;
+    const bool warp_has_bad = __any_sync(0xffffffffu, bad);
     const uint32_t bar0 = smem_addr(&bars[warp][0]);
     if (lane == 0) {
 #pragma unroll
         for (int st = 0; st < STAGES; ++st) mbar_init(bar0 + 8 * st, 1);
     }
     fence_mbar_init();
-    __syncthreads();
-    if (__any_sync(0xffffffffu, bad) && lane == 0) atomicOr(&cta_bad, 1);
-    __syncthreads();
-    if (cta_bad) {
-        // A corrupted table entry: never read that page, poison the group.
-        if (single) {
-            write_group_constant<T>(p, b, h, __int_as_float(0x7fffffff));
-        } else {
-            write_group_partial_nan(p, b, h, split);
-            if (p.fused_merge) arrive_and_merge<T>(p, b, h, seq.splits, reinterpret_cast<float*>(smem), &cta_last);
-        }
-        return;
-    }
+    __syncwarp();
 
     uint8_t* wsm = smem + warp * Shape::kWarpBytes;
     const uint32_t wsm_addr = smem_addr(wsm);
 
-    const int prologue = n_my < STAGES ? n_my : STAGES;
-    for (int i = 0; i < prologue; ++i) {
+    // Fill page i of this warp into its stage (every lane calls; lane 0 issues).
+    auto issue = [&](int i) {
         const long long id = __shfl_sync(0xffffffffu, my_id, i);
+        const bool ok = id >= 0 && id < p.num_blocks;
         if (lane == 0) {
-            const uint32_t bar = bar0 + 8 * i;
-            const uint32_t dst = wsm_addr + i * Shape::kStageBytes;
-            mbar_arrive_expect_tx(bar, Shape::kStageBytes);
-            tma_load_5d(dst, &kmap, 0, 0, 0, h, static_cast<int>(id), bar);
-            tma_load_5d(dst + Shape::kTileBytes, &vmap, 0, 0, 0, h, static_cast<int>(id), bar);
+            const int st = i % STAGES;
+            const uint32_t bar = bar0 + 8 * st;
+            if (ok) {
+                const uint32_t dst = wsm_addr + st * Shape::kStageBytes;
+                mbar_arrive_expect_tx(bar, Shape::kStageBytes);
+                tma_load_5d(dst, &kmap, 0, 0, 0, h, static_cast<int>(id), bar);
+                tma_load_5d(dst + Shape::kTileBytes, &vmap, 0, 0, 0, h, static_cast<int>(id), bar);
+            } else {
+                // No load for a corrupted ID; complete the phase so the ring stays in step.
+                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+            }
         }
-    }
+    };
+
+    const int prologue = n_my < STAGES ? n_my : STAGES;
+    for (int i = 0; i < prologue; ++i) issue(i);
     for (int i = prologue; kPrefetchPages > 0 && i < n_my && i < STAGES + kPrefetchPages; ++i) {
         const long long id = __shfl_sync(0xffffffffu, my_id, i);
-        if (lane == 0) {
+        if (lane == 0 && id >= 0 && id < p.num_blocks) {
             tma_prefetch_l2_5d(&kmap, 0, 0, 0, h, static_cast<int>(id));
             tma_prefetch_l2_5d(&vmap, 0, 0, 0, h, static_cast<int>(id));
         }
@@ -438,39 +437,32 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
         const int64_t page = page_begin + warp + static_cast<int64_t>(i) * NWARPS;
         const int64_t left = seq.len - page * kPageTokens;
         const int valid = left < kPageTokens ? static_cast<int>(left) : kPageTokens;
+        const bool page_ok = !warp_has_bad || __shfl_sync(0xffffffffu, !bad, i);
         typename Warp::PageFrags frags;
-        Warp::load_page(frags, kt, vt, wsm + st * Shape::kStageBytes + Shape::kTileBytes, valid, lane);
+        if (page_ok) Warp::load_page(frags, kt, vt, wsm + st * Shape::kStageBytes + Shape::kTileBytes, valid, lane);
 
         // The page is in registers: refill its stage before the arithmetic.
         if (i + STAGES < n_my) {
             fence_proxy_async_smem();  // this lane's shared reads/writes before the TMA write
             __syncwarp();
-            const long long id = __shfl_sync(0xffffffffu, my_id, i + STAGES);
+            issue(i + STAGES);
             const int ahead = i + STAGES + kPrefetchPages;
             const long long pf = __shfl_sync(0xffffffffu, my_id, ahead & 31);
-            if (lane == 0) {
-                const uint32_t bar = bar0 + 8 * st;
-                mbar_arrive_expect_tx(bar, Shape::kStageBytes);
-                tma_load_5d(kt, &kmap, 0, 0, 0, h, static_cast<int>(id), bar);
-                tma_load_5d(vt, &vmap, 0, 0, 0, h, static_cast<int>(id), bar);
-                if (kPrefetchPages > 0 && ahead < n_my) {
-                    tma_prefetch_l2_5d(&kmap, 0, 0, 0, h, static_cast<int>(pf));
-                    tma_prefetch_l2_5d(&vmap, 0, 0, 0, h, static_cast<int>(pf));
-                }
+            if (kPrefetchPages > 0 && lane == 0 && ahead < n_my && pf >= 0 && pf < p.num_blocks) {
+                tma_prefetch_l2_5d(&kmap, 0, 0, 0, h, static_cast<int>(pf));
+                tma_prefetch_l2_5d(&vmap, 0, 0, 0, h, static_cast<int>(pf));
             }
         }
-        w.attend(frags, valid, p.scale_log2, lane);
+        if (page_ok) w.attend(frags, valid, p.scale_log2, lane);
     }
 
     if (failed) {
         // Drain loads still in flight (bounded) before the stage memory is reused.
         const int last = i + STAGES < n_my ? i + STAGES : n_my;
         for (int j = i; j < last; ++j) mbar_wait_bounded(bar0 + 8 * (j % STAGES), (j / STAGES) & 1);
-        if (lane == 0) {
-            atomicOr(&g_device_status, kStatusWaitTimeout);
-            atomicOr(&cta_bad, 2);
-        }
+        if (lane == 0) atomicOr(&g_device_status, kStatusWaitTimeout);
     }
+    if (lane == 0) warp_flags[warp] = (failed ? 2 : 0) | (warp_has_bad ? 1 : 0);
     w.reduce_l();
 
     __syncthreads();  // every warp is done with its stages: reuse them for the merge
@@ -500,6 +492,9 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
         }
     }
     __syncthreads();
+    int cta_bad = 0;
+#pragma unroll
+    for (int v = 0; v < NWARPS; ++v) cta_bad |= warp_flags[v];
     if (cta_bad) {
         if (single) {
             write_group_constant<T>(p, b, h, __int_as_float(0x7fffffff));
