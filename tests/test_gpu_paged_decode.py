@@ -29,14 +29,13 @@ def _fixture(name):
         return {key: data[key] for key in data.files}
 
 
-def _append_and_decode(inputs, *, force_simt=False, pages_per_split=0, persistent=False):
+def _append_and_decode(inputs, **mode):
     attention, cache = _native()
     t = workload_tensors(inputs)
     cache.write_paged_kv(t['key_new'], t['value_new'], t['key_pool'], t['value_pool'],
                          t['block_table'], positions=t['context_lens'], positions_are_end=True)
     out = attention.paged_decode_attention(
-        t['q'], t['key_pool'], t['value_pool'], t['block_table'], t['context_lens'],
-        force_simt=force_simt, pages_per_split=pages_per_split, persistent=persistent)
+        t['q'], t['key_pool'], t['value_pool'], t['block_table'], t['context_lens'], **mode)
     torch.cuda.synchronize()
     return t, out
 

@@ -1,0 +1,71 @@
+"""KV-head sharding: layout math, and the full-head all-gather over 2 gloo ranks on CPU."""
+import os
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from micro_vllm_b200.sharding import gather_full_heads, kv_head_shard
+
+
+@pytest.mark.parametrize('world', [1, 2, 4, 8])
+@pytest.mark.parametrize('q_heads, kv_heads, batch', [(28, 4, 64), (32, 8, 8), (64, 8, 256),
+                                                      (14, 2, 4), (12, 2, 32)])
+def test_shards_cover_every_head_and_sequence_once(world, q_heads, kv_heads, batch):
+    if kv_heads % world and world % kv_heads:
+        with pytest.raises(ValueError):
+            kv_head_shard(0, world, q_heads=q_heads, kv_heads=kv_heads, batch=batch)
+        return
+    owner = torch.zeros(batch, q_heads, dtype=torch.int64)
+    group = q_heads // kv_heads
+    for rank in range(world):
+        s = kv_head_shard(rank, world, q_heads=q_heads, kv_heads=kv_heads, batch=batch)
+        # whole GQA groups only: the query heads are exactly the group of the KV heads
+        assert s.q_heads == (s.kv_heads[0] * group, s.kv_heads[1] * group)
+        owner[s.batch[0]:s.batch[1], s.q_heads[0]:s.q_heads[1]] += 1
+    assert (owner == 1).all()
+
+
+def test_rejects_bad_ranks_and_head_counts():
+    with pytest.raises(ValueError):
+        kv_head_shard(2, 2, q_heads=28, kv_heads=4, batch=64)
+    with pytest.raises(ValueError):
+        kv_head_shard(0, 3, q_heads=28, kv_heads=4, batch=64)
+    with pytest.raises(ValueError):
+        kv_head_shard(0, 2, q_heads=27, kv_heads=4, batch=64)
+
+
+def _gather_worker(rank, world, port, q_heads, kv_heads, batch, result_queue):
+    os.environ['MASTER_ADDR'] = '127.0.0.1'
+    os.environ['MASTER_PORT'] = str(port)
+    import datetime
+    dist.init_process_group('gloo', rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    try:
+        full = torch.arange(batch * q_heads * 3, dtype=torch.float32).reshape(batch, q_heads, 3)
+        s = kv_head_shard(rank, world, q_heads=q_heads, kv_heads=kv_heads, batch=batch)
+        local = full[s.batch[0]:s.batch[1], s.q_heads[0]:s.q_heads[1]].clone()
+        gathered = gather_full_heads(local, q_heads=q_heads, kv_heads=kv_heads, batch=batch)
+        result_queue.put((rank, bool(torch.equal(gathered, full))))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize('q_heads, kv_heads, batch', [(28, 4, 6), (14, 1, 5)])
+def test_gather_full_heads_over_two_gloo_ranks(q_heads, kv_heads, batch):
+    import socket
+    with socket.socket() as sock:
+        sock.bind(('127.0.0.1', 0))
+        port = sock.getsockname()[1]
+    ctx = mp.get_context('spawn')
+    queue = ctx.Queue()
+    procs = [ctx.Process(target=_gather_worker, args=(r, 2, port, q_heads, kv_heads, batch, queue))
+             for r in range(2)]
+    for proc in procs:
+        proc.start()
+    results = dict(queue.get(timeout=120) for _ in procs)
+    for proc in procs:
+        proc.join(timeout=60)
+        assert proc.exitcode == 0
+    assert results == {0: True, 1: True}
