@@ -74,9 +74,73 @@ __device__ __forceinline__ void merge_row(const DecodeParams& p, T* out, RowOf r
     }
 }
 
-// Merge of the fixed split grid: row (b, hq) has seq.splits pieces at
-// part rows (b * q_heads + hq) * max_splits + j. Sequences that fit one split
-// were finished by the first pass.
+// Merge one (sequence, KV head) segment's n split partials into its G output
+// rows, by the whole CTA. Split j of query row g is part row
+// (b * q_heads + h * G + g) * max_splits + j. `weights` holds G * n floats
+// of shared memory. Two dependent rounds of global loads: the G x n
+// log-sum-exps (staged into `weights`), then the partial rows. Partials are
+// read through L2 (ld.cg): other CTAs wrote them.
+template <typename T>
+__device__ void merge_segment(const DecodeParams& p, int b, int h, int n, float* weights) {
+    const int G = p.group;
+    const int D = p.head_dim;
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int nwarps = blockDim.x >> 5;
+    const int64_t row0 = (static_cast<int64_t>(b) * p.q_heads + h * G) * p.max_splits;
+    for (int idx = threadIdx.x; idx < G * n; idx += blockDim.x) {
+        const int g = idx / n;
+        weights[idx] = __ldcg(p.part_lse + row0 + static_cast<int64_t>(g) * p.max_splits + (idx - g * n));
+    }
+    __syncthreads();
+    for (int g = warp; g < G; g += nwarps) {
+        float* w = weights + g * n;
+        float mx = -INFINITY;
+        bool nan = false;
+        for (int j = lane; j < n; j += 32) {
+            nan |= isnan(w[j]);
+            mx = fmaxf(mx, w[j]);
+        }
+        mx = warp_max(mx);
+        nan = __any_sync(0xffffffffu, nan);
+        float sum = 0.0f;
+        for (int j = lane; j < n; j += 32) sum += fast_exp2(w[j] - mx);
+        const float inv = nan ? __int_as_float(0x7fffffff) : 1.0f / warp_sum(sum);
+        __syncwarp();
+        for (int j = lane; j < n; j += 32) w[j] = fast_exp2(w[j] - mx) * inv;
+    }
+    __syncthreads();
+    T* out = static_cast<T*>(p.out) + b * p.out_stride_seq;
+    for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
+        const int g = idx / D;
+        const int d = idx - g * D;
+        const float* src = p.part_o + (row0 + static_cast<int64_t>(g) * p.max_splits) * D + d;
+        const float* w = weights + g * n;
+        float acc = 0.0f;
+#pragma unroll 8
+        for (int j = 0; j < n; ++j) acc = fmaf(w[j], __ldcg(src + static_cast<int64_t>(j) * D), acc);
+        out[static_cast<int64_t>(h * G + g) * p.out_stride_head + d] = from_float<T>(acc);
+    }
+}
+
+// Merge of the fixed split grid, one CTA per (KV head h, sequence b) when the
+// segment's G x max_splits weights fit the dynamic shared memory it was
+// launched with; sequences that fit one split were finished by the first pass.
+template <typename T>
+__global__ void __launch_bounds__(kMergeThreads) paged_decode_merge_segment_kernel(const DecodeParams p) {
+    extern __shared__ float weights[];
+    wait_for_prior_grid();
+    allow_next_grid();
+    const int h = blockIdx.x;
+    const int b = blockIdx.y;
+    const SeqSplit seq = seq_split(p, b);
+    if (seq.splits <= 1) return;
+    merge_segment<T>(p, b, h, seq.splits, weights);
+}
+
+// Merge of the fixed split grid, one CTA per output row (b, hq): for splits
+// too many to stage a whole segment's weights. Row (b, hq) has seq.splits
+// pieces at part rows (b * q_heads + hq) * max_splits + j.
 template <typename T>
 __global__ void __launch_bounds__(kMergeThreads) paged_decode_merge_kernel(const DecodeParams p) {
     wait_for_prior_grid();

@@ -31,6 +31,7 @@
 #pragma once
 
 #include "mv_device.cuh"
+#include "paged_decode_merge.cuh"
 
 namespace mv {
 
@@ -258,47 +259,6 @@ struct WarpPageAttention {
 };
 
 // ------------------------------------------------------- split-grid kernel
-
-// Merge one (sequence, KV head) segment's n split partials into its G output
-// rows, by the whole CTA; `weights` holds G * n floats of shared memory.
-// Partials were written by other CTAs: read them through L2 (ld.cg).
-template <typename T>
-__device__ void merge_segment(const DecodeParams& p, int b, int h, int n, float* weights) {
-    const int G = p.group;
-    const int D = p.head_dim;
-    const int warp = threadIdx.x >> 5;
-    const int lane = threadIdx.x & 31;
-    const int nwarps = blockDim.x >> 5;
-    const int64_t row0 = (static_cast<int64_t>(b) * p.q_heads + h * G) * p.max_splits;
-    for (int g = warp; g < G; g += nwarps) {
-        const float* lse = p.part_lse + row0 + static_cast<int64_t>(g) * p.max_splits;
-        float mx = -INFINITY;
-        bool nan = false;
-        for (int j = lane; j < n; j += 32) {
-            const float v = __ldcg(lse + j);
-            nan |= isnan(v);
-            mx = fmaxf(mx, v);
-        }
-        mx = warp_max(mx);
-        nan = __any_sync(0xffffffffu, nan);
-        float sum = 0.0f;
-        for (int j = lane; j < n; j += 32) sum += fast_exp2(__ldcg(lse + j) - mx);
-        const float inv = nan ? __int_as_float(0x7fffffff) : 1.0f / warp_sum(sum);
-        for (int j = lane; j < n; j += 32) weights[g * n + j] = fast_exp2(__ldcg(lse + j) - mx) * inv;
-    }
-    __syncthreads();
-    T* out = static_cast<T*>(p.out) + b * p.out_stride_seq;
-    for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
-        const int g = idx / D;
-        const int d = idx - g * D;
-        const float* src = p.part_o + (row0 + static_cast<int64_t>(g) * p.max_splits) * D + d;
-        const float* w = weights + g * n;
-        float acc = 0.0f;
-#pragma unroll 8
-        for (int j = 0; j < n; ++j) acc = fmaf(w[j], __ldcg(src + static_cast<int64_t>(j) * D), acc);
-        out[static_cast<int64_t>(h * G + g) * p.out_stride_head + d] = from_float<T>(acc);
-    }
-}
 
 // After a CTA wrote its split's partial: count it in, and if it is the
 // segment's last split, merge the segment. The counter wraps back to 0 at the
