@@ -470,14 +470,10 @@ int launch_decode(const mv::DecodeParams& p, const Plan& plan, const CUtensorMap
     cudaError_t err = cudaGetLastError();
     if (err != cudaSuccess) return cuda_fail(err, "decode kernel launch");
     if (plan.max_splits > 1 && !plan.fused_merge) {
-        const size_t weights = static_cast<size_t>(p.group) * plan.max_splits * sizeof(float);
-        if (weights <= 48 * 1024) {
-            err = launch_pdl(mv::paged_decode_merge_segment_kernel<T>, dim3(p.kv_heads, p.batch),
-                             dim3(mv::kMergeThreads), weights, stream, p);
-        } else {
-            err = launch_pdl(mv::paged_decode_merge_kernel<T>, merge_grid(p), dim3(mv::kMergeThreads), 0,
-                             stream, p);
-        }
+        // One CTA per output row: measured on B200, many short rows merge faster
+        // than one CTA per (sequence, KV head) looping over its G rows.
+        err = launch_pdl(mv::paged_decode_merge_kernel<T>, merge_grid(p), dim3(mv::kMergeThreads), 0,
+                         stream, p);
         if (err != cudaSuccess) return cuda_fail(err, "merge kernel launch");
     }
     return MV_OK;

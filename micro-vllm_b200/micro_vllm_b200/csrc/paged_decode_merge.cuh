@@ -27,6 +27,37 @@ __device__ __forceinline__ void merge_row(const DecodeParams& p, T* out, RowOf r
     const int tid = threadIdx.x;
     const int lane = tid & 31;
     const int warp = tid >> 5;
+    if (n <= kMergeChunk) {
+        // Two dependent rounds of loads: the log-sum-exps (kept in shared
+        // memory for the max, the sum and the weights), then the partial rows.
+        for (int j = tid; j < n; j += kMergeThreads) weights[j] = __ldcg(p.part_lse + row_of(j));
+        __syncthreads();
+        if (warp == 0) {
+            float mx = -INFINITY;
+            bool nan = false;
+            for (int j = lane; j < n; j += 32) {
+                nan |= isnan(weights[j]);
+                mx = fmaxf(mx, weights[j]);
+            }
+            mx = warp_max(mx);
+            nan = __any_sync(0xffffffffu, nan);
+            float sum = 0.0f;
+            for (int j = lane; j < n; j += 32) sum += fast_exp2(weights[j] - mx);
+            const float inv = 1.0f / warp_sum(sum);
+            __syncwarp();
+            for (int j = lane; j < n; j += 32) weights[j] = nan ? __int_as_float(0x7fffffff)
+                                                                 : fast_exp2(weights[j] - mx) * inv;
+        }
+        __syncthreads();
+        for (int d = tid; d < p.head_dim; d += kMergeThreads) {
+            float acc = 0.0f;
+#pragma unroll 8
+            for (int j = 0; j < n; ++j)
+                acc = fmaf(weights[j], __ldcg(p.part_o + static_cast<int64_t>(row_of(j)) * p.head_dim + d), acc);
+            out[d] = from_float<T>(acc);
+        }
+        return;
+    }
     if (tid == 0) any_nan = 0;
     float mx = -INFINITY;
     for (int j = tid; j < n; j += kMergeThreads) {
@@ -123,24 +154,9 @@ __device__ void merge_segment(const DecodeParams& p, int b, int h, int n, float*
     }
 }
 
-// Merge of the fixed split grid, one CTA per (KV head h, sequence b) when the
-// segment's G x max_splits weights fit the dynamic shared memory it was
-// launched with; sequences that fit one split were finished by the first pass.
-template <typename T>
-__global__ void __launch_bounds__(kMergeThreads) paged_decode_merge_segment_kernel(const DecodeParams p) {
-    extern __shared__ float weights[];
-    wait_for_prior_grid();
-    allow_next_grid();
-    const int h = blockIdx.x;
-    const int b = blockIdx.y;
-    const SeqSplit seq = seq_split(p, b);
-    if (seq.splits <= 1) return;
-    merge_segment<T>(p, b, h, seq.splits, weights);
-}
-
-// Merge of the fixed split grid, one CTA per output row (b, hq): for splits
-// too many to stage a whole segment's weights. Row (b, hq) has seq.splits
-// pieces at part rows (b * q_heads + hq) * max_splits + j.
+// Merge of the fixed split grid, one CTA per output row (b, hq). Row (b, hq)
+// has seq.splits pieces at part rows (b * q_heads + hq) * max_splits + j.
+// Sequences that fit one split were finished by the first pass.
 template <typename T>
 __global__ void __launch_bounds__(kMergeThreads) paged_decode_merge_kernel(const DecodeParams p) {
     wait_for_prior_grid();
