@@ -156,6 +156,38 @@ MV_API int mv_write_paged_kv(const void* key, int64_t key_stride_seq, int64_t ke
                       int32_t dtype, void* stream);
 
 /*
+ * mv_paged_decode for callers that cannot allocate device memory. No
+ * counterpart in the reference (its kernel allocates its own output-sized
+ * buffer). Some callers of a decode kernel may not call cudaMalloc: a plugin
+ * whose host owns every device allocation (a serving engine that reserves all
+ * memory up front and hands the plugin only inputs and outputs), or code that
+ * runs while a stream is being captured into a CUDA graph, where allocation is
+ * not allowed. This entry point takes the same arguments as mv_paged_decode
+ * minus the workspace and allocates nothing: its split-KV scratch is a
+ * file-scope device array of MV_NOALLOC_SCRATCH_BYTES that every GPU loading
+ * the library holds until the process exits.
+ *   - Calls whose split plan needs more scratch than that are rejected with
+ *     MV_ERR_UNSUPPORTED and a message naming the sizes; MV_FLAG_FUSED_MERGE
+ *     is rejected too (its counters would have to start at zero).
+ *   - The first call on a device looks up the array's device address (with
+ *     that device current); make that first call before any stream capture.
+ *   - Every call shares the one array and leaves its partial results in it:
+ *     calls that overlap on the GPU (other streams, other threads) race.
+ */
+#define MV_NOALLOC_SCRATCH_BYTES (16u * 1024u * 1024u)
+
+MV_API int mv_paged_decode_noalloc(const void* q, int64_t q_stride_seq, int64_t q_stride_head,
+                                   const void* k_cache, const void* v_cache, int64_t num_blocks,
+                                   int32_t num_kv_heads, int32_t block_size, int32_t head_dim,
+                                   const void* block_table, int32_t block_table_type,
+                                   int64_t block_table_stride, int64_t blocks_per_seq,
+                                   const void* context_lens, int32_t context_lens_type,
+                                   int64_t max_context_len, int32_t batch, int32_t num_q_heads,
+                                   float scale, void* out, int64_t out_stride_seq,
+                                   int64_t out_stride_head, int32_t pages_per_split,
+                                   uint32_t flags, int32_t dtype, void* stream);
+
+/*
  * Sticky MV_DEVICE_STATUS_* bits kernels have raised on `device` (a bounded
  * wait that gave up). Reading synchronises with the device's legacy stream.
  */

@@ -719,4 +719,61 @@ int mv_clear_device_status(int32_t device) {
     return err == cudaSuccess ? MV_OK : cuda_fail(err, "clearing device status");
 }
 
+// ------------------------------------------------- allocation-free decode
+
+// Split-KV scratch of mv_paged_decode_noalloc: a file-scope device array, so
+// callers that cannot allocate still get the split-KV kernels. Zero at module
+// load; shared by every call on a device.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[MV_NOALLOC_SCRATCH_BYTES];
+
+int mv_paged_decode_noalloc(const void* q, int64_t q_stride_seq, int64_t q_stride_head,
+                            const void* k_cache, const void* v_cache, int64_t num_blocks,
+                            int32_t num_kv_heads, int32_t block_size, int32_t head_dim,
+                            const void* block_table, int32_t block_table_type,
+                            int64_t block_table_stride, int64_t blocks_per_seq,
+                            const void* context_lens, int32_t context_lens_type,
+                            int64_t max_context_len, int32_t batch, int32_t num_q_heads,
+                            float scale, void* out, int64_t out_stride_seq,
+                            int64_t out_stride_head, int32_t pages_per_split, uint32_t flags,
+                            int32_t dtype, void* stream) {
+    if (flags & MV_FLAG_FUSED_MERGE)
+        return fail(MV_ERR_UNSUPPORTED,
+                    "mv_paged_decode_noalloc does not take MV_FLAG_FUSED_MERGE (its counters must start at zero)");
+    size_t needed = 0;
+    int rc = mv_paged_decode_workspace_size(batch, num_q_heads, num_kv_heads, head_dim, block_size,
+                                            max_context_len, pages_per_split, flags, dtype, &needed);
+    if (rc != MV_OK) return rc;
+    if (needed > MV_NOALLOC_SCRATCH_BYTES)
+        return fail(MV_ERR_UNSUPPORTED,
+                    "mv_paged_decode_noalloc: this call needs %zu bytes of split-KV scratch, the "
+                    "built-in array holds %zu; use mv_paged_decode with a workspace, or a larger "
+                    "pages_per_split",
+                    needed, static_cast<size_t>(MV_NOALLOC_SCRATCH_BYTES));
+    // Set-up, once per device, with that device current: the array's name is a
+    // host-side stand-in, so look up its device address.
+    static void* scratch[kMaxDevices] = {nullptr};
+    static std::mutex scratch_mutex;
+    int device = 0;
+    cudaError_t err = cudaGetDevice(&device);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaGetDevice");
+    if (device < 0 || device >= kMaxDevices) return fail(MV_ERR_UNSUPPORTED, "device index %d out of range", device);
+    void* ptr = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(scratch_mutex);
+        if (!scratch[device]) {
+            err = cudaGetSymbolAddress(&scratch[device], g_noalloc_scratch);
+            if (err != cudaSuccess) {
+                scratch[device] = nullptr;
+                return cuda_fail(err, "cudaGetSymbolAddress of the no-alloc scratch");
+            }
+        }
+        ptr = scratch[device];
+    }
+    return mv_paged_decode(q, q_stride_seq, q_stride_head, k_cache, v_cache, num_blocks, num_kv_heads,
+                           block_size, head_dim, block_table, block_table_type, block_table_stride,
+                           blocks_per_seq, context_lens, context_lens_type, max_context_len, batch,
+                           num_q_heads, scale, out, out_stride_seq, out_stride_head, ptr,
+                           MV_NOALLOC_SCRATCH_BYTES, pages_per_split, flags, dtype, stream);
+}
+
 }  // extern "C"
