@@ -47,9 +47,9 @@ for _path in (ROOT, ROOT / 'micro-vllm_b200'):
 METRIC = 'paged decode attn achieved HBM GB/s (% of B200 peak); decode tokens/s'
 DEFAULT_WORKLOAD = 'qwen7b_bf16'
 FALLBACK_HBM_GBS = 6650.0
-# dram__bytes_read.sum + dram__bytes_write.sum per launch of paged_decode_mma_kernel on this
-# workload, from ncu (profiles/paged_decode_mma_qwen7b_bf16.md); None until captured.
-NCU_TRAFFIC_BYTES = {}
+# dram__bytes_read.sum + dram__bytes_write.sum of one paged_decode_mma_kernel launch on this
+# workload, from one ncu capture (profiles/paged_decode_mma_qwen7b_bf16.md).
+NCU_TRAFFIC_BYTES = {'qwen7b_bf16': 329_501_440 + 5_254_912}
 L2_BYTES = 126 * 1024 * 1024
 
 
@@ -471,6 +471,9 @@ def run_ours(args):
                 'us_per_launch': round(attn_ms * 1e3, 3),
                 'algorithmic_bytes_per_launch': attn_bytes,
                 'traffic': traffic,
+                'traffic_source': ('ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch of '
+                                   'paged_decode_mma_kernel (profiles/paged_decode_mma_qwen7b_bf16.md)'
+                                   if traffic else None),
             },
             'e2e': {'value': round(e2e_value, 1), 'unit': 'GB/s',
                     'h2d_bytes_per_step': e2e['h2d'], 'd2h_bytes_per_step': e2e['d2h'],
