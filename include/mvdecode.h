@@ -49,6 +49,7 @@ extern "C" {
 #define MV_FLAG_FORCE_SIMT 1u /* use the CUDA-core kernel even where the tensor-core one applies */
 #define MV_FLAG_PERSISTENT 2u /* tensor-core kernel on the persistent schedule instead of the split grid */
 #define MV_FLAG_FUSED_MERGE 4u /* split grid: the last split CTA of each sequence/head merges it */
+#define MV_FLAG_SPLIT_GRID 8u  /* tensor-core split grid + merge pass instead of the cluster kernel */
 
 /* Status codes. */
 #define MV_OK 0
@@ -64,6 +65,7 @@ extern "C" {
 #define MV_PATH_SIMT 0            /* CUDA cores, one CTA per (split, KV head, sequence) */
 #define MV_PATH_TMA_MMA 1         /* TMA + tensor cores, one CTA per (split, KV head, sequence) */
 #define MV_PATH_TMA_MMA_PERSISTENT 2 /* TMA + tensor cores, persistent, equal page ranges per warp */
+#define MV_PATH_TMA_MMA_CLUSTER 3 /* TMA + tensor cores, one CTA cluster per (sequence, KV head) */
 
 MV_API int mv_abi_version(void);
 

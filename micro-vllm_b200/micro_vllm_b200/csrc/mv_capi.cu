@@ -113,6 +113,10 @@ int ensure_smem(Kernel kernel, size_t bytes) {
 #define MV_STAGES_D256 2
 #endif
 constexpr int kMmaWarps = MV_MMA_WARPS;
+#ifndef MV_CLUSTER_PAGES
+#define MV_CLUSTER_PAGES 64
+#endif
+constexpr int64_t kClusterPages = MV_CLUSTER_PAGES;  // pages per CTA the cluster kernel aims for
 constexpr int kMaxPagesPerSplit = 32 * kMmaWarps;
 
 struct Geometry {
@@ -139,6 +143,7 @@ struct Plan {
     int path;
     int pages_per_split;
     int max_splits;
+    int cluster;     // cluster kernel: CTAs per (sequence, KV head)
     int nt;          // mma n-tiles (8 query heads each)
     int ctas;        // persistent grid size
     int warps;       // persistent warps in the grid
@@ -238,9 +243,25 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
     plan->path = persistent ? MV_PATH_TMA_MMA_PERSISTENT : (mma ? MV_PATH_TMA_MMA : MV_PATH_SIMT);
     plan->nt = group <= 8 ? 1 : 2;
     plan->ctas = plan->warps = 0;
+    plan->cluster = 0;
     plan->counter_bytes = plan->part_o_bytes = plan->part_lse_bytes = 0;
     plan->fused_merge = false;
     const int64_t max_pages = (g.max_context_len + g.block_size - 1) / g.block_size;
+
+    // Sequences up to kClusterPages x 8 pages: split each (sequence, KV head)
+    // over a cluster of up to 8 CTAs of <= kClusterPages pages each and combine
+    // through distributed shared memory -- no partials in HBM, no merge pass.
+    if (mma && !persistent && pages_per_split == 0 && !(flags & MV_FLAG_SPLIT_GRID) &&
+        max_pages <= 8 * kClusterPages) {
+        int csize = 1;
+        while (csize * kClusterPages < max_pages) csize *= 2;
+        plan->path = MV_PATH_TMA_MMA_CLUSTER;
+        plan->cluster = csize;
+        plan->pages_per_split = static_cast<int>((max_pages + csize - 1) / csize);
+        plan->max_splits = 1;
+        plan->workspace = 0;
+        return MV_OK;
+    }
 
     if (persistent) {
         int per_sm = 0;
@@ -439,9 +460,56 @@ int launch_persistent_dispatch(const mv::DecodeParams& p, const CUtensorMap& kma
     }
 }
 
+template <typename T, int D, int NT>
+int launch_cluster(const mv::DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap,
+                   int csize, cudaStream_t stream) {
+    constexpr int STAGES = D == 64 ? MV_STAGES_D64 : (D == 128 ? MV_STAGES_D128 : MV_STAGES_D256);
+    using Shape = mv::ClusterShape<D, NT, kMmaWarps, STAGES>;
+    auto kernel = mv::paged_decode_cluster_kernel<T, D, NT, kMmaWarps, STAGES>;
+    int rc = ensure_smem(kernel, Shape::kSmemBytes);
+    if (rc != MV_OK) return rc;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(csize, p.kv_heads, p.batch);
+    cfg.blockDim = dim3(kMmaWarps * 32);
+    cfg.dynamicSmemBytes = Shape::kSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = csize;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    cudaError_t err = cudaLaunchKernelEx(&cfg, kernel, p, kmap, vmap);
+    return err == cudaSuccess ? MV_OK : cuda_fail(err, "cluster decode kernel launch");
+}
+
+template <typename T>
+int launch_cluster_dispatch(const mv::DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap,
+                            int csize, int nt, cudaStream_t stream) {
+    switch (p.head_dim * 4 + nt) {
+        case 64 * 4 + 1: return launch_cluster<T, 64, 1>(p, kmap, vmap, csize, stream);
+        case 64 * 4 + 2: return launch_cluster<T, 64, 2>(p, kmap, vmap, csize, stream);
+        case 128 * 4 + 1: return launch_cluster<T, 128, 1>(p, kmap, vmap, csize, stream);
+        case 128 * 4 + 2: return launch_cluster<T, 128, 2>(p, kmap, vmap, csize, stream);
+        case 256 * 4 + 1: return launch_cluster<T, 256, 1>(p, kmap, vmap, csize, stream);
+        case 256 * 4 + 2: return launch_cluster<T, 256, 2>(p, kmap, vmap, csize, stream);
+        default: return fail(MV_ERR_UNSUPPORTED, "no tensor-core kernel for head_dim %d", p.head_dim);
+    }
+}
+
 template <typename T>
 int launch_decode(const mv::DecodeParams& p, const Plan& plan, const CUtensorMap* kmap,
                   const CUtensorMap* vmap, cudaStream_t stream) {
+    if (plan.path == MV_PATH_TMA_MMA_CLUSTER) {
+        if constexpr (std::is_same<T, float>::value) {
+            return fail(MV_ERR_UNSUPPORTED, "tensor-core kernel takes fp16/bf16 only");
+        } else {
+            return launch_cluster_dispatch<T>(p, *kmap, *vmap, plan.cluster, plan.nt, stream);
+        }
+    }
     if (plan.path == MV_PATH_TMA_MMA_PERSISTENT) {
         if constexpr (std::is_same<T, float>::value) {
             return fail(MV_ERR_UNSUPPORTED, "tensor-core kernel takes fp16/bf16 only");
@@ -603,7 +671,8 @@ int mv_paged_decode(const void* q, int64_t q_stride_seq, int64_t q_stride_head, 
     }
 
     CUtensorMap kmap, vmap;
-    if (plan.path == MV_PATH_TMA_MMA || plan.path == MV_PATH_TMA_MMA_PERSISTENT) {
+    if (plan.path == MV_PATH_TMA_MMA || plan.path == MV_PATH_TMA_MMA_PERSISTENT ||
+        plan.path == MV_PATH_TMA_MMA_CLUSTER) {
         rc = page_tensor_map(k_cache, num_blocks, num_kv_heads, head_dim, dtype, &kmap);
         if (rc == MV_OK) rc = page_tensor_map(v_cache, num_blocks, num_kv_heads, head_dim, dtype, &vmap);
         if (rc != MV_OK) return rc;

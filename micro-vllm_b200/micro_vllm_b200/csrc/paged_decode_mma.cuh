@@ -30,6 +30,8 @@
 //    segments at its ends, written as partials for the merge pass.
 #pragma once
 
+#include <cooperative_groups.h>
+
 #include "mv_device.cuh"
 #include "paged_decode_merge.cuh"
 
@@ -789,6 +791,238 @@ paged_decode_persistent_kernel(const DecodeParams p, const __grid_constant__ CUt
             }
         }
     }
+}
+
+
+// ------------------------------------------------------------ cluster kernel
+//
+// Split-KV without a merge pass: the C split CTAs of one (sequence, KV head)
+// segment form a thread-block cluster. Each CTA streams an equal share of the
+// segment's pages, combines its warps in shared memory, and leaves its
+// normalised partial and log2-sum-exp there; after a cluster barrier every
+// CTA reads all C partials through distributed shared memory and writes its
+// share of the G x D outputs. No partials go to HBM and nothing waits on
+// another grid.
+
+template <int D, int NT, int NWARPS, int STAGES>
+struct ClusterShape {
+    using Grid = MmaDecodeShape<D, NT, NWARPS, STAGES>;
+    static constexpr int kStageRegion = NWARPS * Grid::kWarpBytes;
+    static constexpr int kResultBytes = 8 * NT * D * 4;  // this CTA's normalised partial [8*NT][D]
+    static constexpr int kSmemBytes = kStageRegion + kResultBytes + 1024;
+};
+
+template <typename T, int D, int NT, int NWARPS, int STAGES>
+__global__ void __launch_bounds__(NWARPS * 32)
+paged_decode_cluster_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap kmap,
+                            const __grid_constant__ CUtensorMap vmap) {
+    namespace cg = cooperative_groups;
+    using Shape = ClusterShape<D, NT, NWARPS, STAGES>;
+    using Grid = typename Shape::Grid;
+    using Warp = WarpPageAttention<T, D, NT>;
+    constexpr int kGP = 8 * NT;
+
+    extern __shared__ uint8_t smem_raw[];
+    __shared__ __align__(8) uint64_t bars[NWARPS][STAGES];
+    __shared__ int warp_flags[NWARPS];
+    __shared__ float cta_lse[kGP];  // per query row; -inf: no pages here; NaN: corrupted ID or timeout
+
+    cg::cluster_group cluster = cg::this_cluster();
+    const int rank = static_cast<int>(cluster.block_rank());
+    const int csize = static_cast<int>(cluster.num_blocks());
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int h = blockIdx.y;
+    const int b = blockIdx.z;
+
+    wait_for_prior_grid();
+    allow_next_grid();
+    const SeqSplit seq = seq_split(p, b);
+    if (seq.state != 0) {
+        // Every CTA of the cluster takes this branch: none waits on another.
+        if (rank == 0) write_group_constant<T>(p, b, h, seq.state == 1 ? 0.0f : __int_as_float(0x7fffffff));
+        return;
+    }
+
+    uint8_t* smem = reinterpret_cast<uint8_t*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    float* cta_o = reinterpret_cast<float*>(smem + Shape::kStageRegion);
+    const int64_t page_begin = seq.pages * rank / csize;
+    const int64_t page_end = seq.pages * (rank + 1) / csize;
+    const int cta_pages = static_cast<int>(page_end - page_begin);
+    const int n_my = warp < cta_pages ? (cta_pages - warp + NWARPS - 1) / NWARPS : 0;
+
+    // Page IDs of this warp's pages, 32 at a time: lane j of `cur` holds page
+    // 32k + j of the warp's sequence (run page warp + i * NWARPS), `nxt` the next 32.
+    auto load_id = [&](int i) -> long long {
+        return i < n_my ? load_index(p.block_table, p.table_i64,
+                                     b * p.table_stride + page_begin + warp + static_cast<int64_t>(i) * NWARPS)
+                        : 0;
+    };
+    long long cur = load_id(lane);
+    long long nxt = load_id(32 + lane);
+    auto id_ok = [&](long long id) { return id >= 0 && id < p.num_blocks; };
+    bool warp_bad = false;
+    {
+        // Whole-warp check of the first batch; later batches are checked as they rotate in.
+        warp_bad = __any_sync(0xffffffffu, lane < n_my && !id_ok(cur));
+    }
+    const uint32_t bar0 = smem_addr(&bars[warp][0]);
+    if (lane == 0) {
+#pragma unroll
+        for (int st = 0; st < STAGES; ++st) mbar_init(bar0 + 8 * st, 1);
+    }
+    fence_mbar_init();
+    __syncwarp();
+
+    uint8_t* wsm = smem + warp * Grid::kWarpBytes;
+    const uint32_t wsm_addr = smem_addr(wsm);
+    auto issue = [&](int i, long long batch) {
+        const long long id = __shfl_sync(0xffffffffu, batch, i & 31);
+        if (lane == 0) {
+            const int st = i % STAGES;
+            const uint32_t bar = bar0 + 8 * st;
+            if (id_ok(id)) {
+                const uint32_t dst = wsm_addr + st * Grid::kStageBytes;
+                mbar_arrive_expect_tx(bar, Grid::kStageBytes);
+                tma_load_5d(dst, &kmap, 0, 0, 0, h, static_cast<int>(id), bar);
+                tma_load_5d(dst + Grid::kTileBytes, &vmap, 0, 0, 0, h, static_cast<int>(id), bar);
+            } else {
+                // No load for a corrupted ID; complete the phase so the ring stays in step.
+                asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+            }
+        }
+    };
+    const int prologue = n_my < STAGES ? n_my : STAGES;
+    for (int i = 0; i < prologue; ++i) issue(i, cur);
+
+    Warp w;
+    w.load_q(p, b, h, lane);
+    w.reset();
+
+    bool failed = false;
+    int i = 0;
+    for (; i < n_my; ++i) {
+        if (i > 0 && (i & 31) == 0) {
+            cur = nxt;
+            nxt = load_id(i + 32 + lane);
+            warp_bad |= __any_sync(0xffffffffu, i + lane < n_my && !id_ok(cur));
+        }
+        const int st = i % STAGES;
+        const bool ok = mbar_wait_bounded(bar0 + 8 * st, (i / STAGES) & 1);
+        if (!__all_sync(0xffffffffu, ok)) {
+            failed = true;
+            break;
+        }
+        const uint32_t kt = wsm_addr + st * Grid::kStageBytes;
+        const uint32_t vt = kt + Grid::kTileBytes;
+        const int64_t page = page_begin + warp + static_cast<int64_t>(i) * NWARPS;
+        const int64_t left = seq.len - page * kPageTokens;
+        const int valid = left < kPageTokens ? static_cast<int>(left) : kPageTokens;
+        const bool page_ok = id_ok(__shfl_sync(0xffffffffu, cur, i & 31));
+        typename Warp::PageFrags frags;
+        if (page_ok) Warp::load_page(frags, kt, vt, wsm + st * Grid::kStageBytes + Grid::kTileBytes, valid, lane);
+        if (i + STAGES < n_my) {
+            fence_proxy_async_smem();  // this lane's shared reads/writes before the TMA write
+            __syncwarp();
+            const int j = i + STAGES;
+            issue(j, (j >> 5) == (i >> 5) ? cur : nxt);
+        }
+        if (page_ok) w.attend(frags, valid, p.scale_log2, lane);
+    }
+    if (failed) {
+        const int last = i + STAGES < n_my ? i + STAGES : n_my;
+        for (int j = i; j < last; ++j) mbar_wait_bounded(bar0 + 8 * (j % STAGES), (j / STAGES) & 1);
+        if (lane == 0) atomicOr(&g_device_status, kStatusWaitTimeout);
+    }
+    if (lane == 0) warp_flags[warp] = (failed ? 2 : 0) | (warp_bad ? 1 : 0);
+    w.reduce_l();
+
+    // Combine the warps through shared memory (their stages are drained).
+    __syncthreads();
+    float* red = reinterpret_cast<float*>(wsm);
+    float* red_m = red + Grid::kQRows * Grid::kRedStride;
+    float* red_l = red_m + Grid::kQRows;
+#pragma unroll
+    for (int mt = 0; mt < Warp::KS; ++mt) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const int d = mt * 16 + (lane >> 2);
+            const int q = nt * 8 + 2 * (lane & 3);
+            red[q * Grid::kRedStride + d] = w.o[mt][nt][0];
+            red[(q + 1) * Grid::kRedStride + d] = w.o[mt][nt][1];
+            red[q * Grid::kRedStride + d + 8] = w.o[mt][nt][2];
+            red[(q + 1) * Grid::kRedStride + d + 8] = w.o[mt][nt][3];
+        }
+    }
+    if (lane < 4) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+            const int q = nt * 8 + 2 * lane;
+            red_m[q] = w.m[nt][0];
+            red_m[q + 1] = w.m[nt][1];
+            red_l[q] = w.l[nt][0];
+            red_l[q + 1] = w.l[nt][1];
+        }
+    }
+    __syncthreads();
+    int cta_bad = 0;
+#pragma unroll
+    for (int v = 0; v < NWARPS; ++v) cta_bad |= warp_flags[v];
+    const int G = p.group;
+    for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
+        const int g = idx / D;
+        const int d = idx - g * D;
+        float mx = -INFINITY;
+#pragma unroll
+        for (int v = 0; v < NWARPS; ++v)
+            mx = fmaxf(mx, reinterpret_cast<const float*>(smem + v * Grid::kWarpBytes)[Grid::kQRows * Grid::kRedStride + g]);
+        float den = 0.0f;
+        float num = 0.0f;
+#pragma unroll
+        for (int v = 0; v < NWARPS; ++v) {
+            const float* wr = reinterpret_cast<const float*>(smem + v * Grid::kWarpBytes);
+            const float* wm = wr + Grid::kQRows * Grid::kRedStride;
+            const float f = mx == -INFINITY ? 0.0f : fast_exp2(wm[g] - mx);
+            den += f * wm[Grid::kQRows + g];
+            num += f * wr[g * Grid::kRedStride + d];
+        }
+        cta_o[g * D + d] = den > 0.0f ? num / den : 0.0f;
+        if (d == 0)
+            cta_lse[g] = cta_bad ? __int_as_float(0x7fffffff) : (den > 0.0f ? mx + log2f(den) : -INFINITY);
+    }
+
+    // Every CTA's partial is in its shared memory: combine across the cluster.
+    cluster.sync();
+    T* out = static_cast<T*>(p.out) + b * p.out_stride_seq;
+    const int total = G * D;
+    const int begin = total * rank / csize;
+    const int end = total * (rank + 1) / csize;
+    for (int idx = begin + static_cast<int>(threadIdx.x); idx < end; idx += blockDim.x) {
+        const int g = idx / D;
+        const int d = idx - g * D;
+        float mx = -INFINITY;
+        bool nan = false;
+        for (int c = 0; c < csize; ++c) {
+            const float v = *cluster.map_shared_rank(&cta_lse[g], c);
+            nan |= isnan(v);
+            mx = fmaxf(mx, v);
+        }
+        float value = __int_as_float(0x7fffffff);
+        if (!nan) {
+            float den = 0.0f;
+            float num = 0.0f;
+            for (int c = 0; c < csize; ++c) {
+                const float v = *cluster.map_shared_rank(&cta_lse[g], c);
+                const float f = v == -INFINITY ? 0.0f : fast_exp2(v - mx);
+                den += f;
+                num += f * *cluster.map_shared_rank(&cta_o[g * D + d], c);
+            }
+            value = num / den;
+        }
+        out[static_cast<int64_t>(h * G + g) * p.out_stride_head + d] = from_float<T>(value);
+    }
+    cluster.sync();  // no CTA leaves while another may still read its shared memory
 }
 
 }  // namespace mv

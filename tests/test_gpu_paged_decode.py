@@ -47,7 +47,8 @@ def _oracle(inputs, key_pool, value_pool):
 
 
 MODES = {
-    'auto': {},                               # tensor-core split grid (fused merge) where the shape allows
+    'auto': {},                               # tensor-core cluster kernel (contexts up to 8192 tokens)
+    'split': dict(split_grid=True),           # tensor-core split grid + merge pass
     'persistent': dict(persistent=True),      # tensor-core persistent schedule + merge pass
     'fused': dict(fused_merge=True),          # split grid, last split CTA merges
     'split4': dict(pages_per_split=4),        # split grid, 4 pages per split
@@ -80,7 +81,10 @@ def test_tensor_core_paths_are_selected_for_qwen_geometry():
     inputs = make_inputs('qwen7b_bf16_small')
     t = workload_tensors(inputs)
     path, pps, splits = attention.paged_decode_plan(28, t['key_pool'], 4096, batch=64)
+    assert path == 'tma_mma_cluster' and pps <= 64
+    path, pps, splits = attention.paged_decode_plan(28, t['key_pool'], 4096, batch=64, split_grid=True)
     assert path == 'tma_mma' and splits >= 2
+    assert attention.paged_decode_plan(28, t['key_pool'], 32768, batch=8)[0] == 'tma_mma'
     assert attention.paged_decode_plan(28, t['key_pool'], 4096, batch=64, persistent=True)[0] == \
         'tma_mma_persistent'
     assert attention.paged_decode_plan(28, t['key_pool'], 4096, batch=64, force_simt=True)[0] == 'simt'
@@ -95,10 +99,30 @@ def test_persistent_ranges_cover_every_length_mix(lens):
                 pool=('factor', 1.3), lens=('fixed', lens), dtype='bfloat16', value_scale=0.5,
                 seed=31 + len(lens))
     inputs = make_inputs(spec)
-    for mode in ('auto', 'persistent'):
+    for mode in ('auto', 'split', 'persistent'):
         t, out = _append_and_decode(inputs, **MODES[mode])
         expected = _oracle(inputs, to_numpy(t['key_pool']), to_numpy(t['value_pool']))
         assert_attention_close(as_float(out), expected, 'bfloat16')
+
+
+@pytest.mark.parametrize('max_len', [16, 64, 65, 128, 129, 300, 1024, 2047, 4096, 8192])
+def test_cluster_sizes_cover_every_bound(max_len):
+    """The cluster kernel splits each sequence over 1..8 CTAs by the host bound;
+    lengths well under the bound leave CTAs of a cluster with no pages."""
+    lens = sorted({1, max(1, max_len // 3), max_len})
+    spec = dict(batch=len(lens), q_heads=28, kv_heads=4, head_dim=128, block_size=16,
+                pool=('factor', 1.2), lens=('fixed', lens), dtype='bfloat16', value_scale=0.5,
+                seed=max_len)
+    inputs = make_inputs(spec)
+    attention, cache = _native()
+    t = workload_tensors(inputs)
+    cache.write_paged_kv(t['key_new'], t['value_new'], t['key_pool'], t['value_pool'],
+                         t['block_table'], positions=t['context_lens'], positions_are_end=True)
+    assert attention.paged_decode_plan(28, t['key_pool'], max_len, batch=len(lens))[0] == 'tma_mma_cluster'
+    out = attention.paged_decode_attention(t['q'], t['key_pool'], t['value_pool'], t['block_table'],
+                                           t['context_lens'], max_context_len=max_len)
+    expected = _oracle(inputs, to_numpy(t['key_pool']), to_numpy(t['value_pool']))
+    assert_attention_close(as_float(out), expected, 'bfloat16')
 
 
 def test_workspace_counters_reset_across_calls_and_paths():
