@@ -49,7 +49,7 @@ extern "C" {
 #define MV_FLAG_FORCE_SIMT 1u /* use the CUDA-core kernel even where the tensor-core one applies */
 #define MV_FLAG_PERSISTENT 2u /* tensor-core kernel on the persistent schedule instead of the split grid */
 #define MV_FLAG_FUSED_MERGE 4u /* split grid: the last split CTA of each sequence/head merges it */
-#define MV_FLAG_SPLIT_GRID 8u  /* tensor-core split grid + merge pass instead of the cluster kernel */
+#define MV_FLAG_CLUSTER 8u /* tensor-core cluster kernel (contexts up to 8192 tokens), no merge pass */
 
 /* Status codes. */
 #define MV_OK 0

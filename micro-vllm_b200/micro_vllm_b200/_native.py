@@ -20,7 +20,7 @@ POSITIONS_START, POSITIONS_END = 0, 1
 FLAG_FORCE_SIMT = 1
 FLAG_PERSISTENT = 2
 FLAG_FUSED_MERGE = 4
-FLAG_SPLIT_GRID = 8
+FLAG_CLUSTER = 8
 PATH_SIMT, PATH_TMA_MMA, PATH_TMA_MMA_PERSISTENT, PATH_TMA_MMA_CLUSTER = 0, 1, 2, 3
 PATH_NAMES = {0: 'simt', 1: 'tma_mma', 2: 'tma_mma_persistent', 3: 'tma_mma_cluster'}
 DEVICE_STATUS_WAIT_TIMEOUT = 1

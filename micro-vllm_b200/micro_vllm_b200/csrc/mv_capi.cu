@@ -248,10 +248,11 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
     plan->fused_merge = false;
     const int64_t max_pages = (g.max_context_len + g.block_size - 1) / g.block_size;
 
-    // Sequences up to kClusterPages x 8 pages: split each (sequence, KV head)
-    // over a cluster of up to 8 CTAs of <= kClusterPages pages each and combine
-    // through distributed shared memory -- no partials in HBM, no merge pass.
-    if (mma && !persistent && pages_per_split == 0 && !(flags & MV_FLAG_SPLIT_GRID) &&
+    // Opt-in: sequences up to kClusterPages x 8 pages split over a cluster of up
+    // to 8 CTAs of <= kClusterPages pages each, combined through distributed
+    // shared memory -- no partials in HBM, no merge pass. Measured on B200 it
+    // loses to the split grid (a cluster's CTAs wait for its slowest one).
+    if (mma && !persistent && pages_per_split == 0 && (flags & MV_FLAG_CLUSTER) &&
         max_pages <= 8 * kClusterPages) {
         int csize = 1;
         while (csize * kClusterPages < max_pages) csize *= 2;

@@ -141,16 +141,29 @@ __device__ void merge_segment(const DecodeParams& p, int b, int h, int n, float*
         for (int j = lane; j < n; j += 32) w[j] = fast_exp2(w[j] - mx) * inv;
     }
     __syncthreads();
+    // Each thread owns a column and walks the rows four at a time, so the loads
+    // of four rows x several splits are in flight together.
     T* out = static_cast<T*>(p.out) + b * p.out_stride_seq;
-    for (int idx = threadIdx.x; idx < G * D; idx += blockDim.x) {
-        const int g = idx / D;
-        const int d = idx - g * D;
-        const float* src = p.part_o + (row0 + static_cast<int64_t>(g) * p.max_splits) * D + d;
-        const float* w = weights + g * n;
-        float acc = 0.0f;
-#pragma unroll 8
-        for (int j = 0; j < n; ++j) acc = fmaf(w[j], __ldcg(src + static_cast<int64_t>(j) * D), acc);
-        out[static_cast<int64_t>(h * G + g) * p.out_stride_head + d] = from_float<T>(acc);
+    for (int d = threadIdx.x; d < D; d += blockDim.x) {
+        for (int g0 = 0; g0 < G; g0 += 4) {
+            float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 2
+            for (int j = 0; j < n; ++j) {
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int g = g0 + u;
+                    if (g < G) {
+                        const float* src = p.part_o + (row0 + static_cast<int64_t>(g) * p.max_splits + j) * D + d;
+                        acc[u] = fmaf(weights[g * n + j], __ldcg(src), acc[u]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                if (g0 + u < G)
+                    out[static_cast<int64_t>(h * G + g0 + u) * p.out_stride_head + d] = from_float<T>(acc[u]);
+            }
+        }
     }
 }
 

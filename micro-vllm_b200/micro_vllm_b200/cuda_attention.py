@@ -215,13 +215,13 @@ def decode_attention_paged(query: torch.Tensor, cache, *, layer_idx: int) -> tor
         cache._device_page_table, length)
 
 
-def _flags(force_simt, persistent, fused_merge=False, split_grid=False):
+def _flags(force_simt, persistent, fused_merge=False, cluster=False):
     return ((_native.FLAG_FORCE_SIMT if force_simt else 0) | (_native.FLAG_PERSISTENT if persistent else 0)
-            | (_native.FLAG_FUSED_MERGE if fused_merge else 0) | (_native.FLAG_SPLIT_GRID if split_grid else 0))
+            | (_native.FLAG_FUSED_MERGE if fused_merge else 0) | (_native.FLAG_CLUSTER if cluster else 0))
 
 
 def paged_decode_plan(query_heads, key_cache, context_bound, *, batch, pages_per_split=0,
-                      force_simt=False, persistent=False, split_grid=False):
+                      force_simt=False, persistent=False, cluster=False):
     """(path, pages_per_split, max_splits) that ``paged_decode_attention`` would use.
 
     path is 'tma_mma_cluster' (TMA + tensor cores, the splits of each
@@ -237,7 +237,7 @@ def paged_decode_plan(query_heads, key_cache, context_bound, *, batch, pages_per
     with torch.cuda.device(key_cache.device):
         _native.check(lib.mv_paged_decode_plan(
             batch, query_heads, kv_heads, dim, block_size, context_bound, pages_per_split,
-            _flags(force_simt, persistent, split_grid=split_grid), DTYPE_CODES[key_cache.dtype],
+            _flags(force_simt, persistent, cluster=cluster), DTYPE_CODES[key_cache.dtype],
             key_cache.data_ptr(), key_cache.data_ptr(), ctypes.byref(path), ctypes.byref(pps),
             ctypes.byref(splits)))
     return _native.PATH_NAMES[path.value], pps.value, splits.value
@@ -248,7 +248,7 @@ def paged_decode_attention(query: torch.Tensor, key_cache: torch.Tensor, value_c
                            scale: float | None = None, *, max_context_len: int | None = None,
                            out: torch.Tensor | None = None, pages_per_split: int = 0,
                            force_simt: bool = False, persistent: bool = False,
-                           fused_merge: bool = False, split_grid: bool = False) -> torch.Tensor:
+                           fused_merge: bool = False, cluster: bool = False) -> torch.Tensor:
     """Batched paged GQA decode over one shared page pool.
 
     query: [B, Hq, D] (or [B, Hq, 1, D]) CUDA fp32/fp16/bf16, feature stride 1.
@@ -261,13 +261,12 @@ def paged_decode_attention(query: torch.Tensor, key_cache: torch.Tensor, value_c
     table capacity max_blocks * bs, so no device read-back is needed. Lengths
     above it produce NaN (the split plan cannot cover them).
     out: optional [B, Hq, D] destination (feature stride 1).
-    pages_per_split / split_grid / persistent / fused_merge / force_simt:
-    kernel selection for tests and tuning (that many pages per split-KV CTA;
-    the split grid + merge pass; the persistent tensor-core schedule; merging
-    splits in the last split CTA; the CUDA-core kernel). By default the
-    library picks the tensor-core cluster kernel for contexts up to 8192
-    tokens, the tensor-core split grid above that, and the CUDA-core kernel
-    for shapes the tensor-core kernels do not take.
+    pages_per_split / cluster / persistent / fused_merge / force_simt: kernel
+    selection for tests and tuning (that many pages per split-KV CTA; the
+    cluster kernel; the persistent tensor-core schedule; merging splits in the
+    last split CTA; the CUDA-core kernel). By default the library picks the
+    tensor-core split grid with a merge pass, and the CUDA-core kernel for
+    shapes the tensor-core kernels do not take.
     Returns out, or a fresh [B, Hq, D] tensor of the query's dtype.
     """
     squeeze = query.dim() == 4
@@ -317,5 +316,5 @@ def paged_decode_attention(query: torch.Tensor, key_cache: torch.Tensor, value_c
          block_table.stride(0), block_table.shape[1], context_lens, int(max_context_len), scale,
          _Pointers(q.data_ptr(), out.data_ptr()), (out.stride(0), out.stride(1)),
          pages_per_split=int(pages_per_split),
-         flags=_flags(force_simt, persistent, fused_merge, split_grid))
+         flags=_flags(force_simt, persistent, fused_merge, cluster))
     return out

@@ -47,8 +47,8 @@ def _oracle(inputs, key_pool, value_pool):
 
 
 MODES = {
-    'auto': {},                               # tensor-core cluster kernel (contexts up to 8192 tokens)
-    'split': dict(split_grid=True),           # tensor-core split grid + merge pass
+    'auto': {},                               # tensor-core split grid + merge pass
+    'cluster': dict(cluster=True),            # tensor-core cluster kernel (contexts up to 8192 tokens)
     'persistent': dict(persistent=True),      # tensor-core persistent schedule + merge pass
     'fused': dict(fused_merge=True),          # split grid, last split CTA merges
     'split4': dict(pages_per_split=4),        # split grid, 4 pages per split
@@ -81,10 +81,10 @@ def test_tensor_core_paths_are_selected_for_qwen_geometry():
     inputs = make_inputs('qwen7b_bf16_small')
     t = workload_tensors(inputs)
     path, pps, splits = attention.paged_decode_plan(28, t['key_pool'], 4096, batch=64)
-    assert path == 'tma_mma_cluster' and pps <= 64
-    path, pps, splits = attention.paged_decode_plan(28, t['key_pool'], 4096, batch=64, split_grid=True)
     assert path == 'tma_mma' and splits >= 2
-    assert attention.paged_decode_plan(28, t['key_pool'], 32768, batch=8)[0] == 'tma_mma'
+    path, pps, splits = attention.paged_decode_plan(28, t['key_pool'], 4096, batch=64, cluster=True)
+    assert path == 'tma_mma_cluster' and pps <= 64
+    assert attention.paged_decode_plan(28, t['key_pool'], 32768, batch=8, cluster=True)[0] == 'tma_mma'
     assert attention.paged_decode_plan(28, t['key_pool'], 4096, batch=64, persistent=True)[0] == \
         'tma_mma_persistent'
     assert attention.paged_decode_plan(28, t['key_pool'], 4096, batch=64, force_simt=True)[0] == 'simt'
@@ -99,7 +99,7 @@ def test_persistent_ranges_cover_every_length_mix(lens):
                 pool=('factor', 1.3), lens=('fixed', lens), dtype='bfloat16', value_scale=0.5,
                 seed=31 + len(lens))
     inputs = make_inputs(spec)
-    for mode in ('auto', 'split', 'persistent'):
+    for mode in ('auto', 'cluster', 'persistent'):
         t, out = _append_and_decode(inputs, **MODES[mode])
         expected = _oracle(inputs, to_numpy(t['key_pool']), to_numpy(t['value_pool']))
         assert_attention_close(as_float(out), expected, 'bfloat16')
@@ -118,9 +118,10 @@ def test_cluster_sizes_cover_every_bound(max_len):
     t = workload_tensors(inputs)
     cache.write_paged_kv(t['key_new'], t['value_new'], t['key_pool'], t['value_pool'],
                          t['block_table'], positions=t['context_lens'], positions_are_end=True)
-    assert attention.paged_decode_plan(28, t['key_pool'], max_len, batch=len(lens))[0] == 'tma_mma_cluster'
+    assert attention.paged_decode_plan(28, t['key_pool'], max_len, batch=len(lens),
+                                       cluster=True)[0] == 'tma_mma_cluster'
     out = attention.paged_decode_attention(t['q'], t['key_pool'], t['value_pool'], t['block_table'],
-                                           t['context_lens'], max_context_len=max_len)
+                                           t['context_lens'], max_context_len=max_len, cluster=True)
     expected = _oracle(inputs, to_numpy(t['key_pool']), to_numpy(t['value_pool']))
     assert_attention_close(as_float(out), expected, 'bfloat16')
 

@@ -68,6 +68,8 @@ def test_python_binding_constants_match_the_header():
     assert constants['MV_PATH_SIMT'] == _native.PATH_SIMT
     assert constants['MV_PATH_TMA_MMA'] == _native.PATH_TMA_MMA
     assert constants['MV_PATH_TMA_MMA_PERSISTENT'] == _native.PATH_TMA_MMA_PERSISTENT
+    assert constants['MV_PATH_TMA_MMA_CLUSTER'] == _native.PATH_TMA_MMA_CLUSTER
+    assert constants['MV_FLAG_CLUSTER'] == _native.FLAG_CLUSTER
     assert constants['MV_DEVICE_STATUS_WAIT_TIMEOUT'] == _native.DEVICE_STATUS_WAIT_TIMEOUT
     assert constants['MV_ABI_VERSION'] == _native.MV_ABI_VERSION
 
