@@ -2,8 +2,11 @@
 """Benchmark: one decode step of one paged GQA attention layer on B200.
 
 A step is the hot path over one batch: append this step's K/V token for every
-sequence into its page (write_paged_kv) and run paged decode attention over
-the whole context (paged_decode_attention). Workload: Qwen2.5-7B decode
+sequence into its page and run paged decode attention over the whole context.
+By default the step is one call, paged_decode_with_append (the decode kernel
+writes each sequence's new row into the page it attends); ``--step separate``
+times the two-call form, write_paged_kv then paged_decode_attention, and
+every run also reports that form's time beside the headline. Workload: Qwen2.5-7B decode
 geometry -- batch 64, 28 query / 4 KV heads, head_dim 128, bf16, context
 lengths uniform in [1024, 4096], 16-token pages in a randomly permuted pool
 1.25x the pages in use, q/K/V ~ 0.5 N(0,1), scale 128^-1/2. Seeded synthetic
@@ -65,6 +68,8 @@ def parse_args(argv=None):
                         help='wall-clock budget of the CPU baseline sample')
     parser.add_argument('--no-cpu-baseline', action='store_true')
     parser.add_argument('--pages-per-split', type=int, default=0)
+    parser.add_argument('--step', choices=('fused', 'separate'), default='fused',
+                        help='one-call append + attention (default) or the append kernel then attention')
     return parser.parse_args(argv)
 
 
@@ -338,7 +343,7 @@ def run_ours(args):
     out = torch.empty_like(data['q'])
     pps = args.pages_per_split
 
-    def step():
+    def separate_step():
         cuda_paged_cache.write_paged_kv(data['k_new'], data['v_new'], data['k_pool'], data['v_pool'],
                                         data['block_table'], positions=data['context_lens'],
                                         positions_are_end=True)
@@ -346,6 +351,14 @@ def run_ours(args):
                                               data['block_table'], data['context_lens'],
                                               max_context_len=max_len, out=out,
                                               pages_per_split=pps)
+
+    def fused_step():
+        cuda_attention.paged_decode_with_append(data['q'], data['k_new'][:, :, 0], data['v_new'][:, :, 0],
+                                                data['k_pool'], data['v_pool'], data['block_table'],
+                                                data['context_lens'], max_context_len=max_len, out=out,
+                                                pages_per_split=pps)
+
+    step, other_step = (fused_step, separate_step) if args.step == 'fused' else (separate_step, fused_step)
 
     def attention_only():
         cuda_attention.paged_decode_attention(data['q'], data['k_pool'], data['v_pool'],
@@ -355,18 +368,23 @@ def run_ours(args):
 
     path, chosen_pps, splits = cuda_attention.paged_decode_plan(
         q_heads, data['k_pool'], max_len, batch=len(lens_host), pages_per_split=pps)
-    launches_per_step = 1 + 1 + (1 if splits > 1 else 0)
+    # The fused step is one decode launch (+ merge); the separate one adds the append kernel.
+    launches_per_step = (1 if args.step == 'fused' and path == 'tma_mma' else 2) + (1 if splits > 1 else 0)
 
     stream = torch.cuda.Stream(device)
     stream.wait_stream(torch.cuda.current_stream(device))
     with torch.cuda.stream(stream):
         for _ in range(3):
             step()
+            other_step()
             attention_only()
     torch.cuda.synchronize(device)
     step_graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(step_graph, stream=stream):
         step()
+    other_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(other_graph, stream=stream):
+        other_step()
     attn_graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(attn_graph, stream=stream):
         attention_only()
@@ -411,16 +429,34 @@ def run_ours(args):
         torch.cuda.synchronize(device)
         attn_ms = statistics.mean(s.elapsed_time(e) for s, e in events)
 
+        # The other form of the step, same loop, reported beside the headline.
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                other_graph.replay()
+        torch.cuda.synchronize(device)
+        barrier()
+        torch.cuda.synchronize(device)
+        other_reps = min(args.steps, 1000)
+        o_start, o_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            o_start.record(stream)
+            for _ in range(other_reps):
+                other_graph.replay()
+            o_end.record(stream)
+        torch.cuda.synchronize(device)
+        barrier()
+        other_ms = o_start.elapsed_time(o_end) * args.steps / other_reps
+
         # End to end through the public API: pinned host inputs in, output back out.
         e2e = run_e2e(args, data, max_len, pps, stream, device, barrier)
     clock_summary = clocks.summary()
 
-    times = torch.tensor([elapsed_ms, attn_ms, e2e['ms']], dtype=torch.float64, device=device)
+    times = torch.tensor([elapsed_ms, attn_ms, e2e['ms'], other_ms], dtype=torch.float64, device=device)
     totals = torch.tensor([float(step_total), float(attn_bytes)], dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
         dist.all_reduce(totals, op=dist.ReduceOp.SUM)
-    elapsed_ms, attn_ms, e2e_ms = times.tolist()
+    elapsed_ms, attn_ms, e2e_ms, other_ms = times.tolist()
     job_step_bytes, job_attn_bytes = totals.tolist()
     ms_per_step = elapsed_ms / args.steps
     value = job_step_bytes * args.steps / (elapsed_ms / 1e3) / 1e9
@@ -450,7 +486,9 @@ def run_ours(args):
                              f'{spec["q_heads"]} q / {spec["kv_heads"]} kv heads, head_dim '
                              f'{spec["head_dim"]}, block {spec["block_size"]}, lens {spec["lens"]}'),
                 'per_rank': {'batch': batch, 'q_heads': q_heads, 'kv_heads': kv_heads},
-                'step': 'append 1 token/sequence + paged decode attention (1 layer)',
+                'step': ('append 1 token/sequence + paged decode attention (1 layer), '
+                         + ('one call: paged_decode_with_append' if args.step == 'fused' else
+                            'two calls: write_paged_kv + paged_decode_attention')),
                 'l2': f'inputs larger than L2: KV pool {2 * data["k_pool"].numel() * data["k_pool"].element_size() / 1e9:.2f} GB per GPU',
                 'parallelism': f'kv-head sharded x{world}, {args.scaling}' if world > 1 else 'single GPU',
                 'timing': 'CUDA events around K CUDA-graph replays, max over ranks',
@@ -478,12 +516,15 @@ def run_ours(args):
             'e2e': {'value': round(e2e_value, 1), 'unit': 'GB/s',
                     'h2d_bytes_per_step': e2e['h2d'], 'd2h_bytes_per_step': e2e['d2h'],
                     'us_per_step': round(e2e_ms / args.steps * 1e3, 3)},
+            'step_forms_us': {args.step: round(ms_per_step * 1e3, 3),
+                              ('separate' if args.step == 'fused' else 'fused'):
+                                  round(other_ms / args.steps * 1e3, 3)},
             'clocks': clock_summary,
             'gpu_launches': launches_per_step * args.steps,
         }
         if world == 1 and not args.no_cpu_baseline:
             result['cpu_baseline'] = cpu_baseline(spec, data, q_heads, kv_heads, args.cpu_seconds)
-    del step_graph, attn_graph
+    del step_graph, attn_graph, other_graph
     if world > 1:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
@@ -506,13 +547,19 @@ def run_e2e(args, data, max_len, pps, stream, device, barrier):
     def step():
         for name in host:
             dev[name].copy_(host[name], non_blocking=True)
-        cuda_paged_cache.write_paged_kv(dev['k_new'], dev['v_new'], data['k_pool'], data['v_pool'],
-                                        data['block_table'], positions=dev['context_lens'],
-                                        positions_are_end=True)
-        cuda_attention.paged_decode_attention(dev['q'], data['k_pool'], data['v_pool'],
-                                              data['block_table'], dev['context_lens'],
-                                              max_context_len=max_len, out=out_dev,
-                                              pages_per_split=pps)
+        if args.step == 'fused':
+            cuda_attention.paged_decode_with_append(dev['q'], dev['k_new'], dev['v_new'], data['k_pool'],
+                                                    data['v_pool'], data['block_table'], dev['context_lens'],
+                                                    max_context_len=max_len, out=out_dev,
+                                                    pages_per_split=pps)
+        else:
+            cuda_paged_cache.write_paged_kv(dev['k_new'], dev['v_new'], data['k_pool'], data['v_pool'],
+                                            data['block_table'], positions=dev['context_lens'],
+                                            positions_are_end=True)
+            cuda_attention.paged_decode_attention(dev['q'], data['k_pool'], data['v_pool'],
+                                                  data['block_table'], dev['context_lens'],
+                                                  max_context_len=max_len, out=out_dev,
+                                                  pages_per_split=pps)
         out_host.copy_(out_dev, non_blocking=True)
 
     steps = min(args.steps, 1000)

@@ -158,6 +158,41 @@ MV_API int mv_write_paged_kv(const void* key, int64_t key_stride_seq, int64_t ke
                       int32_t dtype, void* stream);
 
 /*
+ * One decode step's append and attention in one call: the same result, in the
+ * pool and in out, as mv_write_paged_kv(key, value, ..., positions =
+ * context_lens, MV_POSITIONS_END, num_tokens = 1) followed by
+ * mv_paged_decode(...) on the same stream. With context_lens NULL the row goes
+ * to position max_context_len - 1 of every sequence.
+ *
+ * Replaces the pair of reference calls the decode layer makes per step:
+ * PagedKVCache.append -> _write_paged_kv (src/micro_vllm/paged_kv_cache.py:163-172)
+ * and then decode_attention_paged (src/micro_vllm/model.py:215-216, 177).
+ *
+ * key/value: [batch, num_kv_heads] rows of head_dim elements, feature stride 1,
+ * element strides per sequence and per head. Where the split-grid tensor-core
+ * kernel runs (mv_paged_decode_plan path MV_PATH_TMA_MMA) and the rows are
+ * 16-byte aligned, the CTA that attends a sequence's last page writes the row
+ * into the pool and into its staged copy of that page: no separate append
+ * launch. Otherwise the append kernel runs first (two launches). The page that
+ * receives a sequence's new row must not be read by another sequence in the
+ * same call (as with any in-place append); the other arguments and contracts
+ * are those of mv_paged_decode.
+ */
+MV_API int mv_paged_decode_append(const void* q, int64_t q_stride_seq, int64_t q_stride_head,
+                                  const void* key, int64_t key_stride_seq, int64_t key_stride_head,
+                                  const void* value, int64_t value_stride_seq,
+                                  int64_t value_stride_head, void* k_cache, void* v_cache,
+                                  int64_t num_blocks, int32_t num_kv_heads, int32_t block_size,
+                                  int32_t head_dim, const void* block_table,
+                                  int32_t block_table_type, int64_t block_table_stride,
+                                  int64_t blocks_per_seq, const void* context_lens,
+                                  int32_t context_lens_type, int64_t max_context_len,
+                                  int32_t batch, int32_t num_q_heads, float scale, void* out,
+                                  int64_t out_stride_seq, int64_t out_stride_head, void* workspace,
+                                  size_t workspace_bytes, int32_t pages_per_split, uint32_t flags,
+                                  int32_t dtype, void* stream);
+
+/*
  * mv_paged_decode for callers that cannot allocate device memory. No
  * counterpart in the reference (its kernel allocates its own output-sized
  * buffer). Some callers of a decode kernel may not call cudaMalloc: a plugin

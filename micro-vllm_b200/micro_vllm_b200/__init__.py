@@ -9,7 +9,8 @@ own function names, arguments and errors:
     cuda_paged_cache._write_paged_kv             <- micro_vllm.cuda_paged_cache
     paged_kv_cache.PagedKVCache                  <- micro_vllm.paged_kv_cache
 
-plus batched forms (``paged_decode_attention``, ``write_paged_kv``) over one
+plus batched forms (``paged_decode_attention``, ``write_paged_kv``, and the one-call
+append + attend step ``paged_decode_with_append``) over one
 shared page pool, and KV-head sharding across GPUs (``sharding``).
 """
 __version__ = '0.1.0'

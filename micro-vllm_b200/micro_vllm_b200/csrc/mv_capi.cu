@@ -592,14 +592,25 @@ int mv_paged_decode_plan(int32_t batch, int32_t num_q_heads, int32_t num_kv_head
     return MV_OK;
 }
 
-int mv_paged_decode(const void* q, int64_t q_stride_seq, int64_t q_stride_head, const void* k_cache,
+// This step's new K/V rows for mv_paged_decode_append ([batch, kv_heads], feature stride 1).
+struct NewRows {
+    const void* key;
+    int64_t key_stride_seq;
+    int64_t key_stride_head;
+    const void* value;
+    int64_t value_stride_seq;
+    int64_t value_stride_head;
+};
+
+static int paged_decode_impl(const void* q, int64_t q_stride_seq, int64_t q_stride_head, const void* k_cache,
                     const void* v_cache, int64_t num_blocks, int32_t num_kv_heads, int32_t block_size,
                     int32_t head_dim, const void* block_table, int32_t block_table_type,
                     int64_t block_table_stride, int64_t blocks_per_seq, const void* context_lens,
                     int32_t context_lens_type, int64_t max_context_len, int32_t batch,
                     int32_t num_q_heads, float scale, void* out, int64_t out_stride_seq,
                     int64_t out_stride_head, void* workspace, size_t workspace_bytes,
-                    int32_t pages_per_split, uint32_t flags, int32_t dtype, void* stream) {
+                    int32_t pages_per_split, uint32_t flags, int32_t dtype, void* stream,
+                             const NewRows* rows) {
     if (!q || !k_cache || !v_cache || !block_table || !out)
         return fail(MV_ERR_INVALID_ARGUMENT, "q, k_cache, v_cache, block_table and out must not be NULL");
     if (num_blocks <= 0 || blocks_per_seq <= 0)
@@ -671,6 +682,34 @@ int mv_paged_decode(const void* q, int64_t q_stride_seq, int64_t q_stride_head, 
             p.prefix_out = reinterpret_cast<int64_t*>(base + plan.part_o_bytes + plan.part_lse_bytes);
     }
 
+    p.new_key = nullptr;
+    p.new_value = nullptr;
+    p.new_key_stride[0] = p.new_key_stride[1] = 0;
+    p.new_value_stride[0] = p.new_value_stride[1] = 0;
+    if (rows) {
+        // The split-grid tensor-core kernel writes the rows itself (16-byte
+        // chunks); every other plan runs the append kernel first, as two launches.
+        const uintptr_t bits = reinterpret_cast<uintptr_t>(rows->key) | reinterpret_cast<uintptr_t>(rows->value) |
+                               static_cast<uintptr_t>((rows->key_stride_seq | rows->key_stride_head |
+                                                       rows->value_stride_seq | rows->value_stride_head) * 2);
+        if (plan.path == MV_PATH_TMA_MMA && bits % 16 == 0) {
+            p.new_key = rows->key;
+            p.new_value = rows->value;
+            p.new_key_stride[0] = rows->key_stride_seq;
+            p.new_key_stride[1] = rows->key_stride_head;
+            p.new_value_stride[0] = rows->value_stride_seq;
+            p.new_value_stride[1] = rows->value_stride_head;
+        } else {
+            rc = mv_write_paged_kv(rows->key, rows->key_stride_seq, rows->key_stride_head, 0, rows->value,
+                                   rows->value_stride_seq, rows->value_stride_head, 0, const_cast<void*>(k_cache),
+                                   const_cast<void*>(v_cache), num_blocks, num_kv_heads, block_size, head_dim,
+                                   block_table, block_table_type, block_table_stride, blocks_per_seq,
+                                   context_lens, context_lens_type, MV_POSITIONS_END,
+                                   context_lens ? 0 : max_context_len - 1, batch, 1, dtype, stream);
+            if (rc != MV_OK) return rc;
+        }
+    }
+
     CUtensorMap kmap, vmap;
     if (plan.path == MV_PATH_TMA_MMA || plan.path == MV_PATH_TMA_MMA_PERSISTENT ||
         plan.path == MV_PATH_TMA_MMA_CLUSTER) {
@@ -684,6 +723,42 @@ int mv_paged_decode(const void* q, int64_t q_stride_seq, int64_t q_stride_head, 
         case MV_DTYPE_F16: return launch_decode<__half>(p, plan, &kmap, &vmap, s);
         default: return launch_decode<__nv_bfloat16>(p, plan, &kmap, &vmap, s);
     }
+}
+
+int mv_paged_decode(const void* q, int64_t q_stride_seq, int64_t q_stride_head, const void* k_cache,
+                    const void* v_cache, int64_t num_blocks, int32_t num_kv_heads, int32_t block_size,
+                    int32_t head_dim, const void* block_table, int32_t block_table_type,
+                    int64_t block_table_stride, int64_t blocks_per_seq, const void* context_lens,
+                    int32_t context_lens_type, int64_t max_context_len, int32_t batch,
+                    int32_t num_q_heads, float scale, void* out, int64_t out_stride_seq,
+                    int64_t out_stride_head, void* workspace, size_t workspace_bytes,
+                    int32_t pages_per_split, uint32_t flags, int32_t dtype, void* stream) {
+    return paged_decode_impl(q, q_stride_seq, q_stride_head, k_cache, v_cache, num_blocks, num_kv_heads,
+                             block_size, head_dim, block_table, block_table_type, block_table_stride,
+                             blocks_per_seq, context_lens, context_lens_type, max_context_len, batch,
+                             num_q_heads, scale, out, out_stride_seq, out_stride_head, workspace,
+                             workspace_bytes, pages_per_split, flags, dtype, stream, nullptr);
+}
+
+int mv_paged_decode_append(const void* q, int64_t q_stride_seq, int64_t q_stride_head, const void* key,
+                           int64_t key_stride_seq, int64_t key_stride_head, const void* value,
+                           int64_t value_stride_seq, int64_t value_stride_head, void* k_cache, void* v_cache,
+                           int64_t num_blocks, int32_t num_kv_heads, int32_t block_size, int32_t head_dim,
+                           const void* block_table, int32_t block_table_type, int64_t block_table_stride,
+                           int64_t blocks_per_seq, const void* context_lens, int32_t context_lens_type,
+                           int64_t max_context_len, int32_t batch, int32_t num_q_heads, float scale, void* out,
+                           int64_t out_stride_seq, int64_t out_stride_head, void* workspace,
+                           size_t workspace_bytes, int32_t pages_per_split, uint32_t flags, int32_t dtype,
+                           void* stream) {
+    if (!key || !value) return fail(MV_ERR_INVALID_ARGUMENT, "key and value must not be NULL");
+    if (key_stride_seq < 0 || key_stride_head < 0 || value_stride_seq < 0 || value_stride_head < 0)
+        return fail(MV_ERR_INVALID_ARGUMENT, "strides must be nonnegative");
+    const NewRows rows{key, key_stride_seq, key_stride_head, value, value_stride_seq, value_stride_head};
+    return paged_decode_impl(q, q_stride_seq, q_stride_head, k_cache, v_cache, num_blocks, num_kv_heads,
+                             block_size, head_dim, block_table, block_table_type, block_table_stride,
+                             blocks_per_seq, context_lens, context_lens_type, max_context_len, batch,
+                             num_q_heads, scale, out, out_stride_seq, out_stride_head, workspace,
+                             workspace_bytes, pages_per_split, flags, dtype, stream, &rows);
 }
 
 int mv_write_paged_kv(const void* key, int64_t key_stride_seq, int64_t key_stride_head,

@@ -52,6 +52,13 @@ struct DecodeParams {
     int64_t persistent_warps;  // persistent schedule: warps in the grid
     unsigned int* counters; // split grid: per-(sequence, KV head) arrival counters, zero between calls
     int fused_merge;        // split grid: the last split CTA of a segment merges it
+    // Split grid, fused append: this step's K/V row of every (sequence, KV
+    // head), [batch, kv_heads] with feature stride 1, is written into the pool
+    // at position len - 1 by the CTA that attends that page. nullptr: no append.
+    const void* new_key;
+    const void* new_value;
+    int64_t new_key_stride[2];    // seq, head (elements)
+    int64_t new_value_stride[2];
 };
 
 struct AppendParams {
@@ -133,6 +140,35 @@ __device__ void write_group_constant(const DecodeParams& p, int b, int h, float 
         const int d = idx - g * p.head_dim;
         out[b * p.out_stride_seq + (int64_t)(h * p.group + g) * p.out_stride_head + d] =
             from_float<T>(value);
+    }
+}
+
+// Fused append for a sequence the decode does not attend (empty, or longer
+// than max_context_len): the CTA's threads copy the new K/V row of head h to
+// position len - 1 when the separate append kernel would have written it
+// (position inside the table, page ID inside the pool). 16-byte chunks.
+__device__ inline void append_row_direct(const DecodeParams& p, int b, int h, int64_t len) {
+    const int64_t pos = len - 1;
+    if (pos < 0) return;
+    const int64_t logical = pos / p.block_size;
+    if (logical >= p.blocks_per_seq) return;
+    const int64_t id = load_index(p.block_table, p.table_i64, b * p.table_stride + logical);
+    if (id < 0 || id >= p.num_blocks) return;
+    const int chunks = p.head_dim / 8;  // 16-byte chunks of a 2-byte row
+    const int64_t slot = pos - logical * p.block_size;
+    for (int c = threadIdx.x; c < 2 * chunks; c += blockDim.x) {
+        const int which = c >= chunks;
+        const int cc = c - which * chunks;
+        const int64_t* st = which ? p.new_value_stride : p.new_key_stride;
+        const uint4* src = reinterpret_cast<const uint4*>(
+                               static_cast<const uint16_t*>(which ? p.new_value : p.new_key) + b * st[0] + h * st[1]) +
+                           cc;
+        // The pools are written through the decode's const pointers: the caller passed them writable.
+        uint4* dst = reinterpret_cast<uint4*>(const_cast<uint16_t*>(
+                         static_cast<const uint16_t*>(which ? p.v_cache : p.k_cache)) +
+                         ((id * p.kv_heads + h) * p.block_size + slot) * p.head_dim) +
+                     cc;
+        *dst = *src;
     }
 }
 

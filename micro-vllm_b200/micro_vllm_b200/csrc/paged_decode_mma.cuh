@@ -317,6 +317,7 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
     const SeqSplit seq = seq_split(p, b);
     if (split >= seq.splits) return;
     if (seq.state != 0) {
+        if (p.new_key) append_row_direct(p, b, h, seq.len);
         write_group_constant<T>(p, b, h, seq.state == 1 ? 0.0f : __int_as_float(0x7fffffff));
         return;
     }
@@ -380,6 +381,33 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
         }
     }
 
+    // Fused append: the warp that attends the sequence's last page holds the
+    // new K/V row (16-byte chunks; lanes 0..D/8-1 K, the next D/8 V, wrapping
+    // for D = 256) and writes it into that page after the page's TMA load
+    // landed -- into the staged tile, which this warp then reads, and into the
+    // pool. Only this CTA reads the last page, so nothing else can see the old row.
+    constexpr int kRowChunks = D / 8;
+    constexpr int kNewPerLane = (2 * kRowChunks + 31) / 32;
+    int append_at = -1;  // loop index of the last page in this warp, or -1
+    uint4 new_rows[kNewPerLane];
+    if (p.new_key && split == seq.splits - 1) {
+        const int rel = static_cast<int>(seq.pages - 1 - page_begin);
+        if (rel % NWARPS == warp) {
+            append_at = rel / NWARPS;
+#pragma unroll
+            for (int j = 0; j < kNewPerLane; ++j) {
+                const int c = lane + 32 * j;
+                if (c < 2 * kRowChunks) {
+                    const int which = c >= kRowChunks;
+                    const int64_t* st = which ? p.new_value_stride : p.new_key_stride;
+                    new_rows[j] = reinterpret_cast<const uint4*>(
+                        static_cast<const uint16_t*>(which ? p.new_value : p.new_key) + b * st[0] + h * st[1])
+                        [c - which * kRowChunks];
+                }
+            }
+        }
+    }
+
     Warp w;
     w.load_q(p, b, h, lane);
     w.reset();
@@ -400,6 +428,27 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
         const int64_t left = seq.len - page * kPageTokens;
         const int valid = left < kPageTokens ? static_cast<int>(left) : kPageTokens;
         const bool page_ok = !warp_has_bad || __shfl_sync(0xffffffffu, !bad, i);
+        if (i == append_at && page_ok) {
+            const long long id = __shfl_sync(0xffffffffu, my_id, i);
+            const int slot = valid - 1;
+            uint8_t* tiles = wsm + st * Shape::kStageBytes;
+#pragma unroll
+            for (int j = 0; j < kNewPerLane; ++j) {
+                const int c = lane + 32 * j;
+                if (c < 2 * kRowChunks) {
+                    const int which = c >= kRowChunks;
+                    const int cc = c - which * kRowChunks;
+                    const int r = (cc >> 3) * 16 + slot;  // 64-column box, then token
+                    *reinterpret_cast<uint4*>(tiles + which * Shape::kTileBytes + r * 128 +
+                                              (((cc & 7) ^ (r & 7)) << 4)) = new_rows[j];
+                    uint16_t* pool = const_cast<uint16_t*>(
+                        static_cast<const uint16_t*>(which ? p.v_cache : p.k_cache));
+                    reinterpret_cast<uint4*>(pool + ((id * p.kv_heads + h) * kPageTokens + slot) * D)[cc] =
+                        new_rows[j];
+                }
+            }
+            __syncwarp();
+        }
         typename Warp::PageFrags frags;
         if (page_ok) Warp::load_page(frags, kt, vt, wsm + st * Shape::kStageBytes + Shape::kTileBytes, valid, lane);
 

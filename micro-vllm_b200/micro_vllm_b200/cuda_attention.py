@@ -104,8 +104,10 @@ def _workspace(device, stream, nbytes):
 
 
 def _run(query3, q_strides, key_cache, value_cache, block_table, table_stride, blocks_per_seq,
-         context_lens, max_context_len, scale, out, out_strides, pages_per_split=0, flags=0):
-    """Plan, allocate the split-KV workspace, and launch ``mv_paged_decode``."""
+         context_lens, max_context_len, scale, out, out_strides, pages_per_split=0, flags=0,
+         rows=None):
+    """Plan, allocate the split-KV workspace, and launch ``mv_paged_decode``
+    (``mv_paged_decode_append`` when ``rows`` holds this step's new K/V rows)."""
     lib = _native.library()
     batch, q_heads, dim = query3
     num_blocks, kv_heads, block_size, _ = key_cache.shape
@@ -118,8 +120,14 @@ def _run(query3, q_strides, key_cache, value_cache, block_table, table_stride, b
             dtype, ctypes.byref(size)))
         stream = current_stream_handle(device)
         workspace = _workspace(device, stream, size.value) if size.value else None
-        _native.check(lib.mv_paged_decode(
-            out.q_ptr, q_strides[0], q_strides[1],
+        head = (out.q_ptr, q_strides[0], q_strides[1])
+        if rows is not None:
+            new_key, new_value = rows
+            head += (new_key.data_ptr(), new_key.stride(0), new_key.stride(1),
+                     new_value.data_ptr(), new_value.stride(0), new_value.stride(1))
+        entry = lib.mv_paged_decode if rows is None else lib.mv_paged_decode_append
+        _native.check(entry(
+            *head,
             key_cache.data_ptr(), value_cache.data_ptr(), num_blocks,
             kv_heads, block_size, dim,
             block_table.data_ptr(), INDEX_CODES[block_table.dtype], table_stride, blocks_per_seq,
@@ -269,6 +277,16 @@ def paged_decode_attention(query: torch.Tensor, key_cache: torch.Tensor, value_c
     shapes the tensor-core kernels do not take.
     Returns out, or a fresh [B, Hq, D] tensor of the query's dtype.
     """
+    q, max_context_len, scale, out = _checked_batched(query, key_cache, value_cache, block_table,
+                                                      context_lens, scale, max_context_len, out)
+    _launch_batched(q, key_cache, value_cache, block_table, context_lens, max_context_len, scale, out,
+                    pages_per_split, _flags(force_simt, persistent, fused_merge, cluster))
+    return out
+
+
+def _checked_batched(query, key_cache, value_cache, block_table, context_lens, scale, max_context_len,
+                     out):
+    """Validate the batched decode arguments; returns (q [B,Hq,D], bound, scale, out)."""
     squeeze = query.dim() == 4
     q = query[:, :, 0, :] if squeeze else query
     _check(isinstance(q, torch.Tensor) and q.dim() == 3, 'query must be [B, Hq, D] or [B, Hq, 1, D]')
@@ -312,9 +330,56 @@ def paged_decode_attention(query: torch.Tensor, key_cache: torch.Tensor, value_c
         _check(out.shape == (batch, q_heads, dim) and out.dtype == q.dtype and out.device == q.device,
                'out must be a [B, Hq, D] tensor of the query dtype and device')
         _check(out.stride(2) == 1, 'out requires feature stride 1')
+    return q, max_context_len, scale, out
+
+
+def _launch_batched(q, key_cache, value_cache, block_table, context_lens, max_context_len, scale, out,
+                    pages_per_split, flags, rows=None):
+    batch, q_heads, dim = q.shape
     _run((batch, q_heads, dim), (q.stride(0), q.stride(1)), key_cache, value_cache, block_table,
          block_table.stride(0), block_table.shape[1], context_lens, int(max_context_len), scale,
          _Pointers(q.data_ptr(), out.data_ptr()), (out.stride(0), out.stride(1)),
-         pages_per_split=int(pages_per_split),
-         flags=_flags(force_simt, persistent, fused_merge, cluster))
+         pages_per_split=int(pages_per_split), flags=flags, rows=rows)
+
+
+def paged_decode_with_append(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
+                             key_cache: torch.Tensor, value_cache: torch.Tensor,
+                             block_table: torch.Tensor, context_lens: torch.Tensor,
+                             scale: float | None = None, *, max_context_len: int | None = None,
+                             out: torch.Tensor | None = None, pages_per_split: int = 0,
+                             force_simt: bool = False, persistent: bool = False,
+                             fused_merge: bool = False, cluster: bool = False) -> torch.Tensor:
+    """One decode step of a layer: append this step's K/V row of every sequence, then attend.
+
+    The result, in the pools and in the output, is that of
+    ``write_paged_kv(key, value, key_cache, value_cache, block_table,
+    positions=context_lens, positions_are_end=True)`` followed by
+    ``paged_decode_attention(query, key_cache, value_cache, block_table,
+    context_lens, scale)`` -- the append-before-attend order of the
+    reference's decode layer (src/micro_vllm/model.py:215-216) -- but where
+    the split-grid tensor-core kernel runs, the CTA attending each sequence's
+    last page writes the new row itself, so the step is one kernel (plus the
+    split merge) instead of two. Other plans run the append kernel first.
+
+    key/value: [B, Hkv, D] or [B, Hkv, 1, D] CUDA tensors of the pool dtype,
+    feature stride 1. context_lens count the new token. The page receiving a
+    sequence's new row must not be shared with another sequence of the batch.
+    Other arguments as ``paged_decode_attention``. Returns out.
+    """
+    from . import cuda_paged_cache as cache_ops
+
+    q, max_context_len, scale, out = _checked_batched(query, key_cache, value_cache, block_table,
+                                                      context_lens, scale, max_context_len, out)
+    key4 = key.unsqueeze(2) if key.dim() == 3 else key
+    value4 = value.unsqueeze(2) if value.dim() == 3 else value
+    for tensor in (key4, value4):
+        cache_ops._validate_data(tensor, key_cache)
+    cache_ops._validate_sources(key4, value4, batched=True)
+    _check(key4.shape[0] == q.shape[0] and key4.shape[2] == 1,
+           'new K/V must have shape [B, Hkv, D] or [B, Hkv, 1, D]')
+    cache_ops._validate_pages(key4, key_cache, value_cache)
+    cache_ops._validate_aliases(key4, value4, key_cache, value_cache, block_table)
+    _launch_batched(q, key_cache, value_cache, block_table, context_lens, max_context_len, scale, out,
+                    pages_per_split, _flags(force_simt, persistent, fused_merge, cluster),
+                    rows=(key4[:, :, 0, :], value4[:, :, 0, :]))
     return out

@@ -123,6 +123,19 @@ def test_native_decode_checks_name_cuda_first():
         lib.assert_not_called()
 
 
+def test_batched_step_checks_run_before_loading():
+    """The one-call append + attend step validates on the host before any native call."""
+    q = torch.zeros(2, 4, 8)
+    rows = torch.zeros(2, 2, 8)
+    pages = torch.zeros(4, 2, 16, 8)
+    table = torch.zeros(2, 2, dtype=torch.int32)
+    lens = torch.ones(2, dtype=torch.int32)
+    with patch.object(cuda_attention._native, 'library') as lib:
+        with pytest.raises(RuntimeError, match='CUDA'):
+            cuda_attention.paged_decode_with_append(q, rows, rows, pages, pages.clone(), table, lens)
+        lib.assert_not_called()
+
+
 def test_storage_overlap_detects_views_and_dlpack_aliases():
     from micro_vllm_b200._tensors import storage_overlaps
     base = torch.zeros(64)
