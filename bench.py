@@ -50,10 +50,13 @@ for _path in (ROOT, ROOT / 'micro-vllm_b200'):
 METRIC = 'paged decode attn achieved HBM GB/s (% of B200 peak); decode tokens/s'
 DEFAULT_WORKLOAD = 'qwen7b_bf16'
 FALLBACK_HBM_GBS = 6650.0
-# dram__bytes_read.sum + dram__bytes_write.sum of one paged_decode_mma_kernel launch on this
-# workload, from one ncu capture (profiles/paged_decode_mma_qwen7b_bf16.md).
-NCU_TRAFFIC_BYTES = {'qwen7b_bf16': 329_501_440 + 5_254_912}
+# dram__bytes_read.sum + dram__bytes_write.sum of one step's kernels on this workload, from
+# one ncu capture: paged_decode_mma_kernel with the append fused (329.66 MB + 5.68 MB,
+# profiles/paged_decode_mma_qwen7b_bf16.md) + paged_decode_merge_kernel (2.80 MB read with
+# ncu's cold caches, profiles/paged_decode_merge_qwen7b_bf16.md).
+NCU_TRAFFIC_BYTES = {'qwen7b_bf16': 329_660_160 + 5_680_640 + 2_802_176}
 L2_BYTES = 126 * 1024 * 1024
+KERNEL_CALLS = 8
 
 
 def parse_args(argv=None):
@@ -360,12 +363,6 @@ def run_ours(args):
 
     step, other_step = (fused_step, separate_step) if args.step == 'fused' else (separate_step, fused_step)
 
-    def attention_only():
-        cuda_attention.paged_decode_attention(data['q'], data['k_pool'], data['v_pool'],
-                                              data['block_table'], data['context_lens'],
-                                              max_context_len=max_len, out=out,
-                                              pages_per_split=pps)
-
     path, chosen_pps, splits = cuda_attention.paged_decode_plan(
         q_heads, data['k_pool'], max_len, batch=len(lens_host), pages_per_split=pps)
     # The fused step is one decode launch (+ merge); the separate one adds the append kernel.
@@ -377,7 +374,6 @@ def run_ours(args):
         for _ in range(3):
             step()
             other_step()
-            attention_only()
     torch.cuda.synchronize(device)
     step_graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(step_graph, stream=stream):
@@ -385,9 +381,12 @@ def run_ours(args):
     other_graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(other_graph, stream=stream):
         other_step()
-    attn_graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(attn_graph, stream=stream):
-        attention_only()
+    # The step's kernels back to back, KERNEL_CALLS per graph, so their average
+    # launch duration excludes the per-replay graph launch gap (roofline).
+    kernel_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(kernel_graph, stream=stream):
+        for _ in range(KERNEL_CALLS):
+            step()
     torch.cuda.synchronize(device)
 
     def barrier():
@@ -413,21 +412,21 @@ def run_ours(args):
         barrier()
         elapsed_ms = start.elapsed_time(end)
 
-        # Attention alone, per launch (decode kernel + split merge), for the roofline.
+        # The step's kernels alone (decode + split merge, and the append kernel in the
+        # separate form), average launch duration over back-to-back calls, for the roofline.
         with torch.cuda.stream(stream):
-            for _ in range(args.warmup):
-                attn_graph.replay()
+            for _ in range(max(1, args.warmup // KERNEL_CALLS)):
+                kernel_graph.replay()
         torch.cuda.synchronize(device)
-        reps = min(args.steps, 500)
-        events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                  for _ in range(reps)]
+        reps = max(1, min(args.steps, 2000) // KERNEL_CALLS)
+        k_start, k_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(stream):
-            for s, e in events:
-                s.record(stream)
-                attn_graph.replay()
-                e.record(stream)
+            k_start.record(stream)
+            for _ in range(reps):
+                kernel_graph.replay()
+            k_end.record(stream)
         torch.cuda.synchronize(device)
-        attn_ms = statistics.mean(s.elapsed_time(e) for s, e in events)
+        attn_ms = k_start.elapsed_time(k_end) / (reps * KERNEL_CALLS)
 
         # The other form of the step, same loop, reported beside the headline.
         with torch.cuda.stream(stream):
@@ -465,8 +464,10 @@ def run_ours(args):
     result = None
     if rank == 0:
         peak, peak_kind = peak_hbm()
-        achieved = attn_bytes / (attn_ms / 1e3) / 1e9
-        traffic = NCU_TRAFFIC_BYTES.get(args.workload)
+        achieved = step_total / (attn_ms / 1e3) / 1e9
+        # The capture is of the default step form on one GPU's config-sized slice.
+        traffic = (NCU_TRAFFIC_BYTES.get(args.workload)
+                   if args.step == 'fused' and not args.pages_per_split else None)
         batch = len(lens_host)
         result = {
             'metric': METRIC,
@@ -499,7 +500,11 @@ def run_ours(args):
             'pct_of_hbm_peak': round(100 * value / world / peak, 2),
             'roofline': {
                 'bound': 'hbm',
-                'kernel': 'paged decode attention (paged_decode_mma_kernel + split merge)',
+                'kernel': ('paged_decode_mma_kernel (append fused) + paged_decode_merge_kernel'
+                           if args.step == 'fused' else
+                           'write_paged_kv_kernel + paged_decode_mma_kernel + paged_decode_merge_kernel'),
+                'timing': (f'CUDA events around graphs of {KERNEL_CALLS} back-to-back steps: '
+                           'average launch duration without the per-replay graph launch gap'),
                 'achieved': round(achieved, 1),
                 'peak': peak,
                 'peak_kind': f'{peak_kind} copy bandwidth (MEASURED_PEAKS.json hbm_gbs)'
@@ -507,11 +512,13 @@ def run_ours(args):
                 'unit': 'GB/s',
                 'frac': round(achieved / peak, 4),
                 'us_per_launch': round(attn_ms * 1e3, 3),
-                'algorithmic_bytes_per_launch': attn_bytes,
+                'algorithmic_bytes_per_launch': step_total,
                 'traffic': traffic,
-                'traffic_source': ('ncu dram__bytes_read.sum + dram__bytes_write.sum, one launch of '
-                                   'paged_decode_mma_kernel (profiles/paged_decode_mma_qwen7b_bf16.md)'
-                                   if traffic else None),
+                'traffic_source': ('ncu dram__bytes_read.sum + dram__bytes_write.sum of one step: '
+                                   'paged_decode_mma_kernel (append fused) + paged_decode_merge_kernel '
+                                   '(profiles/paged_decode_mma_qwen7b_bf16.md, '
+                                   'profiles/paged_decode_merge_qwen7b_bf16.md)'
+                                   if traffic and args.step == 'fused' else None),
             },
             'e2e': {'value': round(e2e_value, 1), 'unit': 'GB/s',
                     'h2d_bytes_per_step': e2e['h2d'], 'd2h_bytes_per_step': e2e['d2h'],
@@ -524,7 +531,7 @@ def run_ours(args):
         }
         if world == 1 and not args.no_cpu_baseline:
             result['cpu_baseline'] = cpu_baseline(spec, data, q_heads, kv_heads, args.cpu_seconds)
-    del step_graph, attn_graph, other_graph
+    del step_graph, kernel_graph, other_graph
     if world > 1:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
