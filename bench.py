@@ -467,7 +467,8 @@ def run_ours(args):
         achieved = step_total / (attn_ms / 1e3) / 1e9
         # The capture is of the default step form on one GPU's config-sized slice.
         traffic = (NCU_TRAFFIC_BYTES.get(args.workload)
-                   if args.step == 'fused' and not args.pages_per_split else None)
+                   if args.step == 'fused' and not args.pages_per_split
+                   and (world == 1 or args.scaling == 'weak') else None)
         batch = len(lens_host)
         result = {
             'metric': METRIC,
@@ -522,7 +523,10 @@ def run_ours(args):
             },
             'e2e': {'value': round(e2e_value, 1), 'unit': 'GB/s',
                     'h2d_bytes_per_step': e2e['h2d'], 'd2h_bytes_per_step': e2e['d2h'],
-                    'us_per_step': round(e2e_ms / args.steps * 1e3, 3)},
+                    'us_per_step': round(e2e_ms / args.steps * 1e3, 3),
+                    'how': ('public API (PagedDecodeStep) per step: packed q/k/v + lengths uploaded from '
+                            'pinned host memory and the output downloaded to pinned host memory, on '
+                            'their own streams, two buffer slots, overlapping neighbouring steps')},
             'step_forms_us': {args.step: round(ms_per_step * 1e3, 3),
                               ('separate' if args.step == 'fused' else 'fused'):
                                   round(other_ms / args.steps * 1e3, 3)},
@@ -539,48 +543,82 @@ def run_ours(args):
 
 
 def run_e2e(args, data, max_len, pps, stream, device, barrier):
-    """Same step through the public API with host inputs and a host result."""
+    """Same step through the public API with host inputs and a host result.
+
+    Every step uploads its inputs from pinned host memory in one copy -- q and
+    the new K/V rows packed as one [B, Hq + 2 Hkv, D] block (the layout of a
+    fused QKV projection) followed by the lengths -- runs the step through a bound
+    ``PagedDecodeStep`` (or the two-call form), and downloads its output into
+    pinned host memory. Uploads and downloads run on their own streams with two
+    buffer slots, so step i+1's upload and step i-1's download overlap step i's
+    kernels, as a serving loop runs them.
+    """
     import torch
 
     from micro_vllm_b200 import cuda_attention, cuda_paged_cache
 
-    host = {name: data[name].cpu().pin_memory() for name in ('q', 'k_new', 'v_new', 'context_lens')}
-    dev = {name: torch.empty_like(data[name]) for name in host}
-    out_dev = torch.empty_like(data['q'])
-    out_host = torch.empty(out_dev.shape, dtype=out_dev.dtype).pin_memory()
-    h2d = sum(t.numel() * t.element_size() for t in host.values())
-    d2h = out_host.numel() * out_host.element_size()
+    batch, hq, dim = data['q'].shape
+    hkv = data['k_new'].shape[1]
+    slots = 2
+    # One upload per step: the packed q/k/v rows, then the int32 lengths, as raw bytes.
+    packed = torch.cat([data['q'], data['k_new'][:, :, 0], data['v_new'][:, :, 0]], dim=1)
+    qkv_bytes = packed.numel() * packed.element_size()
+    lens_bytes = data['context_lens'].numel() * data['context_lens'].element_size()
+    staging = torch.cat([packed.reshape(-1).view(torch.uint8), data['context_lens'].view(torch.uint8)])
+    host_in = [staging.cpu().pin_memory() for _ in range(slots)]
+    dev_in = [torch.empty_like(staging) for _ in range(slots)]
+    dev_qkv = [buf[:qkv_bytes].view(packed.dtype).view(packed.shape) for buf in dev_in]
+    dev_lens = [buf[qkv_bytes:].view(data['context_lens'].dtype) for buf in dev_in]
+    dev_out = [torch.empty_like(data['q']) for _ in range(slots)]
+    host_out = [torch.empty(data['q'].shape, dtype=data['q'].dtype).pin_memory() for _ in range(slots)]
+    h2d = qkv_bytes + lens_bytes
+    d2h = host_out[0].numel() * host_out[0].element_size()
+    views = [(qkv[:, :hq], qkv[:, hq:hq + hkv], qkv[:, hq + hkv:]) for qkv in dev_qkv]
+    bound = cuda_attention.PagedDecodeStep(data['k_pool'], data['v_pool'], data['block_table'],
+                                           num_q_heads=hq, max_context_len=max_len, pages_per_split=pps)
+    up, down = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    loaded = [torch.cuda.Event() for _ in range(slots)]
+    computed = [torch.cuda.Event() for _ in range(slots)]
+    read = [torch.cuda.Event() for _ in range(slots)]
+    for event in computed + read:
+        event.record(stream)
 
-    def step():
-        for name in host:
-            dev[name].copy_(host[name], non_blocking=True)
-        if args.step == 'fused':
-            cuda_attention.paged_decode_with_append(dev['q'], dev['k_new'], dev['v_new'], data['k_pool'],
-                                                    data['v_pool'], data['block_table'], dev['context_lens'],
-                                                    max_context_len=max_len, out=out_dev,
-                                                    pages_per_split=pps)
-        else:
-            cuda_paged_cache.write_paged_kv(dev['k_new'], dev['v_new'], data['k_pool'], data['v_pool'],
-                                            data['block_table'], positions=dev['context_lens'],
-                                            positions_are_end=True)
-            cuda_attention.paged_decode_attention(dev['q'], data['k_pool'], data['v_pool'],
-                                                  data['block_table'], dev['context_lens'],
-                                                  max_context_len=max_len, out=out_dev,
-                                                  pages_per_split=pps)
-        out_host.copy_(out_dev, non_blocking=True)
+    def step(i):
+        s = i % slots
+        up.wait_event(computed[s])          # step i-2 has consumed this slot's inputs
+        with torch.cuda.stream(up):
+            dev_in[s].copy_(host_in[s], non_blocking=True)
+        loaded[s].record(up)
+        stream.wait_event(loaded[s])
+        stream.wait_event(read[s])          # step i-2's output has been downloaded
+        q, key, value = views[s]
+        with torch.cuda.stream(stream):
+            if args.step == 'fused':
+                bound(q, dev_lens[s], dev_out[s], key=key, value=value)
+            else:
+                cuda_paged_cache.write_paged_kv(key.unsqueeze(2), value.unsqueeze(2), data['k_pool'],
+                                                data['v_pool'], data['block_table'], positions=dev_lens[s],
+                                                positions_are_end=True)
+                bound(q, dev_lens[s], dev_out[s])
+        computed[s].record(stream)
+        down.wait_event(computed[s])
+        with torch.cuda.stream(down):
+            host_out[s].copy_(dev_out[s], non_blocking=True)
+        read[s].record(down)
 
     steps = min(args.steps, 1000)
-    with torch.cuda.stream(stream):
-        for _ in range(max(args.warmup, 3)):
-            step()
+    for i in range(max(args.warmup, 3)):
+        step(i)
     torch.cuda.synchronize(device)
     barrier()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with torch.cuda.stream(stream):
-        start.record(stream)
-        for _ in range(steps):
-            step()
-        end.record(stream)
+    start.record(stream)
+    up.wait_event(start)
+    for i in range(steps):
+        step(i)
+    stream.wait_stream(up)
+    stream.wait_stream(down)
+    end.record(stream)
     torch.cuda.synchronize(device)
     barrier()
     # Scale to the main loop's step count so value and e2e share one unit basis.

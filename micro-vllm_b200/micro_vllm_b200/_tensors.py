@@ -34,3 +34,14 @@ def storage_overlaps(left: torch.Tensor, right: torch.Tensor) -> bool:
 
 def current_stream_handle(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
+
+
+# The raw handle of the current stream of a device index, without building a
+# torch.cuda.Stream object (torch's own fast accessor where this build has it).
+_raw_stream = getattr(torch._C, '_cuda_getCurrentRawStream', None)
+
+
+def current_stream_raw(device_index: int) -> int:
+    if _raw_stream is not None:
+        return _raw_stream(device_index)
+    return torch.cuda.current_stream(device_index).cuda_stream

@@ -27,7 +27,7 @@ from functools import lru_cache
 import torch
 
 from . import _native
-from ._tensors import DTYPE_CODES, INDEX_CODES, current_stream_handle
+from ._tensors import DTYPE_CODES, INDEX_CODES, current_stream_handle, current_stream_raw
 
 _INT64_MAX = 2 ** 63 - 1
 
@@ -383,3 +383,122 @@ def paged_decode_with_append(query: torch.Tensor, key: torch.Tensor, value: torc
                     pages_per_split, _flags(force_simt, persistent, fused_merge, cluster),
                     rows=(key4[:, :, 0, :], value4[:, :, 0, :]))
     return out
+
+
+class PagedDecodeStep:
+    """A decode step bound to one page pool, validated once and called per step.
+
+    The serving loop calls the same layer geometry every step: the pools, the
+    block table tensor, the head counts, the context bound, the scale and the
+    kernel choice do not change, only the query, this step's new K/V rows, the
+    lengths (device data) and the output. Binding them once moves every check
+    that ``paged_decode_attention`` / ``paged_decode_with_append`` repeat per
+    call to construction, so a call costs a few attribute comparisons and one
+    C-ABI call (``mv_paged_decode`` or ``mv_paged_decode_append``). Results are
+    identical to those functions on the same arguments.
+
+    ``step(query, context_lens, out=None, key=None, value=None)``: query
+    [B, Hq, D] or [B, Hq, 1, D]; context_lens [B] int32/int64 on the pool's
+    device; key/value (both or neither) [B, Hkv, D] or [B, Hkv, 1, D], appended
+    at position context_lens - 1 before attending. The block table's contents
+    may change between calls; its tensor (pointer, shape) may not. Calls on one
+    stream share one split-KV workspace and must be ordered on it.
+    """
+
+    def __init__(self, key_cache: torch.Tensor, value_cache: torch.Tensor, block_table: torch.Tensor, *,
+                 num_q_heads: int, max_context_len: int | None = None, scale: float | None = None,
+                 pages_per_split: int = 0, force_simt: bool = False, persistent: bool = False,
+                 fused_merge: bool = False, cluster: bool = False):
+        batch = block_table.shape[0] if block_table.dim() == 2 else 0
+        dim = key_cache.shape[-1] if key_cache.dim() == 4 else 0
+        probe = torch.empty((max(batch, 1), num_q_heads, max(dim, 1)), dtype=key_cache.dtype,
+                            device=key_cache.device)
+        lens = torch.empty((max(batch, 1),), dtype=torch.int32, device=key_cache.device)
+        _, bound, scale, _ = _checked_batched(probe, key_cache, value_cache, block_table, lens, scale,
+                                              max_context_len, probe)
+        self._lib = _native.library()
+        self._device = key_cache.device
+        self._device_index = key_cache.device.index
+        self._dtype = key_cache.dtype
+        num_blocks, kv_heads, block_size, _ = key_cache.shape
+        self._q_shape = (batch, num_q_heads, dim)
+        self._row_shape = (batch, kv_heads, dim)
+        self._flags = _flags(force_simt, persistent, fused_merge, cluster)
+        self._pps = int(pages_per_split)
+        self._bound = int(bound)
+        self._pools = (key_cache, value_cache)
+        self._table = block_table
+        nbytes = key_cache.numel() * key_cache.element_size()
+        self._pool_ranges = ((key_cache.data_ptr(), key_cache.data_ptr() + nbytes),
+                             (value_cache.data_ptr(), value_cache.data_ptr() + nbytes))
+        dtype = DTYPE_CODES[key_cache.dtype]
+        size = ctypes.c_size_t(0)
+        with torch.cuda.device(self._device):
+            _native.check(self._lib.mv_paged_decode_workspace_size(
+                batch, num_q_heads, kv_heads, dim, block_size, self._bound, self._pps, self._flags, dtype,
+                ctypes.byref(size)))
+        self._workspace_bytes = size.value
+        # Arguments after the query/new-row pointers, with the per-call ones left as None.
+        self._pool_args = (key_cache.data_ptr(), value_cache.data_ptr(), num_blocks, kv_heads, block_size, dim,
+                           block_table.data_ptr(), INDEX_CODES[block_table.dtype], block_table.stride(0),
+                           block_table.shape[1])
+        self._scale = float(scale)
+        self._dtype_code = dtype
+
+    @property
+    def plan(self):
+        """(path, pages_per_split, max_splits) of the bound geometry."""
+        return paged_decode_plan(self._q_shape[1], self._pools[0], self._bound, batch=self._q_shape[0],
+                                 pages_per_split=self._pps,
+                                 force_simt=bool(self._flags & _native.FLAG_FORCE_SIMT),
+                                 persistent=bool(self._flags & _native.FLAG_PERSISTENT),
+                                 cluster=bool(self._flags & _native.FLAG_CLUSTER))
+
+    def _check_rows(self, rows):
+        if rows.dim() == 4:
+            _check(rows.shape[2] == 1, 'new K/V must have shape [B, Hkv, D] or [B, Hkv, 1, D]')
+            rows = rows[:, :, 0]
+        _check(tuple(rows.shape) == self._row_shape and rows.dtype == self._dtype
+               and rows.device == self._device, 'new K/V must be [B, Hkv, D] rows of the pool dtype and device')
+        _check(rows.stride(2) == 1 and rows.stride(0) >= 0 and rows.stride(1) >= 0 and not rows.requires_grad,
+               'K/V require feature stride 1 and nonnegative outer strides')
+        start = rows.data_ptr()
+        for lo, hi in self._pool_ranges:
+            _check(not (lo <= start < hi), 'sources and page table must not alias destination storage')
+        return rows
+
+    def __call__(self, query: torch.Tensor, context_lens: torch.Tensor, out: torch.Tensor | None = None,
+                 key: torch.Tensor | None = None, value: torch.Tensor | None = None) -> torch.Tensor:
+        q = query[:, :, 0] if query.dim() == 4 and query.shape[2] == 1 else query
+        _check(tuple(q.shape) == self._q_shape and q.dtype == self._dtype and q.device == self._device,
+               'query must be [B, Hq, D] (or [B, Hq, 1, D]) of the bound shape, dtype and device')
+        _check(q.stride(2) == 1 and q.stride(0) >= 0 and q.stride(1) >= 0 and not q.requires_grad,
+               'query requires feature stride 1 and nonnegative outer strides')
+        lens_code = INDEX_CODES.get(context_lens.dtype)
+        _check(lens_code is not None and tuple(context_lens.shape) == self._q_shape[:1]
+               and context_lens.device == self._device and context_lens.is_contiguous(),
+               'context lengths must be a contiguous [B] int32/int64 tensor on the pool device')
+        if out is None:
+            out = torch.empty(self._q_shape, dtype=self._dtype, device=self._device)
+        else:
+            _check(tuple(out.shape) == self._q_shape and out.dtype == self._dtype and out.device == self._device
+                   and out.stride(2) == 1, 'out must be a [B, Hq, D] tensor of the query dtype and device')
+        _check((key is None) == (value is None), 'pass both new K and V rows, or neither')
+        if torch.cuda.current_device() != self._device_index:
+            with torch.cuda.device(self._device):
+                return self(query, context_lens, out, key, value)
+        stream = current_stream_raw(self._device_index)
+        workspace = _workspace(self._device, stream, self._workspace_bytes) if self._workspace_bytes else None
+        tail = (context_lens.data_ptr(), lens_code, self._bound, self._q_shape[0], self._q_shape[1], self._scale,
+                out.data_ptr(), out.stride(0), out.stride(1),
+                workspace.data_ptr() if workspace is not None else None, self._workspace_bytes,
+                self._pps, self._flags, self._dtype_code, stream)
+        if key is None:
+            _native.check(self._lib.mv_paged_decode(q.data_ptr(), q.stride(0), q.stride(1), *self._pool_args,
+                                                    *tail))
+        else:
+            key, value = self._check_rows(key), self._check_rows(value)
+            _native.check(self._lib.mv_paged_decode_append(
+                q.data_ptr(), q.stride(0), q.stride(1), key.data_ptr(), key.stride(0), key.stride(1),
+                value.data_ptr(), value.stride(0), value.stride(1), *self._pool_args, *tail))
+        return out

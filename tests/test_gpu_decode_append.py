@@ -210,3 +210,46 @@ def test_one_call_step_in_a_cuda_graph_replays_steps():
     torch.cuda.synchronize()
     assert _same_bits(key_pool, ref['key_pool']) and _same_bits(value_pool, ref['value_pool'])
     assert _same_bits(out, expected)
+
+
+@pytest.mark.parametrize('mode', ['auto', 'split4', 'persistent', 'simt'])
+def test_bound_step_matches_the_one_off_calls(mode):
+    attention, _ = _ops()
+    inputs = make_inputs('qwen72b_bf16_small')
+    t = workload_tensors(inputs)
+    pools = (t['key_pool'].clone(), t['value_pool'].clone())
+    step = attention.PagedDecodeStep(*pools, t['block_table'], num_q_heads=t['q'].shape[1], **MODES[mode])
+    out = step(t['q'], t['context_lens'], key=t['key_new'], value=t['value_new'])
+    k2, v2, o2 = _one_call(t, **MODES[mode])
+    assert _same_bits(pools[0], k2) and _same_bits(pools[1], v2) and _same_bits(out, o2)
+    # Attention only, 4-D query, int64 lengths, caller-provided output.
+    q4 = t['q'].unsqueeze(2)
+    out2 = torch.empty_like(t['q'])
+    step(q4, t['context_lens'].to(torch.int64), out2)
+    expected = attention.paged_decode_attention(t['q'], *pools, t['block_table'], t['context_lens'],
+                                                **MODES[mode])
+    torch.cuda.synchronize()
+    assert _same_bits(out2, expected)
+    assert step.plan == attention.paged_decode_plan(t['q'].shape[1], pools[0], t['block_table'].shape[1] * 16,
+                                                    batch=t['q'].shape[0], **{k: v for k, v in MODES[mode].items()
+                                                                              if k != 'fused_merge'})
+
+
+def test_bound_step_rejects_changed_shapes_and_aliases():
+    attention, _ = _ops()
+    inputs = make_inputs('qwen7b_bf16_small')
+    t = workload_tensors(inputs)
+    step = attention.PagedDecodeStep(t['key_pool'], t['value_pool'], t['block_table'], num_q_heads=28)
+    with pytest.raises(RuntimeError, match='bound shape'):
+        step(t['q'][:, :14], t['context_lens'])
+    with pytest.raises(RuntimeError, match='bound shape'):
+        step(t['q'].float(), t['context_lens'])
+    with pytest.raises(RuntimeError, match='context lengths'):
+        step(t['q'], t['context_lens'][:1])
+    with pytest.raises(RuntimeError, match='both new K and V'):
+        step(t['q'], t['context_lens'], key=t['key_new'])
+    with pytest.raises(RuntimeError, match='alias'):
+        alias = t['key_pool'][:t['q'].shape[0], :, 0, :]
+        step(t['q'], t['context_lens'], key=alias, value=t['value_new'])
+    with pytest.raises(RuntimeError, match='out must be'):
+        step(t['q'], t['context_lens'], torch.empty(1, 28, 128, dtype=t['q'].dtype, device='cuda'))
