@@ -363,6 +363,16 @@ def run_ours(args):
 
     step, other_step = (fused_step, separate_step) if args.step == 'fused' else (separate_step, fused_step)
 
+    # The same step with q and the new K rotated (RoPE) inside the decode kernel.
+    from micro_vllm_b200.rope import rope_tables
+    tables = rope_tables(max_len, data['q'].shape[-1], 1e6, dtype=data['dtype'], device=device)
+
+    def rope_step():
+        cuda_attention.paged_decode_with_append(data['q'], data['k_new'][:, :, 0], data['v_new'][:, :, 0],
+                                                data['k_pool'], data['v_pool'], data['block_table'],
+                                                data['context_lens'], max_context_len=max_len, out=out,
+                                                pages_per_split=pps, rope=tables)
+
     path, chosen_pps, splits = cuda_attention.paged_decode_plan(
         q_heads, data['k_pool'], max_len, batch=len(lens_host), pages_per_split=pps)
     # The fused step is one decode launch (+ merge); the separate one adds the append kernel.
@@ -374,6 +384,7 @@ def run_ours(args):
         for _ in range(3):
             step()
             other_step()
+            rope_step()
     torch.cuda.synchronize(device)
     step_graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(step_graph, stream=stream):
@@ -381,6 +392,9 @@ def run_ours(args):
     other_graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(other_graph, stream=stream):
         other_step()
+    rope_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(rope_graph, stream=stream):
+        rope_step()
     # The step's kernels back to back, KERNEL_CALLS per graph, so their average
     # launch duration excludes the per-replay graph launch gap (roofline).
     kernel_graph = torch.cuda.CUDAGraph()
@@ -446,16 +460,33 @@ def run_ours(args):
         barrier()
         other_ms = o_start.elapsed_time(o_end) * args.steps / other_reps
 
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                rope_graph.replay()
+        torch.cuda.synchronize(device)
+        barrier()
+        torch.cuda.synchronize(device)
+        r_start, r_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            r_start.record(stream)
+            for _ in range(other_reps):
+                rope_graph.replay()
+            r_end.record(stream)
+        torch.cuda.synchronize(device)
+        barrier()
+        rope_ms = r_start.elapsed_time(r_end) * args.steps / other_reps
+
         # End to end through the public API: pinned host inputs in, output back out.
         e2e = run_e2e(args, data, max_len, pps, stream, device, barrier)
     clock_summary = clocks.summary()
 
-    times = torch.tensor([elapsed_ms, attn_ms, e2e['ms'], other_ms], dtype=torch.float64, device=device)
+    times = torch.tensor([elapsed_ms, attn_ms, e2e['ms'], other_ms, rope_ms], dtype=torch.float64,
+                         device=device)
     totals = torch.tensor([float(step_total), float(attn_bytes)], dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
         dist.all_reduce(totals, op=dist.ReduceOp.SUM)
-    elapsed_ms, attn_ms, e2e_ms, other_ms = times.tolist()
+    elapsed_ms, attn_ms, e2e_ms, other_ms, rope_ms = times.tolist()
     job_step_bytes, job_attn_bytes = totals.tolist()
     ms_per_step = elapsed_ms / args.steps
     value = job_step_bytes * args.steps / (elapsed_ms / 1e3) / 1e9
@@ -529,13 +560,14 @@ def run_ours(args):
                             'their own streams, two buffer slots, overlapping neighbouring steps')},
             'step_forms_us': {args.step: round(ms_per_step * 1e3, 3),
                               ('separate' if args.step == 'fused' else 'fused'):
-                                  round(other_ms / args.steps * 1e3, 3)},
+                                  round(other_ms / args.steps * 1e3, 3),
+                              'fused_with_rope': round(rope_ms / args.steps * 1e3, 3)},
             'clocks': clock_summary,
             'gpu_launches': launches_per_step * args.steps,
         }
         if world == 1 and not args.no_cpu_baseline:
             result['cpu_baseline'] = cpu_baseline(spec, data, q_heads, kv_heads, args.cpu_seconds)
-    del step_graph, kernel_graph, other_graph
+    del step_graph, kernel_graph, other_graph, rope_graph
     if world > 1:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()

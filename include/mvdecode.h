@@ -177,11 +177,23 @@ MV_API int mv_write_paged_kv(const void* key, int64_t key_stride_seq, int64_t ke
  * receives a sequence's new row must not be read by another sequence in the
  * same call (as with any in-place append); the other arguments and contracts
  * are those of mv_paged_decode.
+ *
+ * rope_cos/rope_sin (both or NULL): [rope_rows, head_dim] tables of the element
+ * type (row p = the reference's rope_cos_sin at position p,
+ * src/micro_vllm/model.py:79-98). When given, q and key arrive unrotated and
+ * are rotated at position context_lens[b] - 1 inside the decode kernel, as
+ * apply_rope does before the append (model.py:110-123, 214-215); the pool
+ * receives the rotated key. A position without a table row gives a NaN group
+ * and no write. Needs the fused path (fp16/bf16, MV_PATH_TMA_MMA, 16-byte
+ * aligned rows and tables): otherwise MV_ERR_UNSUPPORTED -- rotate with
+ * mv_apply_rope first and pass NULL tables.
  */
 MV_API int mv_paged_decode_append(const void* q, int64_t q_stride_seq, int64_t q_stride_head,
                                   const void* key, int64_t key_stride_seq, int64_t key_stride_head,
                                   const void* value, int64_t value_stride_seq,
-                                  int64_t value_stride_head, void* k_cache, void* v_cache,
+                                  int64_t value_stride_head, const void* rope_cos,
+                                  const void* rope_sin, int64_t rope_rows, void* k_cache,
+                                  void* v_cache,
                                   int64_t num_blocks, int32_t num_kv_heads, int32_t block_size,
                                   int32_t head_dim, const void* block_table,
                                   int32_t block_table_type, int64_t block_table_stride,
@@ -191,6 +203,26 @@ MV_API int mv_paged_decode_append(const void* q, int64_t q_stride_seq, int64_t q
                                   int64_t out_stride_seq, int64_t out_stride_head, void* workspace,
                                   size_t workspace_bytes, int32_t pages_per_split, uint32_t flags,
                                   int32_t dtype, void* stream);
+
+/*
+ * Rotate-half RoPE of rows: out[b, h, t, :] = x * cos[p] + rotate_half(x) * sin[p]
+ * at position p = start_b + t, each product and the sum rounded to the element
+ * type as the reference's apply_rope computes them (src/micro_vllm/model.py:101-123,
+ * called from model.py:214). x/out: [batch, heads, num_tokens, head_dim] with the
+ * given element strides (feature stride 1); out may be x itself (in place).
+ * cos/sin: [table_rows, head_dim] tables of the element type. positions: NULL
+ * (start_b = start) or a device array read per positions_kind, as in
+ * mv_write_paged_kv. A row whose position has no table row becomes NaN.
+ * Replaces the reference's apply_rope for the batched path (no reference
+ * native counterpart: the reference computes it with torch tensor operations).
+ */
+MV_API int mv_apply_rope(const void* x, int64_t x_stride_seq, int64_t x_stride_head,
+                         int64_t x_stride_token, void* out, int64_t out_stride_seq,
+                         int64_t out_stride_head, int64_t out_stride_token, int32_t batch,
+                         int32_t heads, int32_t num_tokens, int32_t head_dim, const void* cos,
+                         const void* sin, int64_t table_rows, const void* positions,
+                         int32_t positions_type, int32_t positions_kind, int64_t start,
+                         int32_t dtype, void* stream);
 
 /*
  * mv_paged_decode for callers that cannot allocate device memory. No

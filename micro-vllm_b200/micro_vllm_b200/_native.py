@@ -36,7 +36,7 @@ STATUS_NAMES = {
 EXPORTED_SYMBOLS = (
     'mv_abi_version', 'mv_last_error', 'mv_paged_decode_workspace_size',
     'mv_paged_decode_plan', 'mv_paged_decode', 'mv_write_paged_kv',
-    'mv_device_status', 'mv_clear_device_status', 'mv_paged_decode_append',
+    'mv_device_status', 'mv_clear_device_status', 'mv_paged_decode_append', 'mv_apply_rope',
 )
 
 _i32, _i64, _u32, _vp, _sz, _f32 = (ctypes.c_int32, ctypes.c_int64, ctypes.c_uint32,
@@ -72,6 +72,7 @@ _SIGNATURES = {
         ctypes.c_int, [_vp, _i64, _i64,            # q, strides
                        _vp, _i64, _i64,            # new key rows, strides
                        _vp, _i64, _i64,            # new value rows, strides
+                       _vp, _vp, _i64,             # RoPE cos, sin tables, rows
                        _vp, _vp, _i64,             # k_cache, v_cache, num_blocks
                        _i32, _i32, _i32,           # kv heads, block size, head dim
                        _vp, _i32, _i64, _i64,      # block table, type, stride, blocks/seq
@@ -79,6 +80,13 @@ _SIGNATURES = {
                        _i32, _i32, _f32,           # batch, q heads, scale
                        _vp, _i64, _i64,            # out, strides
                        _vp, _sz, _i32, _u32, _i32, _vp]),  # workspace, bytes, pps, flags, dtype, stream
+    'mv_apply_rope': (
+        ctypes.c_int, [_vp, _i64, _i64, _i64,      # x, strides
+                       _vp, _i64, _i64, _i64,      # out, strides
+                       _i32, _i32, _i32, _i32,     # batch, heads, tokens, head dim
+                       _vp, _vp, _i64,             # cos, sin tables, rows
+                       _vp, _i32, _i32, _i64,      # positions, type, kind, start
+                       _i32, _vp]),                # dtype, stream
     'mv_device_status': (ctypes.c_int, [_i32, ctypes.POINTER(_u32)]),
     'mv_clear_device_status': (ctypes.c_int, [_i32]),
 }

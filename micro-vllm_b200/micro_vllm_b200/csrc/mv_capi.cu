@@ -17,6 +17,7 @@
 #include "paged_decode_merge.cuh"
 #include "paged_decode_mma.cuh"
 #include "paged_decode_simt.cuh"
+#include "rope.cuh"
 
 namespace {
 
@@ -600,6 +601,9 @@ struct NewRows {
     const void* value;
     int64_t value_stride_seq;
     int64_t value_stride_head;
+    const void* rope_cos;  // nullptr: the rows and q are already rotated
+    const void* rope_sin;
+    int64_t rope_rows;
 };
 
 static int paged_decode_impl(const void* q, int64_t q_stride_seq, int64_t q_stride_head, const void* k_cache,
@@ -686,13 +690,26 @@ static int paged_decode_impl(const void* q, int64_t q_stride_seq, int64_t q_stri
     p.new_value = nullptr;
     p.new_key_stride[0] = p.new_key_stride[1] = 0;
     p.new_value_stride[0] = p.new_value_stride[1] = 0;
+    p.rope_cos = nullptr;
+    p.rope_sin = nullptr;
+    p.rope_rows = 0;
     if (rows) {
         // The split-grid tensor-core kernel writes the rows itself (16-byte
         // chunks); every other plan runs the append kernel first, as two launches.
         const uintptr_t bits = reinterpret_cast<uintptr_t>(rows->key) | reinterpret_cast<uintptr_t>(rows->value) |
                                static_cast<uintptr_t>((rows->key_stride_seq | rows->key_stride_head |
                                                        rows->value_stride_seq | rows->value_stride_head) * 2);
-        if (plan.path == MV_PATH_TMA_MMA && bits % 16 == 0) {
+        const bool fusable = plan.path == MV_PATH_TMA_MMA && bits % 16 == 0;
+        if (rows->rope_cos) {
+            if (!fusable || (reinterpret_cast<uintptr_t>(rows->rope_cos) | reinterpret_cast<uintptr_t>(rows->rope_sin)) % 16)
+                return fail(MV_ERR_UNSUPPORTED,
+                            "RoPE fusion needs the split-grid tensor-core kernel, 16-byte aligned K/V rows and "
+                            "16-byte aligned tables; rotate with mv_apply_rope and call without tables");
+            p.rope_cos = rows->rope_cos;
+            p.rope_sin = rows->rope_sin;
+            p.rope_rows = rows->rope_rows;
+        }
+        if (fusable) {
             p.new_key = rows->key;
             p.new_value = rows->value;
             p.new_key_stride[0] = rows->key_stride_seq;
@@ -742,7 +759,8 @@ int mv_paged_decode(const void* q, int64_t q_stride_seq, int64_t q_stride_head, 
 
 int mv_paged_decode_append(const void* q, int64_t q_stride_seq, int64_t q_stride_head, const void* key,
                            int64_t key_stride_seq, int64_t key_stride_head, const void* value,
-                           int64_t value_stride_seq, int64_t value_stride_head, void* k_cache, void* v_cache,
+                           int64_t value_stride_seq, int64_t value_stride_head, const void* rope_cos,
+                           const void* rope_sin, int64_t rope_rows, void* k_cache, void* v_cache,
                            int64_t num_blocks, int32_t num_kv_heads, int32_t block_size, int32_t head_dim,
                            const void* block_table, int32_t block_table_type, int64_t block_table_stride,
                            int64_t blocks_per_seq, const void* context_lens, int32_t context_lens_type,
@@ -753,7 +771,13 @@ int mv_paged_decode_append(const void* q, int64_t q_stride_seq, int64_t q_stride
     if (!key || !value) return fail(MV_ERR_INVALID_ARGUMENT, "key and value must not be NULL");
     if (key_stride_seq < 0 || key_stride_head < 0 || value_stride_seq < 0 || value_stride_head < 0)
         return fail(MV_ERR_INVALID_ARGUMENT, "strides must be nonnegative");
-    const NewRows rows{key, key_stride_seq, key_stride_head, value, value_stride_seq, value_stride_head};
+    if ((rope_cos == nullptr) != (rope_sin == nullptr))
+        return fail(MV_ERR_INVALID_ARGUMENT, "pass both RoPE tables or neither");
+    if (rope_cos && rope_rows <= 0) return fail(MV_ERR_INVALID_ARGUMENT, "rope_rows must be positive");
+    if (rope_cos && dtype == MV_DTYPE_F32)
+        return fail(MV_ERR_UNSUPPORTED, "RoPE fusion takes fp16/bf16; rotate fp32 rows with mv_apply_rope");
+    const NewRows rows{key, key_stride_seq, key_stride_head, value, value_stride_seq, value_stride_head,
+                       rope_cos, rope_sin, rope_rows};
     return paged_decode_impl(q, q_stride_seq, q_stride_head, k_cache, v_cache, num_blocks, num_kv_heads,
                              block_size, head_dim, block_table, block_table_type, block_table_stride,
                              blocks_per_seq, context_lens, context_lens_type, max_context_len, batch,
@@ -839,6 +863,62 @@ int mv_write_paged_kv(const void* key, int64_t key_stride_seq, int64_t key_strid
         default: err = launch_pdl(mv::write_paged_kv_kernel<2>, grid, block, 0, s, a, total); break;
     }
     return err == cudaSuccess ? MV_OK : cuda_fail(err, "append kernel launch");
+}
+
+int mv_apply_rope(const void* x, int64_t x_stride_seq, int64_t x_stride_head, int64_t x_stride_token, void* out,
+                  int64_t out_stride_seq, int64_t out_stride_head, int64_t out_stride_token, int32_t batch,
+                  int32_t heads, int32_t num_tokens, int32_t head_dim, const void* cos, const void* sin,
+                  int64_t table_rows, const void* positions, int32_t positions_type, int32_t positions_kind,
+                  int64_t start, int32_t dtype, void* stream) {
+    if (!x || !out || !cos || !sin) return fail(MV_ERR_INVALID_ARGUMENT, "x, out and the tables must not be NULL");
+    if (batch <= 0 || heads <= 0 || num_tokens <= 0 || head_dim <= 0 || table_rows <= 0)
+        return fail(MV_ERR_INVALID_ARGUMENT, "sizes must be positive");
+    if (head_dim % 2) return fail(MV_ERR_INVALID_ARGUMENT, "head_dim must be even");
+    if (dtype != MV_DTYPE_F32 && dtype != MV_DTYPE_F16 && dtype != MV_DTYPE_BF16)
+        return fail(MV_ERR_INVALID_ARGUMENT, "dtype must be MV_DTYPE_F32, MV_DTYPE_F16 or MV_DTYPE_BF16");
+    const int64_t strides[6] = {x_stride_seq, x_stride_head, x_stride_token,
+                                out_stride_seq, out_stride_head, out_stride_token};
+    for (int64_t s : strides)
+        if (s < 0) return fail(MV_ERR_INVALID_ARGUMENT, "strides must be nonnegative");
+    int rc = positions ? check_index_type(positions_type, "positions") : MV_OK;
+    if (rc != MV_OK) return rc;
+    if (positions && positions_kind != MV_POSITIONS_START && positions_kind != MV_POSITIONS_END)
+        return fail(MV_ERR_INVALID_ARGUMENT, "positions_kind must be MV_POSITIONS_START or MV_POSITIONS_END");
+    DeviceInfo dev;
+    rc = device_info(&dev);
+    if (rc != MV_OK) return rc;
+    mv::RopeParams r;
+    r.x = x;
+    r.x_stride[0] = x_stride_seq;
+    r.x_stride[1] = x_stride_head;
+    r.x_stride[2] = x_stride_token;
+    r.out = out;
+    r.out_stride[0] = out_stride_seq;
+    r.out_stride[1] = out_stride_head;
+    r.out_stride[2] = out_stride_token;
+    r.batch = batch;
+    r.heads = heads;
+    r.tokens = num_tokens;
+    r.head_dim = head_dim;
+    r.cos = cos;
+    r.sin = sin;
+    r.table_rows = table_rows;
+    r.positions = positions;
+    r.positions_i64 = positions_type == MV_INDEX_I64;
+    r.positions_end = positions_kind == MV_POSITIONS_END;
+    r.start = start;
+    const int64_t total = static_cast<int64_t>(batch) * heads * num_tokens * (head_dim / 2);
+    const int64_t want = (total + mv::kRopeThreads - 1) / mv::kRopeThreads;
+    const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(dev.sms) * 16)));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const dim3 grid(blocks), block(mv::kRopeThreads);
+    cudaError_t err;
+    switch (dtype) {
+        case MV_DTYPE_F32: err = launch_pdl(mv::rope_rows_kernel<float>, grid, block, 0, s, r, total); break;
+        case MV_DTYPE_F16: err = launch_pdl(mv::rope_rows_kernel<__half>, grid, block, 0, s, r, total); break;
+        default: err = launch_pdl(mv::rope_rows_kernel<__nv_bfloat16>, grid, block, 0, s, r, total); break;
+    }
+    return err == cudaSuccess ? MV_OK : cuda_fail(err, "RoPE kernel launch");
 }
 
 int mv_device_status(int32_t device, uint32_t* status) {

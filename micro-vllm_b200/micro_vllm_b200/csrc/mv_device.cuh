@@ -59,6 +59,12 @@ struct DecodeParams {
     const void* new_value;
     int64_t new_key_stride[2];    // seq, head (elements)
     int64_t new_value_stride[2];
+    // Fused RoPE (with the fused append): q and the new K rows arrive unrotated
+    // and are rotated at position len - 1 with rows of these [rope_rows, D]
+    // tables of the element type. nullptr: q and K are already rotated.
+    const void* rope_cos;
+    const void* rope_sin;
+    int64_t rope_rows;
 };
 
 struct AppendParams {
@@ -130,6 +136,34 @@ template <> __device__ __forceinline__ __nv_bfloat16 from_float<__nv_bfloat16>(f
     return __float2bfloat16_rn(v);
 }
 
+// Rotate-half RoPE of one element, rounded like the reference's tensor
+// expression x * cos + rotate_half(x) * sin in the element type
+// (src/micro_vllm/model.py:101-123): each product is rounded to T, then their
+// sum. `partner` is x[d + D/2] for the first half (rotate_half negates it)
+// and x[d - D/2] for the second. No fused multiply-add.
+template <typename T>
+__device__ __forceinline__ float rope_element(float x, float partner, float c, float s, bool first_half) {
+    const float a = to_float<T>(from_float<T>(__fmul_rn(x, c)));
+    const float b = to_float<T>(from_float<T>(__fmul_rn(first_half ? -partner : partner, s)));
+    return to_float<T>(from_float<T>(__fadd_rn(a, b)));
+}
+
+// The same for 8 packed 2-byte elements (one 16-byte chunk of a row).
+template <typename T>
+__device__ __forceinline__ uint4 rope_chunk(uint4 x, uint4 partner, uint4 c, uint4 s, bool first_half) {
+    const T* xv = reinterpret_cast<const T*>(&x);
+    const T* pv = reinterpret_cast<const T*>(&partner);
+    const T* cv = reinterpret_cast<const T*>(&c);
+    const T* sv = reinterpret_cast<const T*>(&s);
+    uint4 out;
+    T* ov = reinterpret_cast<T*>(&out);
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+        ov[e] = from_float<T>(rope_element<T>(to_float<T>(xv[e]), to_float<T>(pv[e]), to_float<T>(cv[e]),
+                                              to_float<T>(sv[e]), first_half));
+    return out;
+}
+
 // Fill out[b, h*G + g, :] for every g of KV head h with one value (0 or NaN).
 template <typename T>
 __device__ void write_group_constant(const DecodeParams& p, int b, int h, float value) {
@@ -147,9 +181,11 @@ __device__ void write_group_constant(const DecodeParams& p, int b, int h, float 
 // than max_context_len): the CTA's threads copy the new K/V row of head h to
 // position len - 1 when the separate append kernel would have written it
 // (position inside the table, page ID inside the pool). 16-byte chunks.
+template <typename T>
 __device__ inline void append_row_direct(const DecodeParams& p, int b, int h, int64_t len) {
     const int64_t pos = len - 1;
     if (pos < 0) return;
+    if (p.rope_cos && pos >= p.rope_rows) return;  // no table row: nothing to write
     const int64_t logical = pos / p.block_size;
     if (logical >= p.blocks_per_seq) return;
     const int64_t id = load_index(p.block_table, p.table_i64, b * p.table_stride + logical);
@@ -160,15 +196,20 @@ __device__ inline void append_row_direct(const DecodeParams& p, int b, int h, in
         const int which = c >= chunks;
         const int cc = c - which * chunks;
         const int64_t* st = which ? p.new_value_stride : p.new_key_stride;
-        const uint4* src = reinterpret_cast<const uint4*>(
-                               static_cast<const uint16_t*>(which ? p.new_value : p.new_key) + b * st[0] + h * st[1]) +
-                           cc;
+        const uint4* row = reinterpret_cast<const uint4*>(
+            static_cast<const uint16_t*>(which ? p.new_value : p.new_key) + b * st[0] + h * st[1]);
+        uint4 v = row[cc];
+        if (p.rope_cos && !which) {
+            const int64_t t = pos * (p.head_dim / 8) + cc;
+            v = rope_chunk<T>(v, row[cc ^ (chunks / 2)], reinterpret_cast<const uint4*>(p.rope_cos)[t],
+                              reinterpret_cast<const uint4*>(p.rope_sin)[t], cc < chunks / 2);
+        }
         // The pools are written through the decode's const pointers: the caller passed them writable.
         uint4* dst = reinterpret_cast<uint4*>(const_cast<uint16_t*>(
                          static_cast<const uint16_t*>(which ? p.v_cache : p.k_cache)) +
                          ((id * p.kv_heads + h) * p.block_size + slot) * p.head_dim) +
                      cc;
-        *dst = *src;
+        *dst = v;
     }
 }
 

@@ -96,6 +96,46 @@ struct WarpPageAttention {
         }
     }
 
+    // Rotate-half RoPE of the loaded query fragments at table row `pos`. Element
+    // d pairs with d + D/2, which this lane holds in the same slot of k-step
+    // ks + KS/2, so the rotation needs no data from other lanes.
+    __device__ __forceinline__ void rope_q(const DecodeParams& p, int64_t pos, int lane) {
+        const T* cos_row = static_cast<const T*>(p.rope_cos) + pos * D;
+        const T* sin_row = static_cast<const T*>(p.rope_sin) + pos * D;
+#pragma unroll
+        for (int ks = 0; ks < KS / 2; ++ks) {
+#pragma unroll
+            for (int w = 0; w < 2; ++w) {
+                const int d = ks * 16 + 2 * (lane & 3) + 8 * w;
+                float c0[2], s0[2], c1[2], s1[2];
+#pragma unroll
+                for (int e = 0; e < 2; ++e) {
+                    c0[e] = to_float<T>(cos_row[d + e]);
+                    s0[e] = to_float<T>(sin_row[d + e]);
+                    c1[e] = to_float<T>(cos_row[d + e + D / 2]);
+                    s1[e] = to_float<T>(sin_row[d + e + D / 2]);
+                }
+#pragma unroll
+                for (int nt = 0; nt < NT; ++nt) {
+                    uint32_t lo = qf[ks][nt][w], hi = qf[ks + KS / 2][nt][w];
+                    const T* lv = reinterpret_cast<const T*>(&lo);
+                    const T* hv = reinterpret_cast<const T*>(&hi);
+                    uint32_t nlo, nhi;
+                    T* nl = reinterpret_cast<T*>(&nlo);
+                    T* nh = reinterpret_cast<T*>(&nhi);
+#pragma unroll
+                    for (int e = 0; e < 2; ++e) {
+                        const float x0 = to_float<T>(lv[e]), x1 = to_float<T>(hv[e]);
+                        nl[e] = from_float<T>(rope_element<T>(x0, x1, c0[e], s0[e], true));
+                        nh[e] = from_float<T>(rope_element<T>(x1, x0, c1[e], s1[e], false));
+                    }
+                    qf[ks][nt][w] = nlo;
+                    qf[ks + KS / 2][nt][w] = nhi;
+                }
+            }
+        }
+    }
+
     // The staged page as mma A fragments: K for S^T = K Q^T, V^T (via .trans)
     // for O^T += V^T P^T. Loading them first frees the stage for the next TMA
     // load before any of the page's arithmetic runs.
@@ -317,10 +357,14 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
     const SeqSplit seq = seq_split(p, b);
     if (split >= seq.splits) return;
     if (seq.state != 0) {
-        if (p.new_key) append_row_direct(p, b, h, seq.len);
+        if (p.new_key) append_row_direct<T>(p, b, h, seq.len);
         write_group_constant<T>(p, b, h, seq.state == 1 ? 0.0f : __int_as_float(0x7fffffff));
         return;
     }
+    // Fused RoPE needs a table row for the step's position. Without one the
+    // group takes the corrupted-page path below (no loads, NaN result through
+    // the split partials) and nothing is appended.
+    const bool rope_missing = p.rope_cos && seq.len - 1 >= p.rope_rows;
     const bool single = seq.splits == 1;
 
     uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -329,7 +373,7 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
     const int64_t page_end_raw = page_begin + p.pages_per_split;
     const int cta_pages =
         static_cast<int>((page_end_raw < seq.pages ? page_end_raw : seq.pages) - page_begin);
-    const int n_my = warp < cta_pages ? (cta_pages - warp + NWARPS - 1) / NWARPS : 0;
+    const int n_my = (warp < cta_pages && !rope_missing) ? (cta_pages - warp + NWARPS - 1) / NWARPS : 0;
 
     // Page IDs of this warp's pages: lane i holds page warp + i * NWARPS of the run.
     // A corrupted ID (outside the pool) is never loaded; the group becomes NaN.
@@ -340,7 +384,7 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
                            b * p.table_stride + page_begin + warp + lane * NWARPS);
         bad = my_id < 0 || my_id >= p.num_blocks;
     }
-    const bool warp_has_bad = __any_sync(0xffffffffu, bad);
+    const bool warp_has_bad = __any_sync(0xffffffffu, bad) || rope_missing;
     const uint32_t bar0 = smem_addr(&bars[warp][0]);
     if (lane == 0) {
 #pragma unroll
@@ -390,7 +434,7 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
     constexpr int kNewPerLane = (2 * kRowChunks + 31) / 32;
     int append_at = -1;  // loop index of the last page in this warp, or -1
     uint4 new_rows[kNewPerLane];
-    if (p.new_key && split == seq.splits - 1) {
+    if (p.new_key && split == seq.splits - 1 && !rope_missing) {
         const int rel = static_cast<int>(seq.pages - 1 - page_begin);
         if (rel % NWARPS == warp) {
             append_at = rel / NWARPS;
@@ -399,10 +443,19 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
                 const int c = lane + 32 * j;
                 if (c < 2 * kRowChunks) {
                     const int which = c >= kRowChunks;
+                    const int cc = c - which * kRowChunks;
                     const int64_t* st = which ? p.new_value_stride : p.new_key_stride;
-                    new_rows[j] = reinterpret_cast<const uint4*>(
-                        static_cast<const uint16_t*>(which ? p.new_value : p.new_key) + b * st[0] + h * st[1])
-                        [c - which * kRowChunks];
+                    const uint4* row = reinterpret_cast<const uint4*>(
+                        static_cast<const uint16_t*>(which ? p.new_value : p.new_key) + b * st[0] + h * st[1]);
+                    new_rows[j] = row[cc];
+                    if (p.rope_cos && !which) {
+                        // The K chunk pairs with the chunk D/2 away (rotate-half).
+                        const int64_t t = (seq.len - 1) * kRowChunks + cc;
+                        new_rows[j] = rope_chunk<T>(new_rows[j], row[cc ^ (kRowChunks / 2)],
+                                                    reinterpret_cast<const uint4*>(p.rope_cos)[t],
+                                                    reinterpret_cast<const uint4*>(p.rope_sin)[t],
+                                                    cc < kRowChunks / 2);
+                    }
                 }
             }
         }
@@ -410,6 +463,7 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
 
     Warp w;
     w.load_q(p, b, h, lane);
+    if (p.rope_cos && !rope_missing) w.rope_q(p, seq.len - 1, lane);
     w.reset();
 
     bool failed = false;

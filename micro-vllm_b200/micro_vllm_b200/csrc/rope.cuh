@@ -1,0 +1,70 @@
+// Rotate-half RoPE of whole rows (the reference's apply_rope for the batched
+// path): out[b, h, t, :] = RoPE(x[b, h, t, :]) at position start_b + t, with
+// rows of caller-supplied cos/sin tables [table_rows, D] of the element type,
+// rounded per operation as the reference's tensor expression is
+// (src/micro_vllm/model.py:101-123; see rope_element). One thread per pair
+// (d, d + D/2) of one row, so out may alias x exactly (in place).
+#pragma once
+
+#include "mv_device.cuh"
+
+namespace mv {
+
+constexpr int kRopeThreads = 256;
+
+struct RopeParams {
+    const void* x;
+    int64_t x_stride[3];     // seq, head, token (elements)
+    void* out;
+    int64_t out_stride[3];
+    int batch;
+    int heads;
+    int tokens;
+    int head_dim;
+    const void* cos;
+    const void* sin;
+    int64_t table_rows;
+    const void* positions;   // nullptr: every sequence starts at `start`
+    int positions_i64;
+    int positions_end;       // positions hold the end of the sequence, not the start
+    int64_t start;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(kRopeThreads) rope_rows_kernel(const RopeParams r, int64_t total) {
+    wait_for_prior_grid();
+    allow_next_grid();
+    const int half = r.head_dim / 2;
+    const int64_t stride = static_cast<int64_t>(blockDim.x) * gridDim.x;
+    for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total; idx += stride) {
+        const int d = static_cast<int>(idx % half);
+        int64_t row = idx / half;
+        const int t = static_cast<int>(row % r.tokens);
+        row /= r.tokens;
+        const int h = static_cast<int>(row % r.heads);
+        const int b = static_cast<int>(row / r.heads);
+        int64_t start = r.start;
+        if (r.positions) {
+            start = load_index(r.positions, r.positions_i64, b);
+            if (r.positions_end) start -= r.tokens;
+        }
+        const int64_t pos = start + t;
+        const T* x = static_cast<const T*>(r.x) + b * r.x_stride[0] + h * r.x_stride[1] + t * r.x_stride[2];
+        T* o = static_cast<T*>(r.out) + b * r.out_stride[0] + h * r.out_stride[1] + t * r.out_stride[2];
+        if (pos < 0 || pos >= r.table_rows) {
+            // No table row for this position: the row becomes NaN, nothing is read.
+            o[d] = o[d + half] = from_float<T>(__int_as_float(0x7fffffff));
+            continue;
+        }
+        const T* c = static_cast<const T*>(r.cos) + pos * r.head_dim;
+        const T* s = static_cast<const T*>(r.sin) + pos * r.head_dim;
+        const float x0 = to_float<T>(x[d]);
+        const float x1 = to_float<T>(x[d + half]);
+        const float y0 = rope_element<T>(x0, x1, to_float<T>(c[d]), to_float<T>(s[d]), true);
+        const float y1 = rope_element<T>(x1, x0, to_float<T>(c[d + half]), to_float<T>(s[d + half]), false);
+        o[d] = from_float<T>(y0);
+        o[d + half] = from_float<T>(y1);
+    }
+}
+
+}  // namespace mv

@@ -122,9 +122,11 @@ def _run(query3, q_strides, key_cache, value_cache, block_table, table_stride, b
         workspace = _workspace(device, stream, size.value) if size.value else None
         head = (out.q_ptr, q_strides[0], q_strides[1])
         if rows is not None:
-            new_key, new_value = rows
+            new_key, new_value, tables = rows
             head += (new_key.data_ptr(), new_key.stride(0), new_key.stride(1),
                      new_value.data_ptr(), new_value.stride(0), new_value.stride(1))
+            head += ((tables[0].data_ptr(), tables[1].data_ptr(), tables[0].shape[0]) if tables is not None
+                     else (None, None, 0))
         entry = lib.mv_paged_decode if rows is None else lib.mv_paged_decode_append
         _native.check(entry(
             *head,
@@ -348,7 +350,8 @@ def paged_decode_with_append(query: torch.Tensor, key: torch.Tensor, value: torc
                              scale: float | None = None, *, max_context_len: int | None = None,
                              out: torch.Tensor | None = None, pages_per_split: int = 0,
                              force_simt: bool = False, persistent: bool = False,
-                             fused_merge: bool = False, cluster: bool = False) -> torch.Tensor:
+                             fused_merge: bool = False, cluster: bool = False,
+                             rope: tuple[torch.Tensor, torch.Tensor] | None = None) -> torch.Tensor:
     """One decode step of a layer: append this step's K/V row of every sequence, then attend.
 
     The result, in the pools and in the output, is that of
@@ -364,6 +367,10 @@ def paged_decode_with_append(query: torch.Tensor, key: torch.Tensor, value: torc
     key/value: [B, Hkv, D] or [B, Hkv, 1, D] CUDA tensors of the pool dtype,
     feature stride 1. context_lens count the new token. The page receiving a
     sequence's new row must not be shared with another sequence of the batch.
+    rope: optional (cos, sin) tables ``rope.rope_tables`` builds; q and key are
+    then unrotated and get RoPE at position context_lens - 1 (the reference's
+    apply_rope before the append, model.py:214-215) -- inside the decode kernel
+    on the fused path, else by the RoPE kernel first.
     Other arguments as ``paged_decode_attention``. Returns out.
     """
     from . import cuda_paged_cache as cache_ops
@@ -379,10 +386,32 @@ def paged_decode_with_append(query: torch.Tensor, key: torch.Tensor, value: torc
            'new K/V must have shape [B, Hkv, D] or [B, Hkv, 1, D]')
     cache_ops._validate_pages(key4, key_cache, value_cache)
     cache_ops._validate_aliases(key4, value4, key_cache, value_cache, block_table)
+    flags = _flags(force_simt, persistent, fused_merge, cluster)
+    key3, value3 = key4[:, :, 0, :], value4[:, :, 0, :]
+    tables = None
+    if rope is not None:
+        from . import rope as rope_ops
+        cos, sin = rope
+        rope_ops.check_tables(cos, sin, q.shape[2], q.dtype, q.device)
+        path = paged_decode_plan(q.shape[1], key_cache, max_context_len, batch=q.shape[0],
+                                 pages_per_split=pages_per_split, force_simt=force_simt,
+                                 persistent=persistent, cluster=cluster)[0]
+        if path == 'tma_mma' and _aligned16(key3, value3, cos, sin):
+            tables = (cos, sin)
+        else:
+            q = rope_ops.apply_rope(q, cos, sin, positions=context_lens, positions_are_end=True)
+            key3 = rope_ops.apply_rope(key3, cos, sin, positions=context_lens, positions_are_end=True)
     _launch_batched(q, key_cache, value_cache, block_table, context_lens, max_context_len, scale, out,
-                    pages_per_split, _flags(force_simt, persistent, fused_merge, cluster),
-                    rows=(key4[:, :, 0, :], value4[:, :, 0, :]))
+                    pages_per_split, flags, rows=(key3, value3, tables))
     return out
+
+
+def _aligned16(*tensors):
+    """Every tensor's start and outer element strides are 16-byte multiples (2-byte types)."""
+    for t in tensors:
+        if t.data_ptr() % 16 or any((t.stride(d) * t.element_size()) % 16 for d in range(t.dim() - 1)):
+            return False
+    return True
 
 
 class PagedDecodeStep:
@@ -400,15 +429,18 @@ class PagedDecodeStep:
     ``step(query, context_lens, out=None, key=None, value=None)``: query
     [B, Hq, D] or [B, Hq, 1, D]; context_lens [B] int32/int64 on the pool's
     device; key/value (both or neither) [B, Hkv, D] or [B, Hkv, 1, D], appended
-    at position context_lens - 1 before attending. The block table's contents
-    may change between calls; its tensor (pointer, shape) may not. Calls on one
-    stream share one split-KV workspace and must be ordered on it.
+    at position context_lens - 1 before attending. With ``rope=(cos, sin)``
+    bound, q and key arrive unrotated and are rotated at that position (inside
+    the decode kernel where it can, else by the RoPE kernel first). The block
+    table's contents may change between calls; its tensor (pointer, shape) may
+    not. Calls on one stream share one split-KV workspace and must be ordered on it.
     """
 
     def __init__(self, key_cache: torch.Tensor, value_cache: torch.Tensor, block_table: torch.Tensor, *,
                  num_q_heads: int, max_context_len: int | None = None, scale: float | None = None,
                  pages_per_split: int = 0, force_simt: bool = False, persistent: bool = False,
-                 fused_merge: bool = False, cluster: bool = False):
+                 fused_merge: bool = False, cluster: bool = False,
+                 rope: tuple[torch.Tensor, torch.Tensor] | None = None):
         batch = block_table.shape[0] if block_table.dim() == 2 else 0
         dim = key_cache.shape[-1] if key_cache.dim() == 4 else 0
         probe = torch.empty((max(batch, 1), num_q_heads, max(dim, 1)), dtype=key_cache.dtype,
@@ -444,6 +476,13 @@ class PagedDecodeStep:
                            block_table.shape[1])
         self._scale = float(scale)
         self._dtype_code = dtype
+        self._rope = None
+        self._rope_in_kernel = False
+        if rope is not None:
+            from . import rope as rope_ops
+            rope_ops.check_tables(rope[0], rope[1], dim, key_cache.dtype, key_cache.device)
+            self._rope = (rope[0], rope[1])
+            self._rope_in_kernel = self.plan[0] == 'tma_mma' and _aligned16(*rope)
 
     @property
     def plan(self):
@@ -494,11 +533,21 @@ class PagedDecodeStep:
                 workspace.data_ptr() if workspace is not None else None, self._workspace_bytes,
                 self._pps, self._flags, self._dtype_code, stream)
         if key is None:
+            _check(self._rope is None, 'a step bound with RoPE tables needs the new K/V rows')
             _native.check(self._lib.mv_paged_decode(q.data_ptr(), q.stride(0), q.stride(1), *self._pool_args,
                                                     *tail))
-        else:
-            key, value = self._check_rows(key), self._check_rows(value)
-            _native.check(self._lib.mv_paged_decode_append(
-                q.data_ptr(), q.stride(0), q.stride(1), key.data_ptr(), key.stride(0), key.stride(1),
-                value.data_ptr(), value.stride(0), value.stride(1), *self._pool_args, *tail))
+            return out
+        key, value = self._check_rows(key), self._check_rows(value)
+        tables = (None, None, 0)
+        if self._rope is not None:
+            cos, sin = self._rope
+            if self._rope_in_kernel and _aligned16(key, value):
+                tables = (cos.data_ptr(), sin.data_ptr(), cos.shape[0])
+            else:
+                from . import rope as rope_ops
+                q = rope_ops.apply_rope(q, cos, sin, positions=context_lens, positions_are_end=True)
+                key = rope_ops.apply_rope(key, cos, sin, positions=context_lens, positions_are_end=True)
+        _native.check(self._lib.mv_paged_decode_append(
+            q.data_ptr(), q.stride(0), q.stride(1), key.data_ptr(), key.stride(0), key.stride(1),
+            value.data_ptr(), value.stride(0), value.stride(1), *tables, *self._pool_args, *tail))
         return out

@@ -16,12 +16,16 @@ per-head restatement the reference's CUDA tests use
 (src/micro_vllm/paged_kv_cache.py:151-161) and the native kernel's page
 placement and invalid-ID skip (src/micro_vllm/csrc/paged_kv_cache.cu:18-41).
 
+``rope`` restates the rotary embedding applied to q and K before the append
+(``rotate_half`` / ``apply_rope``, src/micro_vllm/model.py:101-123).
+
 Parity is pinned: ``tests/golden/make_golden.py`` runs the reference's own
 Python code on seeded inputs and commits the outputs under ``tests/golden/``;
 ``tests/test_oracle_golden.py`` checks this oracle against them.
 """
 from .dtypes import bf16_to_f32, f32_to_bf16, to_float32, from_float32, STORAGE_DTYPES
 from .paged_append import append_tokens
+from .rope import apply_rope
 from .paged_attention import (
     decode_float,
     decode_fp64_per_head,
@@ -30,7 +34,7 @@ from .paged_attention import (
 )
 
 __all__ = [
-    'STORAGE_DTYPES', 'append_tokens', 'bf16_to_f32', 'decode_float',
+    'STORAGE_DTYPES', 'append_tokens', 'apply_rope', 'bf16_to_f32', 'decode_float',
     'decode_fp64_per_head', 'decode_reference', 'f32_to_bf16', 'from_float32',
     'gather_sequence', 'to_float32',
 ]
