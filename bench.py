@@ -715,9 +715,182 @@ def run_reference(args):
     }
 
 
+# ------------------------------------------------------- greedy generation
+
+GENERATE_WORKLOADS = {
+    # Qwen2.5-1.5B architecture, random init N(0, 0.02^2) (RMSNorm scales 1), bf16;
+    # batch 32 prompts of 512 uniform-random token IDs, 128 new tokens, 16-token pages.
+    'qwen15b_generate': dict(num_hidden_layers=28, hidden_size=1536, intermediate_size=8960,
+                             num_attention_heads=12, num_key_value_heads=2, vocab_size=151936,
+                             max_position_embeddings=32768, rope_theta=1000000.0, rms_norm_eps=1e-6,
+                             tie_word_embeddings=True, batch=32, prompt_len=512, new_tokens=128, seed=2024),
+}
+
+
+def _random_qwen2(spec, device, dtype):
+    """Random-init weights in the reference's checkpoint naming, generated on the device."""
+    import torch
+    from types import SimpleNamespace
+
+    gen = torch.Generator(device=device).manual_seed(spec['seed'])
+    hidden, inter = spec['hidden_size'], spec['intermediate_size']
+    dim = hidden // spec['num_attention_heads']
+    kv = spec['num_key_value_heads'] * dim
+
+    def normal(*shape):
+        out = torch.empty(shape, dtype=dtype, device=device)
+        flat = out.view(-1)
+        for start in range(0, flat.numel(), 1 << 26):
+            piece = torch.randn(min(1 << 26, flat.numel() - start), generator=gen, device=device)
+            flat[start:start + piece.numel()] = piece.mul_(0.02)
+        return out
+
+    ones = lambda n: torch.ones(n, dtype=dtype, device=device)  # noqa: E731
+    weights = {'model.embed_tokens.weight': normal(spec['vocab_size'], hidden), 'model.norm.weight': ones(hidden)}
+    for i in range(spec['num_hidden_layers']):
+        p = f'model.layers.{i}.'
+        weights.update({
+            p + 'input_layernorm.weight': ones(hidden), p + 'post_attention_layernorm.weight': ones(hidden),
+            p + 'self_attn.q_proj.weight': normal(hidden, hidden), p + 'self_attn.k_proj.weight': normal(kv, hidden),
+            p + 'self_attn.v_proj.weight': normal(kv, hidden), p + 'self_attn.q_proj.bias': normal(hidden),
+            p + 'self_attn.k_proj.bias': normal(kv), p + 'self_attn.v_proj.bias': normal(kv),
+            p + 'self_attn.o_proj.weight': normal(hidden, hidden),
+            p + 'mlp.gate_proj.weight': normal(inter, hidden), p + 'mlp.up_proj.weight': normal(inter, hidden),
+            p + 'mlp.down_proj.weight': normal(hidden, inter)})
+    keys = ('num_hidden_layers', 'hidden_size', 'intermediate_size', 'num_attention_heads', 'num_key_value_heads',
+            'vocab_size', 'max_position_embeddings', 'rope_theta', 'rms_norm_eps', 'tie_word_embeddings')
+    config = SimpleNamespace(model_type='qwen2', hidden_act='silu', rope_scaling=None, use_sliding_window=False,
+                             layer_types=['full_attention'] * spec['num_hidden_layers'], head_dim=None,
+                             partial_rotary_factor=1.0, **{k: spec[k] for k in keys})
+    return weights, config
+
+
+def run_generate(args):
+    """Greedy generation of the batched runtime: decode tokens/s and the attention share."""
+    import torch
+
+    from micro_vllm_b200.generate import GreedyDecoder
+    from micro_vllm_b200.runtime import prepare_model
+
+    if int(os.environ.get('WORLD_SIZE', '1')) > 1 and int(os.environ.get('RANK', '0')) > 0:
+        return None  # one replica on rank 0; the other ranks idle
+    spec = GENERATE_WORKLOADS[args.workload]
+    device = torch.device('cuda', int(os.environ.get('LOCAL_RANK', '0')))
+    torch.cuda.set_device(device)
+    weights, config = _random_qwen2(spec, device, torch.bfloat16)
+    model = prepare_model(weights, config)
+    batch, prompt_len, new = spec['batch'], spec['prompt_len'], spec['new_tokens']
+    prompts_host = torch.randint(0, spec['vocab_size'], (batch, prompt_len),
+                                 generator=torch.Generator().manual_seed(spec['seed']))
+    decoder = GreedyDecoder(model, batch, prompt_len + new - 1)
+    prompts = prompts_host.to(device)
+    for _ in range(max(args.warmup, 1)):           # warm-up: cuBLAS plans, graph capture
+        decoder.run(prompts, 4)
+    torch.cuda.synchronize(device)
+
+    # Prefill and the decode steps, timed on the device.
+    with ClockSampler(str(device.index)) as clocks:
+        events = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+        decoder.cache.reset()
+        events[0].record()
+        logits = model.prefill(prompts, decoder.cache)
+        decoder.tokens.copy_(logits.argmax(dim=-1))
+        events[1].record()
+        for _ in range(new - 1):
+            decoder.step()
+        events[2].record()
+        torch.cuda.synchronize(device)
+        prefill_ms = events[0].elapsed_time(events[1])
+        decode_ms = events[1].elapsed_time(events[2])
+
+        # Attention alone: the 28 layers' decode-step calls on the same buffers, as one graph.
+        hq, hkv, d = model.num_heads, model.num_kv_heads, model.head_dim
+        qkv = torch.randn(batch, hq + 2 * hkv, d, device=device).to(torch.bfloat16)
+        lens = decoder.cache.lengths.clone()
+        stream = torch.cuda.Stream(device)
+        stream.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(stream):
+            for step in model._steps:
+                step(qkv[:, :hq], lens, key=qkv[:, hq:hq + hkv], value=qkv[:, hq + hkv:])
+        torch.cuda.synchronize(device)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for step in model._steps:
+                step(qkv[:, :hq], lens, key=qkv[:, hq:hq + hkv], value=qkv[:, hq + hkv:])
+        a0, a1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 50
+        a0.record()
+        for _ in range(reps):
+            graph.replay()
+        a1.record()
+        torch.cuda.synchronize(device)
+        attention_ms = a0.elapsed_time(a1) / reps
+
+        # End to end through the public API: pinned host prompts in, host tokens out
+        # (a serving loop keeps its GreedyDecoder: cache and captured graph reused).
+        pinned = prompts_host.pin_memory()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        tokens = decoder.run(pinned.to(device, non_blocking=True), new).cpu()
+        e1.record()
+        torch.cuda.synchronize(device)
+        e2e_ms = e0.elapsed_time(e1)
+        path, _, splits = model._steps[0].plan
+    del graph
+    step_ms = decode_ms / (new - 1)
+    decode_tps = batch * (new - 1) / (decode_ms / 1e3)
+    weight_bytes = sum(t.numel() * t.element_size() for t in model.layers[0].values()) * model.num_layers + \
+        model.embedding.numel() * model.embedding.element_size()
+    peak, peak_kind = peak_hbm()
+    return {
+        'metric': 'decode tokens/s (greedy generation, batch 32, random-init Qwen2.5-1.5B)',
+        'value': round(decode_tps, 1),
+        'unit': 'tokens/s',
+        'n_gpus': 1,
+        'steps': new - 1,
+        'warmup': max(args.warmup, 1),
+        'ms_per_step': round(step_ms, 4),
+        'higher_is_better': True,
+        'scaling': 'weak',
+        'vs_baseline': None,
+        'dtype': 'bf16',
+        'data': 'synthetic (random-init weights N(0, 0.02^2), uniform-random prompt token IDs)',
+        'config': {'workload': (f'{args.workload}: 28 layers, hidden 1536, 12/2 heads, head_dim 128, '
+                                f'FFN 8960, vocab 151936, batch {batch} x {prompt_len} prompt tokens, '
+                                f'{new} new tokens, 16-token pages'),
+                   'timing': 'CUDA events: prefill, then the 127 graph-replayed decode steps',
+                   'attention': 'paged_decode_with_append (RoPE + append + paged decode) per layer'},
+        'prefill_ms': round(prefill_ms, 3),
+        'attention_share': round(attention_ms / step_ms, 4),
+        'attention_ms_per_step': round(attention_ms, 4),
+        'weights_gb': round(weight_bytes / 1e9, 3),
+        'weight_stream_gbs': round(weight_bytes / (step_ms / 1e3) / 1e9, 1),
+        'roofline': {'bound': 'hbm', 'achieved': round(weight_bytes / (step_ms / 1e3) / 1e9, 1), 'peak': peak,
+                     'unit': 'GB/s', 'frac': round(weight_bytes / (step_ms / 1e3) / 1e9 / peak, 4),
+                     'what': 'decode step: every weight byte read once per step (GEMMs at M = 32)',
+                     'peak_kind': peak_kind},
+        'e2e': {'value': round(batch * new / (e2e_ms / 1e3), 1), 'unit': 'tokens/s (all new tokens, incl. prefill)',
+                'ms': round(e2e_ms, 2), 'h2d_bytes_per_step': prompts_host.numel() * 8,
+                'd2h_bytes_per_step': tokens.numel() * 8,
+                'how': 'GreedyDecoder.run from pinned host prompts to host tokens, one batch'},
+        'decode_path': path,
+        'tokens_checksum': int(tokens.sum()),
+        'clocks': clocks.summary(),
+        # This library's kernels in the timed prefill + decode: RoPE q, RoPE K and the
+        # append per prefill layer; the decode kernel (+ split merge) per decode layer.
+        'gpu_launches': model.num_layers * (3 + (new - 1) * (2 if splits > 1 else 1)),
+    }
+
+
 def main(argv=None):
     args = parse_args(argv)
-    if args.impl == 'reference':
+    if args.workload in GENERATE_WORKLOADS:
+        if args.impl == 'reference':
+            result = {'impl': 'reference', 'unavailable': 'the reference generates one request at a time on '
+                      'the CPU path; a 1.5B-parameter batch-32 run is not a bounded sample'}
+        else:
+            result = run_generate(args)
+    elif args.impl == 'reference':
         result = run_reference(args)
     else:
         result = run_ours(args)

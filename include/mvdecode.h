@@ -50,6 +50,7 @@ extern "C" {
 #define MV_FLAG_PERSISTENT 2u /* tensor-core kernel on the persistent schedule instead of the split grid */
 #define MV_FLAG_FUSED_MERGE 4u /* split grid: the last split CTA of each sequence/head merges it */
 #define MV_FLAG_CLUSTER 8u /* tensor-core cluster kernel (contexts up to 8192 tokens), no merge pass */
+#define MV_FLAG_WIDE 16u /* split grid in the wide shape (8 warps, deeper rings; head_dim 64/128) */
 
 /* Status codes. */
 #define MV_OK 0
@@ -223,6 +224,22 @@ MV_API int mv_apply_rope(const void* x, int64_t x_stride_seq, int64_t x_stride_h
                          const void* sin, int64_t table_rows, const void* positions,
                          int32_t positions_type, int32_t positions_kind, int64_t start,
                          int32_t dtype, void* stream);
+
+/*
+ * Row operations of the batched runtime's decode step (the reference computes
+ * them with torch tensor operations; no native counterpart).
+ * mv_rms_norm: out[r] = weight * to_dtype(x[r] * rsqrt(mean(x[r]^2) + eps)) with
+ * fp32 statistics (src/micro_vllm/model.py:25-41); rows of `hidden` elements at
+ * the given element row strides.
+ * mv_silu_mul: out[r] = to_dtype(silu(g)) * u for rows [g | u] of 2 * width
+ * elements (a fused gate/up projection), each step rounded to the element type
+ * as F.silu(gate) * up is (model.py:150-165).
+ */
+MV_API int mv_rms_norm(const void* x, int64_t x_stride_row, const void* weight, void* out,
+                       int64_t out_stride_row, int64_t rows, int32_t hidden, float eps,
+                       int32_t dtype, void* stream);
+MV_API int mv_silu_mul(const void* gate_up, int64_t stride_row, void* out, int64_t out_stride_row,
+                       int64_t rows, int32_t width, int32_t dtype, void* stream);
 
 /*
  * mv_paged_decode for callers that cannot allocate device memory. No

@@ -18,6 +18,7 @@
 #include "paged_decode_mma.cuh"
 #include "paged_decode_simt.cuh"
 #include "rope.cuh"
+#include "row_ops.cuh"
 
 namespace {
 
@@ -114,6 +115,13 @@ int ensure_smem(Kernel kernel, size_t bytes) {
 #define MV_STAGES_D256 2
 #endif
 constexpr int kMmaWarps = MV_MMA_WARPS;
+// The wide split-grid shape for grids of about one CTA per SM: twice the warps,
+// deeper rings (192 KiB of stages), so one CTA keeps as many pages in flight
+// as three default CTAs. head_dim 256 has no wide shape (stages too large).
+constexpr int kWideWarps = 8;
+constexpr int kWideStagesD64 = 6;
+constexpr int kWideStagesD128 = 3;
+constexpr int kMaxPagesPerSplitWide = 32 * kWideWarps;
 #ifndef MV_CLUSTER_PAGES
 #define MV_CLUSTER_PAGES 64
 #endif
@@ -153,6 +161,7 @@ struct Plan {
     size_t part_o_bytes;
     size_t part_lse_bytes;
     bool fused_merge;
+    bool wide;       // split grid in the wide shape (kWideWarps warps, deeper rings)
 };
 
 bool mma_shape_ok(const Geometry& g) {
@@ -221,9 +230,10 @@ int persistent_occupancy_dispatch(int device, int dim, int nt, int* ctas_per_sm)
 }
 
 // Shared memory of the split-grid kernel's TMA stages (reused for the fused merge).
-size_t grid_stage_bytes(int dim) {
-    const int stages = dim == 64 ? MV_STAGES_D64 : (dim == 128 ? MV_STAGES_D128 : MV_STAGES_D256);
-    return static_cast<size_t>(kMmaWarps) * stages * 2 * (16 * static_cast<size_t>(dim) * 2);
+size_t grid_stage_bytes(int dim, bool wide) {
+    const int stages = wide ? (dim == 64 ? kWideStagesD64 : kWideStagesD128)
+                            : (dim == 64 ? MV_STAGES_D64 : (dim == 128 ? MV_STAGES_D128 : MV_STAGES_D256));
+    return static_cast<size_t>(wide ? kWideWarps : kMmaWarps) * stages * 2 * (16 * static_cast<size_t>(dim) * 2);
 }
 
 int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool aligned_for_tma,
@@ -247,6 +257,7 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
     plan->cluster = 0;
     plan->counter_bytes = plan->part_o_bytes = plan->part_lse_bytes = 0;
     plan->fused_merge = false;
+    plan->wide = false;
     const int64_t max_pages = (g.max_context_len + g.block_size - 1) / g.block_size;
 
     // Opt-in: sequences up to kClusterPages x 8 pages split over a cluster of up
@@ -283,7 +294,29 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
         return MV_OK;
     }
 
+    // The wide shape (8 warps, deeper rings, about one CTA per SM) when the
+    // batch has few (sequence, KV head) segments with up to 1024 pages each:
+    // measured on B200 it wins there (e.g. 32 x 2 segments of ~40 pages: 9.8 vs
+    // 12.7 us; 4 x 8 of 1024: 51 vs 56 us) and loses with many segments (the
+    // default grid packs three CTAs per SM) or very few (more, smaller CTAs win).
+    const int64_t segments = static_cast<int64_t>(g.batch) * g.kv_heads;
+    const bool auto_wide = pages_per_split == 0 && !(flags & (MV_FLAG_FUSED_MERGE | MV_FLAG_CLUSTER)) &&
+                           segments >= 16 && segments <= dev.sms / 2 && max_pages <= 1024;
+    plan->wide = plan->path == MV_PATH_TMA_MMA && ((flags & MV_FLAG_WIDE) || auto_wide) && g.head_dim != 256;
+    const int64_t max_pps = plan->wide ? kMaxPagesPerSplitWide : kMaxPagesPerSplit;
     int64_t pps = pages_per_split;
+    if (pps == 0 && plan->wide) {
+        // One split when a sequence fits 64 pages (no merge pass); otherwise
+        // about one wide CTA per SM: each segment's pages over SMs / segments
+        // splits, in multiples of 32 pages (32..256).
+        if (max_pages <= 64) {
+            pps = std::max<int64_t>(1, max_pages);
+        } else {
+            const int64_t per_segment = std::max<int64_t>(1, dev.sms / std::max<int64_t>(segments, 1));
+            pps = (max_pages + per_segment - 1) / per_segment;
+            pps = std::min<int64_t>(std::max<int64_t>((pps + 31) / 32 * 32, 32), kMaxPagesPerSplitWide);
+        }
+    }
     if (pps == 0) {
         // Splits of 16..128 pages, sized so the batch's pages -- estimated as half
         // the max_context_len bound per sequence -- fill about one wave of
@@ -298,9 +331,9 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
         while (pps * 2 <= want && pps < kMaxPagesPerSplit) pps *= 2;
         pps = std::min<int64_t>(pps, kMaxPagesPerSplit);
     }
-    if (plan->path == MV_PATH_TMA_MMA && pps > kMaxPagesPerSplit)
+    if (plan->path == MV_PATH_TMA_MMA && pps > max_pps)
         return fail(MV_ERR_INVALID_ARGUMENT, "pages_per_split above %d for the tensor-core kernel",
-                    kMaxPagesPerSplit);
+                    static_cast<int>(max_pps));
     const int64_t splits = std::max<int64_t>(1, (max_pages + pps - 1) / pps);
     if (splits > 8192) return fail(MV_ERR_UNSUPPORTED, "more than 8192 splits: raise pages_per_split");
     plan->pages_per_split = static_cast<int>(pps);
@@ -315,7 +348,7 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
         // through a latency-bound merge; measured on B200 it cost more than the
         // separate merge pass (launched early with PDL), so it is opt-in.
         plan->fused_merge = (flags & MV_FLAG_FUSED_MERGE) && plan->path == MV_PATH_TMA_MMA &&
-                            static_cast<size_t>(group) * splits * sizeof(float) <= grid_stage_bytes(g.head_dim) &&
+                            static_cast<size_t>(group) * splits * sizeof(float) <= grid_stage_bytes(g.head_dim, plan->wide) &&
                             static_cast<int64_t>(g.batch) * g.kv_heads <= kMaxCounters;
         plan->counter_bytes = kCounterRegion;
     }
@@ -405,28 +438,38 @@ int page_tensor_map(const void* base, int64_t num_blocks, int heads, int dim, in
 
 // ----------------------------------------------------------------- launch
 
-template <typename T, int D, int NT>
-int launch_mma(const mv::DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap, dim3 grid,
-               cudaStream_t stream) {
-    constexpr int STAGES = D == 64 ? MV_STAGES_D64 : (D == 128 ? MV_STAGES_D128 : MV_STAGES_D256);
-    using Shape = mv::MmaDecodeShape<D, NT, kMmaWarps, STAGES>;
-    auto kernel = mv::paged_decode_mma_kernel<T, D, NT, kMmaWarps, STAGES>;
+template <typename T, int D, int NT, int WARPS, int STAGES>
+int launch_mma_shape(const mv::DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap, dim3 grid,
+                     cudaStream_t stream) {
+    using Shape = mv::MmaDecodeShape<D, NT, WARPS, STAGES>;
+    auto kernel = mv::paged_decode_mma_kernel<T, D, NT, WARPS, STAGES>;
     int rc = ensure_smem(kernel, Shape::kSmemBytes);
     if (rc != MV_OK) return rc;
-    cudaError_t err = launch_pdl(kernel, grid, dim3(kMmaWarps * 32), Shape::kSmemBytes, stream, p, kmap, vmap);
+    cudaError_t err = launch_pdl(kernel, grid, dim3(WARPS * 32), Shape::kSmemBytes, stream, p, kmap, vmap);
     return err == cudaSuccess ? MV_OK : cuda_fail(err, "decode kernel launch");
+}
+
+template <typename T, int D, int NT>
+int launch_mma(const mv::DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap, dim3 grid,
+               bool wide, cudaStream_t stream) {
+    constexpr int STAGES = D == 64 ? MV_STAGES_D64 : (D == 128 ? MV_STAGES_D128 : MV_STAGES_D256);
+    if constexpr (D != 256) {
+        constexpr int WIDE_STAGES = D == 64 ? kWideStagesD64 : kWideStagesD128;
+        if (wide) return launch_mma_shape<T, D, NT, kWideWarps, WIDE_STAGES>(p, kmap, vmap, grid, stream);
+    }
+    return launch_mma_shape<T, D, NT, kMmaWarps, STAGES>(p, kmap, vmap, grid, stream);
 }
 
 template <typename T>
 int launch_mma_dispatch(const mv::DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap,
-                        dim3 grid, int nt, cudaStream_t stream) {
+                        dim3 grid, int nt, bool wide, cudaStream_t stream) {
     switch (p.head_dim * 4 + nt) {
-        case 64 * 4 + 1: return launch_mma<T, 64, 1>(p, kmap, vmap, grid, stream);
-        case 64 * 4 + 2: return launch_mma<T, 64, 2>(p, kmap, vmap, grid, stream);
-        case 128 * 4 + 1: return launch_mma<T, 128, 1>(p, kmap, vmap, grid, stream);
-        case 128 * 4 + 2: return launch_mma<T, 128, 2>(p, kmap, vmap, grid, stream);
-        case 256 * 4 + 1: return launch_mma<T, 256, 1>(p, kmap, vmap, grid, stream);
-        case 256 * 4 + 2: return launch_mma<T, 256, 2>(p, kmap, vmap, grid, stream);
+        case 64 * 4 + 1: return launch_mma<T, 64, 1>(p, kmap, vmap, grid, wide, stream);
+        case 64 * 4 + 2: return launch_mma<T, 64, 2>(p, kmap, vmap, grid, wide, stream);
+        case 128 * 4 + 1: return launch_mma<T, 128, 1>(p, kmap, vmap, grid, wide, stream);
+        case 128 * 4 + 2: return launch_mma<T, 128, 2>(p, kmap, vmap, grid, wide, stream);
+        case 256 * 4 + 1: return launch_mma<T, 256, 1>(p, kmap, vmap, grid, wide, stream);
+        case 256 * 4 + 2: return launch_mma<T, 256, 2>(p, kmap, vmap, grid, wide, stream);
         default: return fail(MV_ERR_UNSUPPORTED, "no tensor-core kernel for head_dim %d", p.head_dim);
     }
 }
@@ -525,7 +568,7 @@ int launch_decode(const mv::DecodeParams& p, const Plan& plan, const CUtensorMap
         if constexpr (std::is_same<T, float>::value) {
             return fail(MV_ERR_UNSUPPORTED, "tensor-core kernel takes fp16/bf16 only");
         } else {
-            rc = launch_mma_dispatch<T>(p, *kmap, *vmap, grid, plan.nt, stream);
+            rc = launch_mma_dispatch<T>(p, *kmap, *vmap, grid, plan.nt, plan.wide, stream);
         }
     } else {
         const size_t smem = mv::simt_smem_bytes(p.group, p.head_dim);
@@ -919,6 +962,71 @@ int mv_apply_rope(const void* x, int64_t x_stride_seq, int64_t x_stride_head, in
         default: err = launch_pdl(mv::rope_rows_kernel<__nv_bfloat16>, grid, block, 0, s, r, total); break;
     }
     return err == cudaSuccess ? MV_OK : cuda_fail(err, "RoPE kernel launch");
+}
+
+int mv_rms_norm(const void* x, int64_t x_stride_row, const void* weight, void* out, int64_t out_stride_row,
+                int64_t rows, int32_t hidden, float eps, int32_t dtype, void* stream) {
+    if (!x || !weight || !out) return fail(MV_ERR_INVALID_ARGUMENT, "x, weight and out must not be NULL");
+    if (rows <= 0 || hidden <= 0) return fail(MV_ERR_INVALID_ARGUMENT, "sizes must be positive");
+    if (rows >= (int64_t(1) << 31)) return fail(MV_ERR_UNSUPPORTED, "rows must be below 2^31");
+    if (x_stride_row < hidden || out_stride_row < hidden)
+        return fail(MV_ERR_INVALID_ARGUMENT, "row strides must cover the row");
+    if (!(eps >= 0.0f) || eps == INFINITY) return fail(MV_ERR_INVALID_ARGUMENT, "eps must be finite and nonnegative");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const dim3 grid(static_cast<unsigned>(rows)), block(mv::kRowThreads);
+    cudaError_t err;
+    switch (dtype) {
+        case MV_DTYPE_F32:
+            err = launch_pdl(mv::rms_norm_kernel<float>, grid, block, 0, s, static_cast<const float*>(x), x_stride_row,
+                             static_cast<const float*>(weight), static_cast<float*>(out), out_stride_row, hidden, eps);
+            break;
+        case MV_DTYPE_F16:
+            err = launch_pdl(mv::rms_norm_kernel<__half>, grid, block, 0, s, static_cast<const __half*>(x), x_stride_row,
+                             static_cast<const __half*>(weight), static_cast<__half*>(out), out_stride_row, hidden, eps);
+            break;
+        case MV_DTYPE_BF16:
+            err = launch_pdl(mv::rms_norm_kernel<__nv_bfloat16>, grid, block, 0, s,
+                             static_cast<const __nv_bfloat16*>(x), x_stride_row,
+                             static_cast<const __nv_bfloat16*>(weight), static_cast<__nv_bfloat16*>(out),
+                             out_stride_row, hidden, eps);
+            break;
+        default: return fail(MV_ERR_INVALID_ARGUMENT, "dtype must be MV_DTYPE_F32, MV_DTYPE_F16 or MV_DTYPE_BF16");
+    }
+    return err == cudaSuccess ? MV_OK : cuda_fail(err, "RMSNorm kernel launch");
+}
+
+int mv_silu_mul(const void* gate_up, int64_t stride_row, void* out, int64_t out_stride_row, int64_t rows,
+                int32_t width, int32_t dtype, void* stream) {
+    if (!gate_up || !out) return fail(MV_ERR_INVALID_ARGUMENT, "gate_up and out must not be NULL");
+    if (rows <= 0 || width <= 0) return fail(MV_ERR_INVALID_ARGUMENT, "sizes must be positive");
+    if (stride_row < 2 * static_cast<int64_t>(width) || out_stride_row < width)
+        return fail(MV_ERR_INVALID_ARGUMENT, "row strides must cover the row");
+    DeviceInfo dev;
+    int rc = device_info(&dev);
+    if (rc != MV_OK) return rc;
+    const int64_t total = rows * width;
+    const int64_t want = (total + mv::kRowThreads - 1) / mv::kRowThreads;
+    const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(dev.sms) * 16)));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const dim3 grid(blocks), block(mv::kRowThreads);
+    cudaError_t err;
+    switch (dtype) {
+        case MV_DTYPE_F32:
+            err = launch_pdl(mv::silu_mul_kernel<float>, grid, block, 0, s, static_cast<const float*>(gate_up),
+                             stride_row, static_cast<float*>(out), out_stride_row, static_cast<int>(width), total);
+            break;
+        case MV_DTYPE_F16:
+            err = launch_pdl(mv::silu_mul_kernel<__half>, grid, block, 0, s, static_cast<const __half*>(gate_up),
+                             stride_row, static_cast<__half*>(out), out_stride_row, static_cast<int>(width), total);
+            break;
+        case MV_DTYPE_BF16:
+            err = launch_pdl(mv::silu_mul_kernel<__nv_bfloat16>, grid, block, 0, s,
+                             static_cast<const __nv_bfloat16*>(gate_up), stride_row,
+                             static_cast<__nv_bfloat16*>(out), out_stride_row, static_cast<int>(width), total);
+            break;
+        default: return fail(MV_ERR_INVALID_ARGUMENT, "dtype must be MV_DTYPE_F32, MV_DTYPE_F16 or MV_DTYPE_BF16");
+    }
+    return err == cudaSuccess ? MV_OK : cuda_fail(err, "SiLU-mul kernel launch");
 }
 
 int mv_device_status(int32_t device, uint32_t* status) {

@@ -225,13 +225,14 @@ def decode_attention_paged(query: torch.Tensor, cache, *, layer_idx: int) -> tor
         cache._device_page_table, length)
 
 
-def _flags(force_simt, persistent, fused_merge=False, cluster=False):
+def _flags(force_simt, persistent, fused_merge=False, cluster=False, wide=False):
     return ((_native.FLAG_FORCE_SIMT if force_simt else 0) | (_native.FLAG_PERSISTENT if persistent else 0)
-            | (_native.FLAG_FUSED_MERGE if fused_merge else 0) | (_native.FLAG_CLUSTER if cluster else 0))
+            | (_native.FLAG_FUSED_MERGE if fused_merge else 0) | (_native.FLAG_CLUSTER if cluster else 0)
+            | (_native.FLAG_WIDE if wide else 0))
 
 
 def paged_decode_plan(query_heads, key_cache, context_bound, *, batch, pages_per_split=0,
-                      force_simt=False, persistent=False, cluster=False):
+                      force_simt=False, persistent=False, cluster=False, wide=False):
     """(path, pages_per_split, max_splits) that ``paged_decode_attention`` would use.
 
     path is 'tma_mma_cluster' (TMA + tensor cores, the splits of each
@@ -247,7 +248,7 @@ def paged_decode_plan(query_heads, key_cache, context_bound, *, batch, pages_per
     with torch.cuda.device(key_cache.device):
         _native.check(lib.mv_paged_decode_plan(
             batch, query_heads, kv_heads, dim, block_size, context_bound, pages_per_split,
-            _flags(force_simt, persistent, cluster=cluster), DTYPE_CODES[key_cache.dtype],
+            _flags(force_simt, persistent, cluster=cluster, wide=wide), DTYPE_CODES[key_cache.dtype],
             key_cache.data_ptr(), key_cache.data_ptr(), ctypes.byref(path), ctypes.byref(pps),
             ctypes.byref(splits)))
     return _native.PATH_NAMES[path.value], pps.value, splits.value
@@ -258,7 +259,7 @@ def paged_decode_attention(query: torch.Tensor, key_cache: torch.Tensor, value_c
                            scale: float | None = None, *, max_context_len: int | None = None,
                            out: torch.Tensor | None = None, pages_per_split: int = 0,
                            force_simt: bool = False, persistent: bool = False,
-                           fused_merge: bool = False, cluster: bool = False) -> torch.Tensor:
+                           fused_merge: bool = False, cluster: bool = False, wide: bool = False) -> torch.Tensor:
     """Batched paged GQA decode over one shared page pool.
 
     query: [B, Hq, D] (or [B, Hq, 1, D]) CUDA fp32/fp16/bf16, feature stride 1.
@@ -271,10 +272,11 @@ def paged_decode_attention(query: torch.Tensor, key_cache: torch.Tensor, value_c
     table capacity max_blocks * bs, so no device read-back is needed. Lengths
     above it produce NaN (the split plan cannot cover them).
     out: optional [B, Hq, D] destination (feature stride 1).
-    pages_per_split / cluster / persistent / fused_merge / force_simt: kernel
-    selection for tests and tuning (that many pages per split-KV CTA; the
-    cluster kernel; the persistent tensor-core schedule; merging splits in the
-    last split CTA; the CUDA-core kernel). By default the library picks the
+    pages_per_split / cluster / persistent / fused_merge / wide / force_simt:
+    kernel selection for tests and tuning (that many pages per split-KV CTA;
+    the cluster kernel; the persistent tensor-core schedule; merging splits in
+    the last split CTA; the split grid's wide shape of 8 warps with deeper
+    rings; the CUDA-core kernel). By default the library picks the
     tensor-core split grid with a merge pass, and the CUDA-core kernel for
     shapes the tensor-core kernels do not take.
     Returns out, or a fresh [B, Hq, D] tensor of the query's dtype.
@@ -282,7 +284,7 @@ def paged_decode_attention(query: torch.Tensor, key_cache: torch.Tensor, value_c
     q, max_context_len, scale, out = _checked_batched(query, key_cache, value_cache, block_table,
                                                       context_lens, scale, max_context_len, out)
     _launch_batched(q, key_cache, value_cache, block_table, context_lens, max_context_len, scale, out,
-                    pages_per_split, _flags(force_simt, persistent, fused_merge, cluster))
+                    pages_per_split, _flags(force_simt, persistent, fused_merge, cluster, wide))
     return out
 
 
@@ -350,7 +352,7 @@ def paged_decode_with_append(query: torch.Tensor, key: torch.Tensor, value: torc
                              scale: float | None = None, *, max_context_len: int | None = None,
                              out: torch.Tensor | None = None, pages_per_split: int = 0,
                              force_simt: bool = False, persistent: bool = False,
-                             fused_merge: bool = False, cluster: bool = False,
+                             fused_merge: bool = False, cluster: bool = False, wide: bool = False,
                              rope: tuple[torch.Tensor, torch.Tensor] | None = None) -> torch.Tensor:
     """One decode step of a layer: append this step's K/V row of every sequence, then attend.
 
@@ -386,7 +388,7 @@ def paged_decode_with_append(query: torch.Tensor, key: torch.Tensor, value: torc
            'new K/V must have shape [B, Hkv, D] or [B, Hkv, 1, D]')
     cache_ops._validate_pages(key4, key_cache, value_cache)
     cache_ops._validate_aliases(key4, value4, key_cache, value_cache, block_table)
-    flags = _flags(force_simt, persistent, fused_merge, cluster)
+    flags = _flags(force_simt, persistent, fused_merge, cluster, wide)
     key3, value3 = key4[:, :, 0, :], value4[:, :, 0, :]
     tables = None
     if rope is not None:
@@ -395,7 +397,7 @@ def paged_decode_with_append(query: torch.Tensor, key: torch.Tensor, value: torc
         rope_ops.check_tables(cos, sin, q.shape[2], q.dtype, q.device)
         path = paged_decode_plan(q.shape[1], key_cache, max_context_len, batch=q.shape[0],
                                  pages_per_split=pages_per_split, force_simt=force_simt,
-                                 persistent=persistent, cluster=cluster)[0]
+                                 persistent=persistent, cluster=cluster, wide=wide)[0]
         if path == 'tma_mma' and _aligned16(key3, value3, cos, sin):
             tables = (cos, sin)
         else:
@@ -439,7 +441,7 @@ class PagedDecodeStep:
     def __init__(self, key_cache: torch.Tensor, value_cache: torch.Tensor, block_table: torch.Tensor, *,
                  num_q_heads: int, max_context_len: int | None = None, scale: float | None = None,
                  pages_per_split: int = 0, force_simt: bool = False, persistent: bool = False,
-                 fused_merge: bool = False, cluster: bool = False,
+                 fused_merge: bool = False, cluster: bool = False, wide: bool = False,
                  rope: tuple[torch.Tensor, torch.Tensor] | None = None):
         batch = block_table.shape[0] if block_table.dim() == 2 else 0
         dim = key_cache.shape[-1] if key_cache.dim() == 4 else 0
@@ -455,7 +457,7 @@ class PagedDecodeStep:
         num_blocks, kv_heads, block_size, _ = key_cache.shape
         self._q_shape = (batch, num_q_heads, dim)
         self._row_shape = (batch, kv_heads, dim)
-        self._flags = _flags(force_simt, persistent, fused_merge, cluster)
+        self._flags = _flags(force_simt, persistent, fused_merge, cluster, wide)
         self._pps = int(pages_per_split)
         self._bound = int(bound)
         self._pools = (key_cache, value_cache)
@@ -491,7 +493,8 @@ class PagedDecodeStep:
                                  pages_per_split=self._pps,
                                  force_simt=bool(self._flags & _native.FLAG_FORCE_SIMT),
                                  persistent=bool(self._flags & _native.FLAG_PERSISTENT),
-                                 cluster=bool(self._flags & _native.FLAG_CLUSTER))
+                                 cluster=bool(self._flags & _native.FLAG_CLUSTER),
+                                 wide=bool(self._flags & _native.FLAG_WIDE))
 
     def _check_rows(self, rows):
         if rows.dim() == 4:

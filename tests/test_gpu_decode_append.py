@@ -22,6 +22,7 @@ MODES = {
     'auto': {},                               # split grid: append fused into the decode kernel
     'fused_merge': dict(fused_merge=True),    # split grid, last split CTA merges: append fused
     'split4': dict(pages_per_split=4),        # split grid, many splits: append fused
+    'wide': dict(wide=True),                  # split grid, wide shape: append fused
     'persistent': dict(persistent=True),      # append kernel first, then the persistent kernel
     'cluster': dict(cluster=True),            # append kernel first, then the cluster kernel
     'simt': dict(force_simt=True),            # append kernel first, then the CUDA-core kernel

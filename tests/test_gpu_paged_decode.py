@@ -52,6 +52,7 @@ MODES = {
     'persistent': dict(persistent=True),      # tensor-core persistent schedule + merge pass
     'fused': dict(fused_merge=True),          # split grid, last split CTA merges
     'split4': dict(pages_per_split=4),        # split grid, 4 pages per split
+    'wide': dict(wide=True),                  # split grid, wide shape (8 warps, deeper rings)
     'simt': dict(force_simt=True),            # CUDA-core kernel
 }
 

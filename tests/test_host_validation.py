@@ -145,3 +145,29 @@ def test_storage_overlap_detects_views_and_dlpack_aliases():
     alias = torch.utils.dlpack.from_dlpack(base[8:16])
     assert storage_overlaps(alias, base)
     assert not storage_overlaps(torch.zeros(0), base)
+
+
+def test_batched_cache_and_runtime_refuse_cpu_storage():
+    from micro_vllm_b200.paged_kv_cache import BatchedPagedKVCache
+    from micro_vllm_b200.runtime import prepare_model
+    from tests.golden.model_cases import make_weights, model_config
+    with pytest.raises(ValueError, match='CUDA'):
+        BatchedPagedKVCache.allocate(num_layers=1, batch_size=2, capacity=32, num_kv_heads=1, head_dim=8,
+                                     dtype=torch.float32, device='cpu')
+    with pytest.raises(ValueError, match='positive integers'):
+        BatchedPagedKVCache.allocate(num_layers=1, batch_size=0, capacity=32, num_kv_heads=1, head_dim=8,
+                                     dtype=torch.float32, device='cuda')
+    weights = {k: torch.from_numpy(v) for k, v in make_weights('tiny_qwen2_fp32').items()}
+    with pytest.raises(ValueError, match='CUDA weights'):
+        prepare_model(weights, model_config('tiny_qwen2_fp32'))
+
+
+def test_generate_rejects_bad_arguments_before_any_work():
+    from micro_vllm_b200.generate import _eos_ids, greedy_decode
+    with pytest.raises(ValueError, match='max_new_tokens'):
+        greedy_decode({}, None, torch.zeros(1, 4, dtype=torch.long), 0)
+    with pytest.raises(ValueError, match='equal-length prompts'):
+        greedy_decode({}, None, torch.zeros(4, dtype=torch.long), 2)
+    assert _eos_ids(None, 10) == () and _eos_ids(3, 10) == (3,) and _eos_ids([1, 2], 10) == (1, 2)
+    with pytest.raises(ValueError, match='EOS'):
+        _eos_ids(11, 10)
