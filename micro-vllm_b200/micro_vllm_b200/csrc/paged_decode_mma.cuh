@@ -369,10 +369,9 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
 
     uint8_t* smem = reinterpret_cast<uint8_t*>(
         (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
-    const int64_t page_begin = static_cast<int64_t>(split) * p.pages_per_split;
-    const int64_t page_end_raw = page_begin + p.pages_per_split;
-    const int cta_pages =
-        static_cast<int>((page_end_raw < seq.pages ? page_end_raw : seq.pages) - page_begin);
+    int64_t page_begin, page_end;
+    split_range(p, seq, split, &page_begin, &page_end);
+    const int cta_pages = static_cast<int>(page_end - page_begin);
     const int n_my = (warp < cta_pages && !rope_missing) ? (cta_pages - warp + NWARPS - 1) / NWARPS : 0;
 
     // Page IDs of this warp's pages: lane i holds page warp + i * NWARPS of the run.

@@ -66,9 +66,8 @@ __global__ void __launch_bounds__(kSimtThreads) paged_decode_simt_kernel(const D
         return;
     }
     const bool single = seq.splits == 1;
-    const int64_t page_begin = static_cast<int64_t>(split) * p.pages_per_split;
-    const int64_t page_end_raw = page_begin + p.pages_per_split;
-    const int64_t page_end = page_end_raw < seq.pages ? page_end_raw : seq.pages;
+    int64_t page_begin, page_end;
+    split_range(p, seq, split, &page_begin, &page_end);
 
     if (tid == 0) cta_bad = 0;
     __syncthreads();
