@@ -132,6 +132,43 @@ MV_API int mv_paged_decode(const void* q, int64_t q_stride_seq, int64_t q_stride
                     uint32_t flags, int32_t dtype, void* stream);
 
 /*
+ * GQA decode over contiguous caches: for every sequence b and query head j,
+ *   out[b, j] = softmax(scale * K_b q[b, j]) V_b
+ * over the first context_lens[b] tokens (all sequences: max_context_len when
+ * context_lens is NULL) of K_b = k_cache[b, j / G, 0:len, :], which holds
+ * cache_len tokens. Element strides per sequence, KV head and token (feature
+ * stride 1; zero strides broadcast), for K and V separately.
+ *
+ * Replaces the reference's decode_attention_gqa(query, key, value)
+ * (src/micro_vllm/csrc/decode_attention.cpp:138-142, kernel
+ * decode_attention_online.cu:47-52): that call is batch 1, context_lens NULL,
+ * max_context_len == cache_len == key.size(2), scale == head_dim ** -0.5.
+ * Caches whose base and strides in use are 16-byte multiples run the
+ * tensor-core split grid (fp16/bf16, head_dim 64/128/256, GQA group <= 16),
+ * every other case the CUDA-core kernel; the workspace contract is
+ * mv_paged_decode's, sized by mv_contiguous_decode_plan. Lengths above the
+ * bound give NaN rows, as in mv_paged_decode.
+ */
+MV_API int mv_contiguous_decode_plan(const void* k_cache, int64_t k_stride_seq, int64_t k_stride_head,
+                                     int64_t k_stride_token, const void* v_cache,
+                                     int64_t v_stride_seq, int64_t v_stride_head,
+                                     int64_t v_stride_token, int64_t cache_len,
+                                     int32_t num_kv_heads, int32_t head_dim,
+                                     int64_t max_context_len, int32_t batch, int32_t num_q_heads,
+                                     int32_t pages_per_split, uint32_t flags, int32_t dtype,
+                                     int32_t* path, int32_t* chosen_pages_per_split,
+                                     int32_t* max_splits, size_t* workspace_bytes);
+MV_API int mv_contiguous_decode(const void* q, int64_t q_stride_seq, int64_t q_stride_head,
+                                const void* k_cache, int64_t k_stride_seq, int64_t k_stride_head,
+                                int64_t k_stride_token, const void* v_cache, int64_t v_stride_seq,
+                                int64_t v_stride_head, int64_t v_stride_token, int64_t cache_len,
+                                int32_t num_kv_heads, int32_t head_dim, const void* context_lens,
+                                int32_t context_lens_type, int64_t max_context_len, int32_t batch,
+                                int32_t num_q_heads, float scale, void* out, int64_t out_stride_seq,
+                                int64_t out_stride_head, void* workspace, size_t workspace_bytes,
+                                int32_t pages_per_split, uint32_t flags, int32_t dtype, void* stream);
+
+/*
  * Paged KV append (reshape-and-cache): token t of sequence b goes to logical
  * position start_b + t, i.e. page block_table[b, pos / block_size], slot
  * pos % block_size. Copies are bit-exact (no conversion).

@@ -38,7 +38,7 @@ EXPORTED_SYMBOLS = (
     'mv_abi_version', 'mv_last_error', 'mv_paged_decode_workspace_size',
     'mv_paged_decode_plan', 'mv_paged_decode', 'mv_write_paged_kv',
     'mv_device_status', 'mv_clear_device_status', 'mv_paged_decode_append', 'mv_apply_rope',
-    'mv_rms_norm', 'mv_silu_mul',
+    'mv_rms_norm', 'mv_silu_mul', 'mv_contiguous_decode_plan', 'mv_contiguous_decode',
 )
 
 _i32, _i64, _u32, _vp, _sz, _f32 = (ctypes.c_int32, ctypes.c_int64, ctypes.c_uint32,
@@ -90,6 +90,22 @@ _SIGNATURES = {
                        _vp, _i32, _i32, _i64,      # positions, type, kind, start
                        _i32, _vp]),                # dtype, stream
     'mv_rms_norm': (ctypes.c_int, [_vp, _i64, _vp, _vp, _i64, _i64, _i32, _f32, _i32, _vp]),
+    'mv_contiguous_decode_plan': (
+        ctypes.c_int, [_vp, _i64, _i64, _i64,      # k_cache, strides (sequence, head, token)
+                       _vp, _i64, _i64, _i64,      # v_cache, strides
+                       _i64, _i32, _i32, _i64,     # cache_len, kv heads, head dim, max context len
+                       _i32, _i32, _i32, _u32, _i32,  # batch, q heads, pps, flags, dtype
+                       ctypes.POINTER(_i32), ctypes.POINTER(_i32), ctypes.POINTER(_i32),
+                       ctypes.POINTER(_sz)]),
+    'mv_contiguous_decode': (
+        ctypes.c_int, [_vp, _i64, _i64,            # q, strides
+                       _vp, _i64, _i64, _i64,      # k_cache, strides
+                       _vp, _i64, _i64, _i64,      # v_cache, strides
+                       _i64, _i32, _i32,           # cache_len, kv heads, head dim
+                       _vp, _i32, _i64,            # context lens, type, max context len
+                       _i32, _i32, _f32,           # batch, q heads, scale
+                       _vp, _i64, _i64,            # out, strides
+                       _vp, _sz, _i32, _u32, _i32, _vp]),  # workspace, bytes, pps, flags, dtype, stream
     'mv_silu_mul': (ctypes.c_int, [_vp, _i64, _vp, _i64, _i64, _i32, _i32, _vp]),
     'mv_device_status': (ctypes.c_int, [_i32, ctypes.POINTER(_u32)]),
     'mv_clear_device_status': (ctypes.c_int, [_i32]),

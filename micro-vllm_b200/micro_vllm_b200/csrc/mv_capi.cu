@@ -385,11 +385,14 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 struct MapKey {
     const void* base;
-    int64_t num_blocks;
-    int32_t heads, dim, dtype;
+    int32_t kind;          // 0: page pool, 1: contiguous cache
+    int32_t dim, dtype;
+    int64_t extent[3];     // pool: (pages, heads, 0); contiguous: (tokens, heads, sequences)
+    int64_t stride[3];     // contiguous: element strides (token, head, sequence)
     bool operator==(const MapKey& o) const {
-        return base == o.base && num_blocks == o.num_blocks && heads == o.heads && dim == o.dim &&
-               dtype == o.dtype;
+        return base == o.base && kind == o.kind && dim == o.dim && dtype == o.dtype &&
+               extent[0] == o.extent[0] && extent[1] == o.extent[1] && extent[2] == o.extent[2] &&
+               stride[0] == o.stride[0] && stride[1] == o.stride[1] && stride[2] == o.stride[2];
     }
 };
 
@@ -407,8 +410,23 @@ std::mutex g_map_mutex;
 // Page pool [num_blocks, heads, 16, dim] viewed as 5-D (d % 64, slot, d / 64,
 // head, page) so one box = one page of one head, stored as dim/64 swizzled
 // [16 x 128 B] sub-tiles.
+int cached_tensor_map(const MapKey& key, CUtensorMap* out);
+
 int page_tensor_map(const void* base, int64_t num_blocks, int heads, int dim, int dtype, CUtensorMap* out) {
-    const MapKey key{base, num_blocks, heads, dim, dtype};
+    const MapKey key{base, 0, dim, dtype, {num_blocks, heads, 0}, {0, 0, 0}};
+    return cached_tensor_map(key, out);
+}
+
+// Contiguous cache [sequences, heads, tokens, dim] with element strides, viewed
+// as 5-D (d % 64, token, d / 64, head, sequence): one box = 16 tokens of one
+// head, the same shared-memory tile as a page; tokens past the cache read as 0.
+int contiguous_tensor_map(const void* base, int64_t tokens, int heads, int64_t sequences, int dim,
+                          const int64_t* strides, int dtype, CUtensorMap* out) {
+    const MapKey key{base, 1, dim, dtype, {tokens, heads, sequences}, {strides[0], strides[1], strides[2]}};
+    return cached_tensor_map(key, out);
+}
+
+int cached_tensor_map(const MapKey& key, CUtensorMap* out) {
     std::lock_guard<std::mutex> lock(g_map_mutex);
     for (int i = 0; i < kMapCache; ++i) {
         if (g_maps[i].used && g_maps[i].key == key) {
@@ -418,15 +436,30 @@ int page_tensor_map(const void* base, int64_t num_blocks, int heads, int dim, in
     }
     auto encode = encode_fn();
     if (!encode) return fail(MV_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+    const int dim = key.dim;
     const cuuint64_t row = static_cast<cuuint64_t>(dim) * 2;
-    cuuint64_t dims[5] = {64, 16, static_cast<cuuint64_t>(dim / 64), static_cast<cuuint64_t>(heads),
-                          static_cast<cuuint64_t>(num_blocks)};
-    cuuint64_t strides[4] = {row, 128, 16 * row, static_cast<cuuint64_t>(heads) * 16 * row};
+    cuuint64_t dims[5];
+    cuuint64_t strides[4];
+    if (key.kind == 0) {
+        const cuuint64_t heads = static_cast<cuuint64_t>(key.extent[1]);
+        const cuuint64_t d5[5] = {64, 16, static_cast<cuuint64_t>(dim / 64), heads,
+                                  static_cast<cuuint64_t>(key.extent[0])};
+        const cuuint64_t s4[4] = {row, 128, 16 * row, heads * 16 * row};
+        std::memcpy(dims, d5, sizeof(dims));
+        std::memcpy(strides, s4, sizeof(strides));
+    } else {
+        const cuuint64_t d5[5] = {64, static_cast<cuuint64_t>(key.extent[0]), static_cast<cuuint64_t>(dim / 64),
+                                  static_cast<cuuint64_t>(key.extent[1]), static_cast<cuuint64_t>(key.extent[2])};
+        const cuuint64_t s4[4] = {static_cast<cuuint64_t>(key.stride[0]) * 2, 128,
+                                  static_cast<cuuint64_t>(key.stride[1]) * 2, static_cast<cuuint64_t>(key.stride[2]) * 2};
+        std::memcpy(dims, d5, sizeof(dims));
+        std::memcpy(strides, s4, sizeof(strides));
+    }
     cuuint32_t box[5] = {64, 16, static_cast<cuuint32_t>(dim / 64), 1, 1};
     cuuint32_t elem_strides[5] = {1, 1, 1, 1, 1};
     CUtensorMap map;
-    CUresult r = encode(&map, dtype == MV_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                        5, const_cast<void*>(base), dims, strides, box, elem_strides,
+    CUresult r = encode(&map, key.dtype == MV_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                        5, const_cast<void*>(key.base), dims, strides, box, elem_strides,
                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(MV_ERR_CUDA, "cuTensorMapEncodeTiled failed (CUresult %d)", static_cast<int>(r));
@@ -600,6 +633,48 @@ int check_index_type(int32_t type, const char* what) {
 
 size_t dtype_bytes(int32_t dtype) { return dtype == MV_DTYPE_F32 ? 4 : 2; }
 
+// A contiguous cache can be read with TMA when its base is 16-byte aligned and
+// the token, head and sequence strides in use are positive multiples of 16 bytes.
+bool contiguous_tma_ok(const void* base, const int64_t* s, int heads, int batch) {
+    if (reinterpret_cast<uintptr_t>(base) % 16) return false;
+    if (s[2] <= 0 || (s[2] * 2) % 16) return false;
+    if (heads > 1 && (s[1] <= 0 || (s[1] * 2) % 16)) return false;
+    if (batch > 1 && (s[0] <= 0 || (s[0] * 2) % 16)) return false;
+    return true;
+}
+
+// Strides of a dimension of extent 1 are never used: give the tensor map a valid one.
+void contiguous_map_strides(const int64_t* s, int heads, int batch, int64_t tokens, int64_t* out) {
+    out[0] = s[2];
+    out[1] = heads > 1 ? s[1] : s[2] * ((tokens + 7) / 8 * 8);
+    out[2] = batch > 1 ? s[0] : out[1] * heads;
+}
+
+struct ContiguousCall {
+    const void* k_cache;
+    int64_t k_stride[3];  // sequence, head, token (elements)
+    const void* v_cache;
+    int64_t v_stride[3];
+    int64_t cache_len;
+};
+
+int contiguous_plan(const ContiguousCall& c, int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
+                    int32_t head_dim, int64_t max_context_len, int32_t pages_per_split, uint32_t flags,
+                    int32_t dtype, Plan* plan) {
+    if (!c.k_cache || !c.v_cache) return fail(MV_ERR_INVALID_ARGUMENT, "k_cache and v_cache must not be NULL");
+    if (c.cache_len <= 0) return fail(MV_ERR_INVALID_ARGUMENT, "cache_len must be positive");
+    for (int i = 0; i < 3; ++i)
+        if (c.k_stride[i] < 0 || c.v_stride[i] < 0) return fail(MV_ERR_INVALID_ARGUMENT, "strides must be nonnegative");
+    if (max_context_len < 0) return fail(MV_ERR_INVALID_ARGUMENT, "max_context_len must be nonnegative");
+    const int64_t bound = std::min(max_context_len, c.cache_len);
+    const Geometry g{batch, num_q_heads, num_kv_heads, head_dim, 16, bound, dtype};
+    const bool tma = contiguous_tma_ok(c.k_cache, c.k_stride, num_kv_heads, batch) &&
+                     contiguous_tma_ok(c.v_cache, c.v_stride, num_kv_heads, batch);
+    // The split grid and the CUDA-core kernel read contiguous caches; the
+    // persistent and cluster schedules do not.
+    return make_plan(g, pages_per_split, flags & ~(MV_FLAG_PERSISTENT | MV_FLAG_CLUSTER), tma, plan);
+}
+
 }  // namespace
 
 extern "C" {
@@ -736,6 +811,8 @@ static int paged_decode_impl(const void* q, int64_t q_stride_seq, int64_t q_stri
     p.rope_cos = nullptr;
     p.rope_sin = nullptr;
     p.rope_rows = 0;
+    p.contiguous = 0;
+    for (int i = 0; i < 3; ++i) p.k_stride[i] = p.v_stride[i] = 0;
     if (rows) {
         // The split-grid tensor-core kernel writes the rows itself (16-byte
         // chunks); every other plan runs the append kernel first, as two launches.
@@ -826,6 +903,115 @@ int mv_paged_decode_append(const void* q, int64_t q_stride_seq, int64_t q_stride
                              blocks_per_seq, context_lens, context_lens_type, max_context_len, batch,
                              num_q_heads, scale, out, out_stride_seq, out_stride_head, workspace,
                              workspace_bytes, pages_per_split, flags, dtype, stream, &rows);
+}
+
+int mv_contiguous_decode_plan(const void* k_cache, int64_t k_stride_seq, int64_t k_stride_head,
+                              int64_t k_stride_token, const void* v_cache, int64_t v_stride_seq,
+                              int64_t v_stride_head, int64_t v_stride_token, int64_t cache_len,
+                              int32_t num_kv_heads, int32_t head_dim, int64_t max_context_len, int32_t batch,
+                              int32_t num_q_heads, int32_t pages_per_split, uint32_t flags, int32_t dtype,
+                              int32_t* path, int32_t* chosen_pages_per_split, int32_t* max_splits,
+                              size_t* workspace_bytes) {
+    if (!path || !chosen_pages_per_split || !max_splits || !workspace_bytes)
+        return fail(MV_ERR_INVALID_ARGUMENT, "outputs must not be NULL");
+    const ContiguousCall c{k_cache, {k_stride_seq, k_stride_head, k_stride_token},
+                           v_cache, {v_stride_seq, v_stride_head, v_stride_token}, cache_len};
+    Plan plan;
+    int rc = contiguous_plan(c, batch, num_q_heads, num_kv_heads, head_dim, max_context_len, pages_per_split,
+                             flags, dtype, &plan);
+    if (rc != MV_OK) return rc;
+    *path = plan.path;
+    *chosen_pages_per_split = plan.pages_per_split;
+    *max_splits = plan.max_splits;
+    *workspace_bytes = plan.workspace;
+    return MV_OK;
+}
+
+int mv_contiguous_decode(const void* q, int64_t q_stride_seq, int64_t q_stride_head, const void* k_cache,
+                         int64_t k_stride_seq, int64_t k_stride_head, int64_t k_stride_token, const void* v_cache,
+                         int64_t v_stride_seq, int64_t v_stride_head, int64_t v_stride_token, int64_t cache_len,
+                         int32_t num_kv_heads, int32_t head_dim, const void* context_lens,
+                         int32_t context_lens_type, int64_t max_context_len, int32_t batch, int32_t num_q_heads,
+                         float scale, void* out, int64_t out_stride_seq, int64_t out_stride_head,
+                         void* workspace, size_t workspace_bytes, int32_t pages_per_split, uint32_t flags,
+                         int32_t dtype, void* stream) {
+    if (!q || !out) return fail(MV_ERR_INVALID_ARGUMENT, "q and out must not be NULL");
+    if (q_stride_seq < 0 || q_stride_head < 0 || out_stride_seq < 0 || out_stride_head < 0)
+        return fail(MV_ERR_INVALID_ARGUMENT, "strides must be nonnegative");
+    int rc = context_lens ? check_index_type(context_lens_type, "context_lens") : MV_OK;
+    if (rc != MV_OK) return rc;
+    if (!context_lens && max_context_len <= 0)
+        return fail(MV_ERR_INVALID_ARGUMENT, "context length must be positive");
+    if (!(scale == scale) || scale == INFINITY || scale == -INFINITY)
+        return fail(MV_ERR_INVALID_ARGUMENT, "scale must be finite");
+    const ContiguousCall c{k_cache, {k_stride_seq, k_stride_head, k_stride_token},
+                           v_cache, {v_stride_seq, v_stride_head, v_stride_token}, cache_len};
+    Plan plan;
+    rc = contiguous_plan(c, batch, num_q_heads, num_kv_heads, head_dim, max_context_len, pages_per_split, flags,
+                         dtype, &plan);
+    if (rc != MV_OK) return rc;
+    if (plan.workspace > 0 && (!workspace || workspace_bytes < plan.workspace))
+        return fail(MV_ERR_WORKSPACE_TOO_SMALL, "workspace of %zu bytes needed, %zu given", plan.workspace,
+                    workspace ? workspace_bytes : static_cast<size_t>(0));
+    if (plan.workspace > 0 && reinterpret_cast<uintptr_t>(workspace) % 16)
+        return fail(MV_ERR_INVALID_ARGUMENT, "workspace must be 16-byte aligned");
+
+    const int64_t bound = std::min(max_context_len, cache_len);
+    const int64_t runs = (cache_len + 15) / 16;  // 16-token runs stand in for pages
+    mv::DecodeParams p;
+    std::memset(&p, 0, sizeof(p));
+    p.q = q;
+    p.q_stride_seq = q_stride_seq;
+    p.q_stride_head = q_stride_head;
+    p.k_cache = k_cache;
+    p.v_cache = v_cache;
+    p.num_blocks = runs;
+    p.kv_heads = num_kv_heads;
+    p.block_size = 16;
+    p.head_dim = head_dim;
+    p.group = num_q_heads / num_kv_heads;
+    p.q_heads = num_q_heads;
+    p.batch = batch;
+    p.block_table = nullptr;
+    p.blocks_per_seq = runs;
+    p.context_lens = context_lens;
+    p.lens_i64 = context_lens_type == MV_INDEX_I64;
+    p.uniform_len = bound;
+    p.max_context_len = bound;
+    p.scale_log2 = scale * 1.4426950408889634f;
+    p.out = out;
+    p.out_stride_seq = out_stride_seq;
+    p.out_stride_head = out_stride_head;
+    p.pages_per_split = plan.pages_per_split;
+    p.max_splits = plan.max_splits;
+    p.fused_merge = plan.fused_merge ? 1 : 0;
+    p.contiguous = 1;
+    for (int i = 0; i < 3; ++i) {
+        p.k_stride[i] = c.k_stride[i];
+        p.v_stride[i] = c.v_stride[i];
+    }
+    if (plan.workspace > 0) {
+        uint8_t* base = static_cast<uint8_t*>(workspace);
+        if (plan.fused_merge) p.counters = reinterpret_cast<unsigned*>(base);
+        base += plan.counter_bytes;
+        p.part_o = reinterpret_cast<float*>(base);
+        p.part_lse = reinterpret_cast<float*>(base + plan.part_o_bytes);
+    }
+    CUtensorMap kmap, vmap;
+    if (plan.path == MV_PATH_TMA_MMA) {
+        int64_t ks[3], vs[3];
+        contiguous_map_strides(c.k_stride, num_kv_heads, batch, cache_len, ks);
+        contiguous_map_strides(c.v_stride, num_kv_heads, batch, cache_len, vs);
+        rc = contiguous_tensor_map(k_cache, cache_len, num_kv_heads, batch, head_dim, ks, dtype, &kmap);
+        if (rc == MV_OK) rc = contiguous_tensor_map(v_cache, cache_len, num_kv_heads, batch, head_dim, vs, dtype, &vmap);
+        if (rc != MV_OK) return rc;
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    switch (dtype) {
+        case MV_DTYPE_F32: return launch_decode<float>(p, plan, &kmap, &vmap, s);
+        case MV_DTYPE_F16: return launch_decode<__half>(p, plan, &kmap, &vmap, s);
+        default: return launch_decode<__nv_bfloat16>(p, plan, &kmap, &vmap, s);
+    }
 }
 
 int mv_write_paged_kv(const void* key, int64_t key_stride_seq, int64_t key_stride_head,

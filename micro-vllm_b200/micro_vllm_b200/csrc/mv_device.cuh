@@ -65,6 +65,13 @@ struct DecodeParams {
     const void* rope_cos;
     const void* rope_sin;
     int64_t rope_rows;
+    // Contiguous caches (no block table; block_table is nullptr): token t of
+    // KV head h of sequence b at k_cache + b*k_stride[0] + h*k_stride[1] +
+    // t*k_stride[2] (V likewise with v_stride); "pages" are runs of
+    // block_size tokens, and max_context_len never exceeds the cache length.
+    int contiguous;
+    int64_t k_stride[3];
+    int64_t v_stride[3];
 };
 
 struct AppendParams {

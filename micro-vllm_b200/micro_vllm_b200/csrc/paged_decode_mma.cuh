@@ -379,9 +379,10 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
     long long my_id = 0;
     bool bad = false;
     if (lane < n_my) {
-        my_id = load_index(p.block_table, p.table_i64,
-                           b * p.table_stride + page_begin + warp + lane * NWARPS);
-        bad = my_id < 0 || my_id >= p.num_blocks;
+        const int64_t page = page_begin + warp + lane * NWARPS;
+        // A contiguous cache's "page" is a run of 16 tokens: its index is its ID.
+        my_id = p.contiguous ? page : load_index(p.block_table, p.table_i64, b * p.table_stride + page);
+        bad = !p.contiguous && (my_id < 0 || my_id >= p.num_blocks);
     }
     const bool warp_has_bad = __any_sync(0xffffffffu, bad) || rope_missing;
     const uint32_t bar0 = smem_addr(&bars[warp][0]);
@@ -405,8 +406,14 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
             if (ok) {
                 const uint32_t dst = wsm_addr + st * Shape::kStageBytes;
                 mbar_arrive_expect_tx(bar, Shape::kStageBytes);
-                tma_load_5d(dst, &kmap, 0, 0, 0, h, static_cast<int>(id), bar);
-                tma_load_5d(dst + Shape::kTileBytes, &vmap, 0, 0, 0, h, static_cast<int>(id), bar);
+                if (p.contiguous) {
+                    // Map (d%64, token, d/64, head, sequence): tokens past the cache read as 0.
+                    tma_load_5d(dst, &kmap, 0, static_cast<int>(id) * kPageTokens, 0, h, b, bar);
+                    tma_load_5d(dst + Shape::kTileBytes, &vmap, 0, static_cast<int>(id) * kPageTokens, 0, h, b, bar);
+                } else {
+                    tma_load_5d(dst, &kmap, 0, 0, 0, h, static_cast<int>(id), bar);
+                    tma_load_5d(dst + Shape::kTileBytes, &vmap, 0, 0, 0, h, static_cast<int>(id), bar);
+                }
             } else {
                 // No load for a corrupted ID; complete the phase so the ring stays in step.
                 asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");

@@ -28,7 +28,7 @@ __host__ __device__ inline size_t simt_smem_bytes(int group, int head_dim) {
                           + group * kSimtTile              // scores, then weights
                           + static_cast<size_t>(group) * head_dim  // running output
                           + 3 * static_cast<size_t>(group);         // m, l, rescale
-    return ((floats * 4 + 15) / 16) * 16 + kSimtTile * sizeof(int64_t);
+    return ((floats * 4 + 15) / 16) * 16 + 2 * kSimtTile * sizeof(int64_t);
 }
 
 template <typename T>
@@ -48,7 +48,8 @@ __global__ void __launch_bounds__(kSimtThreads) paged_decode_simt_kernel(const D
     float* l_s = m_s + G;
     float* r_s = l_s + G;
     int64_t* off_s = reinterpret_cast<int64_t*>(
-        reinterpret_cast<uint8_t*>(sm) + simt_smem_bytes(G, D) - kSimtTile * sizeof(int64_t));
+        reinterpret_cast<uint8_t*>(sm) + simt_smem_bytes(G, D) - 2 * kSimtTile * sizeof(int64_t));
+    int64_t* voff_s = off_s + kSimtTile;  // V offsets (contiguous caches; paged K and V share offsets)
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
@@ -71,7 +72,7 @@ __global__ void __launch_bounds__(kSimtThreads) paged_decode_simt_kernel(const D
 
     if (tid == 0) cta_bad = 0;
     __syncthreads();
-    for (int64_t pg = page_begin + tid; pg < page_end; pg += blockDim.x) {
+    for (int64_t pg = page_begin + tid; !p.contiguous && pg < page_end; pg += blockDim.x) {
         const int64_t id = load_index(p.block_table, p.table_i64, b * p.table_stride + pg);
         if (id < 0 || id >= p.num_blocks) atomicOr(&cta_bad, 1);
     }
@@ -104,16 +105,21 @@ __global__ void __launch_bounds__(kSimtThreads) paged_decode_simt_kernel(const D
         const int count = static_cast<int>(tok_end - t0 < kSimtTile ? tok_end - t0 : kSimtTile);
         if (tid < count) {
             const int64_t tok = t0 + tid;
-            const int64_t pg = tok / bs;
-            const int64_t id = load_index(p.block_table, p.table_i64, b * p.table_stride + pg);
-            off_s[tid] = ((id * p.kv_heads + h) * bs + (tok - pg * bs)) * D;
+            if (p.contiguous) {
+                off_s[tid] = b * p.k_stride[0] + h * p.k_stride[1] + tok * p.k_stride[2];
+                voff_s[tid] = b * p.v_stride[0] + h * p.v_stride[1] + tok * p.v_stride[2];
+            } else {
+                const int64_t pg = tok / bs;
+                const int64_t id = load_index(p.block_table, p.table_i64, b * p.table_stride + pg);
+                off_s[tid] = voff_s[tid] = ((id * p.kv_heads + h) * bs + (tok - pg * bs)) * D;
+            }
         }
         __syncthreads();
         for (int idx = tid; idx < count * D; idx += blockDim.x) {
             const int t = idx / D;
             const int d = idx - t * D;
             k_s[t * DP + d] = to_float<T>(kc[off_s[t] + d]);
-            v_s[t * DP + d] = to_float<T>(vc[off_s[t] + d]);
+            v_s[t * DP + d] = to_float<T>(vc[voff_s[t] + d]);
         }
         __syncthreads();
         for (int idx = tid; idx < G * kSimtTile; idx += blockDim.x) {

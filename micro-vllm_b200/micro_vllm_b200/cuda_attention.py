@@ -54,6 +54,26 @@ def _validate_gqa_strides(tensor):
     _check(all(tensor.stride(d) >= 0 for d in range(3)), 'GQA requires nonnegative outer strides')
 
 
+def _validate_gqa_inputs(query, key, value):
+    """decode_attention.cpp:61-82, same order and messages."""
+    for tensor in (query, key, value):
+        _validate_gqa_tensor(tensor)
+    _check(query.dtype == key.dtype == value.dtype, 'Q, K, V must use the same dtype')
+    _check(query.device == key.device == value.device, 'Q, K, V must use the same device')
+    _check(query.dim() == 4 and key.dim() == 4 and value.dim() == 4,
+           'Q must have shape [1,Hq,1,D] and K/V must have shape [1,Hkv,L,D]')
+    for tensor in (query, key, value):
+        _validate_gqa_strides(tensor)
+    _check(query.shape[0] == 1 and key.shape[0] == 1 and value.shape[0] == 1,
+           'GQA currently requires batch size 1')
+    _check(query.numel() > 0 and key.numel() > 0 and value.numel() > 0,
+           'head counts, context length, and head dimension must be positive')
+    _check(query.shape[2] == 1, 'GQA decode requires exactly one query token')
+    _check(key.shape == value.shape, 'K and V must have the same shape')
+    _check(query.shape[3] == key.shape[3], 'Q and K/V must share the head dimension')
+    _check(query.shape[1] % key.shape[1] == 0, 'query head count must be divisible by KV head count')
+
+
 def _validate_paged_table(table, key, query, length):
     _validate_storage(table)
     _check(table.dtype == torch.int64, 'page table requires int64')
@@ -142,6 +162,36 @@ def _run(query3, q_strides, key_cache, value_cache, block_table, table_stride, b
             pages_per_split, flags, dtype, stream))
 
 
+def _run_contiguous(q3, q_strides, key, value, context_lens, bound, scale, out, out_strides,
+                    pages_per_split=0, flags=0):
+    """Plan, allocate the split-KV workspace, and launch ``mv_contiguous_decode``.
+    key/value: [B, Hkv, L, D] views (any nonnegative outer strides)."""
+    lib = _native.library()
+    batch, q_heads, dim = q3
+    kv_heads, cache_len = key.shape[1], key.shape[2]
+    dtype = DTYPE_CODES[key.dtype]
+    device = key.device
+    ks = (key.stride(0), key.stride(1), key.stride(2))
+    vs = (value.stride(0), value.stride(1), value.stride(2))
+    with torch.cuda.device(device):
+        path, pps, splits = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
+        size = ctypes.c_size_t(0)
+        _native.check(lib.mv_contiguous_decode_plan(
+            key.data_ptr(), *ks, value.data_ptr(), *vs, cache_len, kv_heads, dim, bound, batch, q_heads,
+            pages_per_split, flags, dtype, ctypes.byref(path), ctypes.byref(pps), ctypes.byref(splits),
+            ctypes.byref(size)))
+        stream = current_stream_handle(device)
+        workspace = _workspace(device, stream, size.value) if size.value else None
+        _native.check(lib.mv_contiguous_decode(
+            out.q_ptr, q_strides[0], q_strides[1], key.data_ptr(), *ks, value.data_ptr(), *vs, cache_len,
+            kv_heads, dim, context_lens.data_ptr() if context_lens is not None else None,
+            INDEX_CODES[context_lens.dtype] if context_lens is not None else 0, bound, batch, q_heads,
+            float(scale), out.out_ptr, out_strides[0], out_strides[1],
+            workspace.data_ptr() if workspace is not None else None,
+            workspace.numel() if workspace is not None else 0, pages_per_split, flags, dtype, stream))
+    return _native.PATH_NAMES[path.value], pps.value, splits.value
+
+
 class _Pointers:
     __slots__ = ('q_ptr', 'out_ptr')
 
@@ -153,6 +203,15 @@ class _Pointers:
 class _DecodeAttentionExtension:
     """The object ``_load_extension()`` returns, shaped like the reference's pybind module."""
 
+    def decode_attention_gqa(self, query, key, value):
+        """Q [1,Hq,1,D] over contiguous K/V [1,Hkv,L,D] (any nonnegative outer strides); fresh output."""
+        _validate_gqa_inputs(query, key, value)
+        output = torch.empty(query.shape, dtype=query.dtype, device=query.device)
+        _run_contiguous((1, query.shape[1], query.shape[3]), (0, query.stride(1)), key, value, None,
+                        key.shape[2], query.shape[3] ** -0.5, _Pointers(query.data_ptr(), output.data_ptr()),
+                        (0, output.stride(1)))
+        return output
+
     def _decode_attention_paged(self, query, key_pages, value_pages, table, length):
         """Internal paged decode for Q [1,Hq,1,D] over pages [P,Hkv,B,D]; fresh output."""
         _validate_paged_inputs(query, key_pages, value_pages, table, length)
@@ -162,6 +221,18 @@ class _DecodeAttentionExtension:
              query.shape[3] ** -0.5, _Pointers(query.data_ptr(), output.data_ptr()),
              (0, output.stride(1)))
         return output
+
+
+def decode_attention_gqa(query: torch.Tensor, key: torch.Tensor, value: torch.Tensor) -> torch.Tensor:
+    """Online decode for Q [1,Hq,1,D] and original K/V [1,Hkv,L,D] (cuda_attention.py:63-83).
+
+    Consecutive groups of Hq/Hkv query heads share each KV head; all L
+    positions are attended; feature stride 1 and any nonnegative outer
+    strides (cache-prefix views, zero-stride broadcasts) are read in place.
+    float32/float16 in, fp32 accumulation, fresh contiguous output of Q's
+    shape and dtype. Runs libmvdecode.so's contiguous-cache decode.
+    """
+    return _load_extension().decode_attention_gqa(query, key, value)
 
 
 @lru_cache(maxsize=1)
@@ -554,3 +625,72 @@ class PagedDecodeStep:
             q.data_ptr(), q.stride(0), q.stride(1), key.data_ptr(), key.stride(0), key.stride(1),
             value.data_ptr(), value.stride(0), value.stride(1), *tables, *self._pool_args, *tail))
         return out
+
+
+def contiguous_decode_attention(query: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
+                                context_lens: torch.Tensor | None = None, scale: float | None = None, *,
+                                max_context_len: int | None = None, out: torch.Tensor | None = None,
+                                pages_per_split: int = 0, force_simt: bool = False,
+                                wide: bool = False) -> torch.Tensor:
+    """Batched GQA decode over contiguous caches (the batched form of ``decode_attention_gqa``).
+
+    query: [B, Hq, D] or [B, Hq, 1, D]; key_cache/value_cache: [B, Hkv, L, D]
+    views with feature stride 1 and any nonnegative outer strides (e.g. the
+    prefix of a larger cache buffer); context_lens: optional [B] int32/int64
+    device lengths (<= L), else every sequence attends max_context_len
+    (default L) tokens. fp32/fp16/bf16. Returns out ([B, Hq, D]).
+    """
+    squeeze = query.dim() == 4
+    q = query[:, :, 0, :] if squeeze else query
+    _check(isinstance(q, torch.Tensor) and q.dim() == 3, 'query must be [B, Hq, D] or [B, Hq, 1, D]')
+    for tensor in (q, key_cache, value_cache) + ((context_lens,) if context_lens is not None else ()):
+        _validate_storage(tensor)
+    _check(q.dtype in DTYPE_CODES and q.dtype == key_cache.dtype == value_cache.dtype,
+           'Q and K/V caches must share a float32, float16 or bfloat16 dtype')
+    _check(q.device == key_cache.device == value_cache.device, 'Q and K/V caches must use the same device')
+    _check(key_cache.dim() == 4 and key_cache.shape == value_cache.shape,
+           'K/V caches must both have shape [B,Hkv,L,D]')
+    batch, q_heads, dim = q.shape
+    _check(key_cache.shape[0] == batch and key_cache.shape[3] == dim and batch > 0 and q_heads > 0
+           and key_cache.numel() > 0, 'K/V caches must match the query batch and head dimension')
+    _check(q_heads % key_cache.shape[1] == 0, 'query head count must be divisible by KV head count')
+    for tensor in (q, key_cache, value_cache):
+        _check(tensor.stride(-1) == 1 and all(tensor.stride(d) >= 0 for d in range(tensor.dim() - 1)),
+               'tensors require feature stride 1 and nonnegative outer strides')
+    if context_lens is not None:
+        _check(context_lens.dtype in INDEX_CODES and context_lens.shape == (batch,)
+               and context_lens.is_contiguous() and context_lens.device == q.device,
+               'context lengths must be a contiguous [B] int32/int64 tensor on the query device')
+    cache_len = key_cache.shape[2]
+    bound = cache_len if max_context_len is None else int(max_context_len)
+    _check(bound >= 0, 'max_context_len must be nonnegative')
+    if scale is None:
+        scale = dim ** -0.5
+    if out is None:
+        out = torch.empty((batch, q_heads, dim), dtype=q.dtype, device=q.device)
+    else:
+        _validate_storage(out)
+        _check(out.shape == (batch, q_heads, dim) and out.dtype == q.dtype and out.device == q.device
+               and out.stride(2) == 1, 'out must be a [B, Hq, D] tensor of the query dtype and device')
+    _run_contiguous((batch, q_heads, dim), (q.stride(0), q.stride(1)), key_cache, value_cache, context_lens,
+                    bound, scale, _Pointers(q.data_ptr(), out.data_ptr()), (out.stride(0), out.stride(1)),
+                    pages_per_split=int(pages_per_split), flags=_flags(force_simt, False, wide=wide))
+    return out
+
+
+def contiguous_decode_plan(key_cache, value_cache, query_heads, *, max_context_len=None, pages_per_split=0,
+                           force_simt=False, wide=False):
+    """(path, pages_per_split, max_splits) that ``contiguous_decode_attention`` would use."""
+    lib = _native.library()
+    batch, kv_heads, cache_len, dim = key_cache.shape
+    bound = cache_len if max_context_len is None else int(max_context_len)
+    path, pps, splits = ctypes.c_int32(), ctypes.c_int32(), ctypes.c_int32()
+    size = ctypes.c_size_t(0)
+    with torch.cuda.device(key_cache.device):
+        _native.check(lib.mv_contiguous_decode_plan(
+            key_cache.data_ptr(), key_cache.stride(0), key_cache.stride(1), key_cache.stride(2),
+            value_cache.data_ptr(), value_cache.stride(0), value_cache.stride(1), value_cache.stride(2),
+            cache_len, kv_heads, dim, bound, batch, query_heads, pages_per_split,
+            _flags(force_simt, False, wide=wide), DTYPE_CODES[key_cache.dtype], ctypes.byref(path),
+            ctypes.byref(pps), ctypes.byref(splits), ctypes.byref(size)))
+    return _native.PATH_NAMES[path.value], pps.value, splits.value
