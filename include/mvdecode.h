@@ -132,6 +132,35 @@ MV_API int mv_paged_decode(const void* q, int64_t q_stride_seq, int64_t q_stride
                     uint32_t flags, int32_t dtype, void* stream);
 
 /*
+ * Attention of a chunk of num_tokens new tokens per sequence over its pages:
+ * query token t of sequence b (q[b, t], [batch, num_tokens, num_q_heads,
+ * head_dim] with the given element strides) attends the first
+ * context_lens[b] - (num_tokens - 1 - t) tokens -- its causal prefix, the
+ * chunk's own earlier tokens included; context_lens counts the tokens after
+ * the chunk, whose K/V must already be in the pages (mv_write_paged_kv).
+ *
+ * Replaces the reference's cached multi-token path, which gathers the pages
+ * into contiguous K/V and runs causal attention
+ * (src/micro_vllm/model.py:178-182, paged_kv_cache.py:178-193,
+ * attention.py:57-94). Runs the split grid or the CUDA-core kernel with one
+ * query row per (sequence, token): each row reads its own prefix, so this
+ * suits short chunks. Workspace: mv_paged_decode_workspace_size with
+ * batch x num_tokens rows. Other contracts as mv_paged_decode.
+ */
+MV_API int mv_paged_chunk_attention(const void* q, int64_t q_stride_seq, int64_t q_stride_token,
+                                    int64_t q_stride_head, const void* k_cache, const void* v_cache,
+                                    int64_t num_blocks, int32_t num_kv_heads, int32_t block_size,
+                                    int32_t head_dim, const void* block_table,
+                                    int32_t block_table_type, int64_t block_table_stride,
+                                    int64_t blocks_per_seq, const void* context_lens,
+                                    int32_t context_lens_type, int64_t max_context_len,
+                                    int32_t batch, int32_t num_tokens, int32_t num_q_heads,
+                                    float scale, void* out, int64_t out_stride_seq,
+                                    int64_t out_stride_token, int64_t out_stride_head,
+                                    void* workspace, size_t workspace_bytes, int32_t pages_per_split,
+                                    uint32_t flags, int32_t dtype, void* stream);
+
+/*
  * GQA decode over contiguous caches: for every sequence b and query head j,
  *   out[b, j] = softmax(scale * K_b q[b, j]) V_b
  * over the first context_lens[b] tokens (all sequences: max_context_len when

@@ -39,6 +39,7 @@ EXPORTED_SYMBOLS = (
     'mv_paged_decode_plan', 'mv_paged_decode', 'mv_write_paged_kv',
     'mv_device_status', 'mv_clear_device_status', 'mv_paged_decode_append', 'mv_apply_rope',
     'mv_rms_norm', 'mv_silu_mul', 'mv_contiguous_decode_plan', 'mv_contiguous_decode',
+    'mv_paged_chunk_attention',
 )
 
 _i32, _i64, _u32, _vp, _sz, _f32 = (ctypes.c_int32, ctypes.c_int64, ctypes.c_uint32,
@@ -90,6 +91,15 @@ _SIGNATURES = {
                        _vp, _i32, _i32, _i64,      # positions, type, kind, start
                        _i32, _vp]),                # dtype, stream
     'mv_rms_norm': (ctypes.c_int, [_vp, _i64, _vp, _vp, _i64, _i64, _i32, _f32, _i32, _vp]),
+    'mv_paged_chunk_attention': (
+        ctypes.c_int, [_vp, _i64, _i64, _i64,      # q, strides (sequence, token, head)
+                       _vp, _vp, _i64,             # k_cache, v_cache, num_blocks
+                       _i32, _i32, _i32,           # kv heads, block size, head dim
+                       _vp, _i32, _i64, _i64,      # block table, type, stride, blocks/seq
+                       _vp, _i32, _i64,            # context lens, type, max context len
+                       _i32, _i32, _i32, _f32,     # batch, tokens, q heads, scale
+                       _vp, _i64, _i64, _i64,      # out, strides (sequence, token, head)
+                       _vp, _sz, _i32, _u32, _i32, _vp]),  # workspace, bytes, pps, flags, dtype, stream
     'mv_contiguous_decode_plan': (
         ctypes.c_int, [_vp, _i64, _i64, _i64,      # k_cache, strides (sequence, head, token)
                        _vp, _i64, _i64, _i64,      # v_cache, strides

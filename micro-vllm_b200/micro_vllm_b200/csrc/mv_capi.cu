@@ -712,6 +712,13 @@ int mv_paged_decode_plan(int32_t batch, int32_t num_q_heads, int32_t num_kv_head
 }
 
 // This step's new K/V rows for mv_paged_decode_append ([batch, kv_heads], feature stride 1).
+// A chunk of several new tokens per sequence (rows = batch x num_tokens).
+struct ChunkRows {
+    int32_t num_tokens;
+    int64_t q_stride_token;
+    int64_t out_stride_token;
+};
+
 struct NewRows {
     const void* key;
     int64_t key_stride_seq;
@@ -732,7 +739,7 @@ static int paged_decode_impl(const void* q, int64_t q_stride_seq, int64_t q_stri
                     int32_t num_q_heads, float scale, void* out, int64_t out_stride_seq,
                     int64_t out_stride_head, void* workspace, size_t workspace_bytes,
                     int32_t pages_per_split, uint32_t flags, int32_t dtype, void* stream,
-                             const NewRows* rows) {
+                             const NewRows* rows, const ChunkRows* chunk = nullptr) {
     if (!q || !k_cache || !v_cache || !block_table || !out)
         return fail(MV_ERR_INVALID_ARGUMENT, "q, k_cache, v_cache, block_table and out must not be NULL");
     if (num_blocks <= 0 || blocks_per_seq <= 0)
@@ -741,7 +748,9 @@ static int paged_decode_impl(const void* q, int64_t q_stride_seq, int64_t q_stri
     if (q_stride_seq < 0 || q_stride_head < 0 || out_stride_seq < 0 || out_stride_head < 0 ||
         block_table_stride < 0)
         return fail(MV_ERR_INVALID_ARGUMENT, "strides must be nonnegative");
-    if (batch > 1 && block_table_stride < blocks_per_seq)
+    const int32_t tokens = chunk ? chunk->num_tokens : 1;
+    const int32_t sequences = batch / tokens;  // `batch` counts query rows
+    if (sequences > 1 && block_table_stride < blocks_per_seq)
         return fail(MV_ERR_INVALID_ARGUMENT, "block_table_stride is smaller than blocks_per_seq");
     int rc = check_index_type(block_table_type, "block_table");
     if (rc == MV_OK && context_lens) rc = check_index_type(context_lens_type, "context_lens");
@@ -813,6 +822,9 @@ static int paged_decode_impl(const void* q, int64_t q_stride_seq, int64_t q_stri
     p.rope_rows = 0;
     p.contiguous = 0;
     for (int i = 0; i < 3; ++i) p.k_stride[i] = p.v_stride[i] = 0;
+    p.q_tokens = tokens;
+    p.q_stride_token = chunk ? chunk->q_stride_token : 0;
+    p.out_stride_token = chunk ? chunk->out_stride_token : 0;
     if (rows) {
         // The split-grid tensor-core kernel writes the rows itself (16-byte
         // chunks); every other plan runs the append kernel first, as two launches.
@@ -903,6 +915,30 @@ int mv_paged_decode_append(const void* q, int64_t q_stride_seq, int64_t q_stride
                              blocks_per_seq, context_lens, context_lens_type, max_context_len, batch,
                              num_q_heads, scale, out, out_stride_seq, out_stride_head, workspace,
                              workspace_bytes, pages_per_split, flags, dtype, stream, &rows);
+}
+
+int mv_paged_chunk_attention(const void* q, int64_t q_stride_seq, int64_t q_stride_token, int64_t q_stride_head,
+                             const void* k_cache, const void* v_cache, int64_t num_blocks, int32_t num_kv_heads,
+                             int32_t block_size, int32_t head_dim, const void* block_table,
+                             int32_t block_table_type, int64_t block_table_stride, int64_t blocks_per_seq,
+                             const void* context_lens, int32_t context_lens_type, int64_t max_context_len,
+                             int32_t batch, int32_t num_tokens, int32_t num_q_heads, float scale, void* out,
+                             int64_t out_stride_seq, int64_t out_stride_token, int64_t out_stride_head,
+                             void* workspace, size_t workspace_bytes, int32_t pages_per_split, uint32_t flags,
+                             int32_t dtype, void* stream) {
+    if (num_tokens <= 0 || batch <= 0) return fail(MV_ERR_INVALID_ARGUMENT, "batch and num_tokens must be positive");
+    if (static_cast<int64_t>(batch) * num_tokens > 65535)
+        return fail(MV_ERR_UNSUPPORTED, "batch x num_tokens is limited to 65535 query rows");
+    if (q_stride_token < 0 || out_stride_token < 0) return fail(MV_ERR_INVALID_ARGUMENT, "strides must be nonnegative");
+    const ChunkRows chunk{num_tokens, q_stride_token, out_stride_token};
+    // The split grid and the CUDA-core kernel take query rows; the persistent
+    // and cluster schedules do not.
+    return paged_decode_impl(q, q_stride_seq, q_stride_head, k_cache, v_cache, num_blocks, num_kv_heads, block_size,
+                             head_dim, block_table, block_table_type, block_table_stride, blocks_per_seq,
+                             context_lens, context_lens_type, max_context_len, batch * num_tokens, num_q_heads,
+                             scale, out, out_stride_seq, out_stride_head, workspace, workspace_bytes,
+                             pages_per_split, flags & ~(MV_FLAG_PERSISTENT | MV_FLAG_CLUSTER), dtype, stream, nullptr,
+                             &chunk);
 }
 
 int mv_contiguous_decode_plan(const void* k_cache, int64_t k_stride_seq, int64_t k_stride_head,

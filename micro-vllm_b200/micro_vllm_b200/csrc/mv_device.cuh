@@ -72,6 +72,14 @@ struct DecodeParams {
     int contiguous;
     int64_t k_stride[3];
     int64_t v_stride[3];
+    // Query rows: `batch` counts rows, and row z is token t = z % q_tokens of
+    // sequence z / q_tokens (a chunk of q_tokens new tokens per sequence; 1
+    // for decode). Row t attends the first len - (q_tokens - 1 - t) tokens,
+    // len being the sequence's length after the chunk; q and out of row z at
+    // seq * *_stride_seq + t * *_stride_token.
+    int q_tokens;
+    int64_t q_stride_token;
+    int64_t out_stride_token;
 };
 
 struct AppendParams {
@@ -103,7 +111,23 @@ __device__ __forceinline__ int64_t load_index(const void* base, int is64, int64_
                 : static_cast<int64_t>(__ldg(static_cast<const int*>(base) + i));
 }
 
-// How one sequence is cut into split-KV chunks of pages_per_split pages.
+__device__ __forceinline__ int64_t row_seq(const DecodeParams& p, int64_t z) {
+    return p.q_tokens > 1 ? z / p.q_tokens : z;
+}
+
+__device__ __forceinline__ int64_t row_q_offset(const DecodeParams& p, int64_t z) {
+    if (p.q_tokens <= 1) return z * p.q_stride_seq;
+    const int64_t b = z / p.q_tokens;
+    return b * p.q_stride_seq + (z - b * p.q_tokens) * p.q_stride_token;
+}
+
+__device__ __forceinline__ int64_t row_out_offset(const DecodeParams& p, int64_t z) {
+    if (p.q_tokens <= 1) return z * p.out_stride_seq;
+    const int64_t b = z / p.q_tokens;
+    return b * p.out_stride_seq + (z - b * p.q_tokens) * p.out_stride_token;
+}
+
+// How one query row's context is cut into split-KV chunks of pages_per_split pages.
 struct SeqSplit {
     int64_t len;
     int64_t pages;
@@ -113,7 +137,9 @@ struct SeqSplit {
 
 __device__ __forceinline__ SeqSplit seq_split(const DecodeParams& p, int b) {
     SeqSplit s;
-    s.len = p.context_lens ? load_index(p.context_lens, p.lens_i64, b) : p.uniform_len;
+    const int64_t seq = row_seq(p, b);
+    s.len = p.context_lens ? load_index(p.context_lens, p.lens_i64, seq) : p.uniform_len;
+    if (p.q_tokens > 1) s.len -= p.q_tokens - 1 - (b - seq * p.q_tokens);  // causal within the chunk
     const bool in_range = s.len >= 0 && s.len <= p.max_context_len &&
                           s.len <= p.blocks_per_seq * p.block_size;
     if (!in_range) {
@@ -190,8 +216,7 @@ __device__ void write_group_constant(const DecodeParams& p, int b, int h, float 
     for (int idx = threadIdx.x; idx < total; idx += blockDim.x) {
         const int g = idx / p.head_dim;
         const int d = idx - g * p.head_dim;
-        out[b * p.out_stride_seq + (int64_t)(h * p.group + g) * p.out_stride_head + d] =
-            from_float<T>(value);
+        out[row_out_offset(p, b) + (int64_t)(h * p.group + g) * p.out_stride_head + d] = from_float<T>(value);
     }
 }
 

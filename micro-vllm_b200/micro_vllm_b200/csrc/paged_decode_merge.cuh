@@ -143,7 +143,7 @@ __device__ void merge_segment(const DecodeParams& p, int b, int h, int n, float*
     __syncthreads();
     // Each thread owns a column and walks the rows four at a time, so the loads
     // of four rows x several splits are in flight together.
-    T* out = static_cast<T*>(p.out) + b * p.out_stride_seq;
+    T* out = static_cast<T*>(p.out) + row_out_offset(p, b);
     for (int d = threadIdx.x; d < D; d += blockDim.x) {
         for (int g0 = 0; g0 < G; g0 += 4) {
             float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
@@ -178,7 +178,7 @@ __global__ void __launch_bounds__(kMergeThreads) paged_decode_merge_kernel(const
     const int b = blockIdx.y;
     const SeqSplit seq = seq_split(p, b);
     if (seq.splits <= 1) return;
-    T* out = static_cast<T*>(p.out) + b * p.out_stride_seq + static_cast<int64_t>(hq) * p.out_stride_head;
+    T* out = static_cast<T*>(p.out) + row_out_offset(p, b) + static_cast<int64_t>(hq) * p.out_stride_head;
     const int64_t base = (static_cast<int64_t>(b) * p.q_heads + hq) * p.max_splits;
     merge_row<T>(p, out, [&](int j) -> long long { return base + j; }, seq.splits);
 }

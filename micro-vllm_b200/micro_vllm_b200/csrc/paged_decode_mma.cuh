@@ -76,7 +76,7 @@ struct WarpPageAttention {
 
     // Lane holds q[g][16 ks + 2(lane%4) + {0,1,8,9}] for g = nt*8 + lane/4 (0 beyond the group).
     __device__ __forceinline__ void load_q(const DecodeParams& p, int b, int h, int lane) {
-        const uint16_t* qbase = static_cast<const uint16_t*>(p.q) + b * p.q_stride_seq;
+        const uint16_t* qbase = static_cast<const uint16_t*>(p.q) + row_q_offset(p, b);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
             const int g = nt * 8 + (lane >> 2);
@@ -381,7 +381,8 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
     if (lane < n_my) {
         const int64_t page = page_begin + warp + lane * NWARPS;
         // A contiguous cache's "page" is a run of 16 tokens: its index is its ID.
-        my_id = p.contiguous ? page : load_index(p.block_table, p.table_i64, b * p.table_stride + page);
+        my_id = p.contiguous ? page
+                             : load_index(p.block_table, p.table_i64, row_seq(p, b) * p.table_stride + page);
         bad = !p.contiguous && (my_id < 0 || my_id >= p.num_blocks);
     }
     const bool warp_has_bad = __any_sync(0xffffffffu, bad) || rope_missing;
@@ -408,8 +409,9 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
                 mbar_arrive_expect_tx(bar, Shape::kStageBytes);
                 if (p.contiguous) {
                     // Map (d%64, token, d/64, head, sequence): tokens past the cache read as 0.
-                    tma_load_5d(dst, &kmap, 0, static_cast<int>(id) * kPageTokens, 0, h, b, bar);
-                    tma_load_5d(dst + Shape::kTileBytes, &vmap, 0, static_cast<int>(id) * kPageTokens, 0, h, b, bar);
+                    const int seq = static_cast<int>(row_seq(p, b));
+                    tma_load_5d(dst, &kmap, 0, static_cast<int>(id) * kPageTokens, 0, h, seq, bar);
+                    tma_load_5d(dst + Shape::kTileBytes, &vmap, 0, static_cast<int>(id) * kPageTokens, 0, h, seq, bar);
                 } else {
                     tma_load_5d(dst, &kmap, 0, 0, 0, h, static_cast<int>(id), bar);
                     tma_load_5d(dst + Shape::kTileBytes, &vmap, 0, 0, 0, h, static_cast<int>(id), bar);
@@ -600,7 +602,7 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
         }
         const float value = num / den;
         if (single) {
-            out[b * p.out_stride_seq + static_cast<int64_t>(h * p.group + g) * p.out_stride_head + d] =
+            out[row_out_offset(p, b) + static_cast<int64_t>(h * p.group + g) * p.out_stride_head + d] =
                 from_float<T>(value);
         } else {
             const int64_t row = (static_cast<int64_t>(b) * p.q_heads + h * p.group + g) * p.max_splits + split;

@@ -72,8 +72,9 @@ __global__ void __launch_bounds__(kSimtThreads) paged_decode_simt_kernel(const D
 
     if (tid == 0) cta_bad = 0;
     __syncthreads();
+    const int64_t seq_row = row_seq(p, b);  // the sequence this query row belongs to
     for (int64_t pg = page_begin + tid; !p.contiguous && pg < page_end; pg += blockDim.x) {
-        const int64_t id = load_index(p.block_table, p.table_i64, b * p.table_stride + pg);
+        const int64_t id = load_index(p.block_table, p.table_i64, seq_row * p.table_stride + pg);
         if (id < 0 || id >= p.num_blocks) atomicOr(&cta_bad, 1);
     }
     __syncthreads();
@@ -83,7 +84,7 @@ __global__ void __launch_bounds__(kSimtThreads) paged_decode_simt_kernel(const D
         return;
     }
 
-    const T* q = static_cast<const T*>(p.q) + b * p.q_stride_seq;
+    const T* q = static_cast<const T*>(p.q) + row_q_offset(p, b);
     for (int idx = tid; idx < G * D; idx += blockDim.x) {
         const int g = idx / D;
         const int d = idx - g * D;
@@ -106,11 +107,11 @@ __global__ void __launch_bounds__(kSimtThreads) paged_decode_simt_kernel(const D
         if (tid < count) {
             const int64_t tok = t0 + tid;
             if (p.contiguous) {
-                off_s[tid] = b * p.k_stride[0] + h * p.k_stride[1] + tok * p.k_stride[2];
-                voff_s[tid] = b * p.v_stride[0] + h * p.v_stride[1] + tok * p.v_stride[2];
+                off_s[tid] = seq_row * p.k_stride[0] + h * p.k_stride[1] + tok * p.k_stride[2];
+                voff_s[tid] = seq_row * p.v_stride[0] + h * p.v_stride[1] + tok * p.v_stride[2];
             } else {
                 const int64_t pg = tok / bs;
-                const int64_t id = load_index(p.block_table, p.table_i64, b * p.table_stride + pg);
+                const int64_t id = load_index(p.block_table, p.table_i64, seq_row * p.table_stride + pg);
                 off_s[tid] = voff_s[tid] = ((id * p.kv_heads + h) * bs + (tok - pg * bs)) * D;
             }
         }
@@ -169,7 +170,7 @@ __global__ void __launch_bounds__(kSimtThreads) paged_decode_simt_kernel(const D
         const int g = idx / D;
         const int d = idx - g * D;
         if (single) {
-            out[b * p.out_stride_seq + static_cast<int64_t>(h * G + g) * p.out_stride_head + d] =
+            out[row_out_offset(p, b) + static_cast<int64_t>(h * G + g) * p.out_stride_head + d] =
                 from_float<T>(acc[idx]);
         } else {
             const int64_t row = (static_cast<int64_t>(b) * p.q_heads + h * G + g) * p.max_splits + split;

@@ -694,3 +694,51 @@ def contiguous_decode_plan(key_cache, value_cache, query_heads, *, max_context_l
             _flags(force_simt, False, wide=wide), DTYPE_CODES[key_cache.dtype], ctypes.byref(path),
             ctypes.byref(pps), ctypes.byref(splits), ctypes.byref(size)))
     return _native.PATH_NAMES[path.value], pps.value, splits.value
+
+
+def paged_chunk_attention(query: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
+                          block_table: torch.Tensor, context_lens: torch.Tensor, scale: float | None = None, *,
+                          max_context_len: int | None = None, out: torch.Tensor | None = None,
+                          pages_per_split: int = 0, force_simt: bool = False, wide: bool = False) -> torch.Tensor:
+    """Causal attention of a chunk of T new tokens per sequence over its pages.
+
+    query: [B, Hq, T, D] (the reference's layout for a cached chunk), feature
+    stride 1. The chunk's K/V must already be appended; context_lens [B]
+    counts each sequence's tokens after the chunk, and token t attends the
+    first context_lens - (T - 1 - t) of them (model.py:178-182 gathers the
+    pages and runs causal attention for this; nothing is gathered here).
+    Other arguments as ``paged_decode_attention``. Returns [B, Hq, T, D].
+    """
+    _check(isinstance(query, torch.Tensor) and query.dim() == 4, 'query must be [B, Hq, T, D]')
+    batch, q_heads, tokens, dim = query.shape
+    # Validate with one token's view; the token stride is passed separately.
+    q0, bound, scale, _ = _checked_batched(query[:, :, 0, :], key_cache, value_cache, block_table, context_lens,
+                                           scale, max_context_len, None)
+    _check(tokens > 0 and query.stride(2) >= 0, 'query requires a positive token count and nonnegative strides')
+    if out is None:
+        out = torch.empty(query.shape, dtype=query.dtype, device=query.device)
+    else:
+        _validate_storage(out)
+        _check(out.shape == query.shape and out.dtype == query.dtype and out.device == query.device
+               and out.stride(3) == 1, 'out must be a [B, Hq, T, D] tensor of the query dtype and device')
+    lib = _native.library()
+    num_blocks, kv_heads, block_size, _ = key_cache.shape
+    flags = _flags(force_simt, False, wide=wide)
+    dtype = DTYPE_CODES[key_cache.dtype]
+    device = key_cache.device
+    with torch.cuda.device(device):
+        size = ctypes.c_size_t(0)
+        _native.check(lib.mv_paged_decode_workspace_size(
+            batch * tokens, q_heads, kv_heads, dim, block_size, int(bound), int(pages_per_split), flags, dtype,
+            ctypes.byref(size)))
+        stream = current_stream_handle(device)
+        workspace = _workspace(device, stream, size.value) if size.value else None
+        _native.check(lib.mv_paged_chunk_attention(
+            query.data_ptr(), query.stride(0), query.stride(2), query.stride(1),
+            key_cache.data_ptr(), value_cache.data_ptr(), num_blocks, kv_heads, block_size, dim,
+            block_table.data_ptr(), INDEX_CODES[block_table.dtype], block_table.stride(0), block_table.shape[1],
+            context_lens.data_ptr(), INDEX_CODES[context_lens.dtype], int(bound), batch, tokens, q_heads,
+            float(scale), out.data_ptr(), out.stride(0), out.stride(2), out.stride(1),
+            workspace.data_ptr() if workspace is not None else None,
+            workspace.numel() if workspace is not None else 0, int(pages_per_split), flags, dtype, stream))
+    return out

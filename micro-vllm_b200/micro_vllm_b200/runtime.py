@@ -8,8 +8,9 @@ bias-free output projection, SiLU-gated MLP (src/micro_vllm/model.py:25-165,
 189-241) -- for a batch of B requests of equal prompt length:
 
 * ``prefill``: the prompt of every sequence in one pass; RoPE and the cache
-  append run as this library's kernels, prompt self-attention is the
-  library SDPA kernel (prefill is outside this path).
+  append run as this library's kernels; the first chunk's self-attention is
+  the library SDPA kernel, a chunk after cached tokens attends its causal
+  prefix straight from the pages (``paged_chunk_attention``).
 * ``decode``: one token per sequence; each layer's attention is one
   ``PagedDecodeStep`` call that rotates q and the new K (RoPE), appends K/V
   and attends over the pages in one kernel (plus the split merge).
@@ -25,7 +26,7 @@ from collections.abc import Mapping
 import torch
 import torch.nn.functional as F
 
-from .cuda_attention import PagedDecodeStep
+from .cuda_attention import PagedDecodeStep, paged_chunk_attention
 from .paged_kv_cache import BatchedPagedKVCache
 from .rope import apply_rope, rope_tables
 from .row_ops import rms_norm, silu_mul
@@ -126,6 +127,7 @@ class PreparedModel:
         if start + tokens > min(cache.capacity, self.max_positions):
             raise ValueError('sequence length exceeds the cache capacity or the configured context length')
         hq, hkv, d = self.num_heads, self.num_kv_heads, self.head_dim
+        ends = cache.lengths + tokens  # each sequence's length after the chunk
         x = F.embedding(input_ids, self.embedding)
         for i, w in enumerate(self.layers):
             h = rms_norm(x, w['input_layernorm.weight'], self.eps)
@@ -137,11 +139,9 @@ class PreparedModel:
             if start == 0:
                 heads = F.scaled_dot_product_attention(q, k, v, is_causal=True, enable_gqa=True)
             else:
-                # Chunk after cached tokens: attend over the gathered prefix + chunk.
-                keys, values = zip(*(cache.gather(i, b, start + tokens) for b in range(batch)))
-                mask = torch.ones(tokens, start + tokens, dtype=torch.bool, device=x.device).tril(start)
-                heads = F.scaled_dot_product_attention(q, torch.cat(keys), torch.cat(values), attn_mask=mask,
-                                                       enable_gqa=True)
+                # A chunk after cached tokens attends its causal prefix straight from the pages.
+                heads = paged_chunk_attention(q, *cache.pools(i), cache.block_table, ends,
+                                              max_context_len=start + tokens)
             merged = heads.transpose(1, 2).reshape(batch * tokens, hq * d)
             x = torch.addmm(x.reshape(batch * tokens, -1), merged, w['self_attn.o_proj.weight'].t()).view(x.shape)
             x = self._mlp(x, w)
