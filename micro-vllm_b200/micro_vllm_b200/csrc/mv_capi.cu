@@ -318,7 +318,7 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
         }
     }
     if (pps == 0) {
-        // Splits of 16..128 pages, sized so the batch's pages -- estimated as half
+        // Splits of 16..128 pages (tensor cores), sized so the batch's pages -- estimated as half
         // the max_context_len bound per sequence -- fill about one wave of
         // resident CTAs (three per SM). Measured on B200: longer splits lose to
         // the tail of the last wave, shorter ones to per-CTA start-up and the
@@ -327,7 +327,10 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
         const int64_t pages = static_cast<int64_t>(g.batch) * g.kv_heads * std::max<int64_t>(max_pages, 1) / 2;
         const int64_t target = static_cast<int64_t>(dev.sms) * 3;
         const int64_t want = (pages + target - 1) / target;
-        pps = 16;
+        // The CUDA-core kernel walks 32-token tiles one after another, so small
+        // batches want splits down to one tile each (more CTAs, shorter chains).
+        pps = plan->path == MV_PATH_SIMT ? std::max<int64_t>(1, (mv::kSimtTile + g.block_size - 1) / g.block_size)
+                                         : 16;
         while (pps * 2 <= want && pps < kMaxPagesPerSplit) pps *= 2;
         pps = std::min<int64_t>(pps, kMaxPagesPerSplit);
     }
