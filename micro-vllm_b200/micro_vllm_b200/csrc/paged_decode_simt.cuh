@@ -18,6 +18,7 @@
 namespace mv {
 
 constexpr int kSimtThreads = 128;
+constexpr int kSimtLoads = 8;   // K/V tile elements each thread has in flight
 constexpr int kSimtTile = 32;  // tokens per tile == warp width (one lane per token)
 
 // Shared-memory floats the SIMT kernel needs (+ token offsets as int64).
@@ -116,11 +117,30 @@ __global__ void __launch_bounds__(kSimtThreads) paged_decode_simt_kernel(const D
             }
         }
         __syncthreads();
-        for (int idx = tid; idx < count * D; idx += blockDim.x) {
-            const int t = idx / D;
-            const int d = idx - t * D;
-            k_s[t * DP + d] = to_float<T>(kc[off_s[t] + d]);
-            v_s[t * DP + d] = to_float<T>(vc[voff_s[t] + d]);
+        // kSimtLoads elements of K and V per thread in flight at once (loads
+        // first, then the shared-memory stores), not one round trip each.
+        for (int base = 0; base < count * D; base += kSimtThreads * kSimtLoads) {
+            float kv[kSimtLoads], vv[kSimtLoads];
+#pragma unroll
+            for (int u = 0; u < kSimtLoads; ++u) {
+                const int idx = base + u * kSimtThreads + tid;
+                if (idx < count * D) {
+                    const int t = idx / D;
+                    const int d = idx - t * D;
+                    kv[u] = to_float<T>(kc[off_s[t] + d]);
+                    vv[u] = to_float<T>(vc[voff_s[t] + d]);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kSimtLoads; ++u) {
+                const int idx = base + u * kSimtThreads + tid;
+                if (idx < count * D) {
+                    const int t = idx / D;
+                    const int d = idx - t * D;
+                    k_s[t * DP + d] = kv[u];
+                    v_s[t * DP + d] = vv[u];
+                }
+            }
         }
         __syncthreads();
         for (int idx = tid; idx < G * kSimtTile; idx += blockDim.x) {
@@ -130,9 +150,17 @@ __global__ void __launch_bounds__(kSimtThreads) paged_decode_simt_kernel(const D
             if (t < count) {
                 const float* qr = q_s + g * DP;
                 const float* kr = k_s + t * DP;
-                float dot = 0.0f;
-                for (int d = 0; d < D; ++d) dot = fmaf(qr[d], kr[d], dot);
-                s = dot * p.scale_log2;
+                // Four independent partial sums: the shared-memory loads and FMAs pipeline.
+                float d0 = 0.0f, d1 = 0.0f, d2 = 0.0f, d3 = 0.0f;
+                int d = 0;
+                for (; d + 3 < D; d += 4) {
+                    d0 = fmaf(qr[d], kr[d], d0);
+                    d1 = fmaf(qr[d + 1], kr[d + 1], d1);
+                    d2 = fmaf(qr[d + 2], kr[d + 2], d2);
+                    d3 = fmaf(qr[d + 3], kr[d + 3], d3);
+                }
+                for (; d < D; ++d) d0 = fmaf(qr[d], kr[d], d0);
+                s = ((d0 + d1) + (d2 + d3)) * p.scale_log2;
             }
             p_s[idx] = s;
         }
