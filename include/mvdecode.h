@@ -237,10 +237,11 @@ MV_API int mv_write_paged_kv(const void* key, int64_t key_stride_seq, int64_t ke
  *
  * key/value: [batch, num_kv_heads] rows of head_dim elements, feature stride 1,
  * element strides per sequence and per head. Where the split-grid tensor-core
- * kernel runs (mv_paged_decode_plan path MV_PATH_TMA_MMA) and the rows are
- * 16-byte aligned, the CTA that attends a sequence's last page writes the row
- * into the pool and into its staged copy of that page: no separate append
- * launch. Otherwise the append kernel runs first (two launches). The page that
+ * kernel runs (mv_paged_decode_plan path MV_PATH_TMA_MMA) with 16-byte aligned
+ * rows, or the CUDA-core kernel (MV_PATH_SIMT), the CTA that attends a
+ * sequence's last page writes the row into the pool and into its staged copy
+ * of that page: no separate append launch. Otherwise the append kernel runs
+ * first (two launches). The page that
  * receives a sequence's new row must not be read by another sequence in the
  * same call (as with any in-place append); the other arguments and contracts
  * are those of mv_paged_decode.
@@ -251,9 +252,9 @@ MV_API int mv_write_paged_kv(const void* key, int64_t key_stride_seq, int64_t ke
  * are rotated at position context_lens[b] - 1 inside the decode kernel, as
  * apply_rope does before the append (model.py:110-123, 214-215); the pool
  * receives the rotated key. A position without a table row gives a NaN group
- * and no write. Needs the fused path (fp16/bf16, MV_PATH_TMA_MMA, 16-byte
- * aligned rows and tables): otherwise MV_ERR_UNSUPPORTED -- rotate with
- * mv_apply_rope first and pass NULL tables.
+ * and no write. Needs the fused path (an even head_dim; on MV_PATH_TMA_MMA
+ * 16-byte aligned rows and tables): otherwise MV_ERR_UNSUPPORTED -- rotate
+ * with mv_apply_rope first and pass NULL tables.
  */
 MV_API int mv_paged_decode_append(const void* q, int64_t q_stride_seq, int64_t q_stride_head,
                                   const void* key, int64_t key_stride_seq, int64_t key_stride_head,

@@ -829,17 +829,23 @@ static int paged_decode_impl(const void* q, int64_t q_stride_seq, int64_t q_stri
     p.q_stride_token = chunk ? chunk->q_stride_token : 0;
     p.out_stride_token = chunk ? chunk->out_stride_token : 0;
     if (rows) {
-        // The split-grid tensor-core kernel writes the rows itself (16-byte
-        // chunks); every other plan runs the append kernel first, as two launches.
+        // The split-grid tensor-core kernel (16-byte chunks) and the CUDA-core
+        // kernel (elements) write the rows themselves; the persistent and
+        // cluster schedules, and unaligned rows on the tensor-core path, run the
+        // append kernel first, as two launches.
         const uintptr_t bits = reinterpret_cast<uintptr_t>(rows->key) | reinterpret_cast<uintptr_t>(rows->value) |
                                static_cast<uintptr_t>((rows->key_stride_seq | rows->key_stride_head |
                                                        rows->value_stride_seq | rows->value_stride_head) * 2);
-        const bool fusable = plan.path == MV_PATH_TMA_MMA && bits % 16 == 0;
+        const bool fusable = (plan.path == MV_PATH_TMA_MMA && bits % 16 == 0) || plan.path == MV_PATH_SIMT;
         if (rows->rope_cos) {
-            if (!fusable || (reinterpret_cast<uintptr_t>(rows->rope_cos) | reinterpret_cast<uintptr_t>(rows->rope_sin)) % 16)
+            const bool tables_ok = plan.path == MV_PATH_SIMT ||
+                                   (reinterpret_cast<uintptr_t>(rows->rope_cos) |
+                                    reinterpret_cast<uintptr_t>(rows->rope_sin)) % 16 == 0;
+            if (!fusable || !tables_ok || head_dim % 2)
                 return fail(MV_ERR_UNSUPPORTED,
-                            "RoPE fusion needs the split-grid tensor-core kernel, 16-byte aligned K/V rows and "
-                            "16-byte aligned tables; rotate with mv_apply_rope and call without tables");
+                            "RoPE fusion needs the split grid or the CUDA-core kernel, an even head_dim and, on the "
+                            "tensor-core path, 16-byte aligned K/V rows and tables; rotate with mv_apply_rope and "
+                            "call without tables");
             p.rope_cos = rows->rope_cos;
             p.rope_sin = rows->rope_sin;
             p.rope_rows = rows->rope_rows;
@@ -909,8 +915,6 @@ int mv_paged_decode_append(const void* q, int64_t q_stride_seq, int64_t q_stride
     if ((rope_cos == nullptr) != (rope_sin == nullptr))
         return fail(MV_ERR_INVALID_ARGUMENT, "pass both RoPE tables or neither");
     if (rope_cos && rope_rows <= 0) return fail(MV_ERR_INVALID_ARGUMENT, "rope_rows must be positive");
-    if (rope_cos && dtype == MV_DTYPE_F32)
-        return fail(MV_ERR_UNSUPPORTED, "RoPE fusion takes fp16/bf16; rotate fp32 rows with mv_apply_rope");
     const NewRows rows{key, key_stride_seq, key_stride_head, value, value_stride_seq, value_stride_head,
                        rope_cos, rope_sin, rope_rows};
     return paged_decode_impl(q, q_stride_seq, q_stride_head, k_cache, v_cache, num_blocks, num_kv_heads,

@@ -9,6 +9,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 namespace mv {
 
 // Sticky per-device error bits (MV_DEVICE_STATUS_*), raised by kernels whose
@@ -253,6 +255,42 @@ __device__ inline void append_row_direct(const DecodeParams& p, int b, int h, in
                          ((id * p.kv_heads + h) * p.block_size + slot) * p.head_dim) +
                      cc;
         *dst = v;
+    }
+}
+
+// Element-wise form of the fused append for kernels without 16-byte rows (any
+// head_dim, alignment and element type): value row copied bit for bit, key row
+// too or rotated (RoPE) at position len - 1. Skips exactly where the append
+// kernel skips; `row` is the query row (one token per sequence).
+template <typename T>
+__device__ inline void append_row_elements(const DecodeParams& p, int b, int h, int64_t len) {
+    using Raw = typename std::conditional<sizeof(T) == 2, uint16_t, uint32_t>::type;
+    const int64_t pos = len - 1;
+    if (pos < 0) return;
+    if (p.rope_cos && pos >= p.rope_rows) return;
+    const int64_t logical = pos / p.block_size;
+    if (logical >= p.blocks_per_seq) return;
+    const int64_t id = load_index(p.block_table, p.table_i64, b * p.table_stride + logical);
+    if (id < 0 || id >= p.num_blocks) return;
+    const int64_t dst = ((id * p.kv_heads + h) * p.block_size + (pos - logical * p.block_size)) * p.head_dim;
+    const Raw* krow = static_cast<const Raw*>(p.new_key) + b * p.new_key_stride[0] + h * p.new_key_stride[1];
+    const Raw* vrow = static_cast<const Raw*>(p.new_value) + b * p.new_value_stride[0] + h * p.new_value_stride[1];
+    Raw* kpool = const_cast<Raw*>(static_cast<const Raw*>(p.k_cache));
+    Raw* vpool = const_cast<Raw*>(static_cast<const Raw*>(p.v_cache));
+    const int half = p.head_dim / 2;
+    for (int d = threadIdx.x; d < p.head_dim; d += blockDim.x) {
+        vpool[dst + d] = vrow[d];
+        if (p.rope_cos) {
+            const T* kr = reinterpret_cast<const T*>(krow);
+            const bool first = d < half;
+            const float x = to_float<T>(kr[d]);
+            const float partner = to_float<T>(kr[first ? d + half : d - half]);
+            const float c = to_float<T>(static_cast<const T*>(p.rope_cos)[pos * p.head_dim + d]);
+            const float sn = to_float<T>(static_cast<const T*>(p.rope_sin)[pos * p.head_dim + d]);
+            reinterpret_cast<T*>(kpool)[dst + d] = from_float<T>(rope_element<T>(x, partner, c, sn, first));
+        } else {
+            kpool[dst + d] = krow[d];
+        }
     }
 }
 

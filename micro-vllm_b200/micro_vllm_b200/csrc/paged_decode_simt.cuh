@@ -64,14 +64,17 @@ __global__ void __launch_bounds__(kSimtThreads) paged_decode_simt_kernel(const D
     const SeqSplit seq = seq_split(p, b);
     if (split >= seq.splits) return;
     if (seq.state != 0) {
+        if (p.new_key) append_row_elements<T>(p, b, h, seq.len);
         write_group_constant<T>(p, b, h, seq.state == 1 ? 0.0f : __int_as_float(0x7fffffff));
         return;
     }
     const bool single = seq.splits == 1;
+    // Fused RoPE without a table row for the step's position: NaN, no append.
+    const bool rope_missing = p.rope_cos && seq.len - 1 >= p.rope_rows;
     int64_t page_begin, page_end;
     split_range(p, seq, split, &page_begin, &page_end);
 
-    if (tid == 0) cta_bad = 0;
+    if (tid == 0) cta_bad = rope_missing ? 1 : 0;
     __syncthreads();
     const int64_t seq_row = row_seq(p, b);  // the sequence this query row belongs to
     for (int64_t pg = page_begin + tid; !p.contiguous && pg < page_end; pg += blockDim.x) {
@@ -80,6 +83,10 @@ __global__ void __launch_bounds__(kSimtThreads) paged_decode_simt_kernel(const D
     }
     __syncthreads();
     if (cta_bad) {
+        // The fused append still writes the new row when its own page is valid,
+        // exactly as the append kernel would (a position without a RoPE table row
+        // is skipped inside).
+        if (p.new_key && split == seq.splits - 1) append_row_elements<T>(p, b, h, seq.len);
         if (single) write_group_constant<T>(p, b, h, __int_as_float(0x7fffffff));
         else write_group_partial_nan(p, b, h, split);
         return;
@@ -96,6 +103,25 @@ __global__ void __launch_bounds__(kSimtThreads) paged_decode_simt_kernel(const D
         m_s[g] = -INFINITY;
         l_s[g] = 0.0f;
     }
+    if (p.rope_cos) {
+        // Rotate the staged query rows at the step's position, pair (d, d + D/2) per thread.
+        __syncthreads();
+        const int half = D / 2;
+        const int64_t pos = seq.len - 1;
+        const T* cs = static_cast<const T*>(p.rope_cos) + pos * D;
+        const T* sn = static_cast<const T*>(p.rope_sin) + pos * D;
+        for (int idx = tid; idx < G * half; idx += blockDim.x) {
+            const int g = idx / half;
+            const int d = idx - g * half;
+            float* row = q_s + g * DP;
+            const float x0 = row[d], x1 = row[d + half];
+            row[d] = rope_element<T>(x0, x1, to_float<T>(cs[d]), to_float<T>(sn[d]), true);
+            row[d + half] = rope_element<T>(x1, x0, to_float<T>(cs[d + half]), to_float<T>(sn[d + half]), false);
+        }
+    }
+    // Fused append: this split holds the step's new token (position len - 1)
+    // when it holds the sequence's last page.
+    const int64_t new_tok = (p.new_key && split == seq.splits - 1) ? seq.len - 1 : -1;
 
     const T* kc = static_cast<const T*>(p.k_cache);
     const T* vc = static_cast<const T*>(p.v_cache);
@@ -143,6 +169,34 @@ __global__ void __launch_bounds__(kSimtThreads) paged_decode_simt_kernel(const D
             }
         }
         __syncthreads();
+        if (new_tok >= t0 && new_tok < t0 + count) {
+            // The tile's old row of the new token is read (by every thread, above):
+            // replace it in shared memory and in the pool with the new K/V row.
+            using Raw = typename std::conditional<sizeof(T) == 2, uint16_t, uint32_t>::type;
+            const int r = static_cast<int>(new_tok - t0);
+            const T* krow = static_cast<const T*>(p.new_key) + b * p.new_key_stride[0] + h * p.new_key_stride[1];
+            const T* vrow = static_cast<const T*>(p.new_value) + b * p.new_value_stride[0] + h * p.new_value_stride[1];
+            const int half = D / 2;
+            for (int d = tid; d < D; d += blockDim.x) {
+                T kval = krow[d];
+                if (p.rope_cos) {
+                    const bool first = d < half;
+                    kval = from_float<T>(rope_element<T>(
+                        to_float<T>(krow[d]), to_float<T>(krow[first ? d + half : d - half]),
+                        to_float<T>(static_cast<const T*>(p.rope_cos)[new_tok * D + d]),
+                        to_float<T>(static_cast<const T*>(p.rope_sin)[new_tok * D + d]), first));
+                }
+                k_s[r * DP + d] = to_float<T>(kval);
+                v_s[r * DP + d] = to_float<T>(vrow[d]);
+                // The pool rows are written through the decode's const pointers (the caller's writable pools).
+                Raw* kpool = const_cast<Raw*>(static_cast<const Raw*>(p.k_cache));
+                Raw* vpool = const_cast<Raw*>(static_cast<const Raw*>(p.v_cache));
+                kpool[off_s[r] + d] = p.rope_cos ? *reinterpret_cast<const Raw*>(&kval)
+                                                 : reinterpret_cast<const Raw*>(krow)[d];
+                vpool[voff_s[r] + d] = reinterpret_cast<const Raw*>(vrow)[d];
+            }
+            __syncthreads();
+        }
         for (int idx = tid; idx < G * kSimtTile; idx += blockDim.x) {
             const int g = idx / kSimtTile;
             const int t = idx - g * kSimtTile;

@@ -433,9 +433,10 @@ def paged_decode_with_append(query: torch.Tensor, key: torch.Tensor, value: torc
     ``paged_decode_attention(query, key_cache, value_cache, block_table,
     context_lens, scale)`` -- the append-before-attend order of the
     reference's decode layer (src/micro_vllm/model.py:215-216) -- but where
-    the split-grid tensor-core kernel runs, the CTA attending each sequence's
-    last page writes the new row itself, so the step is one kernel (plus the
-    split merge) instead of two. Other plans run the append kernel first.
+    the split-grid tensor-core kernel or the CUDA-core kernel runs, the CTA
+    attending each sequence's last page writes the new row itself, so the step
+    is one kernel (plus the split merge) instead of two. The persistent and
+    cluster schedules run the append kernel first.
 
     key/value: [B, Hkv, D] or [B, Hkv, 1, D] CUDA tensors of the pool dtype,
     feature stride 1. context_lens count the new token. The page receiving a
@@ -469,7 +470,7 @@ def paged_decode_with_append(query: torch.Tensor, key: torch.Tensor, value: torc
         path = paged_decode_plan(q.shape[1], key_cache, max_context_len, batch=q.shape[0],
                                  pages_per_split=pages_per_split, force_simt=force_simt,
                                  persistent=persistent, cluster=cluster, wide=wide)[0]
-        if path == 'tma_mma' and _aligned16(key3, value3, cos, sin):
+        if (path == 'tma_mma' and _aligned16(key3, value3, cos, sin)) or path == 'simt':
             tables = (cos, sin)
         else:
             q = rope_ops.apply_rope(q, cos, sin, positions=context_lens, positions_are_end=True)
@@ -555,7 +556,9 @@ class PagedDecodeStep:
             from . import rope as rope_ops
             rope_ops.check_tables(rope[0], rope[1], dim, key_cache.dtype, key_cache.device)
             self._rope = (rope[0], rope[1])
-            self._rope_in_kernel = self.plan[0] == 'tma_mma' and _aligned16(*rope)
+            path = self.plan[0]
+            self._rope_kernel_path = path
+            self._rope_in_kernel = (path == 'tma_mma' and _aligned16(*rope)) or path == 'simt'
 
     @property
     def plan(self):
@@ -615,7 +618,7 @@ class PagedDecodeStep:
         tables = (None, None, 0)
         if self._rope is not None:
             cos, sin = self._rope
-            if self._rope_in_kernel and _aligned16(key, value):
+            if self._rope_in_kernel and (self._rope_kernel_path == 'simt' or _aligned16(key, value)):
                 tables = (cos.data_ptr(), sin.data_ptr(), cos.shape[0])
             else:
                 from . import rope as rope_ops

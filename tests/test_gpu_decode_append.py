@@ -25,7 +25,7 @@ MODES = {
     'wide': dict(wide=True),                  # split grid, wide shape: append fused
     'persistent': dict(persistent=True),      # append kernel first, then the persistent kernel
     'cluster': dict(cluster=True),            # append kernel first, then the cluster kernel
-    'simt': dict(force_simt=True),            # append kernel first, then the CUDA-core kernel
+    'simt': dict(force_simt=True),            # CUDA-core kernel: append fused (element-wise)
 }
 
 
