@@ -1179,12 +1179,25 @@ int mv_apply_rope(const void* x, int64_t x_stride_seq, int64_t x_stride_head, in
     r.positions_i64 = positions_type == MV_INDEX_I64;
     r.positions_end = positions_kind == MV_POSITIONS_END;
     r.start = start;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const dim3 block(mv::kRopeThreads);
+    cudaError_t err;
+    // Two-byte rows of a multiple of 16 elements, everything 16-byte aligned: 16-byte chunks.
+    uintptr_t bits = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out) |
+                     reinterpret_cast<uintptr_t>(cos) | reinterpret_cast<uintptr_t>(sin);
+    for (int64_t st : strides) bits |= static_cast<uintptr_t>(st * 2);
+    if (dtype != MV_DTYPE_F32 && head_dim % 16 == 0 && bits % 16 == 0) {
+        const int64_t total = static_cast<int64_t>(batch) * heads * num_tokens * (head_dim / 16);
+        const int64_t want = (total + mv::kRopeThreads - 1) / mv::kRopeThreads;
+        const dim3 grid(static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(dev.sms) * 16))));
+        err = dtype == MV_DTYPE_F16 ? launch_pdl(mv::rope_rows_vec_kernel<__half>, grid, block, 0, s, r, total)
+                                    : launch_pdl(mv::rope_rows_vec_kernel<__nv_bfloat16>, grid, block, 0, s, r, total);
+        return err == cudaSuccess ? MV_OK : cuda_fail(err, "RoPE kernel launch");
+    }
     const int64_t total = static_cast<int64_t>(batch) * heads * num_tokens * (head_dim / 2);
     const int64_t want = (total + mv::kRopeThreads - 1) / mv::kRopeThreads;
     const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(dev.sms) * 16)));
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const dim3 grid(blocks), block(mv::kRopeThreads);
-    cudaError_t err;
+    const dim3 grid(blocks);
     switch (dtype) {
         case MV_DTYPE_F32: err = launch_pdl(mv::rope_rows_kernel<float>, grid, block, 0, s, r, total); break;
         case MV_DTYPE_F16: err = launch_pdl(mv::rope_rows_kernel<__half>, grid, block, 0, s, r, total); break;
@@ -1204,6 +1217,33 @@ int mv_rms_norm(const void* x, int64_t x_stride_row, const void* weight, void* o
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     const dim3 grid(static_cast<unsigned>(rows)), block(mv::kRowThreads);
     cudaError_t err;
+    const size_t elem = dtype == MV_DTYPE_F32 ? 4 : 2;
+    const int per_chunk = static_cast<int>(16 / elem);
+    const uintptr_t bits = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(weight) |
+                           reinterpret_cast<uintptr_t>(out) | static_cast<uintptr_t>(x_stride_row * elem) |
+                           static_cast<uintptr_t>(out_stride_row * elem);
+    if (hidden % per_chunk == 0 && bits % 16 == 0 && hidden / per_chunk <= mv::kRowThreads * mv::kNormMaxChunks) {
+        switch (dtype) {
+            case MV_DTYPE_F32:
+                err = launch_pdl(mv::rms_norm_vec_kernel<float>, grid, block, 0, s, static_cast<const float*>(x),
+                                 x_stride_row, static_cast<const float*>(weight), static_cast<float*>(out),
+                                 out_stride_row, hidden, eps);
+                break;
+            case MV_DTYPE_F16:
+                err = launch_pdl(mv::rms_norm_vec_kernel<__half>, grid, block, 0, s, static_cast<const __half*>(x),
+                                 x_stride_row, static_cast<const __half*>(weight), static_cast<__half*>(out),
+                                 out_stride_row, hidden, eps);
+                break;
+            case MV_DTYPE_BF16:
+                err = launch_pdl(mv::rms_norm_vec_kernel<__nv_bfloat16>, grid, block, 0, s,
+                                 static_cast<const __nv_bfloat16*>(x), x_stride_row,
+                                 static_cast<const __nv_bfloat16*>(weight), static_cast<__nv_bfloat16*>(out),
+                                 out_stride_row, hidden, eps);
+                break;
+            default: return fail(MV_ERR_INVALID_ARGUMENT, "dtype must be MV_DTYPE_F32, MV_DTYPE_F16 or MV_DTYPE_BF16");
+        }
+        return err == cudaSuccess ? MV_OK : cuda_fail(err, "RMSNorm kernel launch");
+    }
     switch (dtype) {
         case MV_DTYPE_F32:
             err = launch_pdl(mv::rms_norm_kernel<float>, grid, block, 0, s, static_cast<const float*>(x), x_stride_row,
@@ -1233,12 +1273,40 @@ int mv_silu_mul(const void* gate_up, int64_t stride_row, void* out, int64_t out_
     DeviceInfo dev;
     int rc = device_info(&dev);
     if (rc != MV_OK) return rc;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const dim3 block(mv::kRowThreads);
+    cudaError_t err;
+    const size_t elem = dtype == MV_DTYPE_F32 ? 4 : 2;
+    const int per_chunk = static_cast<int>(16 / elem);
+    const uintptr_t bits = reinterpret_cast<uintptr_t>(gate_up) | reinterpret_cast<uintptr_t>(out) |
+                           static_cast<uintptr_t>(stride_row * elem) | static_cast<uintptr_t>(out_stride_row * elem);
+    if (width % per_chunk == 0 && bits % 16 == 0) {
+        const int64_t total = rows * (width / per_chunk);
+        const int64_t want = (total + mv::kRowThreads - 1) / mv::kRowThreads;
+        const dim3 grid(static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(dev.sms) * 16))));
+        switch (dtype) {
+            case MV_DTYPE_F32:
+                err = launch_pdl(mv::silu_mul_vec_kernel<float>, grid, block, 0, s, static_cast<const float*>(gate_up),
+                                 stride_row, static_cast<float*>(out), out_stride_row, static_cast<int>(width), total);
+                break;
+            case MV_DTYPE_F16:
+                err = launch_pdl(mv::silu_mul_vec_kernel<__half>, grid, block, 0, s,
+                                 static_cast<const __half*>(gate_up), stride_row, static_cast<__half*>(out),
+                                 out_stride_row, static_cast<int>(width), total);
+                break;
+            case MV_DTYPE_BF16:
+                err = launch_pdl(mv::silu_mul_vec_kernel<__nv_bfloat16>, grid, block, 0, s,
+                                 static_cast<const __nv_bfloat16*>(gate_up), stride_row,
+                                 static_cast<__nv_bfloat16*>(out), out_stride_row, static_cast<int>(width), total);
+                break;
+            default: return fail(MV_ERR_INVALID_ARGUMENT, "dtype must be MV_DTYPE_F32, MV_DTYPE_F16 or MV_DTYPE_BF16");
+        }
+        return err == cudaSuccess ? MV_OK : cuda_fail(err, "SiLU-mul kernel launch");
+    }
     const int64_t total = rows * width;
     const int64_t want = (total + mv::kRowThreads - 1) / mv::kRowThreads;
     const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(dev.sms) * 16)));
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const dim3 grid(blocks), block(mv::kRowThreads);
-    cudaError_t err;
+    const dim3 grid(blocks);
     switch (dtype) {
         case MV_DTYPE_F32:
             err = launch_pdl(mv::silu_mul_kernel<float>, grid, block, 0, s, static_cast<const float*>(gate_up),

@@ -58,4 +58,98 @@ silu_mul_kernel(const T* gate_up, int64_t stride, T* out, int64_t out_stride, in
     }
 }
 
+// 16-byte vector forms (8 two-byte or 4 four-byte elements per chunk), used
+// when widths, strides and addresses allow; same arithmetic per element.
+template <typename T>
+struct Chunk {
+    static constexpr int kElems = 16 / sizeof(T);
+};
+
+// One CTA per row; the row stays in registers between the two passes
+// (at most kMaxChunks 16-byte chunks per thread).
+constexpr int kNormMaxChunks = 4;
+
+template <typename T>
+__global__ void __launch_bounds__(kRowThreads)
+rms_norm_vec_kernel(const T* x, int64_t x_stride, const T* weight, T* out, int64_t out_stride, int hidden, float eps) {
+    constexpr int E = Chunk<T>::kElems;
+    wait_for_prior_grid();
+    allow_next_grid();
+    const uint4* row = reinterpret_cast<const uint4*>(x + blockIdx.x * x_stride);
+    uint4* orow = reinterpret_cast<uint4*>(out + blockIdx.x * out_stride);
+    const uint4* wrow = reinterpret_cast<const uint4*>(weight);
+    const int chunks = hidden / E;
+    uint4 v[kNormMaxChunks];
+    float ss = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kNormMaxChunks; ++k) {
+        const int c = threadIdx.x + k * kRowThreads;
+        if (c < chunks) {
+            v[k] = row[c];
+            const T* e = reinterpret_cast<const T*>(&v[k]);
+#pragma unroll
+            for (int i = 0; i < E; ++i) {
+                const float f = to_float<T>(e[i]);
+                ss = __fmaf_rn(f, f, ss);
+            }
+        }
+    }
+    ss = warp_sum(ss);
+    __shared__ float partial[kRowThreads / 32];
+    __shared__ float scale;
+    if ((threadIdx.x & 31) == 0) partial[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float total = 0.0f;
+        for (int w = 0; w < kRowThreads / 32; ++w) total += partial[w];
+        scale = rsqrtf(total / static_cast<float>(hidden) + eps);
+    }
+    __syncthreads();
+    const float r = scale;
+#pragma unroll
+    for (int k = 0; k < kNormMaxChunks; ++k) {
+        const int c = threadIdx.x + k * kRowThreads;
+        if (c < chunks) {
+            const uint4 wv = wrow[c];
+            const T* e = reinterpret_cast<const T*>(&v[k]);
+            const T* we = reinterpret_cast<const T*>(&wv);
+            uint4 o;
+            T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+            for (int i = 0; i < E; ++i) {
+                const T normalized = from_float<T>(__fmul_rn(to_float<T>(e[i]), r));
+                oe[i] = from_float<T>(__fmul_rn(to_float<T>(we[i]), to_float<T>(normalized)));
+            }
+            orow[c] = o;
+        }
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kRowThreads)
+silu_mul_vec_kernel(const T* gate_up, int64_t stride, T* out, int64_t out_stride, int width, int64_t total_chunks) {
+    constexpr int E = Chunk<T>::kElems;
+    wait_for_prior_grid();
+    allow_next_grid();
+    const int chunks = width / E;
+    const int64_t step = static_cast<int64_t>(blockDim.x) * gridDim.x;
+    for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total_chunks; idx += step) {
+        const int64_t r = idx / chunks;
+        const int c = static_cast<int>(idx - r * chunks);
+        const uint4 gv = *reinterpret_cast<const uint4*>(gate_up + r * stride + c * E);
+        const uint4 uv = *reinterpret_cast<const uint4*>(gate_up + r * stride + width + c * E);
+        const T* g = reinterpret_cast<const T*>(&gv);
+        const T* u = reinterpret_cast<const T*>(&uv);
+        uint4 o;
+        T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+        for (int i = 0; i < E; ++i) {
+            const float gf = to_float<T>(g[i]);
+            const float silu = to_float<T>(from_float<T>(gf / (1.0f + expf(-gf))));
+            oe[i] = from_float<T>(__fmul_rn(silu, to_float<T>(u[i])));
+        }
+        *reinterpret_cast<uint4*>(out + r * out_stride + c * E) = o;
+    }
+}
+
 }  // namespace mv

@@ -145,3 +145,19 @@ def test_bound_step_with_rope_matches_the_one_off_call():
     assert _bits_equal(out, ref) and _bits_equal(pools[0], ref_pools[0]) and _bits_equal(pools[1], ref_pools[1])
     with pytest.raises(RuntimeError, match='needs the new K/V rows'):
         step(t['q'], t['context_lens'])
+
+
+@pytest.mark.parametrize('dtype', ['bfloat16', 'float16'])
+def test_unaligned_rows_take_the_element_kernel_with_the_same_bits(dtype):
+    """Rows whose stride is not a 16-byte multiple use the element-wise kernel;
+    both kernels give the oracle's bits."""
+    from micro_vllm_b200.rope import apply_rope
+    cos, sin = _tables(64, 128, dtype)
+    base = torch.randn(2, 3, 5, 129, device='cuda').to(TORCH_DTYPES[dtype])
+    x = base[..., :128]                              # token stride 129 elements: not 16-byte aligned
+    aligned = x.contiguous()
+    a = apply_rope(x, cos, sin, start=7)
+    b = apply_rope(aligned, cos, sin, start=7)
+    assert _bits_equal(a, b)
+    expected = oracle_rope(to_numpy(aligned), to_numpy(cos)[7:12][None, None], to_numpy(sin)[7:12][None, None], dtype)
+    assert np.array_equal(to_numpy(a).view(np.uint8), expected.view(np.uint8))

@@ -56,3 +56,19 @@ def test_silu_mul_matches_the_reference_expression(dtype):
     diff = (out.float() - expected.float()).abs()
     assert (diff <= ULP[dtype] * 2 * expected.float().abs() + 1e-30).all()
     assert (diff == 0).float().mean() > 0.99
+
+
+@pytest.mark.parametrize('dtype', [torch.float32, torch.bfloat16])
+def test_odd_widths_and_unaligned_rows_take_the_element_kernels(dtype):
+    """Widths that are not a multiple of a 16-byte chunk, rows at odd offsets."""
+    from micro_vllm_b200.row_ops import rms_norm, silu_mul
+    gen = torch.Generator(device='cuda').manual_seed(2)
+    gate_up = (torch.randn(7, 2 * 37, generator=gen, device='cuda') * 3).to(dtype)
+    gate, up = gate_up.chunk(2, dim=-1)
+    diff = (silu_mul(gate_up).float() - (F.silu(gate) * up).float()).abs()
+    assert (diff <= ULP[dtype] * 2 * (F.silu(gate) * up).float().abs() + 1e-30).all()
+    x = (torch.randn(9, 101, generator=gen, device='cuda') * 2).to(dtype)
+    w = torch.ones(101, device='cuda', dtype=dtype)
+    expected = reference_rms_norm(x, w, 1e-6)
+    assert ((rms_norm(x, w, 1e-6).float() - expected.float()).abs()
+            <= ULP[dtype] * 2 * expected.float().abs() + 1e-30).all()
