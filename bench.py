@@ -71,6 +71,9 @@ def parse_args(argv=None):
                         help='wall-clock budget of the CPU baseline sample')
     parser.add_argument('--no-cpu-baseline', action='store_true')
     parser.add_argument('--pages-per-split', type=int, default=0)
+    parser.add_argument('--nvtx-steps', type=int, default=0,
+                        help='generation workload: run prefill and this many eager decode steps inside NVTX '
+                             'ranges "prefill" and "decode" (for a profiler launch list), print nothing else')
     parser.add_argument('--step', choices=('fused', 'separate'), default='fused',
                         help='one-call append + attention (default) or the append kernel then attention')
     return parser.parse_args(argv)
@@ -782,6 +785,23 @@ def run_generate(args):
     batch, prompt_len, new = spec['batch'], spec['prompt_len'], spec['new_tokens']
     prompts_host = torch.randint(0, spec['vocab_size'], (batch, prompt_len),
                                  generator=torch.Generator().manual_seed(spec['seed']))
+    if args.nvtx_steps:
+        # Profiling aid: eager prefill and decode steps in named NVTX ranges.
+        decoder = GreedyDecoder(model, batch, prompt_len + args.nvtx_steps + 1, use_graph=False)
+        prompts = prompts_host.to(device)
+        decoder.run(prompts, 2)
+        decoder.cache.reset()
+        torch.cuda.synchronize(device)
+        torch.cuda.nvtx.range_push('prefill')
+        decoder.tokens.copy_(model.prefill(prompts, decoder.cache).argmax(dim=-1))
+        torch.cuda.synchronize(device)
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.nvtx.range_push('decode')
+        for _ in range(args.nvtx_steps):
+            decoder.step()
+        torch.cuda.synchronize(device)
+        torch.cuda.nvtx.range_pop()
+        return None
     decoder = GreedyDecoder(model, batch, prompt_len + new - 1)
     prompts = prompts_host.to(device)
     for _ in range(max(args.warmup, 1)):           # warm-up: cuBLAS plans, graph capture
@@ -882,9 +902,89 @@ def run_generate(args):
     }
 
 
+def run_kernels(args):
+    """Each of this library's kernels on the config-4 shapes, CUDA-event timed (and a
+    fixed sequence of calls a profiler can select launches from)."""
+    import torch
+
+    from micro_vllm_b200 import cuda_attention
+    from micro_vllm_b200.rope import apply_rope, rope_tables
+    from micro_vllm_b200.row_ops import rms_norm, silu_mul
+
+    device = torch.device('cuda', int(os.environ.get('LOCAL_RANK', '0')))
+    torch.cuda.set_device(device)
+    gen = torch.Generator(device=device).manual_seed(5)
+    bf16 = torch.bfloat16
+
+    def randn(*shape, dtype=bf16):
+        return torch.randn(shape, generator=gen, device=device).to(dtype)
+
+    def pool(batch, kv_heads, dim, lo, hi, dtype, seed):
+        lens = torch.randint(lo, hi + 1, (batch,), generator=torch.Generator().manual_seed(seed))
+        pages = (lens + 15) // 16
+        table = torch.full((batch, int(pages.max())), -1, dtype=torch.int32)
+        perm = torch.randperm(int(pages.sum()), generator=torch.Generator().manual_seed(seed + 1)).to(torch.int32)
+        offset = 0
+        for b, n in enumerate(pages.tolist()):
+            table[b, :n] = perm[offset:offset + n]
+            offset += n
+        k = randn(int(pages.sum()), kv_heads, 16, dim, dtype=dtype)
+        v = randn(int(pages.sum()), kv_heads, 16, dim, dtype=dtype)
+        return k, v, table.to(device), lens.to(torch.int32).to(device)
+
+    cos, sin = rope_tables(4096, 128, 1e6, dtype=bf16, device=device)
+    g_k, g_v, g_table, g_lens = pool(32, 2, 128, 513, 639, bf16, 1)     # config-4 decode attention
+    g_q, g_rows = randn(32, 12, 128), randn(32, 2, 2, 128)
+    c_k, c_v, c_table, c_lens = pool(4, 2, 64, 1, 512, torch.float32, 2)  # config-1 fp32 decode
+    c_q, c_rows = randn(4, 14, 64, dtype=torch.float32), randn(4, 2, 2, 64, dtype=torch.float32)
+    x, h, w = randn(32, 12, 512, 128), randn(16384, 1536), torch.ones(1536, dtype=bf16, device=device)
+    gate_up = randn(16384, 2 * 8960)
+    calls = {
+        'decode_config4_wide_rope': lambda: cuda_attention.paged_decode_with_append(
+            g_q, g_rows[:, 0], g_rows[:, 1], g_k, g_v, g_table, g_lens, max_context_len=int(g_table.shape[1] * 16),
+            rope=(cos, sin)),
+        'decode_config1_simt_fp32': lambda: cuda_attention.paged_decode_with_append(
+            c_q, c_rows[:, 0], c_rows[:, 1], c_k, c_v, c_table, c_lens, max_context_len=int(c_table.shape[1] * 16)),
+        'rope_prefill_32x12x512x128': lambda: apply_rope(x, cos, sin, start=0),
+        'rms_norm_prefill_16384x1536': lambda: rms_norm(h, w, 1e-6),
+        'silu_mul_prefill_16384x8960': lambda: silu_mul(gate_up),
+    }
+    timings = {}
+    stream = torch.cuda.Stream(device)
+    for name, fn in calls.items():
+        stream.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(stream):
+            for _ in range(max(args.warmup, 1)):
+                fn()
+        torch.cuda.synchronize(device)
+        # Back-to-back calls captured in one graph, so host overhead is not timed.
+        calls_per_graph = max(1, min(args.steps, 20))
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            for _ in range(calls_per_graph):
+                fn()
+        graph.replay()
+        torch.cuda.synchronize(device)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        reps = 10
+        start.record()
+        for _ in range(reps):
+            graph.replay()
+        end.record()
+        torch.cuda.synchronize(device)
+        timings[name] = round(start.elapsed_time(end) * 1e3 / (reps * calls_per_graph), 2)
+        del graph
+    return {'metric': 'per-call device time of this library\'s kernels on config-4 / config-1 shapes',
+            'unit': 'us per call', 'values': timings,
+            'config': {'workload': 'kernels_qwen15b',
+                       'timing': 'CUDA events around replays of a graph of back-to-back calls'}}
+
+
 def main(argv=None):
     args = parse_args(argv)
-    if args.workload in GENERATE_WORKLOADS:
+    if args.workload == 'kernels_qwen15b':
+        result = run_kernels(args)
+    elif args.workload in GENERATE_WORKLOADS:
         if args.impl == 'reference':
             result = {'impl': 'reference', 'unavailable': 'the reference generates one request at a time on '
                       'the CPU path; a 1.5B-parameter batch-32 run is not a bounded sample'}

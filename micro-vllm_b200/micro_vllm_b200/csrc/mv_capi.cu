@@ -1186,12 +1186,12 @@ int mv_apply_rope(const void* x, int64_t x_stride_seq, int64_t x_stride_head, in
     uintptr_t bits = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out) |
                      reinterpret_cast<uintptr_t>(cos) | reinterpret_cast<uintptr_t>(sin);
     for (int64_t st : strides) bits |= static_cast<uintptr_t>(st * 2);
-    if (dtype != MV_DTYPE_F32 && head_dim % 16 == 0 && bits % 16 == 0) {
-        const int64_t total = static_cast<int64_t>(batch) * heads * num_tokens * (head_dim / 16);
-        const int64_t want = (total + mv::kRopeThreads - 1) / mv::kRopeThreads;
-        const dim3 grid(static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(dev.sms) * 16))));
-        err = dtype == MV_DTYPE_F16 ? launch_pdl(mv::rope_rows_vec_kernel<__half>, grid, block, 0, s, r, total)
-                                    : launch_pdl(mv::rope_rows_vec_kernel<__nv_bfloat16>, grid, block, 0, s, r, total);
+    const int64_t row_chunks = static_cast<int64_t>(num_tokens) * (head_dim / 16);
+    if (dtype != MV_DTYPE_F32 && head_dim % 16 == 0 && bits % 16 == 0 && heads <= 65535 && batch <= 65535 &&
+        row_chunks < (int64_t(1) << 30)) {
+        const dim3 grid(static_cast<unsigned>((row_chunks + mv::kRopeThreads - 1) / mv::kRopeThreads), heads, batch);
+        err = dtype == MV_DTYPE_F16 ? launch_pdl(mv::rope_rows_vec_kernel<__half>, grid, block, 0, s, r)
+                                    : launch_pdl(mv::rope_rows_vec_kernel<__nv_bfloat16>, grid, block, 0, s, r);
         return err == cudaSuccess ? MV_OK : cuda_fail(err, "RoPE kernel launch");
     }
     const int64_t total = static_cast<int64_t>(batch) * heads * num_tokens * (head_dim / 2);
@@ -1222,6 +1222,30 @@ int mv_rms_norm(const void* x, int64_t x_stride_row, const void* weight, void* o
     const uintptr_t bits = reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(weight) |
                            reinterpret_cast<uintptr_t>(out) | static_cast<uintptr_t>(x_stride_row * elem) |
                            static_cast<uintptr_t>(out_stride_row * elem);
+    if (hidden % per_chunk == 0 && bits % 16 == 0 && hidden / per_chunk <= 32 * mv::kWarpNormChunks) {
+        // Rows that fit a warp: one warp per row, eight rows per CTA.
+        const dim3 wgrid(static_cast<unsigned>((rows + mv::kRowThreads / 32 - 1) / (mv::kRowThreads / 32)));
+        switch (dtype) {
+            case MV_DTYPE_F32:
+                err = launch_pdl(mv::rms_norm_warp_kernel<float>, wgrid, block, 0, s, static_cast<const float*>(x),
+                                 x_stride_row, static_cast<const float*>(weight), static_cast<float*>(out),
+                                 out_stride_row, hidden, eps, rows);
+                break;
+            case MV_DTYPE_F16:
+                err = launch_pdl(mv::rms_norm_warp_kernel<__half>, wgrid, block, 0, s, static_cast<const __half*>(x),
+                                 x_stride_row, static_cast<const __half*>(weight), static_cast<__half*>(out),
+                                 out_stride_row, hidden, eps, rows);
+                break;
+            case MV_DTYPE_BF16:
+                err = launch_pdl(mv::rms_norm_warp_kernel<__nv_bfloat16>, wgrid, block, 0, s,
+                                 static_cast<const __nv_bfloat16*>(x), x_stride_row,
+                                 static_cast<const __nv_bfloat16*>(weight), static_cast<__nv_bfloat16*>(out),
+                                 out_stride_row, hidden, eps, rows);
+                break;
+            default: return fail(MV_ERR_INVALID_ARGUMENT, "dtype must be MV_DTYPE_F32, MV_DTYPE_F16 or MV_DTYPE_BF16");
+        }
+        return err == cudaSuccess ? MV_OK : cuda_fail(err, "RMSNorm kernel launch");
+    }
     if (hidden % per_chunk == 0 && bits % 16 == 0 && hidden / per_chunk <= mv::kRowThreads * mv::kNormMaxChunks) {
         switch (dtype) {
             case MV_DTYPE_F32:
@@ -1281,23 +1305,23 @@ int mv_silu_mul(const void* gate_up, int64_t stride_row, void* out, int64_t out_
     const uintptr_t bits = reinterpret_cast<uintptr_t>(gate_up) | reinterpret_cast<uintptr_t>(out) |
                            static_cast<uintptr_t>(stride_row * elem) | static_cast<uintptr_t>(out_stride_row * elem);
     if (width % per_chunk == 0 && bits % 16 == 0) {
-        const int64_t total = rows * (width / per_chunk);
-        const int64_t want = (total + mv::kRowThreads - 1) / mv::kRowThreads;
-        const dim3 grid(static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(dev.sms) * 16))));
+        const int chunks = width / per_chunk;
+        const dim3 grid((chunks + mv::kRowThreads - 1) / mv::kRowThreads,
+                        static_cast<unsigned>(std::min<int64_t>(rows, 65535)));
         switch (dtype) {
             case MV_DTYPE_F32:
                 err = launch_pdl(mv::silu_mul_vec_kernel<float>, grid, block, 0, s, static_cast<const float*>(gate_up),
-                                 stride_row, static_cast<float*>(out), out_stride_row, static_cast<int>(width), total);
+                                 stride_row, static_cast<float*>(out), out_stride_row, static_cast<int>(width), rows);
                 break;
             case MV_DTYPE_F16:
                 err = launch_pdl(mv::silu_mul_vec_kernel<__half>, grid, block, 0, s,
                                  static_cast<const __half*>(gate_up), stride_row, static_cast<__half*>(out),
-                                 out_stride_row, static_cast<int>(width), total);
+                                 out_stride_row, static_cast<int>(width), rows);
                 break;
             case MV_DTYPE_BF16:
                 err = launch_pdl(mv::silu_mul_vec_kernel<__nv_bfloat16>, grid, block, 0, s,
                                  static_cast<const __nv_bfloat16*>(gate_up), stride_row,
-                                 static_cast<__nv_bfloat16*>(out), out_stride_row, static_cast<int>(width), total);
+                                 static_cast<__nv_bfloat16*>(out), out_stride_row, static_cast<int>(width), rows);
                 break;
             default: return fail(MV_ERR_INVALID_ARGUMENT, "dtype must be MV_DTYPE_F32, MV_DTYPE_F16 or MV_DTYPE_BF16");
         }

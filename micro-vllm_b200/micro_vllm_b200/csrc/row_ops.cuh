@@ -125,17 +125,71 @@ rms_norm_vec_kernel(const T* x, int64_t x_stride, const T* weight, T* out, int64
     }
 }
 
+// One warp per row for rows of up to 32 x kWarpNormChunks chunks (hidden <= 2048
+// two-byte elements): the reduction stays in the warp, no shared memory or
+// block barrier, and a CTA covers kRowThreads / 32 rows.
+constexpr int kWarpNormChunks = 8;
+
 template <typename T>
 __global__ void __launch_bounds__(kRowThreads)
-silu_mul_vec_kernel(const T* gate_up, int64_t stride, T* out, int64_t out_stride, int width, int64_t total_chunks) {
+rms_norm_warp_kernel(const T* x, int64_t x_stride, const T* weight, T* out, int64_t out_stride, int hidden,
+                     float eps, int64_t rows) {
     constexpr int E = Chunk<T>::kElems;
     wait_for_prior_grid();
     allow_next_grid();
-    const int chunks = width / E;
-    const int64_t step = static_cast<int64_t>(blockDim.x) * gridDim.x;
-    for (int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; idx < total_chunks; idx += step) {
-        const int64_t r = idx / chunks;
-        const int c = static_cast<int>(idx - r * chunks);
+    const int lane = threadIdx.x & 31;
+    const int64_t r = static_cast<int64_t>(blockIdx.x) * (kRowThreads / 32) + (threadIdx.x >> 5);
+    if (r >= rows) return;
+    const uint4* row = reinterpret_cast<const uint4*>(x + r * x_stride);
+    uint4* orow = reinterpret_cast<uint4*>(out + r * out_stride);
+    const uint4* wrow = reinterpret_cast<const uint4*>(weight);
+    const int chunks = hidden / E;
+    uint4 v[kWarpNormChunks];
+    float ss = 0.0f;
+#pragma unroll
+    for (int k = 0; k < kWarpNormChunks; ++k) {
+        const int c = lane + 32 * k;
+        if (c < chunks) {
+            v[k] = row[c];
+            const T* e = reinterpret_cast<const T*>(&v[k]);
+#pragma unroll
+            for (int i = 0; i < E; ++i) {
+                const float f = to_float<T>(e[i]);
+                ss = __fmaf_rn(f, f, ss);
+            }
+        }
+    }
+    const float scale = rsqrtf(warp_sum(ss) / static_cast<float>(hidden) + eps);
+#pragma unroll
+    for (int k = 0; k < kWarpNormChunks; ++k) {
+        const int c = lane + 32 * k;
+        if (c < chunks) {
+            const uint4 wv = wrow[c];
+            const T* e = reinterpret_cast<const T*>(&v[k]);
+            const T* we = reinterpret_cast<const T*>(&wv);
+            uint4 o;
+            T* oe = reinterpret_cast<T*>(&o);
+#pragma unroll
+            for (int i = 0; i < E; ++i) {
+                const T normalized = from_float<T>(__fmul_rn(to_float<T>(e[i]), scale));
+                oe[i] = from_float<T>(__fmul_rn(to_float<T>(we[i]), to_float<T>(normalized)));
+            }
+            orow[c] = o;
+        }
+    }
+}
+
+// Grid (chunk blocks, row blocks): no index division per element; rows beyond
+// the grid's y extent are taken in steps of gridDim.y.
+template <typename T>
+__global__ void __launch_bounds__(kRowThreads)
+silu_mul_vec_kernel(const T* gate_up, int64_t stride, T* out, int64_t out_stride, int width, int64_t rows) {
+    constexpr int E = Chunk<T>::kElems;
+    wait_for_prior_grid();
+    allow_next_grid();
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= width / E) return;
+    for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
         const uint4 gv = *reinterpret_cast<const uint4*>(gate_up + r * stride + c * E);
         const uint4 uv = *reinterpret_cast<const uint4*>(gate_up + r * stride + width + c * E);
         const T* g = reinterpret_cast<const T*>(&gv);
