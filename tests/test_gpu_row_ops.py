@@ -18,7 +18,7 @@ ULP = {torch.float32: 2 ** -22, torch.float16: 2 ** -10, torch.bfloat16: 2 ** -7
 
 
 @pytest.mark.parametrize('dtype', [torch.float32, torch.float16, torch.bfloat16])
-@pytest.mark.parametrize('shape', [(32, 1536), (3, 7, 256), (1, 33), (512, 4096)])
+@pytest.mark.parametrize('shape', [(32, 1536), (3, 7, 256), (1, 33), (512, 4096), (2048, 1536), (4096, 896)])
 def test_rms_norm_matches_the_reference_within_one_rounding(dtype, shape):
     from micro_vllm_b200.row_ops import rms_norm
     gen = torch.Generator(device='cuda').manual_seed(0)
