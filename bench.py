@@ -939,6 +939,24 @@ def run_kernels(args):
     c_q, c_rows = randn(4, 14, 64, dtype=torch.float32), randn(4, 2, 2, 64, dtype=torch.float32)
     x, h, w = randn(32, 12, 512, 128), randn(16384, 1536), torch.ones(1536, dtype=bf16, device=device)
     gate_up = randn(16384, 2 * 8960)
+    # Contiguous caches [64, 4, 4096, 128] (Qwen2.5-7B geometry), lengths U[1024, 4096].
+    cc_k, cc_v = randn(64, 4, 4096, 128), randn(64, 4, 4096, 128)
+    cc_lens = torch.randint(1024, 4097, (64,), generator=torch.Generator().manual_seed(3)).to(torch.int32)
+    cc_q = randn(64, 28, 128)
+    # Chunks of 4 new tokens per sequence over pages (Qwen2.5-7B geometry, 16 sequences).
+    ch_k, ch_v, ch_table, ch_lens = pool(16, 4, 128, 1024, 4096, bf16, 4)
+    ch_q = randn(16, 28, 4, 128)
+    kv_bytes = lambda lens, heads, dim, elem: int(lens.to(torch.int64).sum()) * 2 * heads * dim * elem  # noqa: E731
+    algorithmic = {
+        'decode_config4_wide_rope': kv_bytes(g_lens.cpu(), 2, 128, 2),
+        'decode_config1_simt_fp32': kv_bytes(c_lens.cpu(), 2, 64, 4),
+        'rope_prefill_32x12x512x128': 2 * x.numel() * 2,
+        'rms_norm_prefill_16384x1536': 2 * h.numel() * 2,
+        'silu_mul_prefill_16384x8960': gate_up.numel() * 2 + gate_up.numel(),
+        'contiguous_decode_qwen7b_geometry': kv_bytes(cc_lens, 4, 128, 2),
+        'chunk_attention_qwen7b_geometry_t4': kv_bytes(ch_lens.cpu(), 4, 128, 2),
+    }
+    cc_lens = cc_lens.to(device)
     calls = {
         'decode_config4_wide_rope': lambda: cuda_attention.paged_decode_with_append(
             g_q, g_rows[:, 0], g_rows[:, 1], g_k, g_v, g_table, g_lens, max_context_len=int(g_table.shape[1] * 16),
@@ -948,6 +966,10 @@ def run_kernels(args):
         'rope_prefill_32x12x512x128': lambda: apply_rope(x, cos, sin, start=0),
         'rms_norm_prefill_16384x1536': lambda: rms_norm(h, w, 1e-6),
         'silu_mul_prefill_16384x8960': lambda: silu_mul(gate_up),
+        'contiguous_decode_qwen7b_geometry': lambda: cuda_attention.contiguous_decode_attention(
+            cc_q, cc_k, cc_v, cc_lens),
+        'chunk_attention_qwen7b_geometry_t4': lambda: cuda_attention.paged_chunk_attention(
+            ch_q, ch_k, ch_v, ch_table, ch_lens),
     }
     timings = {}
     stream = torch.cuda.Stream(device)
@@ -974,8 +996,12 @@ def run_kernels(args):
         torch.cuda.synchronize(device)
         timings[name] = round(start.elapsed_time(end) * 1e3 / (reps * calls_per_graph), 2)
         del graph
+    gbs = {name: round(algorithmic[name] / (us * 1e3), 1) for name, us in timings.items() if name in algorithmic}
     return {'metric': 'per-call device time of this library\'s kernels on config-4 / config-1 shapes',
             'unit': 'us per call', 'values': timings,
+            'algorithmic_gbs': gbs,
+            'note': ('algorithmic bytes: K and V read once (decode, contiguous decode; the chunk entry counts '
+                     'them once though each of its rows reads its own prefix), rows in and out (row kernels)'),
             'config': {'workload': 'kernels_qwen15b',
                        'timing': 'CUDA events around replays of a graph of back-to-back calls'}}
 
