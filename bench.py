@@ -71,6 +71,8 @@ def parse_args(argv=None):
                         help='wall-clock budget of the CPU baseline sample')
     parser.add_argument('--no-cpu-baseline', action='store_true')
     parser.add_argument('--pages-per-split', type=int, default=0)
+    parser.add_argument('--kernels', default='',
+                        help='kernels_qwen15b workload: time only the entries whose names contain this text')
     parser.add_argument('--nvtx-steps', type=int, default=0,
                         help='generation workload: run prefill and this many eager decode steps inside NVTX '
                              'ranges "prefill" and "decode" (for a profiler launch list), print nothing else')
@@ -946,6 +948,12 @@ def run_kernels(args):
     # Chunks of 4 new tokens per sequence over pages (Qwen2.5-7B geometry, 16 sequences).
     ch_k, ch_v, ch_table, ch_lens = pool(16, 4, 128, 1024, 4096, bf16, 4)
     ch_q = randn(16, 28, 4, 128)
+    # A 256-token prefill chunk after 1024 cached tokens (Qwen2.5-1.5B heads, 4 sequences).
+    cp_k, cp_v, cp_table, cp_lens = pool(4, 2, 128, 1280, 1280, bf16, 5)
+    cp_q = randn(4, 12, 256, 128)
+    # Flops of a chunk: each query row attends its causal prefix, 4 D flops per (row, token).
+    chunk_flops = lambda lens, tokens, q_heads, dim: sum(  # noqa: E731
+        4 * dim * q_heads * (int(n) - t) for n in lens.tolist() for t in range(tokens))
     kv_bytes = lambda lens, heads, dim, elem: int(lens.to(torch.int64).sum()) * 2 * heads * dim * elem  # noqa: E731
     algorithmic = {
         'decode_config4_wide_rope': kv_bytes(g_lens.cpu(), 2, 128, 2),
@@ -970,9 +978,17 @@ def run_kernels(args):
             cc_q, cc_k, cc_v, cc_lens),
         'chunk_attention_qwen7b_geometry_t4': lambda: cuda_attention.paged_chunk_attention(
             ch_q, ch_k, ch_v, ch_table, ch_lens),
+        'chunk_attention_qwen7b_geometry_t4_rows': lambda: cuda_attention.paged_chunk_attention(
+            ch_q, ch_k, ch_v, ch_table, ch_lens, rows_kernel=True),
+        'chunk_prefill_qwen15b_t256_after_1024': lambda: cuda_attention.paged_chunk_attention(
+            cp_q, cp_k, cp_v, cp_table, cp_lens),
+        'chunk_prefill_qwen15b_t256_after_1024_rows': lambda: cuda_attention.paged_chunk_attention(
+            cp_q, cp_k, cp_v, cp_table, cp_lens, rows_kernel=True),
     }
+    flops = {name: chunk_flops(cp_lens.cpu(), 256, 12, 128) for name in calls if name.startswith('chunk_prefill')}
     timings = {}
     stream = torch.cuda.Stream(device)
+    calls = {name: fn for name, fn in calls.items() if args.kernels in name}
     for name, fn in calls.items():
         stream.wait_stream(torch.cuda.current_stream(device))
         with torch.cuda.stream(stream):
@@ -996,10 +1012,12 @@ def run_kernels(args):
         torch.cuda.synchronize(device)
         timings[name] = round(start.elapsed_time(end) * 1e3 / (reps * calls_per_graph), 2)
         del graph
+    algorithmic['chunk_attention_qwen7b_geometry_t4_rows'] = algorithmic['chunk_attention_qwen7b_geometry_t4']
     gbs = {name: round(algorithmic[name] / (us * 1e3), 1) for name, us in timings.items() if name in algorithmic}
+    tflops = {name: round(flops[name] / (us * 1e6), 1) for name, us in timings.items() if name in flops}
     return {'metric': 'per-call device time of this library\'s kernels on config-4 / config-1 shapes',
             'unit': 'us per call', 'values': timings,
-            'algorithmic_gbs': gbs,
+            'algorithmic_gbs': gbs, 'algorithmic_tflops': tflops,
             'note': ('algorithmic bytes: K and V read once (decode, contiguous decode; the chunk entry counts '
                      'them once though each of its rows reads its own prefix), rows in and out (row kernels)'),
             'config': {'workload': 'kernels_qwen15b',

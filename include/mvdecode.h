@@ -51,6 +51,7 @@ extern "C" {
 #define MV_FLAG_FUSED_MERGE 4u /* split grid: the last split CTA of each sequence/head merges it */
 #define MV_FLAG_CLUSTER 8u /* tensor-core cluster kernel (contexts up to 8192 tokens), no merge pass */
 #define MV_FLAG_WIDE 16u /* split grid in the wide shape (8 warps, deeper rings; head_dim 64/128) */
+#define MV_FLAG_CHUNK_ROWS 32u /* mv_paged_chunk_attention: one query row per token, not query tiles */
 
 /* Status codes. */
 #define MV_OK 0
@@ -142,11 +143,25 @@ MV_API int mv_paged_decode(const void* q, int64_t q_stride_seq, int64_t q_stride
  * Replaces the reference's cached multi-token path, which gathers the pages
  * into contiguous K/V and runs causal attention
  * (src/micro_vllm/model.py:178-182, paged_kv_cache.py:178-193,
- * attention.py:57-94). Runs the split grid or the CUDA-core kernel with one
- * query row per (sequence, token): each row reads its own prefix, so this
- * suits short chunks. Workspace: mv_paged_decode_workspace_size with
- * batch x num_tokens rows. Other contracts as mv_paged_decode.
+ * attention.py:57-94). fp16/bf16 with head_dim 64 or 128, 16-token pages,
+ * at least 16 (token x query head) rows per (sequence, KV head) and a 4-byte
+ * aligned query run as query tiles on tensor cores: 64 such rows per CTA
+ * share one stream of the pages. Otherwise -- or with MV_FLAG_CHUNK_ROWS --
+ * the split grid or the CUDA-core kernel run one decode query row per
+ * (sequence, token), each reading its own prefix. Workspace:
+ * mv_paged_chunk_workspace_size. Flags PERSISTENT, CLUSTER, WIDE and
+ * FUSED_MERGE are ignored. Other contracts as mv_paged_decode.
  */
+/*
+ * Workspace bytes mv_paged_chunk_attention needs for this geometry (the same
+ * arguments, num_tokens per sequence). No reference counterpart: the
+ * reference's chunk path allocates its gathered K/V itself.
+ */
+MV_API int mv_paged_chunk_workspace_size(int32_t batch, int32_t num_tokens, int32_t num_q_heads,
+                                         int32_t num_kv_heads, int32_t head_dim, int32_t block_size,
+                                         int64_t max_context_len, int32_t pages_per_split, uint32_t flags,
+                                         int32_t dtype, size_t* bytes);
+
 MV_API int mv_paged_chunk_attention(const void* q, int64_t q_stride_seq, int64_t q_stride_token,
                                     int64_t q_stride_head, const void* k_cache, const void* v_cache,
                                     int64_t num_blocks, int32_t num_kv_heads, int32_t block_size,

@@ -22,6 +22,7 @@ FLAG_PERSISTENT = 2
 FLAG_FUSED_MERGE = 4
 FLAG_CLUSTER = 8
 FLAG_WIDE = 16
+FLAG_CHUNK_ROWS = 32
 PATH_SIMT, PATH_TMA_MMA, PATH_TMA_MMA_PERSISTENT, PATH_TMA_MMA_CLUSTER = 0, 1, 2, 3
 PATH_NAMES = {0: 'simt', 1: 'tma_mma', 2: 'tma_mma_persistent', 3: 'tma_mma_cluster'}
 DEVICE_STATUS_WAIT_TIMEOUT = 1
@@ -39,7 +40,7 @@ EXPORTED_SYMBOLS = (
     'mv_paged_decode_plan', 'mv_paged_decode', 'mv_write_paged_kv',
     'mv_device_status', 'mv_clear_device_status', 'mv_paged_decode_append', 'mv_apply_rope',
     'mv_rms_norm', 'mv_silu_mul', 'mv_contiguous_decode_plan', 'mv_contiguous_decode',
-    'mv_paged_chunk_attention',
+    'mv_paged_chunk_workspace_size', 'mv_paged_chunk_attention',
 )
 
 _i32, _i64, _u32, _vp, _sz, _f32 = (ctypes.c_int32, ctypes.c_int64, ctypes.c_uint32,
@@ -91,6 +92,8 @@ _SIGNATURES = {
                        _vp, _i32, _i32, _i64,      # positions, type, kind, start
                        _i32, _vp]),                # dtype, stream
     'mv_rms_norm': (ctypes.c_int, [_vp, _i64, _vp, _vp, _i64, _i64, _i32, _f32, _i32, _vp]),
+    'mv_paged_chunk_workspace_size': (
+        ctypes.c_int, [_i32, _i32, _i32, _i32, _i32, _i32, _i64, _i32, _u32, _i32, ctypes.POINTER(_sz)]),
     'mv_paged_chunk_attention': (
         ctypes.c_int, [_vp, _i64, _i64, _i64,      # q, strides (sequence, token, head)
                        _vp, _vp, _i64,             # k_cache, v_cache, num_blocks

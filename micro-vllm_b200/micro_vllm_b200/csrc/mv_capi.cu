@@ -14,6 +14,7 @@
 
 #include "mvdecode.h"
 #include "paged_append.cuh"
+#include "paged_chunk_mma.cuh"
 #include "paged_decode_merge.cuh"
 #include "paged_decode_mma.cuh"
 #include "paged_decode_simt.cuh"
@@ -95,6 +96,18 @@ int ensure_smem(Kernel kernel, size_t bytes) {
     if (bytes <= 48 * 1024) return MV_OK;
     cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            static_cast<int>(bytes));
+    return err == cudaSuccess ? MV_OK : cuda_fail(err, "cudaFuncSetAttribute");
+}
+
+// As ensure_smem, and prefer the largest shared-memory carveout: left to
+// itself the driver may pick a carveout that holds fewer CTAs than the
+// kernel's registers allow.
+template <typename Kernel>
+int ensure_smem_carveout(Kernel kernel, size_t bytes) {
+    int rc = ensure_smem(kernel, bytes);
+    if (rc != MV_OK) return rc;
+    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                           static_cast<int>(cudaSharedmemCarveoutMaxShared));
     return err == cudaSuccess ? MV_OK : cuda_fail(err, "cudaFuncSetAttribute");
 }
 
@@ -363,6 +376,57 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
                         "GQA group %d x head_dim %d needs %zu bytes of shared memory (device limit %d)",
                         group, g.head_dim, smem, dev.smem_optin);
     }
+    return MV_OK;
+}
+
+// Plan of a chunk of `tokens` query tokens per sequence; g.batch counts query
+// rows (sequences x tokens). Where the query-tile kernel applies -- the split
+// grid's tensor-core plan, head_dim 64/128 and at least 16 rows (token x
+// query head) per (sequence, KV head) -- its splits are sized for tiles of 64
+// rows: enough equal splits of the max_context_len bound for about two waves
+// of resident tile CTAs (three per SM), none shorter than kChunkMinPages pages.
+// The plan is the split grid's either way, so a call whose query is not
+// aligned for the tile kernel runs the row-per-token kernel on the same splits.
+constexpr int64_t kChunkCtasPerSm = 3;
+constexpr int64_t kChunkMinPages = 32;
+
+int make_chunk_plan(const Geometry& g, int32_t tokens, int32_t pages_per_split, uint32_t flags,
+                    bool aligned_for_tma, Plan* plan, bool* tiles) {
+    int rc = make_plan(g, pages_per_split, flags, aligned_for_tma, plan);
+    if (rc != MV_OK) return rc;
+    const int group = g.q_heads / g.kv_heads;
+    *tiles = !(flags & MV_FLAG_CHUNK_ROWS) && plan->path == MV_PATH_TMA_MMA &&
+             (g.head_dim == 64 || g.head_dim == 128) && static_cast<int64_t>(tokens) * group >= 16 &&
+             pages_per_split <= mv::kChunkMaxPages;
+    if (!*tiles) return MV_OK;
+    DeviceInfo dev;
+    rc = device_info(&dev);
+    if (rc != MV_OK) return rc;
+    const int64_t max_pages = std::max<int64_t>(1, (g.max_context_len + 15) / 16);
+    int64_t pps = pages_per_split;
+    if (pps == 0) {
+        const int64_t sequences = g.batch / tokens;
+        const int64_t q_tiles = (static_cast<int64_t>(tokens) * group + mv::kChunkRows - 1) / mv::kChunkRows;
+        const int64_t tiles_total = sequences * g.kv_heads * q_tiles;
+        const int64_t target = static_cast<int64_t>(dev.sms) * kChunkCtasPerSm * 2;
+        int64_t splits = std::max<int64_t>(1, (target + tiles_total - 1) / tiles_total);
+        splits = std::min<int64_t>(splits, std::max<int64_t>(1, (max_pages + kChunkMinPages - 1) / kChunkMinPages));
+        pps = std::min<int64_t>((max_pages + splits - 1) / splits, mv::kChunkMaxPages);
+    }
+    const int64_t splits = std::max<int64_t>(1, (max_pages + pps - 1) / pps);
+    if (splits > 8192) return fail(MV_ERR_UNSUPPORTED, "more than 8192 splits: raise pages_per_split");
+    plan->wide = false;
+    plan->fused_merge = false;
+    plan->pages_per_split = static_cast<int>(pps);
+    plan->max_splits = static_cast<int>(splits);
+    plan->counter_bytes = plan->part_o_bytes = plan->part_lse_bytes = 0;
+    if (splits > 1) {
+        const size_t rows = static_cast<size_t>(g.batch) * g.q_heads * splits;
+        plan->part_o_bytes = round256(rows * g.head_dim * sizeof(float));
+        plan->part_lse_bytes = round256(rows * sizeof(float));
+        plan->counter_bytes = kCounterRegion;
+    }
+    plan->workspace = plan->counter_bytes + plan->part_o_bytes + plan->part_lse_bytes;
     return MV_OK;
 }
 
@@ -653,6 +717,40 @@ void contiguous_map_strides(const int64_t* s, int heads, int batch, int64_t toke
     out[2] = batch > 1 ? s[0] : out[1] * heads;
 }
 
+// A chunk runs on the split grid (query tiles or rows), never the persistent,
+// cluster or opted-in wide schedules, and merges in a separate pass.
+uint32_t chunk_flags(uint32_t flags) {
+    return flags & ~(MV_FLAG_PERSISTENT | MV_FLAG_CLUSTER | MV_FLAG_WIDE | MV_FLAG_FUSED_MERGE);
+}
+
+// Query tiles of chunk rows on tensor cores, then the split merge.
+template <typename T>
+int launch_chunk_tiles(const mv::DecodeParams& p, const Plan& plan, const CUtensorMap& kmap, const CUtensorMap& vmap,
+                       int sequences, cudaStream_t stream) {
+    const int q_tiles = (p.q_tokens * p.group + mv::kChunkRows - 1) / mv::kChunkRows;
+    const dim3 grid(static_cast<unsigned>(q_tiles) * plan.max_splits, p.kv_heads, sequences);
+    cudaError_t err;
+    if (p.head_dim == 64) {
+        auto kernel = mv::paged_chunk_mma_kernel<T, 64>;
+        int rc = ensure_smem_carveout(kernel, mv::ChunkShape<64>::kSmemBytes);
+        if (rc != MV_OK) return rc;
+        err = launch_pdl(kernel, grid, dim3(mv::kChunkThreads), mv::ChunkShape<64>::kSmemBytes, stream, p, kmap, vmap,
+                         q_tiles);
+    } else {
+        auto kernel = mv::paged_chunk_mma_kernel<T, 128>;
+        int rc = ensure_smem_carveout(kernel, mv::ChunkShape<128>::kSmemBytes);
+        if (rc != MV_OK) return rc;
+        err = launch_pdl(kernel, grid, dim3(mv::kChunkThreads), mv::ChunkShape<128>::kSmemBytes, stream, p, kmap,
+                         vmap, q_tiles);
+    }
+    if (err != cudaSuccess) return cuda_fail(err, "chunk attention kernel launch");
+    if (plan.max_splits > 1) {
+        err = launch_pdl(mv::paged_decode_merge_kernel<T>, merge_grid(p), dim3(mv::kMergeThreads), 0, stream, p);
+        if (err != cudaSuccess) return cuda_fail(err, "merge kernel launch");
+    }
+    return MV_OK;
+}
+
 struct ContiguousCall {
     const void* k_cache;
     int64_t k_stride[3];  // sequence, head, token (elements)
@@ -695,6 +793,22 @@ int mv_paged_decode_workspace_size(int32_t batch, int32_t num_q_heads, int32_t n
     Plan plan;
     // Alignment never changes the split shape, so plan as if aligned.
     int rc = make_plan(g, pages_per_split, flags, true, &plan);
+    if (rc != MV_OK) return rc;
+    *bytes = plan.workspace;
+    return MV_OK;
+}
+
+int mv_paged_chunk_workspace_size(int32_t batch, int32_t num_tokens, int32_t num_q_heads, int32_t num_kv_heads,
+                                  int32_t head_dim, int32_t block_size, int64_t max_context_len,
+                                  int32_t pages_per_split, uint32_t flags, int32_t dtype, size_t* bytes) {
+    if (!bytes) return fail(MV_ERR_INVALID_ARGUMENT, "bytes must not be NULL");
+    if (num_tokens <= 0 || batch <= 0) return fail(MV_ERR_INVALID_ARGUMENT, "batch and num_tokens must be positive");
+    if (static_cast<int64_t>(batch) * num_tokens > 65535)
+        return fail(MV_ERR_UNSUPPORTED, "batch x num_tokens is limited to 65535 query rows");
+    const Geometry g{batch * num_tokens, num_q_heads, num_kv_heads, head_dim, block_size, max_context_len, dtype};
+    Plan plan;
+    bool tiles = false;
+    int rc = make_chunk_plan(g, num_tokens, pages_per_split, chunk_flags(flags), true, &plan, &tiles);
     if (rc != MV_OK) return rc;
     *bytes = plan.workspace;
     return MV_OK;
@@ -765,7 +879,9 @@ static int paged_decode_impl(const void* q, int64_t q_stride_seq, int64_t q_stri
 
     const Geometry g{batch, num_q_heads, num_kv_heads, head_dim, block_size, max_context_len, dtype};
     Plan plan;
-    rc = make_plan(g, pages_per_split, flags, tma_aligned(k_cache, v_cache), &plan);
+    bool tiles = false;
+    rc = chunk ? make_chunk_plan(g, tokens, pages_per_split, flags, tma_aligned(k_cache, v_cache), &plan, &tiles)
+               : make_plan(g, pages_per_split, flags, tma_aligned(k_cache, v_cache), &plan);
     if (rc != MV_OK) return rc;
     if (plan.workspace > 0 && (!workspace || workspace_bytes < plan.workspace))
         return fail(MV_ERR_WORKSPACE_TOO_SMALL, "workspace of %zu bytes needed, %zu given", plan.workspace,
@@ -876,6 +992,13 @@ static int paged_decode_impl(const void* q, int64_t q_stride_seq, int64_t q_stri
         if (rc != MV_OK) return rc;
     }
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    // Chunks of tokens as query tiles on tensor cores where the chunk plan
+    // allows them and the query's element pairs are 4-byte aligned.
+    if (tiles && reinterpret_cast<uintptr_t>(q) % 4 == 0 &&
+        ((q_stride_seq | q_stride_head | chunk->q_stride_token) & 1) == 0) {
+        return dtype == MV_DTYPE_F16 ? launch_chunk_tiles<__half>(p, plan, kmap, vmap, sequences, s)
+                                     : launch_chunk_tiles<__nv_bfloat16>(p, plan, kmap, vmap, sequences, s);
+    }
     switch (dtype) {
         case MV_DTYPE_F32: return launch_decode<float>(p, plan, &kmap, &vmap, s);
         case MV_DTYPE_F16: return launch_decode<__half>(p, plan, &kmap, &vmap, s);
@@ -938,14 +1061,11 @@ int mv_paged_chunk_attention(const void* q, int64_t q_stride_seq, int64_t q_stri
         return fail(MV_ERR_UNSUPPORTED, "batch x num_tokens is limited to 65535 query rows");
     if (q_stride_token < 0 || out_stride_token < 0) return fail(MV_ERR_INVALID_ARGUMENT, "strides must be nonnegative");
     const ChunkRows chunk{num_tokens, q_stride_token, out_stride_token};
-    // The split grid and the CUDA-core kernel take query rows; the persistent
-    // and cluster schedules do not.
     return paged_decode_impl(q, q_stride_seq, q_stride_head, k_cache, v_cache, num_blocks, num_kv_heads, block_size,
                              head_dim, block_table, block_table_type, block_table_stride, blocks_per_seq,
                              context_lens, context_lens_type, max_context_len, batch * num_tokens, num_q_heads,
                              scale, out, out_stride_seq, out_stride_head, workspace, workspace_bytes,
-                             pages_per_split, flags & ~(MV_FLAG_PERSISTENT | MV_FLAG_CLUSTER), dtype, stream, nullptr,
-                             &chunk);
+                             pages_per_split, chunk_flags(flags), dtype, stream, nullptr, &chunk);
 }
 
 int mv_contiguous_decode_plan(const void* k_cache, int64_t k_stride_seq, int64_t k_stride_head,

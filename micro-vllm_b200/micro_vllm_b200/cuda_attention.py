@@ -702,7 +702,8 @@ def contiguous_decode_plan(key_cache, value_cache, query_heads, *, max_context_l
 def paged_chunk_attention(query: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
                           block_table: torch.Tensor, context_lens: torch.Tensor, scale: float | None = None, *,
                           max_context_len: int | None = None, out: torch.Tensor | None = None,
-                          pages_per_split: int = 0, force_simt: bool = False, wide: bool = False) -> torch.Tensor:
+                          pages_per_split: int = 0, force_simt: bool = False,
+                          rows_kernel: bool = False) -> torch.Tensor:
     """Causal attention of a chunk of T new tokens per sequence over its pages.
 
     query: [B, Hq, T, D] (the reference's layout for a cached chunk), feature
@@ -710,6 +711,10 @@ def paged_chunk_attention(query: torch.Tensor, key_cache: torch.Tensor, value_ca
     counts each sequence's tokens after the chunk, and token t attends the
     first context_lens - (T - 1 - t) of them (model.py:178-182 gathers the
     pages and runs causal attention for this; nothing is gathered here).
+    The chunk runs as query tiles on tensor cores (64 rows of token x head per
+    CTA, each page streamed once per tile) where the shape allows (fp16/bf16,
+    head_dim 64/128, 16-token pages, T x G >= 16), else -- or with
+    ``rows_kernel`` -- as one decode query row per token.
     Other arguments as ``paged_decode_attention``. Returns [B, Hq, T, D].
     """
     _check(isinstance(query, torch.Tensor) and query.dim() == 4, 'query must be [B, Hq, T, D]')
@@ -726,13 +731,13 @@ def paged_chunk_attention(query: torch.Tensor, key_cache: torch.Tensor, value_ca
                and out.stride(3) == 1, 'out must be a [B, Hq, T, D] tensor of the query dtype and device')
     lib = _native.library()
     num_blocks, kv_heads, block_size, _ = key_cache.shape
-    flags = _flags(force_simt, False, wide=wide)
+    flags = _flags(force_simt, False) | (_native.FLAG_CHUNK_ROWS if rows_kernel else 0)
     dtype = DTYPE_CODES[key_cache.dtype]
     device = key_cache.device
     with torch.cuda.device(device):
         size = ctypes.c_size_t(0)
-        _native.check(lib.mv_paged_decode_workspace_size(
-            batch * tokens, q_heads, kv_heads, dim, block_size, int(bound), int(pages_per_split), flags, dtype,
+        _native.check(lib.mv_paged_chunk_workspace_size(
+            batch, tokens, q_heads, kv_heads, dim, block_size, int(bound), int(pages_per_split), flags, dtype,
             ctypes.byref(size)))
         stream = current_stream_handle(device)
         workspace = _workspace(device, stream, size.value) if size.value else None

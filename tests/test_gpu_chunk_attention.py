@@ -15,7 +15,8 @@ from tests.helpers import as_float, assert_attention_close, to_torch, workload_t
 
 pytestmark = pytest.mark.gpu
 
-MODES = {'auto': {}, 'simt': dict(force_simt=True), 'wide': dict(wide=True), 'split4': dict(pages_per_split=4)}
+MODES = {'auto': {}, 'simt': dict(force_simt=True), 'rows': dict(rows_kernel=True),
+         'split4': dict(pages_per_split=4), 'rows_split4': dict(pages_per_split=4, rows_kernel=True)}
 
 
 def _chunk_oracle(inputs, q_np, tokens, dtype):
@@ -49,6 +50,91 @@ def test_chunk_rows_match_the_oracle(name, tokens, mode):
     assert out.shape == q.shape
     expected = _chunk_oracle(inputs, q_np, tokens, dtype)
     assert_attention_close(as_float(out), expected, dtype)
+
+
+def _random_chunk(inputs, tokens, seed):
+    from oracle.dtypes import from_float32
+    dtype = inputs['spec']['dtype']
+    batch, hq, dim = inputs['q'].shape
+    rng = np.random.default_rng(seed)
+    scale = inputs['spec']['value_scale']
+    q_np = from_float32(rng.standard_normal((batch, hq, tokens, dim), dtype=np.float32) * np.float32(scale), dtype)
+    return q_np, to_torch(q_np, dtype)
+
+
+# (workload, tokens, pages_per_split): long chunks whose rows span several
+# 64-row query tiles, head_dim 64 and 128, one and several splits per row.
+TILE_CASES = [('qwen3_8b_bf16_small', 64, 0), ('qwen3_8b_bf16_small', 100, 8), ('qwen05b_bf16', 48, 0),
+              ('qwen05b_fp16', 70, 3), ('qwen72b_bf16_small', 9, 1), ('qwen7b_bf16_small', 130, 0)]
+
+
+@pytest.mark.parametrize('name, tokens, pps', TILE_CASES)
+def test_query_tiles_match_the_oracle_and_the_row_kernel(name, tokens, pps):
+    """The tile kernel and the row-per-token kernel both meet the oracle's bar."""
+    from micro_vllm_b200 import cuda_attention
+    inputs = make_inputs(name)
+    dtype = inputs['spec']['dtype']
+    t = workload_tensors(inputs)
+    q_np, q = _random_chunk(inputs, tokens, 7 + tokens)
+    args = (q, t['key_pool'], t['value_pool'], t['block_table'], t['context_lens'])
+    tiles = cuda_attention.paged_chunk_attention(*args, pages_per_split=pps)
+    rows = cuda_attention.paged_chunk_attention(*args, pages_per_split=pps, rows_kernel=True)
+    expected = _chunk_oracle(inputs, q_np, tokens, dtype)
+    assert_attention_close(as_float(tiles), expected, dtype)
+    assert_attention_close(as_float(rows), expected, dtype)
+
+
+@pytest.mark.parametrize('pps', [0, 8])
+def test_corrupted_page_poisons_only_the_rows_that_reach_it(pps):
+    """A bad page ID poisons exactly the chunk rows whose context covers it
+    (rows before it in the same tile stay finite); other sequences are untouched."""
+    from micro_vllm_b200 import cuda_attention
+    inputs = make_inputs('qwen3_8b_bf16_small')   # lengths 700 and 1029
+    inputs['block_table'] = inputs['block_table'].copy()
+    num_pages = inputs['key_pool'].shape[0]
+    inputs['block_table'][1, 62] = num_pages + 5     # tokens 992..1007 of sequence 1
+    inputs['block_table'][0, 43] = -3                # tokens 688..703 of sequence 0
+    t = workload_tensors(inputs)
+    q_np, q = _random_chunk(inputs, 64, 11)
+    out = cuda_attention.paged_chunk_attention(q, t['key_pool'], t['value_pool'], t['block_table'],
+                                               t['context_lens'], pages_per_split=pps)
+    expected = _chunk_oracle(inputs, q_np, 64, 'bfloat16')
+    nan_tokens = np.isnan(expected[1, 0, :, 0])
+    assert nan_tokens.any() and not nan_tokens.all()
+    assert_attention_close(as_float(out), expected, 'bfloat16')
+
+
+LONG_SPEC = dict(batch=2, q_heads=8, kv_heads=2, head_dim=64, block_size=16, pool=('factor', 1.25),
+                 lens=('fixed', [2100, 1500]), dtype='bfloat16', value_scale=1.0, seed=9101)
+
+
+@pytest.mark.parametrize('pps', [1, 0])
+def test_query_tiles_with_many_splits(pps):
+    """132 one-page splits per row (the merge pass combines up to 132 partials),
+    and the automatic plan's few long splits."""
+    from micro_vllm_b200 import cuda_attention
+    inputs = make_inputs(LONG_SPEC)
+    t = workload_tensors(inputs)
+    q_np, q = _random_chunk(inputs, 8, 5)
+    out = cuda_attention.paged_chunk_attention(q, t['key_pool'], t['value_pool'], t['block_table'],
+                                               t['context_lens'], pages_per_split=pps)
+    assert_attention_close(as_float(out), _chunk_oracle(inputs, q_np, 8, 'bfloat16'), 'bfloat16')
+
+
+def test_unaligned_query_runs_the_row_kernel_on_the_tile_plan():
+    """A query whose element pairs are not 4-byte aligned cannot feed the tile
+    kernel; the row-per-token kernel runs on the same splits and workspace."""
+    from micro_vllm_b200 import cuda_attention
+    from tests.helpers import to_numpy
+    inputs = make_inputs('qwen3_8b_bf16_small')
+    t = workload_tensors(inputs)
+    batch, hq, dim = t['q'].shape
+    store = torch.randn(batch, hq, 24, dim + 1, device='cuda').to(torch.bfloat16)
+    q = store[..., 1:]                                    # 2-byte offset, odd strides
+    out = cuda_attention.paged_chunk_attention(q, t['key_pool'], t['value_pool'], t['block_table'],
+                                               t['context_lens'])
+    expected = _chunk_oracle(inputs, to_numpy(q.contiguous()), 24, 'bfloat16')
+    assert_attention_close(as_float(out), expected, 'bfloat16')
 
 
 def test_one_token_chunk_equals_decode_bit_for_bit():

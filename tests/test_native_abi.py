@@ -34,7 +34,8 @@ def test_header_declares_the_expected_entry_points():
         'mv_paged_decode_plan', 'mv_paged_decode', 'mv_write_paged_kv',
         'mv_device_status', 'mv_clear_device_status', 'mv_paged_decode_noalloc',
         'mv_paged_decode_append', 'mv_apply_rope', 'mv_rms_norm', 'mv_silu_mul',
-        'mv_contiguous_decode_plan', 'mv_contiguous_decode', 'mv_paged_chunk_attention'}
+        'mv_contiguous_decode_plan', 'mv_contiguous_decode', 'mv_paged_chunk_workspace_size',
+        'mv_paged_chunk_attention'}
 
 
 def test_library_loads_and_exports_every_declared_symbol():
@@ -73,6 +74,7 @@ def test_python_binding_constants_match_the_header():
     assert constants['MV_PATH_TMA_MMA_CLUSTER'] == _native.PATH_TMA_MMA_CLUSTER
     assert constants['MV_FLAG_CLUSTER'] == _native.FLAG_CLUSTER
     assert constants['MV_FLAG_WIDE'] == _native.FLAG_WIDE
+    assert constants['MV_FLAG_CHUNK_ROWS'] == _native.FLAG_CHUNK_ROWS
     assert constants['MV_DEVICE_STATUS_WAIT_TIMEOUT'] == _native.DEVICE_STATUS_WAIT_TIMEOUT
     assert constants['MV_ABI_VERSION'] == _native.MV_ABI_VERSION
 
