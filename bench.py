@@ -537,9 +537,9 @@ def run_ours(args):
             'pct_of_hbm_peak': round(100 * value / world / peak, 2),
             'roofline': {
                 'bound': 'hbm',
-                'kernel': ('paged_decode_mma_kernel (append fused) + paged_decode_merge_kernel'
+                'kernel': ('paged_decode_mma_kernel (append fused) + paged_decode_merge_warp_kernel'
                            if args.step == 'fused' else
-                           'write_paged_kv_kernel + paged_decode_mma_kernel + paged_decode_merge_kernel'),
+                           'write_paged_kv_kernel + paged_decode_mma_kernel + paged_decode_merge_warp_kernel'),
                 'timing': (f'CUDA events around graphs of {KERNEL_CALLS} back-to-back steps: '
                            'average launch duration without the per-replay graph launch gap'),
                 'achieved': round(achieved, 1),

@@ -577,6 +577,18 @@ int launch_mma_dispatch(const mv::DecodeParams& p, const CUtensorMap& kmap, cons
 // One CTA per output row (query head, sequence).
 dim3 merge_grid(const mv::DecodeParams& p) { return dim3(p.q_heads, p.batch); }
 
+// The split grid's merge pass: a warp per output row where head_dim <= 128 is a
+// multiple of 4 and rows have at most 32 pieces, else a CTA per row.
+template <typename T>
+cudaError_t launch_split_merge(const mv::DecodeParams& p, cudaStream_t stream) {
+    if (p.head_dim % 4 == 0 && p.head_dim <= 128 && p.max_splits <= 32) {
+        const int64_t rows = static_cast<int64_t>(p.batch) * p.q_heads;
+        const dim3 grid(static_cast<unsigned>((rows + mv::kWarpMergeRows - 1) / mv::kWarpMergeRows));
+        return launch_pdl(mv::paged_decode_merge_warp_kernel<T>, grid, dim3(mv::kWarpMergeRows * 32), 0, stream, p);
+    }
+    return launch_pdl(mv::paged_decode_merge_kernel<T>, merge_grid(p), dim3(mv::kMergeThreads), 0, stream, p);
+}
+
 template <typename T, int D, int NT>
 int launch_persistent(const mv::DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap,
                       int ctas, cudaStream_t stream) {
@@ -683,10 +695,9 @@ int launch_decode(const mv::DecodeParams& p, const Plan& plan, const CUtensorMap
     cudaError_t err = cudaGetLastError();
     if (err != cudaSuccess) return cuda_fail(err, "decode kernel launch");
     if (plan.max_splits > 1 && !plan.fused_merge) {
-        // One CTA per output row: measured on B200, many short rows merge faster
-        // than one CTA per (sequence, KV head) looping over its G rows.
-        err = launch_pdl(mv::paged_decode_merge_kernel<T>, merge_grid(p), dim3(mv::kMergeThreads), 0,
-                         stream, p);
+        // Per output row: measured on B200, many short rows merge faster than
+        // one CTA per (sequence, KV head) looping over its G rows.
+        err = launch_split_merge<T>(p, stream);
         if (err != cudaSuccess) return cuda_fail(err, "merge kernel launch");
     }
     return MV_OK;
@@ -745,7 +756,7 @@ int launch_chunk_tiles(const mv::DecodeParams& p, const Plan& plan, const CUtens
     }
     if (err != cudaSuccess) return cuda_fail(err, "chunk attention kernel launch");
     if (plan.max_splits > 1) {
-        err = launch_pdl(mv::paged_decode_merge_kernel<T>, merge_grid(p), dim3(mv::kMergeThreads), 0, stream, p);
+        err = launch_split_merge<T>(p, stream);
         if (err != cudaSuccess) return cuda_fail(err, "merge kernel launch");
     }
     return MV_OK;

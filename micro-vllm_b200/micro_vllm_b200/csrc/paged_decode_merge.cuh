@@ -183,6 +183,70 @@ __global__ void __launch_bounds__(kMergeThreads) paged_decode_merge_kernel(const
     merge_row<T>(p, out, [&](int j) -> long long { return base + j; }, seq.splits);
 }
 
+// Warp-per-row merge of the split grid for head_dim <= 128 (a multiple of 4)
+// and at most 32 pieces: lane j holds piece j's log-sum-exp and every lane
+// one float4 column of up to kWarpMergeBatch pieces' partial rows, all loaded
+// together -- one dependent round of loads where the CTA-per-row merge takes
+// two (log-sum-exps, then partials). The row's piece count reads only the
+// caller's lengths, so it is computed before waiting for the first pass.
+constexpr int kWarpMergeRows = 4;    // rows (warps) per CTA
+constexpr int kWarpMergeBatch = 8;   // pieces whose partials are in flight together
+
+template <typename T>
+__global__ void __launch_bounds__(kWarpMergeRows * 32) paged_decode_merge_warp_kernel(const DecodeParams p) {
+    const int lane = threadIdx.x & 31;
+    const int64_t row = static_cast<int64_t>(blockIdx.x) * kWarpMergeRows + (threadIdx.x >> 5);  // z * q_heads + hq
+    allow_next_grid();
+    int n = 0;
+    int64_t z = 0;
+    if (row < static_cast<int64_t>(p.batch) * p.q_heads) {
+        z = row / p.q_heads;
+        n = seq_split(p, z).splits;
+    }
+    wait_for_prior_grid();
+    if (n <= 1) return;
+    const int hq = static_cast<int>(row - z * p.q_heads);
+    const int c4n = p.head_dim >> 2;
+    const int64_t base = row * p.max_splits;
+    const float4* src = reinterpret_cast<const float4*>(p.part_o + base * p.head_dim) + lane;
+    const bool col = lane < c4n;
+    float lse = lane < n ? __ldcg(p.part_lse + base + lane) : -INFINITY;
+    float4 v[kWarpMergeBatch];
+#pragma unroll
+    for (int j = 0; j < kWarpMergeBatch; ++j)
+        v[j] = col && j < n ? __ldcg(src + static_cast<int64_t>(j) * c4n) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    const bool nan = __any_sync(0xffffffffu, isnan(lse));
+    const float mx = warp_max(lse);
+    const float e = lane < n ? fast_exp2(lse - mx) : 0.0f;
+    const float w = e * (1.0f / warp_sum(e));
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int j0 = 0; j0 < n; j0 += kWarpMergeBatch) {
+        if (j0 > 0) {
+#pragma unroll
+            for (int j = 0; j < kWarpMergeBatch; ++j)
+                v[j] = col && j0 + j < n ? __ldcg(src + static_cast<int64_t>(j0 + j) * c4n)
+                                         : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+#pragma unroll
+        for (int j = 0; j < kWarpMergeBatch; ++j) {
+            const float wj = __shfl_sync(0xffffffffu, w, (j0 + j) & 31);
+            if (j0 + j < n) {
+                acc.x = fmaf(wj, v[j].x, acc.x);
+                acc.y = fmaf(wj, v[j].y, acc.y);
+                acc.z = fmaf(wj, v[j].z, acc.z);
+                acc.w = fmaf(wj, v[j].w, acc.w);
+            }
+        }
+    }
+    if (!col) return;
+    const float q = __int_as_float(0x7fffffff);
+    T* out = static_cast<T*>(p.out) + row_out_offset(p, z) + static_cast<int64_t>(hq) * p.out_stride_head + lane * 4;
+    out[0] = from_float<T>(nan ? q : acc.x);
+    out[1] = from_float<T>(nan ? q : acc.y);
+    out[2] = from_float<T>(nan ? q : acc.z);
+    out[3] = from_float<T>(nan ? q : acc.w);
+}
+
 // Merge of the persistent schedule. Row (b, hq) belongs to segment (b, h =
 // hq / G). It writes the constant result of sequences with no pages (zeros or
 // NaN), and for a segment cut across warps w0..w1 combines their partials.
