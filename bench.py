@@ -52,9 +52,9 @@ DEFAULT_WORKLOAD = 'qwen7b_bf16'
 FALLBACK_HBM_GBS = 6650.0
 # dram__bytes_read.sum + dram__bytes_write.sum of one step's kernels on this workload, from
 # one ncu capture: paged_decode_mma_kernel with the append fused (329.66 MB + 5.68 MB,
-# profiles/paged_decode_mma_qwen7b_bf16.md) + paged_decode_merge_kernel (2.80 MB read with
-# ncu's cold caches, profiles/paged_decode_merge_qwen7b_bf16.md).
-NCU_TRAFFIC_BYTES = {'qwen7b_bf16': 329_660_160 + 5_680_640 + 2_802_176}
+# profiles/paged_decode_mma_qwen7b_bf16.md) + paged_decode_merge_warp_kernel (2.78 MB read with
+# ncu's cold caches, profiles/paged_decode_merge_warp_qwen7b_bf16.md).
+NCU_TRAFFIC_BYTES = {'qwen7b_bf16': 329_660_160 + 5_680_640 + 2_784_768}
 L2_BYTES = 126 * 1024 * 1024
 KERNEL_CALLS = 8
 
@@ -552,9 +552,9 @@ def run_ours(args):
                 'algorithmic_bytes_per_launch': step_total,
                 'traffic': traffic,
                 'traffic_source': ('ncu dram__bytes_read.sum + dram__bytes_write.sum of one step: '
-                                   'paged_decode_mma_kernel (append fused) + paged_decode_merge_kernel '
+                                   'paged_decode_mma_kernel (append fused) + paged_decode_merge_warp_kernel '
                                    '(profiles/paged_decode_mma_qwen7b_bf16.md, '
-                                   'profiles/paged_decode_merge_qwen7b_bf16.md)'
+                                   'profiles/paged_decode_merge_warp_qwen7b_bf16.md)'
                                    if traffic and args.step == 'fused' else None),
             },
             'e2e': {'value': round(e2e_value, 1), 'unit': 'GB/s',
