@@ -706,7 +706,7 @@ def run_reference(args):
             total_elapsed += elapsed
     value = round(statistics.median(values), 3)
     description = describe_sample(sample, args.steps, total_elapsed)
-    return {
+    line = {
         'impl': 'reference',
         'metric': METRIC, 'value': value, 'unit': 'GB/s', 'n_gpus': args.gpus,
         'steps': args.steps, 'warmup': args.warmup,
@@ -718,6 +718,65 @@ def run_reference(args):
                          'sample': description},
         'e2e': {'value': value, 'unit': 'GB/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
     }
+    gpu = reference_gpu_kernels(spec)
+    if gpu is not None:
+        line['reference_gpu_kernels'] = gpu
+    return line
+
+
+def reference_gpu_kernels(spec, steps=5, warmup=2):
+    """The reference's own CUDA extensions on the workload, for comparison.
+
+    oracle/build_ref.py compiles them from the reference's sources into
+    oracle/_ref. One step is the reference model's decode-step attention for
+    every sequence, one request per call as the reference serves them:
+    ``write_paged_kv`` of the new K/V row then ``_decode_attention_paged``
+    (src/micro_vllm/model.py:215-216, 177). bf16 workloads run in fp16 (the
+    same bytes; the reference kernels take fp16/fp32 only). Device time of
+    eager steps between CUDA events. None when the modules or a GPU are absent.
+    """
+    import torch
+
+    from oracle.build_ref import load
+
+    attn, cache = load('_micro_vllm_decode_attention'), load('_micro_vllm_paged_cache')
+    if attn is None or cache is None or not torch.cuda.is_available():
+        return None
+    run_spec = dict(spec, dtype='float16') if spec['dtype'] == 'bfloat16' else dict(spec)
+    device = torch.device('cuda', 0)
+    try:
+        data = make_workload(run_spec, spec['q_heads'], spec['kv_heads'], (0, spec['batch']), spec['seed'], device)
+        lens = [int(x) for x in data['host_lens'].tolist()]
+        bs = spec['block_size']
+        tables = [data['host_table'][b, :-(-n // bs)].to(torch.int64).to(device) for b, n in enumerate(lens)]
+        queries = [data['q'][b:b + 1].unsqueeze(2) for b in range(len(lens))]
+        keys = [data['k_new'][b:b + 1] for b in range(len(lens))]
+        values = [data['v_new'][b:b + 1] for b in range(len(lens))]
+        k_pool, v_pool = data['k_pool'], data['v_pool']
+
+        def step():
+            for b, n in enumerate(lens):
+                cache.write_paged_kv(keys[b], values[b], k_pool, v_pool, tables[b], n - 1)
+                attn._decode_attention_paged(queries[b], k_pool, v_pool, tables[b], n)
+
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize(device)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(steps):
+            step()
+        end.record()
+        torch.cuda.synchronize(device)
+        ms = start.elapsed_time(end) / steps
+    except RuntimeError as exc:
+        return {'unavailable': str(exc).splitlines()[0][:200]}
+    total, _ = step_bytes(run_spec, lens, spec['q_heads'], spec['kv_heads'])
+    return {'value': round(total / (ms * 1e-3) / 1e9, 1), 'unit': 'GB/s', 'us_per_step': round(ms * 1e3, 1),
+            'dtype': 'fp16' + (' (bf16 workload: same bytes)' if spec['dtype'] == 'bfloat16' else ''),
+            'how': (f'reference CUDA extensions built from its sources (oracle/build_ref.py): per sequence '
+                    f'write_paged_kv + _decode_attention_paged, {len(lens)} sequences per step, eager, '
+                    f'CUDA events around {steps} steps')}
 
 
 # ------------------------------------------------------- greedy generation
