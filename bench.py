@@ -1038,11 +1038,13 @@ def run_kernels(args):
         'chunk_attention_qwen7b_geometry_t4': lambda: cuda_attention.paged_chunk_attention(
             ch_q, ch_k, ch_v, ch_table, ch_lens),
         'chunk_attention_qwen7b_geometry_t4_rows': lambda: cuda_attention.paged_chunk_attention(
-            ch_q, ch_k, ch_v, ch_table, ch_lens, rows_kernel=True),
+            ch_q, ch_k, ch_v, ch_table, ch_lens, kernel='rows'),
         'chunk_prefill_qwen15b_t256_after_1024': lambda: cuda_attention.paged_chunk_attention(
             cp_q, cp_k, cp_v, cp_table, cp_lens),
+        'chunk_prefill_qwen15b_t256_after_1024_mma_sync': lambda: cuda_attention.paged_chunk_attention(
+            cp_q, cp_k, cp_v, cp_table, cp_lens, kernel='mma_sync'),
         'chunk_prefill_qwen15b_t256_after_1024_rows': lambda: cuda_attention.paged_chunk_attention(
-            cp_q, cp_k, cp_v, cp_table, cp_lens, rows_kernel=True),
+            cp_q, cp_k, cp_v, cp_table, cp_lens, kernel='rows'),
     }
     flops = {name: chunk_flops(cp_lens.cpu(), 256, 12, 128) for name in calls if name.startswith('chunk_prefill')}
     timings = {}

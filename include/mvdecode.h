@@ -52,6 +52,7 @@ extern "C" {
 #define MV_FLAG_CLUSTER 8u /* tensor-core cluster kernel (contexts up to 8192 tokens), no merge pass */
 #define MV_FLAG_WIDE 16u /* split grid in the wide shape (8 warps, deeper rings; head_dim 64/128) */
 #define MV_FLAG_CHUNK_ROWS 32u /* mv_paged_chunk_attention: one query row per token, not query tiles */
+#define MV_FLAG_CHUNK_MMA_SYNC 64u /* mv_paged_chunk_attention: 64-row mma.sync tiles, not tcgen05 tiles */
 
 /* Status codes. */
 #define MV_OK 0
@@ -145,8 +146,10 @@ MV_API int mv_paged_decode(const void* q, int64_t q_stride_seq, int64_t q_stride
  * (src/micro_vllm/model.py:178-182, paged_kv_cache.py:178-193,
  * attention.py:57-94). fp16/bf16 with head_dim 64 or 128, 16-token pages,
  * at least 16 (token x query head) rows per (sequence, KV head) and a 4-byte
- * aligned query run as query tiles on tensor cores: 64 such rows per CTA
- * share one stream of the pages. Otherwise -- or with MV_FLAG_CHUNK_ROWS --
+ * aligned query run as query tiles on tensor cores that share one stream of
+ * the pages: 128 rows per CTA on tcgen05 (TMEM accumulators) from 64 rows up
+ * with a 16-byte aligned query, else 64 rows per CTA on mma.sync
+ * (MV_FLAG_CHUNK_MMA_SYNC forces these). Otherwise -- or with MV_FLAG_CHUNK_ROWS --
  * the split grid or the CUDA-core kernel run one decode query row per
  * (sequence, token), each reading its own prefix. Workspace:
  * mv_paged_chunk_workspace_size. Flags PERSISTENT, CLUSTER, WIDE and

@@ -15,6 +15,7 @@
 #include "mvdecode.h"
 #include "paged_append.cuh"
 #include "paged_chunk_mma.cuh"
+#include "paged_chunk_umma.cuh"
 #include "paged_decode_merge.cuh"
 #include "paged_decode_mma.cuh"
 #include "paged_decode_simt.cuh"
@@ -175,6 +176,7 @@ struct Plan {
     size_t part_lse_bytes;
     bool fused_merge;
     bool wide;       // split grid in the wide shape (kWideWarps warps, deeper rings)
+    bool chunk_umma; // chunk query tiles of 128 rows on tcgen05 (else 64 rows on mma.sync)
 };
 
 bool mma_shape_ok(const Geometry& g) {
@@ -271,6 +273,7 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
     plan->counter_bytes = plan->part_o_bytes = plan->part_lse_bytes = 0;
     plan->fused_merge = false;
     plan->wide = false;
+    plan->chunk_umma = false;
     const int64_t max_pages = (g.max_context_len + g.block_size - 1) / g.block_size;
 
     // Opt-in: sequences up to kClusterPages x 8 pages split over a cluster of up
@@ -380,14 +383,18 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
 }
 
 // Plan of a chunk of `tokens` query tokens per sequence; g.batch counts query
-// rows (sequences x tokens). Where the query-tile kernel applies -- the split
-// grid's tensor-core plan, head_dim 64/128 and at least 16 rows (token x
-// query head) per (sequence, KV head) -- its splits are sized for tiles of 64
-// rows: enough equal splits of the max_context_len bound for about two waves
-// of resident tile CTAs (three per SM), none shorter than kChunkMinPages pages.
-// The plan is the split grid's either way, so a call whose query is not
-// aligned for the tile kernel runs the row-per-token kernel on the same splits.
+// rows (sequences x tokens). Where query tiles apply -- the split grid's
+// tensor-core plan, head_dim 64/128 and at least 16 rows (token x query head)
+// per (sequence, KV head) -- the chunk runs as tiles of 128 rows on tcgen05
+// (at least kUmmaMinRows rows, unless MV_FLAG_CHUNK_MMA_SYNC) or of 64 rows on
+// mma.sync, and its splits are sized for those tiles: enough equal splits of
+// the max_context_len bound for about two waves of resident tile CTAs, none
+// shorter than kChunkMinPages pages. The plan is the split grid's either way,
+// so a call whose query is not aligned for a tile kernel runs the next kernel
+// down (tcgen05 -> mma.sync tiles -> row per token) on the same splits.
 constexpr int64_t kChunkCtasPerSm = 3;
+constexpr int64_t kUmmaCtasPerSm = 2;
+constexpr int64_t kUmmaMinRows = 64;
 constexpr int64_t kChunkMinPages = 32;
 
 int make_chunk_plan(const Geometry& g, int32_t tokens, int32_t pages_per_split, uint32_t flags,
@@ -402,13 +409,15 @@ int make_chunk_plan(const Geometry& g, int32_t tokens, int32_t pages_per_split, 
     DeviceInfo dev;
     rc = device_info(&dev);
     if (rc != MV_OK) return rc;
+    plan->chunk_umma = !(flags & MV_FLAG_CHUNK_MMA_SYNC) && static_cast<int64_t>(tokens) * group >= kUmmaMinRows;
+    const int64_t tile_rows = plan->chunk_umma ? mv::kUmmaRows : mv::kChunkRows;
     const int64_t max_pages = std::max<int64_t>(1, (g.max_context_len + 15) / 16);
     int64_t pps = pages_per_split;
     if (pps == 0) {
         const int64_t sequences = g.batch / tokens;
-        const int64_t q_tiles = (static_cast<int64_t>(tokens) * group + mv::kChunkRows - 1) / mv::kChunkRows;
+        const int64_t q_tiles = (static_cast<int64_t>(tokens) * group + tile_rows - 1) / tile_rows;
         const int64_t tiles_total = sequences * g.kv_heads * q_tiles;
-        const int64_t target = static_cast<int64_t>(dev.sms) * kChunkCtasPerSm * 2;
+        const int64_t target = static_cast<int64_t>(dev.sms) * (plan->chunk_umma ? kUmmaCtasPerSm : kChunkCtasPerSm) * 2;
         int64_t splits = std::max<int64_t>(1, (target + tiles_total - 1) / tiles_total);
         splits = std::min<int64_t>(splits, std::max<int64_t>(1, (max_pages + kChunkMinPages - 1) / kChunkMinPages));
         pps = std::min<int64_t>((max_pages + splits - 1) / splits, mv::kChunkMaxPages);
@@ -452,7 +461,7 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 
 struct MapKey {
     const void* base;
-    int32_t kind;          // 0: page pool, 1: contiguous cache
+    int32_t kind;          // 0: page pool, 1: contiguous cache, 2: page pool in 64-dim boxes
     int32_t dim, dtype;
     int64_t extent[3];     // pool: (pages, heads, 0); contiguous: (tokens, heads, sequences)
     int64_t stride[3];     // contiguous: element strides (token, head, sequence)
@@ -484,6 +493,13 @@ int page_tensor_map(const void* base, int64_t num_blocks, int heads, int dim, in
     return cached_tensor_map(key, out);
 }
 
+// The same pool with one 64-dim half of a page (16 rows of 128 B) per box, so
+// a page's halves can land in separate places.
+int page_half_tensor_map(const void* base, int64_t num_blocks, int heads, int dim, int dtype, CUtensorMap* out) {
+    const MapKey key{base, 2, dim, dtype, {num_blocks, heads, 0}, {0, 0, 0}};
+    return cached_tensor_map(key, out);
+}
+
 // Contiguous cache [sequences, heads, tokens, dim] with element strides, viewed
 // as 5-D (d % 64, token, d / 64, head, sequence): one box = 16 tokens of one
 // head, the same shared-memory tile as a page; tokens past the cache read as 0.
@@ -507,7 +523,7 @@ int cached_tensor_map(const MapKey& key, CUtensorMap* out) {
     const cuuint64_t row = static_cast<cuuint64_t>(dim) * 2;
     cuuint64_t dims[5];
     cuuint64_t strides[4];
-    if (key.kind == 0) {
+    if (key.kind == 0 || key.kind == 2) {
         const cuuint64_t heads = static_cast<cuuint64_t>(key.extent[1]);
         const cuuint64_t d5[5] = {64, 16, static_cast<cuuint64_t>(dim / 64), heads,
                                   static_cast<cuuint64_t>(key.extent[0])};
@@ -522,7 +538,7 @@ int cached_tensor_map(const MapKey& key, CUtensorMap* out) {
         std::memcpy(dims, d5, sizeof(dims));
         std::memcpy(strides, s4, sizeof(strides));
     }
-    cuuint32_t box[5] = {64, 16, static_cast<cuuint32_t>(dim / 64), 1, 1};
+    cuuint32_t box[5] = {64, 16, key.kind == 2 ? 1u : static_cast<cuuint32_t>(dim / 64), 1, 1};
     cuuint32_t elem_strides[5] = {1, 1, 1, 1, 1};
     CUtensorMap map;
     CUresult r = encode(&map, key.dtype == MV_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
@@ -737,11 +753,30 @@ uint32_t chunk_flags(uint32_t flags) {
 // Query tiles of chunk rows on tensor cores, then the split merge.
 template <typename T>
 int launch_chunk_tiles(const mv::DecodeParams& p, const Plan& plan, const CUtensorMap& kmap, const CUtensorMap& vmap,
-                       int sequences, cudaStream_t stream) {
-    const int q_tiles = (p.q_tokens * p.group + mv::kChunkRows - 1) / mv::kChunkRows;
+                       int sequences, bool umma, cudaStream_t stream) {
+    const int tile_rows = umma ? mv::kUmmaRows : mv::kChunkRows;
+    const int q_tiles = (p.q_tokens * p.group + tile_rows - 1) / tile_rows;
     const dim3 grid(static_cast<unsigned>(q_tiles) * plan.max_splits, p.kv_heads, sequences);
     cudaError_t err;
-    if (p.head_dim == 64) {
+    CUtensorMap khalf;
+    if (umma) {
+        const int dtype = std::is_same<T, __half>::value ? MV_DTYPE_F16 : MV_DTYPE_BF16;
+        int rc = page_half_tensor_map(p.k_cache, p.num_blocks, p.kv_heads, p.head_dim, dtype, &khalf);
+        if (rc != MV_OK) return rc;
+    }
+    if (umma && p.head_dim == 64) {
+        auto kernel = mv::paged_chunk_umma_kernel<T, 64>;
+        int rc = ensure_smem_carveout(kernel, mv::UmmaShape<64>::kSmemBytes);
+        if (rc != MV_OK) return rc;
+        err = launch_pdl(kernel, grid, dim3(mv::kUmmaThreads), mv::UmmaShape<64>::kSmemBytes, stream, p, khalf, vmap,
+                         q_tiles);
+    } else if (umma) {
+        auto kernel = mv::paged_chunk_umma_kernel<T, 128>;
+        int rc = ensure_smem_carveout(kernel, mv::UmmaShape<128>::kSmemBytes);
+        if (rc != MV_OK) return rc;
+        err = launch_pdl(kernel, grid, dim3(mv::kUmmaThreads), mv::UmmaShape<128>::kSmemBytes, stream, p, khalf,
+                         vmap, q_tiles);
+    } else if (p.head_dim == 64) {
         auto kernel = mv::paged_chunk_mma_kernel<T, 64>;
         int rc = ensure_smem_carveout(kernel, mv::ChunkShape<64>::kSmemBytes);
         if (rc != MV_OK) return rc;
@@ -1007,8 +1042,11 @@ static int paged_decode_impl(const void* q, int64_t q_stride_seq, int64_t q_stri
     // allows them and the query's element pairs are 4-byte aligned.
     if (tiles && reinterpret_cast<uintptr_t>(q) % 4 == 0 &&
         ((q_stride_seq | q_stride_head | chunk->q_stride_token) & 1) == 0) {
-        return dtype == MV_DTYPE_F16 ? launch_chunk_tiles<__half>(p, plan, kmap, vmap, sequences, s)
-                                     : launch_chunk_tiles<__nv_bfloat16>(p, plan, kmap, vmap, sequences, s);
+        // tcgen05 tiles load 16-byte pieces of query rows.
+        const bool umma = plan.chunk_umma && reinterpret_cast<uintptr_t>(q) % 16 == 0 &&
+                          ((q_stride_seq | q_stride_head | chunk->q_stride_token) & 7) == 0;
+        return dtype == MV_DTYPE_F16 ? launch_chunk_tiles<__half>(p, plan, kmap, vmap, sequences, umma, s)
+                                     : launch_chunk_tiles<__nv_bfloat16>(p, plan, kmap, vmap, sequences, umma, s);
     }
     switch (dtype) {
         case MV_DTYPE_F32: return launch_decode<float>(p, plan, &kmap, &vmap, s);

@@ -66,6 +66,19 @@ __device__ __forceinline__ ChunkRow chunk_row(const DecodeParams& p, int b, int 
     return c;
 }
 
+// Longest context among a tile's attending rows [first_rr, last_rr] (0 if
+// none). Rows are token-major, row r attends seq_len - (T - 1 - r / G)
+// tokens, and a row attends when that is in [1, cap] (chunk_row), so the
+// tile's lengths are consecutive integers and the longest attending one is
+// min(last row's, cap).
+__device__ __forceinline__ int64_t tile_max_len(const DecodeParams& p, int64_t seq_len, int first_rr, int last_rr) {
+    const int64_t cap = min(p.max_context_len, p.blocks_per_seq * p.block_size);
+    const int64_t lo = seq_len - (p.q_tokens - 1 - first_rr / p.group);
+    const int64_t hi = seq_len - (p.q_tokens - 1 - last_rr / p.group);
+    if (hi < 1 || lo > cap) return 0;
+    return min(hi, cap);
+}
+
 template <typename T, int D>
 __global__ void __launch_bounds__(kChunkThreads, 3)
 paged_chunk_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap kmap,
@@ -96,15 +109,7 @@ paged_chunk_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
     // The tile's rows are token-major, so its last real row has its longest context.
     const int rows_total = p.q_tokens * G;
     const int last_rr = min(tile * kChunkRows + kChunkRows, rows_total) - 1;
-    int64_t max_len = 0;
-    for (int rr = tile * kChunkRows; rr <= last_rr; rr += G) {  // one row per chunk token suffices
-        const ChunkRow c = chunk_row(p, b, rr, seq_len);
-        if (c.state == 0 && c.len > max_len) max_len = c.len;
-    }
-    {
-        const ChunkRow c = chunk_row(p, b, last_rr, seq_len);
-        if (c.state == 0 && c.len > max_len) max_len = c.len;
-    }
+    const int64_t max_len = tile_max_len(p, seq_len, tile * kChunkRows, last_rr);
     // Warps that hold rows of this tile; the others leave at once.
     const int active = min(kChunkWarps, (rows_total - tile * kChunkRows + 15) / 16);
     const int64_t pages_max = (max_len + 15) / 16;

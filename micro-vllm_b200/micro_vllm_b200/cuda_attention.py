@@ -703,7 +703,7 @@ def paged_chunk_attention(query: torch.Tensor, key_cache: torch.Tensor, value_ca
                           block_table: torch.Tensor, context_lens: torch.Tensor, scale: float | None = None, *,
                           max_context_len: int | None = None, out: torch.Tensor | None = None,
                           pages_per_split: int = 0, force_simt: bool = False,
-                          rows_kernel: bool = False) -> torch.Tensor:
+                          kernel: str = 'auto') -> torch.Tensor:
     """Causal attention of a chunk of T new tokens per sequence over its pages.
 
     query: [B, Hq, T, D] (the reference's layout for a cached chunk), feature
@@ -711,10 +711,11 @@ def paged_chunk_attention(query: torch.Tensor, key_cache: torch.Tensor, value_ca
     counts each sequence's tokens after the chunk, and token t attends the
     first context_lens - (T - 1 - t) of them (model.py:178-182 gathers the
     pages and runs causal attention for this; nothing is gathered here).
-    The chunk runs as query tiles on tensor cores (64 rows of token x head per
-    CTA, each page streamed once per tile) where the shape allows (fp16/bf16,
-    head_dim 64/128, 16-token pages, T x G >= 16), else -- or with
-    ``rows_kernel`` -- as one decode query row per token.
+    ``kernel``: 'auto' runs query tiles on tensor cores where the shape allows
+    (fp16/bf16, head_dim 64/128, 16-token pages, T x G >= 16 rows per KV
+    head): 128 rows per CTA on tcgen05 from 64 rows up with a 16-byte aligned
+    query, else 64 rows per CTA on mma.sync; 'mma_sync' forces the 64-row
+    tiles; 'rows' (or an ineligible shape) runs one decode query row per token.
     Other arguments as ``paged_decode_attention``. Returns [B, Hq, T, D].
     """
     _check(isinstance(query, torch.Tensor) and query.dim() == 4, 'query must be [B, Hq, T, D]')
@@ -731,7 +732,9 @@ def paged_chunk_attention(query: torch.Tensor, key_cache: torch.Tensor, value_ca
                and out.stride(3) == 1, 'out must be a [B, Hq, T, D] tensor of the query dtype and device')
     lib = _native.library()
     num_blocks, kv_heads, block_size, _ = key_cache.shape
-    flags = _flags(force_simt, False) | (_native.FLAG_CHUNK_ROWS if rows_kernel else 0)
+    _check(kernel in ('auto', 'mma_sync', 'rows'), "kernel must be 'auto', 'mma_sync' or 'rows'")
+    flags = _flags(force_simt, False) | {'auto': 0, 'mma_sync': _native.FLAG_CHUNK_MMA_SYNC,
+                                         'rows': _native.FLAG_CHUNK_ROWS}[kernel]
     dtype = DTYPE_CODES[key_cache.dtype]
     device = key_cache.device
     with torch.cuda.device(device):

@@ -15,8 +15,10 @@ from tests.helpers import as_float, assert_attention_close, to_torch, workload_t
 
 pytestmark = pytest.mark.gpu
 
-MODES = {'auto': {}, 'simt': dict(force_simt=True), 'rows': dict(rows_kernel=True),
-         'split4': dict(pages_per_split=4), 'rows_split4': dict(pages_per_split=4, rows_kernel=True)}
+MODES = {'auto': {}, 'simt': dict(force_simt=True), 'rows': dict(kernel='rows'),
+         'mma_sync': dict(kernel='mma_sync'), 'split4': dict(pages_per_split=4),
+         'rows_split4': dict(pages_per_split=4, kernel='rows'),
+         'mma_sync_split4': dict(pages_per_split=4, kernel='mma_sync')}
 
 
 def _chunk_oracle(inputs, q_np, tokens, dtype):
@@ -78,10 +80,12 @@ def test_query_tiles_match_the_oracle_and_the_row_kernel(name, tokens, pps):
     q_np, q = _random_chunk(inputs, tokens, 7 + tokens)
     args = (q, t['key_pool'], t['value_pool'], t['block_table'], t['context_lens'])
     tiles = cuda_attention.paged_chunk_attention(*args, pages_per_split=pps)
-    rows = cuda_attention.paged_chunk_attention(*args, pages_per_split=pps, rows_kernel=True)
+    rows = cuda_attention.paged_chunk_attention(*args, pages_per_split=pps, kernel='rows')
+    mma_sync = cuda_attention.paged_chunk_attention(*args, pages_per_split=pps, kernel='mma_sync')
     expected = _chunk_oracle(inputs, q_np, tokens, dtype)
     assert_attention_close(as_float(tiles), expected, dtype)
     assert_attention_close(as_float(rows), expected, dtype)
+    assert_attention_close(as_float(mma_sync), expected, dtype)
 
 
 @pytest.mark.parametrize('pps', [0, 8])
