@@ -388,8 +388,8 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
 // per (sequence, KV head) -- the chunk runs as tiles of 128 rows on tcgen05
 // (at least kUmmaMinRows rows, unless MV_FLAG_CHUNK_MMA_SYNC) or of 64 rows on
 // mma.sync, and its splits are sized for those tiles: enough equal splits of
-// the max_context_len bound for about two waves of resident tile CTAs, none
-// shorter than kChunkMinPages pages. The plan is the split grid's either way,
+// the max_context_len bound for about one wave (tcgen05) or two waves
+// (mma.sync) of resident tile CTAs, none shorter than kChunkMinPages pages. The plan is the split grid's either way,
 // so a call whose query is not aligned for a tile kernel runs the next kernel
 // down (tcgen05 -> mma.sync tiles -> row per token) on the same splits.
 constexpr int64_t kChunkCtasPerSm = 3;
@@ -417,7 +417,9 @@ int make_chunk_plan(const Geometry& g, int32_t tokens, int32_t pages_per_split, 
         const int64_t sequences = g.batch / tokens;
         const int64_t q_tiles = (static_cast<int64_t>(tokens) * group + tile_rows - 1) / tile_rows;
         const int64_t tiles_total = sequences * g.kv_heads * q_tiles;
-        const int64_t target = static_cast<int64_t>(dev.sms) * (plan->chunk_umma ? kUmmaCtasPerSm : kChunkCtasPerSm) * 2;
+        // tcgen05 tiles: one wave of resident CTAs (measured best; more splits
+        // mostly add partials); mma.sync tiles: two waves.
+        const int64_t target = static_cast<int64_t>(dev.sms) * (plan->chunk_umma ? kUmmaCtasPerSm : kChunkCtasPerSm * 2);
         int64_t splits = std::max<int64_t>(1, (target + tiles_total - 1) / tiles_total);
         splits = std::min<int64_t>(splits, std::max<int64_t>(1, (max_pages + kChunkMinPages - 1) / kChunkMinPages));
         pps = std::min<int64_t>((max_pages + splits - 1) / splits, mv::kChunkMaxPages);

@@ -19,8 +19,9 @@
 // row's max grows by more than 2^8, so the sums stay exact in fp32 and the
 // read-modify-write of O is rare.
 //
-// Warps: 0-3 softmax (warp w owns TMEM lanes 32w..32w+31), 4 issues the MMAs
-// (one thread) and owns the TMEM allocation, 5 and 6 issue the TMA loads of
+// Warps: 0-3 softmax (warp w owns TMEM lanes 32w..32w+31), 4 issues the S
+// MMAs (one thread) and owns the TMEM allocation, 7 issues the P.V MMAs (so a
+// group's P.V never queues behind the next group's S), 5 and 6 issue the TMA loads of
 // the K and the V pages into separate rings: a K page is released as soon as
 // its S MMAs complete, so K runs a group or more ahead of the softmax, and V
 // only has to arrive by its group's P.V. S is double-buffered (S of group
@@ -44,7 +45,8 @@ constexpr int kUmmaSoftmaxWarps = 4;
 constexpr int kUmmaMmaWarp = 4;
 constexpr int kUmmaKWarp = 5;
 constexpr int kUmmaVWarp = 6;
-constexpr int kUmmaThreads = 7 * 32;
+constexpr int kUmmaPvWarp = 7;
+constexpr int kUmmaThreads = 8 * 32;
 constexpr int kUmmaGroupPages = 4;          // pages (of 16 tokens) per softmax group
 constexpr int kUmmaTmemCols = 256;
 
@@ -143,6 +145,7 @@ paged_chunk_umma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
     __shared__ __align__(8) uint64_t s_full[2];
     __shared__ __align__(8) uint64_t p_ready[2];
     __shared__ __align__(8) uint64_t o_done;
+    __shared__ __align__(8) uint64_t p_free[2];
     __shared__ __align__(8) uint64_t drained;
     __shared__ int s_ids[kChunkMaxPages];
     __shared__ int s_first_bad;
@@ -184,15 +187,20 @@ paged_chunk_umma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
         for (int i = 0; i < 2; ++i) {
             mbar_init(smem_addr(&s_full[i]), 1);
             mbar_init(smem_addr(&p_ready[i]), kUmmaSoftmaxWarps);
+            mbar_init(smem_addr(&p_free[i]), 1);
         }
         mbar_init(smem_addr(&o_done), 1);
-        mbar_init(smem_addr(&drained), 1);
+        mbar_init(smem_addr(&drained), 2);   // one final commit per MMA issuer
         s_failed = 0;
     }
     if (warp == kUmmaMmaWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&s_tmem)),
                      "r"(kUmmaTmemCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    if (threadIdx.x == kUmmaVWarp * 32) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&kmap)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&vmap)) : "memory");
     }
     if (warp == kUmmaKWarp) {
         // The split's page IDs, and its first corrupted one (never loaded).
@@ -262,9 +270,11 @@ paged_chunk_umma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
         uint64_t* empty = is_k ? k_empty : v_empty;
         const CUtensorMap* map = is_k ? &kmap : &vmap;
         const uint32_t ring = is_k ? k_ring : v_ring;
-        int issued = 0;
-        if (lane == 0) {
-            for (int j = 0; j < n_use; ++j) {
+        // Four lanes issue the four pages of a group together (one TMA
+        // instruction for all four), each waiting for its own stage.
+        if (lane < kUmmaGroupPages) {
+            int last = -1;   // this lane's last page issued
+            for (int j = lane; j < n_use; j += kUmmaGroupPages) {
                 const int st = j % NS;
                 if (j >= NS && !mbar_wait_bounded(smem_addr(&empty[st]), ((j / NS) - 1) & 1)) {
                     s_failed = 1;
@@ -282,79 +292,81 @@ paged_chunk_umma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
                 } else {
                     tma_load_5d(ring + st * Shape::kTileBytes, map, 0, 0, 0, h, s_ids[j], bar);
                 }
-                issued = j + 1;
+                last = j;
             }
-            // Every load issued lands before the CTA can exit.
-            for (int j = issued > NS ? issued - NS : 0; j < issued; ++j)
+            // Every load issued lands before the CTA can exit: only this lane's
+            // last NS / 4 pages can still be in flight.
+            for (int j = last; j >= 0 && j > last - NS; j -= kUmmaGroupPages)
                 mbar_wait_bounded(smem_addr(&full[j % NS]), (j / NS) & 1);
         }
         __syncwarp();
-    } else if (warp == kUmmaMmaWarp) {
-        // MMA issuer: S of group g + 1 while group g's softmax runs, then PV of group g.
+    } else if (warp == kUmmaMmaWarp || warp == kUmmaPvWarp) {
+        // MMA issuers, one thread each. Warp 4: S of group g into buffer g % 2 once
+        // the P.V of group g - 2 (which read P from that buffer) completed, so S
+        // runs up to two groups ahead of the softmax. Warp 7: P.V of group g once
+        // the softmax stored its P.
         if (lane == 0) {
-            const uint32_t s_idesc = umma_idesc<T>(kUmmaRows, kUmmaGroupPages * 16, 0);
-            const uint32_t o_idesc = umma_idesc<T>(kUmmaRows, D, 1);
-            auto issue_s = [&](int g) -> bool {
-                // All 64 rows of the group slot are read; rows of pages past
-                // n_use hold older pages and their scores are masked.
-                const uint32_t s_col = tmem + Shape::kSCol + (g & 1) * 64;
-                for (int jj = 0; jj < kUmmaGroupPages; ++jj) {
-                    const int j = g * kUmmaGroupPages + jj;
-                    if (j >= n_use) break;
-                    if (!mbar_wait_bounded(smem_addr(&k_full[j % NS]), (j / NS) & 1)) return false;
-                }
-                const uint32_t k_slot = k_ring + ((g * kUmmaGroupPages) % NS / kUmmaGroupPages) * Shape::kKSlotBytes;
+            bool ok = true;
+            if (warp == kUmmaMmaWarp) {
+                const uint32_t s_idesc = umma_idesc<T>(kUmmaRows, kUmmaGroupPages * 16, 0);
+                for (int g = 0; ok && g < n_groups; ++g) {
+                    if (g >= 2 && !mbar_wait_bounded(smem_addr(&p_free[g & 1]), ((g >> 1) - 1) & 1)) {
+                        ok = false;
+                        break;
+                    }
+                    for (int jj = 0; jj < kUmmaGroupPages && ok; ++jj) {
+                        const int j = g * kUmmaGroupPages + jj;
+                        if (j >= n_use) break;
+                        ok = mbar_wait_bounded(smem_addr(&k_full[j % NS]), (j / NS) & 1);
+                    }
+                    if (!ok) break;
+                    tmem_fence_after();
+                    // All 64 rows of the group slot are read; rows of pages past
+                    // n_use hold older pages and their scores are masked.
+                    const uint32_t s_col = tmem + Shape::kSCol + (g & 1) * 64;
+                    const uint32_t k_slot = k_ring + ((g * kUmmaGroupPages) % NS / kUmmaGroupPages) * Shape::kKSlotBytes;
 #pragma unroll
-                for (int ks = 0; ks < KS; ++ks) {
-                    const uint64_t a = umma_sw128_desc(q_base + (ks >> 2) * (kUmmaRows * 128) + (ks & 3) * 32, 16, 1024);
-                    const uint64_t bd = umma_sw128_desc(k_slot + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024);
-                    umma_ss(s_col, a, bd, s_idesc, ks > 0);
+                    for (int ks = 0; ks < KS; ++ks) {
+                        const uint64_t a = umma_sw128_desc(q_base + (ks >> 2) * (kUmmaRows * 128) + (ks & 3) * 32, 16, 1024);
+                        const uint64_t bd = umma_sw128_desc(k_slot + (ks >> 2) * 8192 + (ks & 3) * 32, 16, 1024);
+                        umma_ss(s_col, a, bd, s_idesc, ks > 0);
+                    }
+                    umma_commit(smem_addr(&s_full[g & 1]));
+                    // The group's K pages are free once these MMAs complete.
+                    for (int jj = 0; jj < kUmmaGroupPages; ++jj) {
+                        const int j = g * kUmmaGroupPages + jj;
+                        if (j >= n_use) break;
+                        umma_commit(smem_addr(&k_empty[j % NS]));
+                    }
                 }
-                umma_commit(smem_addr(&s_full[g & 1]));
-                // The group's K pages are free once these MMAs complete.
-                for (int jj = 0; jj < kUmmaGroupPages; ++jj) {
-                    const int j = g * kUmmaGroupPages + jj;
-                    if (j >= n_use) break;
-                    umma_commit(smem_addr(&k_empty[j % NS]));
-                }
-                return true;
-            };
-            bool ok = n_groups == 0 || issue_s(0);
-            for (int g = 0; ok && g < n_groups; ++g) {
-                if (g + 1 < n_groups) {
-                    // S of group g + 1 overwrites the buffer P of group g - 1 lives in.
-                    if (g >= 1 && !mbar_wait_bounded(smem_addr(&o_done), (g - 1) & 1)) {
+            } else {
+                const uint32_t o_idesc = umma_idesc<T>(kUmmaRows, D, 1);
+                for (int g = 0; ok && g < n_groups; ++g) {
+                    if (!mbar_wait_bounded(smem_addr(&p_ready[g & 1]), (g >> 1) & 1)) {
                         ok = false;
                         break;
                     }
-                    if (!issue_s(g + 1)) {
-                        ok = false;
-                        break;
+                    tmem_fence_after();
+                    const uint32_t p_col = tmem + Shape::kSCol + (g & 1) * 64;
+                    for (int jj = 0; jj < kUmmaGroupPages && ok; ++jj) {
+                        const int j = g * kUmmaGroupPages + jj;
+                        if (j >= n_use) break;
+                        if (!mbar_wait_bounded(smem_addr(&v_full[j % NS]), (j / NS) & 1)) {
+                            ok = false;
+                            break;
+                        }
+                        const uint32_t v_tile = v_ring + (j % NS) * Shape::kTileBytes;
+                        umma_ts(tmem + Shape::kOCol, p_col + jj * 8, umma_sw128_desc(v_tile, 2048, 1024), o_idesc,
+                                g > 0 || jj > 0);
                     }
-                }
-                if (!mbar_wait_bounded(smem_addr(&p_ready[g & 1]), (g >> 1) & 1)) {
-                    ok = false;
-                    break;
-                }
-                tmem_fence_after();
-                const uint32_t p_col = tmem + Shape::kSCol + (g & 1) * 64;
-                for (int jj = 0; jj < kUmmaGroupPages && ok; ++jj) {
-                    const int j = g * kUmmaGroupPages + jj;
-                    if (j >= n_use) break;
-                    if (!mbar_wait_bounded(smem_addr(&v_full[j % NS]), (j / NS) & 1)) {
-                        ok = false;
-                        break;
+                    if (!ok) break;
+                    umma_commit(smem_addr(&o_done));
+                    umma_commit(smem_addr(&p_free[g & 1]));
+                    for (int jj = 0; jj < kUmmaGroupPages; ++jj) {
+                        const int j = g * kUmmaGroupPages + jj;
+                        if (j >= n_use) break;
+                        umma_commit(smem_addr(&v_empty[j % NS]));
                     }
-                    const uint32_t v_tile = v_ring + (j % NS) * Shape::kTileBytes;
-                    umma_ts(tmem + Shape::kOCol, p_col + jj * 8, umma_sw128_desc(v_tile, 2048, 1024), o_idesc,
-                            g > 0 || jj > 0);
-                }
-                if (!ok) break;
-                umma_commit(smem_addr(&o_done));
-                for (int jj = 0; jj < kUmmaGroupPages; ++jj) {
-                    const int j = g * kUmmaGroupPages + jj;
-                    if (j >= n_use) break;
-                    umma_commit(smem_addr(&v_empty[j % NS]));
                 }
             }
             if (!ok) {
