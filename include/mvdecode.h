@@ -89,7 +89,9 @@ MV_API int mv_paged_decode_workspace_size(int32_t batch, int32_t num_q_heads, in
 
 /*
  * Which kernel mv_paged_decode would run, and its split-KV shape. k_cache and
- * v_cache are only inspected for alignment.
+ * v_cache are only inspected for alignment. With pages_per_split == 0 the
+ * default tensor-core split grid may give each sequence's first split up to
+ * twice chosen_pages_per_split pages (at most 128); max_splits counts that.
  */
 MV_API int mv_paged_decode_plan(int32_t batch, int32_t num_q_heads, int32_t num_kv_heads,
                          int32_t head_dim, int32_t block_size, int64_t max_context_len,

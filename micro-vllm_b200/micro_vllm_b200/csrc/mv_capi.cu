@@ -166,6 +166,7 @@ struct Plan {
     int path;
     int pages_per_split;
     int max_splits;
+    int first_pages; // split grid: pages of split 0 when longer than pages_per_split (split-major order), else 0
     int cluster;     // cluster kernel: CTAs per (sequence, KV head)
     int nt;          // mma n-tiles (8 query heads each)
     int ctas;        // persistent grid size
@@ -274,6 +275,7 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
     plan->fused_merge = false;
     plan->wide = false;
     plan->chunk_umma = false;
+    plan->first_pages = 0;
     const int64_t max_pages = (g.max_context_len + g.block_size - 1) / g.block_size;
 
     // Opt-in: sequences up to kClusterPages x 8 pages split over a cluster of up
@@ -333,6 +335,7 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
             pps = std::min<int64_t>(std::max<int64_t>((pps + 31) / 32 * 32, 32), kMaxPagesPerSplitWide);
         }
     }
+    const bool auto_pps = pps == 0;
     if (pps == 0) {
         // Splits of 16..128 pages (tensor cores), sized so the batch's pages -- estimated as half
         // the max_context_len bound per sequence -- fill about one wave of
@@ -353,7 +356,25 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
     if (plan->path == MV_PATH_TMA_MMA && pps > max_pps)
         return fail(MV_ERR_INVALID_ARGUMENT, "pages_per_split above %d for the tensor-core kernel",
                     static_cast<int>(max_pps));
-    const int64_t splits = std::max<int64_t>(1, (max_pages + pps - 1) / pps);
+    // The automatic plan of the (default-shape) tensor-core split grid makes
+    // each sequence's first split twice as long (up to kMaxPagesPerSplit pages)
+    // and dispatches the grid split-major: every first split starts in the
+    // first wave, the shorter later splits fill the tail, and sequences of up
+    // to 2 x pps pages need no merge. Measured on B200 (Qwen2.5-7B geometry,
+    // batch 64, 1k-4k tokens): 62.1 us per step against 65.0 us with uniform
+    // 64-page splits and 62.8 us with uniform 128-page splits.
+    // Only where the grid is more than one wave: with every CTA resident at
+    // once the longest split sets the time (batch 1 x 4096 tokens: 13.8 us
+    // with a 32-page first split, 10.3 us without).
+    if (auto_pps && plan->path == MV_PATH_TMA_MMA && !plan->wide) {
+        const int64_t first = std::min<int64_t>(2 * pps, kMaxPagesPerSplit);
+        const int64_t est_ctas = static_cast<int64_t>(g.batch) * g.kv_heads *
+                                 ((std::max<int64_t>(max_pages, 1) / 2 + pps - 1) / pps);
+        if (first > pps && est_ctas > static_cast<int64_t>(dev.sms) * 3) plan->first_pages = static_cast<int>(first);
+    }
+    const int64_t first = plan->first_pages;
+    const int64_t splits = first > 0 ? (max_pages <= first ? 1 : 1 + (max_pages - first + pps - 1) / pps)
+                                     : std::max<int64_t>(1, (max_pages + pps - 1) / pps);
     if (splits > 8192) return fail(MV_ERR_UNSUPPORTED, "more than 8192 splits: raise pages_per_split");
     plan->pages_per_split = static_cast<int>(pps);
     plan->max_splits = static_cast<int>(splits);
@@ -428,6 +449,7 @@ int make_chunk_plan(const Geometry& g, int32_t tokens, int32_t pages_per_split, 
     if (splits > 8192) return fail(MV_ERR_UNSUPPORTED, "more than 8192 splits: raise pages_per_split");
     plan->wide = false;
     plan->fused_merge = false;
+    plan->first_pages = 0;
     plan->pages_per_split = static_cast<int>(pps);
     plan->max_splits = static_cast<int>(splits);
     plan->counter_bytes = plan->part_o_bytes = plan->part_lse_bytes = 0;
@@ -964,6 +986,7 @@ static int paged_decode_impl(const void* q, int64_t q_stride_seq, int64_t q_stri
     p.out_stride_head = out_stride_head;
     p.pages_per_split = plan.pages_per_split;
     p.max_splits = plan.max_splits;
+    p.first_pages = plan.first_pages;
     p.part_o = nullptr;
     p.part_lse = nullptr;
     p.prefix_out = nullptr;
@@ -1198,6 +1221,7 @@ int mv_contiguous_decode(const void* q, int64_t q_stride_seq, int64_t q_stride_h
     p.out_stride_head = out_stride_head;
     p.pages_per_split = plan.pages_per_split;
     p.max_splits = plan.max_splits;
+    p.first_pages = plan.first_pages;
     p.fused_merge = plan.fused_merge ? 1 : 0;
     p.contiguous = 1;
     for (int i = 0; i < 3; ++i) {

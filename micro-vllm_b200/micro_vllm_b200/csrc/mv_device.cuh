@@ -50,6 +50,12 @@ struct DecodeParams {
     float* part_lse;        // [batch, q_heads, max_splits]            log2-sum-exp of each split
     int pages_per_split;
     int max_splits;
+    // Split grid: pages of split 0 when it is longer than the rest (0: every
+    // split has pages_per_split pages). A nonzero value also orders the grid
+    // split-major: every sequence's split 0 is dispatched before any split 1,
+    // so the long first splits start in the first wave and the short later
+    // ones fill the tail.
+    int first_pages;
     int64_t* prefix_out;    // persistent schedule: per-sequence page prefix sums [batch + 1]
     int64_t persistent_warps;  // persistent schedule: warps in the grid
     unsigned int* counters; // split grid: per-(sequence, KV head) arrival counters, zero between calls
@@ -129,7 +135,8 @@ __device__ __forceinline__ int64_t row_out_offset(const DecodeParams& p, int64_t
     return b * p.out_stride_seq + (z - b * p.q_tokens) * p.out_stride_token;
 }
 
-// How one query row's context is cut into split-KV chunks of pages_per_split pages.
+// How one query row's context is cut into split-KV chunks: a first split of
+// first_pages pages (when set), then splits of pages_per_split pages.
 struct SeqSplit {
     int64_t len;
     int64_t pages;
@@ -152,19 +159,34 @@ __device__ __forceinline__ SeqSplit seq_split(const DecodeParams& p, int b) {
         s.state = 0;
     }
     s.pages = s.state == 0 ? (s.len + p.block_size - 1) / p.block_size : 0;
-    // Splits of pages_per_split pages, the last one partial. Measured on B200,
-    // evening out the splits' sizes was slower: the small last splits fill the
-    // tail of the grid.
-    const int64_t splits = (s.pages + p.pages_per_split - 1) / p.pages_per_split;
+    // The last split is partial. Measured on B200, evening out the splits'
+    // sizes was slower: the small last splits fill the tail of the grid.
+    const int64_t splits = p.first_pages > 0
+                               ? (s.pages <= p.first_pages
+                                      ? 1
+                                      : 1 + (s.pages - p.first_pages + p.pages_per_split - 1) / p.pages_per_split)
+                               : (s.pages + p.pages_per_split - 1) / p.pages_per_split;
     s.splits = splits < 1 ? 1 : static_cast<int>(splits);
     return s;
+}
+
+// First page of split `split`; it does not depend on the sequence's length.
+__device__ __forceinline__ int64_t split_begin(const DecodeParams& p, int split) {
+    if (p.first_pages > 0)
+        return split == 0 ? 0 : p.first_pages + static_cast<int64_t>(split - 1) * p.pages_per_split;
+    return static_cast<int64_t>(split) * p.pages_per_split;
+}
+
+// Pages a full split `split` holds.
+__device__ __forceinline__ int split_pages(const DecodeParams& p, int split) {
+    return p.first_pages > 0 && split == 0 ? p.first_pages : p.pages_per_split;
 }
 
 // Pages [begin, end) of split `split` of a sequence.
 __device__ __forceinline__ void split_range(const DecodeParams& p, const SeqSplit& s, int split, int64_t* begin,
                                             int64_t* end) {
-    *begin = static_cast<int64_t>(split) * p.pages_per_split;
-    const int64_t raw = *begin + p.pages_per_split;
+    *begin = split_begin(p, split);
+    const int64_t raw = *begin + split_pages(p, split);
     *end = raw < s.pages ? raw : s.pages;
 }
 

@@ -348,9 +348,20 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int split = blockIdx.x;
-    const int h = blockIdx.y;
-    const int b = blockIdx.z;
+    int split, h, b;
+    if (p.first_pages > 0) {
+        // Split-major order over the (splits, kv_heads, batch) grid: linear
+        // block index = (split * kv_heads + h) * batch + b.
+        const int64_t lin = blockIdx.x + static_cast<int64_t>(gridDim.x) *
+                                             (blockIdx.y + static_cast<int64_t>(gridDim.y) * blockIdx.z);
+        b = static_cast<int>(lin % gridDim.z);
+        h = static_cast<int>((lin / gridDim.z) % gridDim.y);
+        split = static_cast<int>(lin / (static_cast<int64_t>(gridDim.z) * gridDim.y));
+    } else {
+        split = blockIdx.x;
+        h = blockIdx.y;
+        b = blockIdx.z;
+    }
 
     wait_for_prior_grid();
     allow_next_grid();

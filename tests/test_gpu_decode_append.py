@@ -254,3 +254,32 @@ def test_bound_step_rejects_changed_shapes_and_aliases():
         step(t['q'], t['context_lens'], key=alias, value=t['value_new'])
     with pytest.raises(RuntimeError, match='out must be'):
         step(t['q'], t['context_lens'], torch.empty(1, 28, 128, dtype=t['q'].dtype, device='cuda'))
+
+
+@pytest.mark.parametrize('lens', [('uniform', 100, 700), ('uniform', 1, 700),
+                                  ('fixed', [700] * 120 + [0, 1, 15, 16, 17, 511, 512, 513])])
+def test_first_split_schedule_of_multi_wave_grids(lens):
+    """Grids of more than one wave of CTAs take a first split twice the split
+    size, dispatched split-major. Check the shape the plan reports, then the
+    one-call step and the two-call path against each other, the uniform-split
+    plan of the same size, and the oracle, with empty and page-edge lengths."""
+    spec = dict(batch=128, q_heads=28, kv_heads=4, head_dim=128, block_size=16, pool=('factor', 1.25),
+                lens=lens, dtype='bfloat16', value_scale=0.5, seed=4242)
+    inputs = make_inputs(spec)
+    t = workload_tensors(inputs)
+    attention, _ = _ops()
+    max_pages = t['block_table'].shape[1]
+    path, pps, splits = attention.paged_decode_plan(28, t['key_pool'], max_pages * 16, batch=128)
+    assert path == 'tma_mma' and 2 * pps < max_pages
+    assert splits == 1 + -(-(max_pages - 2 * pps) // pps)   # a first split of 2 x pps pages
+    key_pool, value_pool, out = _one_call(t)
+    ref_k, ref_v, ref_out = _two_calls(t)
+    assert _same_bits(key_pool, ref_k) and _same_bits(value_pool, ref_v)
+    assert _same_bits(out, ref_out)
+    _, _, uniform = _two_calls(t, pages_per_split=pps)
+    expected = decode_float(inputs['q'], to_numpy(key_pool), to_numpy(value_pool), inputs['block_table'],
+                            inputs['context_lens'], 128 ** -0.5, 'bfloat16')
+    assert_attention_close(as_float(out), expected, 'bfloat16')
+    assert_attention_close(as_float(uniform), expected, 'bfloat16')
+    empty = inputs['context_lens'] == 0
+    assert (as_float(out)[empty] == 0).all()
