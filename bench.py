@@ -51,10 +51,10 @@ METRIC = 'paged decode attn achieved HBM GB/s (% of B200 peak); decode tokens/s'
 DEFAULT_WORKLOAD = 'qwen7b_bf16'
 FALLBACK_HBM_GBS = 6650.0
 # dram__bytes_read.sum + dram__bytes_write.sum of one step's kernels on this workload, from
-# one ncu capture: paged_decode_mma_kernel with the append fused (329.66 MB + 5.68 MB,
-# profiles/paged_decode_mma_qwen7b_bf16.md) + paged_decode_merge_warp_kernel (2.78 MB read with
+# one ncu capture: paged_decode_mma_kernel with the append fused (329.75 MB + 7.62 MB,
+# profiles/paged_decode_mma_qwen7b_bf16.md) + paged_decode_merge_warp_kernel (1.52 MB read with
 # ncu's cold caches, profiles/paged_decode_merge_warp_qwen7b_bf16.md).
-NCU_TRAFFIC_BYTES = {'qwen7b_bf16': 329_660_160 + 5_680_640 + 2_784_768}
+NCU_TRAFFIC_BYTES = {'qwen7b_bf16': 329_753_088 + 7_615_744 + 1_524_992}
 L2_BYTES = 126 * 1024 * 1024
 KERNEL_CALLS = 8
 
