@@ -51,10 +51,10 @@ METRIC = 'paged decode attn achieved HBM GB/s (% of B200 peak); decode tokens/s'
 DEFAULT_WORKLOAD = 'qwen7b_bf16'
 FALLBACK_HBM_GBS = 6650.0
 # dram__bytes_read.sum + dram__bytes_write.sum of one step's kernels on this workload, from
-# one ncu capture: paged_decode_mma_kernel with the append fused (329.75 MB + 7.62 MB,
-# profiles/paged_decode_mma_qwen7b_bf16.md) + paged_decode_merge_warp_kernel (1.52 MB read with
+# one ncu capture: paged_decode_mma_kernel with the append fused (329.73 MB + 5.03 MB,
+# profiles/paged_decode_mma_qwen7b_bf16.md) + paged_decode_merge_warp_kernel (1.53 MB read with
 # ncu's cold caches, profiles/paged_decode_merge_warp_qwen7b_bf16.md).
-NCU_TRAFFIC_BYTES = {'qwen7b_bf16': 329_753_088 + 7_615_744 + 1_524_992}
+NCU_TRAFFIC_BYTES = {'qwen7b_bf16': 329_734_144 + 5_028_096 + 1_525_760}
 L2_BYTES = 126 * 1024 * 1024
 KERNEL_CALLS = 8
 
@@ -378,6 +378,14 @@ def run_ours(args):
                                                 data['context_lens'], max_context_len=max_len, out=out,
                                                 pages_per_split=pps, rope=tables)
 
+    # The same step with the split grid's per-page math on CUDA cores (fp32 FMA)
+    # instead of the tensor-core tile: the comparison behind the tensor-core choice.
+    def cuda_core_step():
+        cuda_attention.paged_decode_with_append(data['q'], data['k_new'][:, :, 0], data['v_new'][:, :, 0],
+                                                data['k_pool'], data['v_pool'], data['block_table'],
+                                                data['context_lens'], max_context_len=max_len, out=out,
+                                                pages_per_split=pps, cuda_core_math=True)
+
     path, chosen_pps, splits = cuda_attention.paged_decode_plan(
         q_heads, data['k_pool'], max_len, batch=len(lens_host), pages_per_split=pps)
     # The fused step is one decode launch (+ merge); the separate one adds the append kernel.
@@ -390,6 +398,7 @@ def run_ours(args):
             step()
             other_step()
             rope_step()
+            cuda_core_step()
     torch.cuda.synchronize(device)
     step_graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(step_graph, stream=stream):
@@ -400,6 +409,9 @@ def run_ours(args):
     rope_graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(rope_graph, stream=stream):
         rope_step()
+    cuda_core_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(cuda_core_graph, stream=stream):
+        cuda_core_step()
     # The step's kernels back to back, KERNEL_CALLS per graph, so their average
     # launch duration excludes the per-replay graph launch gap (roofline).
     kernel_graph = torch.cuda.CUDAGraph()
@@ -447,51 +459,41 @@ def run_ours(args):
         torch.cuda.synchronize(device)
         attn_ms = k_start.elapsed_time(k_end) / (reps * KERNEL_CALLS)
 
-        # The other form of the step, same loop, reported beside the headline.
-        with torch.cuda.stream(stream):
-            for _ in range(args.warmup):
-                other_graph.replay()
-        torch.cuda.synchronize(device)
-        barrier()
-        torch.cuda.synchronize(device)
+        # The other forms of the step, same loop, reported beside the headline.
         other_reps = min(args.steps, 1000)
-        o_start, o_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(stream):
-            o_start.record(stream)
-            for _ in range(other_reps):
-                other_graph.replay()
-            o_end.record(stream)
-        torch.cuda.synchronize(device)
-        barrier()
-        other_ms = o_start.elapsed_time(o_end) * args.steps / other_reps
 
-        with torch.cuda.stream(stream):
-            for _ in range(args.warmup):
-                rope_graph.replay()
-        torch.cuda.synchronize(device)
-        barrier()
-        torch.cuda.synchronize(device)
-        r_start, r_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        with torch.cuda.stream(stream):
-            r_start.record(stream)
-            for _ in range(other_reps):
-                rope_graph.replay()
-            r_end.record(stream)
-        torch.cuda.synchronize(device)
-        barrier()
-        rope_ms = r_start.elapsed_time(r_end) * args.steps / other_reps
+        def time_form(graph):
+            with torch.cuda.stream(stream):
+                for _ in range(args.warmup):
+                    graph.replay()
+            torch.cuda.synchronize(device)
+            barrier()
+            torch.cuda.synchronize(device)
+            f_start, f_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                f_start.record(stream)
+                for _ in range(other_reps):
+                    graph.replay()
+                f_end.record(stream)
+            torch.cuda.synchronize(device)
+            barrier()
+            return f_start.elapsed_time(f_end) * args.steps / other_reps
+
+        other_ms = time_form(other_graph)
+        rope_ms = time_form(rope_graph)
+        cuda_core_ms = time_form(cuda_core_graph)
 
         # End to end through the public API: pinned host inputs in, output back out.
         e2e = run_e2e(args, data, max_len, pps, stream, device, barrier)
     clock_summary = clocks.summary()
 
-    times = torch.tensor([elapsed_ms, attn_ms, e2e['ms'], other_ms, rope_ms], dtype=torch.float64,
+    times = torch.tensor([elapsed_ms, attn_ms, e2e['ms'], other_ms, rope_ms, cuda_core_ms], dtype=torch.float64,
                          device=device)
     totals = torch.tensor([float(step_total), float(attn_bytes)], dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
         dist.all_reduce(totals, op=dist.ReduceOp.SUM)
-    elapsed_ms, attn_ms, e2e_ms, other_ms, rope_ms = times.tolist()
+    elapsed_ms, attn_ms, e2e_ms, other_ms, rope_ms, cuda_core_ms = times.tolist()
     job_step_bytes, job_attn_bytes = totals.tolist()
     ms_per_step = elapsed_ms / args.steps
     value = job_step_bytes * args.steps / (elapsed_ms / 1e3) / 1e9
@@ -566,13 +568,14 @@ def run_ours(args):
             'step_forms_us': {args.step: round(ms_per_step * 1e3, 3),
                               ('separate' if args.step == 'fused' else 'fused'):
                                   round(other_ms / args.steps * 1e3, 3),
-                              'fused_with_rope': round(rope_ms / args.steps * 1e3, 3)},
+                              'fused_with_rope': round(rope_ms / args.steps * 1e3, 3),
+                              'fused_cuda_core_math': round(cuda_core_ms / args.steps * 1e3, 3)},
             'clocks': clock_summary,
             'gpu_launches': launches_per_step * args.steps,
         }
         if world == 1 and not args.no_cpu_baseline:
             result['cpu_baseline'] = cpu_baseline(spec, data, q_heads, kv_heads, args.cpu_seconds)
-    del step_graph, kernel_graph, other_graph, rope_graph
+    del step_graph, kernel_graph, other_graph, rope_graph, cuda_core_graph
     if world > 1:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()

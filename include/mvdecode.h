@@ -53,6 +53,8 @@ extern "C" {
 #define MV_FLAG_WIDE 16u /* split grid in the wide shape (8 warps, deeper rings; head_dim 64/128) */
 #define MV_FLAG_CHUNK_ROWS 32u /* mv_paged_chunk_attention: one query row per token, not query tiles */
 #define MV_FLAG_CHUNK_MMA_SYNC 64u /* mv_paged_chunk_attention: 64-row mma.sync tiles, not tcgen05 tiles */
+#define MV_FLAG_CUDA_CORE_MATH 128u /* split grid (default shape, GQA group <= 8, head_dim 64/128): the same TMA
+                                      pipeline with fp32 FMA math instead of the tensor-core tile (for comparison) */
 
 /* Status codes. */
 #define MV_OK 0

@@ -24,6 +24,7 @@ FLAG_CLUSTER = 8
 FLAG_WIDE = 16
 FLAG_CHUNK_ROWS = 32
 FLAG_CHUNK_MMA_SYNC = 64
+FLAG_CUDA_CORE_MATH = 128
 PATH_SIMT, PATH_TMA_MMA, PATH_TMA_MMA_PERSISTENT, PATH_TMA_MMA_CLUSTER = 0, 1, 2, 3
 PATH_NAMES = {0: 'simt', 1: 'tma_mma', 2: 'tma_mma_persistent', 3: 'tma_mma_cluster'}
 DEVICE_STATUS_WAIT_TIMEOUT = 1

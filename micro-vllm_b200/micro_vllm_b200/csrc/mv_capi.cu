@@ -178,6 +178,7 @@ struct Plan {
     bool fused_merge;
     bool wide;       // split grid in the wide shape (kWideWarps warps, deeper rings)
     bool chunk_umma; // chunk query tiles of 128 rows on tcgen05 (else 64 rows on mma.sync)
+    bool cuda_core;  // split grid with CUDA-core math (MV_FLAG_CUDA_CORE_MATH)
 };
 
 bool mma_shape_ok(const Geometry& g) {
@@ -276,6 +277,7 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
     plan->wide = false;
     plan->chunk_umma = false;
     plan->first_pages = 0;
+    plan->cuda_core = false;
     const int64_t max_pages = (g.max_context_len + g.block_size - 1) / g.block_size;
 
     // Opt-in: sequences up to kClusterPages x 8 pages split over a cluster of up
@@ -321,6 +323,10 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
     const bool auto_wide = pages_per_split == 0 && !(flags & (MV_FLAG_FUSED_MERGE | MV_FLAG_CLUSTER)) &&
                            segments >= 16 && segments <= dev.sms / 2 && max_pages <= 1024;
     plan->wide = plan->path == MV_PATH_TMA_MMA && ((flags & MV_FLAG_WIDE) || auto_wide) && g.head_dim != 256;
+    // The CUDA-core variant runs the default shape only (it is a comparison point).
+    plan->cuda_core = plan->path == MV_PATH_TMA_MMA && (flags & MV_FLAG_CUDA_CORE_MATH) && group <= 8 &&
+                      (g.head_dim == 64 || g.head_dim == 128);
+    if (plan->cuda_core) plan->wide = false;
     const int64_t max_pps = plan->wide ? kMaxPagesPerSplitWide : kMaxPagesPerSplit;
     int64_t pps = pages_per_split;
     if (pps == 0 && plan->wide) {
@@ -578,21 +584,25 @@ int cached_tensor_map(const MapKey& key, CUtensorMap* out) {
 
 // ----------------------------------------------------------------- launch
 
-template <typename T, int D, int NT, int WARPS, int STAGES>
+template <typename T, int D, int NT, int WARPS, int STAGES, bool FMA = false>
 int launch_mma_shape(const mv::DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap, dim3 grid,
                      cudaStream_t stream) {
     using Shape = mv::MmaDecodeShape<D, NT, WARPS, STAGES>;
-    auto kernel = mv::paged_decode_mma_kernel<T, D, NT, WARPS, STAGES>;
-    int rc = ensure_smem(kernel, Shape::kSmemBytes);
+    auto kernel = mv::paged_decode_mma_kernel<T, D, NT, WARPS, STAGES, FMA>;
+    constexpr int smem = Shape::kSmemBytes + (FMA ? mv::fma_extra_smem<T, D, WARPS>() : 0);
+    int rc = ensure_smem(kernel, smem);
     if (rc != MV_OK) return rc;
-    cudaError_t err = launch_pdl(kernel, grid, dim3(WARPS * 32), Shape::kSmemBytes, stream, p, kmap, vmap);
+    cudaError_t err = launch_pdl(kernel, grid, dim3(WARPS * 32), smem, stream, p, kmap, vmap);
     return err == cudaSuccess ? MV_OK : cuda_fail(err, "decode kernel launch");
 }
 
 template <typename T, int D, int NT>
 int launch_mma(const mv::DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap, dim3 grid,
-               bool wide, cudaStream_t stream) {
+               bool wide, bool cuda_core, cudaStream_t stream) {
     constexpr int STAGES = D == 64 ? MV_STAGES_D64 : (D == 128 ? MV_STAGES_D128 : MV_STAGES_D256);
+    if constexpr (NT == 1 && D != 256) {
+        if (cuda_core) return launch_mma_shape<T, D, 1, kMmaWarps, STAGES, true>(p, kmap, vmap, grid, stream);
+    }
     if constexpr (D != 256) {
         constexpr int WIDE_STAGES = D == 64 ? kWideStagesD64 : kWideStagesD128;
         if (wide) return launch_mma_shape<T, D, NT, kWideWarps, WIDE_STAGES>(p, kmap, vmap, grid, stream);
@@ -602,14 +612,14 @@ int launch_mma(const mv::DecodeParams& p, const CUtensorMap& kmap, const CUtenso
 
 template <typename T>
 int launch_mma_dispatch(const mv::DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap,
-                        dim3 grid, int nt, bool wide, cudaStream_t stream) {
+                        dim3 grid, int nt, bool wide, bool cuda_core, cudaStream_t stream) {
     switch (p.head_dim * 4 + nt) {
-        case 64 * 4 + 1: return launch_mma<T, 64, 1>(p, kmap, vmap, grid, wide, stream);
-        case 64 * 4 + 2: return launch_mma<T, 64, 2>(p, kmap, vmap, grid, wide, stream);
-        case 128 * 4 + 1: return launch_mma<T, 128, 1>(p, kmap, vmap, grid, wide, stream);
-        case 128 * 4 + 2: return launch_mma<T, 128, 2>(p, kmap, vmap, grid, wide, stream);
-        case 256 * 4 + 1: return launch_mma<T, 256, 1>(p, kmap, vmap, grid, wide, stream);
-        case 256 * 4 + 2: return launch_mma<T, 256, 2>(p, kmap, vmap, grid, wide, stream);
+        case 64 * 4 + 1: return launch_mma<T, 64, 1>(p, kmap, vmap, grid, wide, cuda_core, stream);
+        case 64 * 4 + 2: return launch_mma<T, 64, 2>(p, kmap, vmap, grid, wide, cuda_core, stream);
+        case 128 * 4 + 1: return launch_mma<T, 128, 1>(p, kmap, vmap, grid, wide, cuda_core, stream);
+        case 128 * 4 + 2: return launch_mma<T, 128, 2>(p, kmap, vmap, grid, wide, cuda_core, stream);
+        case 256 * 4 + 1: return launch_mma<T, 256, 1>(p, kmap, vmap, grid, wide, cuda_core, stream);
+        case 256 * 4 + 2: return launch_mma<T, 256, 2>(p, kmap, vmap, grid, wide, cuda_core, stream);
         default: return fail(MV_ERR_UNSUPPORTED, "no tensor-core kernel for head_dim %d", p.head_dim);
     }
 }
@@ -720,7 +730,7 @@ int launch_decode(const mv::DecodeParams& p, const Plan& plan, const CUtensorMap
         if constexpr (std::is_same<T, float>::value) {
             return fail(MV_ERR_UNSUPPORTED, "tensor-core kernel takes fp16/bf16 only");
         } else {
-            rc = launch_mma_dispatch<T>(p, *kmap, *vmap, grid, plan.nt, plan.wide, stream);
+            rc = launch_mma_dispatch<T>(p, *kmap, *vmap, grid, plan.nt, plan.wide, plan.cuda_core, stream);
         }
     } else {
         const size_t smem = mv::simt_smem_bytes(p.group, p.head_dim);

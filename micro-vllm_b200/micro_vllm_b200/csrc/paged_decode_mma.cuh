@@ -300,6 +300,175 @@ struct WarpPageAttention {
     }
 };
 
+// CUDA-core variant of the per-page math (MV_FLAG_CUDA_CORE_MATH, GQA group
+// <= 8, head_dim 64/128), kept to compare with the tensor-core tile on the
+// same TMA pipeline and grid: fp32 FMA dot products straight from the staged
+// page in shared memory, q in shared memory as fp32.
+//   S: lane = (token t = lane % 16, half of the row lane / 16); the halves'
+//      sums meet through one shuffle; the online softmax runs per token lane.
+//   P.V: lane = D / 32 columns of O for all eight query heads; P of the page
+//      goes through a 16 x 8 fp32 buffer of the warp in shared memory.
+// P stays fp32 (the tensor-core tile rounds it to the element type).
+template <typename T, int D>
+struct WarpPageFma {
+    static constexpr int kG = 8;                  // query heads per tile (q rows past the group are 0)
+    static constexpr int kHalfChunks = D / 16;    // 16-byte chunks in half a row
+    static constexpr int kCols = D / 32;          // O columns per lane
+    static constexpr int kQBytes = kG * D * 4;    // q of the group, fp32
+    static constexpr int kPBytes = 16 * kG * 4;   // P of one page, per warp
+
+    float m[kG];          // running max (exp2 domain), the same on every lane
+    float l[kG];          // denominators: lanes 0..15 hold their token's share
+    float o[kG][kCols];   // O[g][lane * kCols + j]
+
+    __device__ __forceinline__ void reset() {
+#pragma unroll
+        for (int g = 0; g < kG; ++g) {
+            m[g] = -INFINITY;
+            l[g] = 0.0f;
+#pragma unroll
+            for (int j = 0; j < kCols; ++j) o[g][j] = 0.0f;
+        }
+    }
+
+    // q rows h*G + g of row b into qs[g][d] as fp32 (0 for g >= group), rotated
+    // at table row `pos` when rope is set; every thread of the CTA takes part
+    // (the caller synchronises the CTA afterwards).
+    __device__ static void load_q(const DecodeParams& p, int b, int h, int64_t pos, bool rope, float* qs) {
+        const T* qbase = static_cast<const T*>(p.q) + row_q_offset(p, b);
+        for (int idx = threadIdx.x; idx < kG * D; idx += blockDim.x) {
+            const int g = idx / D;
+            const int d = idx - g * D;
+            float v = 0.0f;
+            if (g < p.group) {
+                const T* row = qbase + static_cast<int64_t>(h * p.group + g) * p.q_stride_head;
+                v = to_float<T>(row[d]);
+                if (rope) {
+                    const bool first = d < D / 2;
+                    const float partner = to_float<T>(row[first ? d + D / 2 : d - D / 2]);
+                    const float c = to_float<T>(static_cast<const T*>(p.rope_cos)[pos * D + d]);
+                    const float sn = to_float<T>(static_cast<const T*>(p.rope_sin)[pos * D + d]);
+                    v = rope_element<T>(v, partner, c, sn, first);
+                }
+            }
+            qs[idx] = v;
+        }
+    }
+
+    static __device__ __forceinline__ void unpack8(const uint4& raw, float (&f)[8]) {
+        const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) f[i] = to_float<T>(e[i]);
+    }
+
+    // One page: K tile at kt, V tile at vt (generic pointers into the stage,
+    // 128-byte swizzled 16 x 64 boxes), `valid` of its 16 tokens in use.
+    __device__ __forceinline__ void attend(const uint8_t* kt, const uint8_t* vt, const float* qs, float* pbuf,
+                                           int valid, float scale_log2, int lane) {
+        const int t = lane & 15;
+        const int half = lane >> 4;
+        float s[kG];
+#pragma unroll
+        for (int g = 0; g < kG; ++g) s[g] = 0.0f;
+#pragma unroll
+        for (int j = 0; j < kHalfChunks; ++j) {
+            const int gc = half * kHalfChunks + j;   // row chunk: dims 8 gc .. 8 gc + 7
+            const int c = gc & 7;
+            float kf[8];
+            unpack8(*reinterpret_cast<const uint4*>(kt + (gc >> 3) * 2048 + t * 128 + ((c ^ (t & 7)) << 4)), kf);
+#pragma unroll
+            for (int g = 0; g < kG; ++g) {
+                const float4 q0 = *reinterpret_cast<const float4*>(qs + g * D + gc * 8);
+                const float4 q1 = *reinterpret_cast<const float4*>(qs + g * D + gc * 8 + 4);
+                float acc = s[g];
+                acc = fmaf(kf[0], q0.x, acc);
+                acc = fmaf(kf[1], q0.y, acc);
+                acc = fmaf(kf[2], q0.z, acc);
+                acc = fmaf(kf[3], q0.w, acc);
+                acc = fmaf(kf[4], q1.x, acc);
+                acc = fmaf(kf[5], q1.y, acc);
+                acc = fmaf(kf[6], q1.z, acc);
+                acc = fmaf(kf[7], q1.w, acc);
+                s[g] = acc;
+            }
+        }
+        const bool in = t < valid;
+        float a[kG];
+        float pv[kG];
+#pragma unroll
+        for (int g = 0; g < kG; ++g) {
+            const float sum = s[g] + __shfl_xor_sync(0xffffffffu, s[g], 16);   // every lane takes part
+            const float x = in ? sum * scale_log2 : -INFINITY;
+            float mx = x;
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            const float mn = fmaxf(m[g], mx);   // finite: token 0 of a page is always in use
+            a[g] = fast_exp2(m[g] - mn);
+            pv[g] = in ? fast_exp2(x - mn) : 0.0f;
+            m[g] = mn;
+            l[g] = l[g] * a[g] + (half == 0 ? pv[g] : 0.0f);
+        }
+        if (half == 0) {
+            *reinterpret_cast<float4*>(pbuf + t * kG) = make_float4(pv[0], pv[1], pv[2], pv[3]);
+            *reinterpret_cast<float4*>(pbuf + t * kG + 4) = make_float4(pv[4], pv[5], pv[6], pv[7]);
+        }
+        __syncwarp();
+#pragma unroll
+        for (int g = 0; g < kG; ++g)
+#pragma unroll
+            for (int j = 0; j < kCols; ++j) o[g][j] *= a[g];
+        const int d0 = lane * kCols;
+        const int c = (d0 & 63) >> 3;
+        const uint8_t* vcol = vt + (d0 >> 6) * 2048 + (d0 & 7) * 2;
+        for (int tt = 0; tt < valid; ++tt) {
+            const float4 p0 = *reinterpret_cast<const float4*>(pbuf + tt * kG);
+            const float4 p1 = *reinterpret_cast<const float4*>(pbuf + tt * kG + 4);
+            const uint8_t* src = vcol + tt * 128 + ((c ^ (tt & 7)) << 4);
+            float vf[kCols];
+            if constexpr (kCols == 4) {
+                const uint2 raw = *reinterpret_cast<const uint2*>(src);
+                const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) vf[j] = to_float<T>(e[j]);
+            } else {
+                const uint32_t raw = *reinterpret_cast<const uint32_t*>(src);
+                const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+                for (int j = 0; j < kCols; ++j) vf[j] = to_float<T>(e[j]);
+            }
+            const float pw[kG] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+#pragma unroll
+            for (int g = 0; g < kG; ++g)
+#pragma unroll
+                for (int j = 0; j < kCols; ++j) o[g][j] = fmaf(pw[g], vf[j], o[g][j]);
+        }
+        __syncwarp();   // every lane read pbuf before the next page writes it
+    }
+
+    // Full denominators on every lane (lanes 16..31 contribute 0).
+    __device__ __forceinline__ void reduce_l() {
+#pragma unroll
+        for (int g = 0; g < kG; ++g)
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) l[g] += __shfl_xor_sync(0xffffffffu, l[g], off);
+    }
+
+    // The warp's state into the CTA merge buffers (the tensor-core tile's format).
+    __device__ __forceinline__ void store_red(float* red, float* red_m, float* red_l, int stride, int lane) const {
+#pragma unroll
+        for (int g = 0; g < kG; ++g)
+#pragma unroll
+            for (int j = 0; j < kCols; ++j) red[g * stride + lane * kCols + j] = o[g][j];
+        if (lane == 0) {
+#pragma unroll
+            for (int g = 0; g < kG; ++g) {
+                red_m[g] = m[g];
+                red_l[g] = l[g];
+            }
+        }
+    }
+};
+
 // ------------------------------------------------------- split-grid kernel
 
 // After a CTA wrote its split's partial: count it in, and if it is the
@@ -334,12 +503,20 @@ struct MmaDecodeShape {
     static_assert(kRedBytes <= kWarpBytes, "warp merge buffer must fit the warp's stages");
 };
 
-template <typename T, int D, int NT, int NWARPS, int STAGES>
+// Shared memory the CUDA-core variant adds after the stages: q of the group
+// (fp32) and each warp's P buffer.
+template <typename T, int D, int NWARPS>
+constexpr int fma_extra_smem() {
+    return WarpPageFma<T, D>::kQBytes + NWARPS * WarpPageFma<T, D>::kPBytes;
+}
+
+template <typename T, int D, int NT, int NWARPS, int STAGES, bool FMA = false>
 __global__ void __launch_bounds__(NWARPS * 32)
 paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap kmap,
                         const __grid_constant__ CUtensorMap vmap) {
     using Shape = MmaDecodeShape<D, NT, NWARPS, STAGES>;
     using Warp = WarpPageAttention<T, D, NT>;
+    static_assert(!FMA || (NT == 1 && (D == 64 || D == 128)), "CUDA-core variant: group <= 8, head_dim 64/128");
 
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t bars[NWARPS][STAGES];
@@ -480,9 +657,16 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
         }
     }
 
-    Warp w;
-    w.load_q(p, b, h, lane);
-    if (p.rope_cos && !rope_missing) w.rope_q(p, seq.len - 1, lane);
+    std::conditional_t<FMA, WarpPageFma<T, D>, Warp> w;
+    float* fma_q = reinterpret_cast<float*>(smem + NWARPS * Shape::kWarpBytes);
+    float* fma_p = fma_q + 8 * D + warp * 16 * 8;
+    if constexpr (FMA) {
+        WarpPageFma<T, D>::load_q(p, b, h, seq.len - 1, p.rope_cos && !rope_missing, fma_q);
+        __syncthreads();
+    } else {
+        w.load_q(p, b, h, lane);
+        if (p.rope_cos && !rope_missing) w.rope_q(p, seq.len - 1, lane);
+    }
     w.reset();
 
     bool failed = false;
@@ -522,6 +706,17 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
             }
             __syncwarp();
         }
+        if constexpr (FMA) {
+            // The math reads the stage itself: refill it afterwards.
+            if (page_ok)
+                w.attend(wsm + st * Shape::kStageBytes, wsm + st * Shape::kStageBytes + Shape::kTileBytes, fma_q,
+                         fma_p, valid, p.scale_log2, lane);
+            if (i + STAGES < n_my) {
+                fence_proxy_async_smem();
+                __syncwarp();
+                issue(i + STAGES);
+            }
+        } else {
         typename Warp::PageFrags frags;
         if (page_ok) Warp::load_page(frags, kt, vt, wsm + st * Shape::kStageBytes + Shape::kTileBytes, valid, lane);
 
@@ -538,6 +733,7 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
             }
         }
         if (page_ok) w.attend(frags, valid, p.scale_log2, lane);
+        }
     }
 
     if (failed) {
@@ -553,6 +749,9 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
     float* red = reinterpret_cast<float*>(wsm);
     float* red_m = red + Shape::kQRows * Shape::kRedStride;
     float* red_l = red_m + Shape::kQRows;
+    if constexpr (FMA) {
+        w.store_red(red, red_m, red_l, Shape::kRedStride, lane);
+    } else {
 #pragma unroll
     for (int mt = 0; mt < Warp::KS; ++mt) {
 #pragma unroll
@@ -574,6 +773,7 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
             red_l[q] = w.l[nt][0];
             red_l[q + 1] = w.l[nt][1];
         }
+    }
     }
     __syncthreads();
     int cta_bad = 0;

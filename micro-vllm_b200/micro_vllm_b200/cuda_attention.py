@@ -296,14 +296,14 @@ def decode_attention_paged(query: torch.Tensor, cache, *, layer_idx: int) -> tor
         cache._device_page_table, length)
 
 
-def _flags(force_simt, persistent, fused_merge=False, cluster=False, wide=False):
+def _flags(force_simt, persistent, fused_merge=False, cluster=False, wide=False, cuda_core_math=False):
     return ((_native.FLAG_FORCE_SIMT if force_simt else 0) | (_native.FLAG_PERSISTENT if persistent else 0)
             | (_native.FLAG_FUSED_MERGE if fused_merge else 0) | (_native.FLAG_CLUSTER if cluster else 0)
-            | (_native.FLAG_WIDE if wide else 0))
+            | (_native.FLAG_WIDE if wide else 0) | (_native.FLAG_CUDA_CORE_MATH if cuda_core_math else 0))
 
 
 def paged_decode_plan(query_heads, key_cache, context_bound, *, batch, pages_per_split=0,
-                      force_simt=False, persistent=False, cluster=False, wide=False):
+                      force_simt=False, persistent=False, cluster=False, wide=False, cuda_core_math=False):
     """(path, pages_per_split, max_splits) that ``paged_decode_attention`` would use.
 
     path is 'tma_mma_cluster' (TMA + tensor cores, the splits of each
@@ -319,7 +319,8 @@ def paged_decode_plan(query_heads, key_cache, context_bound, *, batch, pages_per
     with torch.cuda.device(key_cache.device):
         _native.check(lib.mv_paged_decode_plan(
             batch, query_heads, kv_heads, dim, block_size, context_bound, pages_per_split,
-            _flags(force_simt, persistent, cluster=cluster, wide=wide), DTYPE_CODES[key_cache.dtype],
+            _flags(force_simt, persistent, cluster=cluster, wide=wide, cuda_core_math=cuda_core_math),
+            DTYPE_CODES[key_cache.dtype],
             key_cache.data_ptr(), key_cache.data_ptr(), ctypes.byref(path), ctypes.byref(pps),
             ctypes.byref(splits)))
     return _native.PATH_NAMES[path.value], pps.value, splits.value
@@ -330,7 +331,8 @@ def paged_decode_attention(query: torch.Tensor, key_cache: torch.Tensor, value_c
                            scale: float | None = None, *, max_context_len: int | None = None,
                            out: torch.Tensor | None = None, pages_per_split: int = 0,
                            force_simt: bool = False, persistent: bool = False,
-                           fused_merge: bool = False, cluster: bool = False, wide: bool = False) -> torch.Tensor:
+                           fused_merge: bool = False, cluster: bool = False, wide: bool = False,
+                           cuda_core_math: bool = False) -> torch.Tensor:
     """Batched paged GQA decode over one shared page pool.
 
     query: [B, Hq, D] (or [B, Hq, 1, D]) CUDA fp32/fp16/bf16, feature stride 1.
@@ -347,7 +349,9 @@ def paged_decode_attention(query: torch.Tensor, key_cache: torch.Tensor, value_c
     kernel selection for tests and tuning (that many pages per split-KV CTA;
     the cluster kernel; the persistent tensor-core schedule; merging splits in
     the last split CTA; the split grid's wide shape of 8 warps with deeper
-    rings; the CUDA-core kernel). By default the library picks the
+    rings; the CUDA-core kernel). cuda_core_math: the split grid's TMA pipeline
+    with fp32 FMA math instead of the tensor-core tile (GQA group <= 8,
+    head_dim 64/128; a comparison point). By default the library picks the
     tensor-core split grid with a merge pass, and the CUDA-core kernel for
     shapes the tensor-core kernels do not take.
     Returns out, or a fresh [B, Hq, D] tensor of the query's dtype.
@@ -355,7 +359,7 @@ def paged_decode_attention(query: torch.Tensor, key_cache: torch.Tensor, value_c
     q, max_context_len, scale, out = _checked_batched(query, key_cache, value_cache, block_table,
                                                       context_lens, scale, max_context_len, out)
     _launch_batched(q, key_cache, value_cache, block_table, context_lens, max_context_len, scale, out,
-                    pages_per_split, _flags(force_simt, persistent, fused_merge, cluster, wide))
+                    pages_per_split, _flags(force_simt, persistent, fused_merge, cluster, wide, cuda_core_math))
     return out
 
 
@@ -424,7 +428,8 @@ def paged_decode_with_append(query: torch.Tensor, key: torch.Tensor, value: torc
                              out: torch.Tensor | None = None, pages_per_split: int = 0,
                              force_simt: bool = False, persistent: bool = False,
                              fused_merge: bool = False, cluster: bool = False, wide: bool = False,
-                             rope: tuple[torch.Tensor, torch.Tensor] | None = None) -> torch.Tensor:
+                             rope: tuple[torch.Tensor, torch.Tensor] | None = None,
+                             cuda_core_math: bool = False) -> torch.Tensor:
     """One decode step of a layer: append this step's K/V row of every sequence, then attend.
 
     The result, in the pools and in the output, is that of
@@ -460,7 +465,7 @@ def paged_decode_with_append(query: torch.Tensor, key: torch.Tensor, value: torc
            'new K/V must have shape [B, Hkv, D] or [B, Hkv, 1, D]')
     cache_ops._validate_pages(key4, key_cache, value_cache)
     cache_ops._validate_aliases(key4, value4, key_cache, value_cache, block_table)
-    flags = _flags(force_simt, persistent, fused_merge, cluster, wide)
+    flags = _flags(force_simt, persistent, fused_merge, cluster, wide, cuda_core_math)
     key3, value3 = key4[:, :, 0, :], value4[:, :, 0, :]
     tables = None
     if rope is not None:

@@ -26,6 +26,7 @@ MODES = {
     'persistent': dict(persistent=True),      # append kernel first, then the persistent kernel
     'cluster': dict(cluster=True),            # append kernel first, then the cluster kernel
     'simt': dict(force_simt=True),            # CUDA-core kernel: append fused (element-wise)
+    'cuda_core_math': dict(cuda_core_math=True),  # split grid, fp32 FMA math: append fused
 }
 
 

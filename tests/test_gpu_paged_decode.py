@@ -54,6 +54,7 @@ MODES = {
     'split4': dict(pages_per_split=4),        # split grid, 4 pages per split
     'wide': dict(wide=True),                  # split grid, wide shape (8 warps, deeper rings)
     'simt': dict(force_simt=True),            # CUDA-core kernel
+    'cuda_core_math': dict(cuda_core_math=True),  # split grid, fp32 FMA math (group <= 8, D 64/128)
 }
 
 

@@ -76,6 +76,7 @@ def test_python_binding_constants_match_the_header():
     assert constants['MV_FLAG_WIDE'] == _native.FLAG_WIDE
     assert constants['MV_FLAG_CHUNK_ROWS'] == _native.FLAG_CHUNK_ROWS
     assert constants['MV_FLAG_CHUNK_MMA_SYNC'] == _native.FLAG_CHUNK_MMA_SYNC
+    assert constants['MV_FLAG_CUDA_CORE_MATH'] == _native.FLAG_CUDA_CORE_MATH
     assert constants['MV_DEVICE_STATUS_WAIT_TIMEOUT'] == _native.DEVICE_STATUS_WAIT_TIMEOUT
     assert constants['MV_ABI_VERSION'] == _native.MV_ABI_VERSION
 
