@@ -411,11 +411,23 @@ paged_chunk_umma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
             tmem_wait_ld();
             const int tok0 = g * kUmmaGroupPages * 16;
             const int avail = min(kUmmaGroupPages * 16, (n_use - g * kUmmaGroupPages) * 16);
+            // A group inside every row's causal prefix (all of it but the
+            // diagonal and the split's last pages) needs no mask, and with a
+            // positive scale the max of the raw scores gives the scaled max:
+            // the scale is then folded into the exponent's FFMA below.
+            const bool unmasked = p.scale_log2 > 0.0f && avail == kUmmaGroupPages * 16 &&
+                                  __all_sync(0xffffffffu, tok0 + kUmmaGroupPages * 16 - 1 <= pos);
             float gmax = -INFINITY;
+            if (unmasked) {
 #pragma unroll
-            for (int i = 0; i < 64; ++i) {
-                s[i] = (i < avail && tok0 + i <= pos) ? s[i] * p.scale_log2 : -INFINITY;
-                gmax = fmaxf(gmax, s[i]);
+                for (int i = 0; i < 64; ++i) gmax = fmaxf(gmax, s[i]);
+                gmax *= p.scale_log2;
+            } else {
+#pragma unroll
+                for (int i = 0; i < 64; ++i) {
+                    s[i] = (i < avail && tok0 + i <= pos) ? s[i] * p.scale_log2 : -INFINITY;
+                    gmax = fmaxf(gmax, s[i]);
+                }
             }
             const float m_new = fmaxf(m_run, gmax);
             const bool grow = m_run != -INFINITY && m_new > m_run + 8.0f;
@@ -446,12 +458,22 @@ paged_chunk_umma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
             const float base = m_run == -INFINITY ? 0.0f : m_run;
             uint32_t pk[32];
             float sum = 0.0f;
+            if (unmasked) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) {
-                const float p0 = fast_exp2(s[2 * i] - base);
-                const float p1 = fast_exp2(s[2 * i + 1] - base);
-                sum += p0 + p1;
-                pk[i] = Op::pack(p0, p1);
+                for (int i = 0; i < 32; ++i) {
+                    const float p0 = fast_exp2(fmaf(s[2 * i], p.scale_log2, -base));
+                    const float p1 = fast_exp2(fmaf(s[2 * i + 1], p.scale_log2, -base));
+                    sum += p0 + p1;
+                    pk[i] = Op::pack(p0, p1);
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 32; ++i) {
+                    const float p0 = fast_exp2(s[2 * i] - base);
+                    const float p1 = fast_exp2(s[2 * i + 1] - base);
+                    sum += p0 + p1;
+                    pk[i] = Op::pack(p0, p1);
+                }
             }
             l_run += sum;
             tmem_st16(s_col, pk);
