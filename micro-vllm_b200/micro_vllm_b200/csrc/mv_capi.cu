@@ -415,7 +415,7 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
 // per (sequence, KV head) -- the chunk runs as tiles of 128 rows on tcgen05
 // (at least kUmmaMinRows rows, unless MV_FLAG_CHUNK_MMA_SYNC) or of 64 rows on
 // mma.sync, and its splits are sized for those tiles: enough equal splits of
-// the max_context_len bound for about one wave (tcgen05) or two waves
+// the max_context_len bound for at most one wave (tcgen05, rounded down) or two waves
 // (mma.sync) of resident tile CTAs, none shorter than kChunkMinPages pages. The plan is the split grid's either way,
 // so a call whose query is not aligned for a tile kernel runs the next kernel
 // down (tcgen05 -> mma.sync tiles -> row per token) on the same splits.
@@ -444,10 +444,17 @@ int make_chunk_plan(const Geometry& g, int32_t tokens, int32_t pages_per_split, 
         const int64_t sequences = g.batch / tokens;
         const int64_t q_tiles = (static_cast<int64_t>(tokens) * group + tile_rows - 1) / tile_rows;
         const int64_t tiles_total = sequences * g.kv_heads * q_tiles;
-        // tcgen05 tiles: one wave of resident CTAs (measured best; more splits
-        // mostly add partials); mma.sync tiles: two waves.
+        // tcgen05 tiles: at most one wave of resident CTAs, rounding the split
+        // count down -- every split adds a partial row per query row (written,
+        // then read by the merge: 4 sequences x 256 tokens x 12 heads x 3
+        // splits is 19 MB against 5 MB of K/V), so splitting pays only while
+        // the tiles leave much of the GPU idle. Measured on B200 (graph of
+        // back-to-back calls): 96 tiles: 3 splits 33.1 us, 1 split 40.2 us;
+        // 192 tiles: 1 split 63.1 / 40.5 us against 2 splits 84.1 / 64.0 us.
+        // mma.sync tiles: two waves.
         const int64_t target = static_cast<int64_t>(dev.sms) * (plan->chunk_umma ? kUmmaCtasPerSm : kChunkCtasPerSm * 2);
-        int64_t splits = std::max<int64_t>(1, (target + tiles_total - 1) / tiles_total);
+        int64_t splits = plan->chunk_umma ? std::max<int64_t>(1, target / tiles_total)
+                                          : std::max<int64_t>(1, (target + tiles_total - 1) / tiles_total);
         splits = std::min<int64_t>(splits, std::max<int64_t>(1, (max_pages + kChunkMinPages - 1) / kChunkMinPages));
         pps = std::min<int64_t>((max_pages + splits - 1) / splits, mv::kChunkMaxPages);
     }
