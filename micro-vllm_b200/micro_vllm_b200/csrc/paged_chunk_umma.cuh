@@ -147,7 +147,8 @@ paged_chunk_umma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
     __shared__ __align__(8) uint64_t o_done;
     __shared__ __align__(8) uint64_t p_free[2];
     __shared__ __align__(8) uint64_t drained;
-    __shared__ int s_ids[kChunkMaxPages];
+    __shared__ int s_ids[kChunkMaxPages];      // page IDs of the K producer
+    __shared__ int s_vids[kChunkMaxPages];     // the same, loaded by the V producer
     __shared__ int s_first_bad;
     __shared__ uint32_t s_tmem;
     __shared__ volatile int s_failed;
@@ -178,12 +179,6 @@ paged_chunk_umma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
     const uint32_t v_ring = k_ring + Shape::kRingBytes;
 
     if (threadIdx.x == 0) {
-        for (int st = 0; st < NS; ++st) {
-            mbar_init(smem_addr(&k_full[st]), 1);
-            mbar_init(smem_addr(&k_empty[st]), 1);
-            mbar_init(smem_addr(&v_full[st]), 1);
-            mbar_init(smem_addr(&v_empty[st]), 1);
-        }
         for (int i = 0; i < 2; ++i) {
             mbar_init(smem_addr(&s_full[i]), 1);
             mbar_init(smem_addr(&p_ready[i]), kUmmaSoftmaxWarps);
@@ -198,20 +193,33 @@ paged_chunk_umma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
                      "r"(kUmmaTmemCols));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
-    if (threadIdx.x == kUmmaVWarp * 32) {
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&kmap)) : "memory");
-        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&vmap)) : "memory");
-    }
-    if (warp == kUmmaKWarp) {
-        // The split's page IDs, and its first corrupted one (never loaded).
-        int first_bad = n_pages;
+    // Producers (warp 5: K pages, warp 6: V pages) start before the CTA-wide
+    // barrier: each initialises its own ring's barriers, loads the split's
+    // page IDs itself and issues the ring's first pages, so those loads
+    // overlap the Q rows' loads below.
+    int first_bad = n_pages;   // the split's first corrupted page (never loaded)
+    int prod_next = 0;         // producer lanes: next page to issue
+    if (warp == kUmmaKWarp || warp == kUmmaVWarp) {
+        const bool is_k = warp == kUmmaKWarp;
+        uint64_t* full = is_k ? k_full : v_full;
+        uint64_t* empty = is_k ? k_empty : v_empty;
+        int* ids = is_k ? s_ids : s_vids;
+        if (lane == 0) {
+            for (int st = 0; st < NS; ++st) {
+                mbar_init(smem_addr(&full[st]), 1);
+                mbar_init(smem_addr(&empty[st]), 1);
+            }
+            fence_mbar_init();
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(is_k ? &kmap : &vmap))
+                         : "memory");
+        }
         for (int i0 = 0; i0 < n_pages; i0 += 32) {
             const int i = i0 + lane;
             bool bad = false;
             if (i < n_pages) {
                 const int64_t id = load_index(p.block_table, p.table_i64, b * p.table_stride + page_begin + i);
                 bad = id < 0 || id >= p.num_blocks;
-                s_ids[i] = bad ? 0 : static_cast<int>(id);
+                ids[i] = bad ? 0 : static_cast<int>(id);
             }
             const unsigned mask = __ballot_sync(0xffffffffu, bad);
             if (mask) {
@@ -219,7 +227,27 @@ paged_chunk_umma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
                 break;
             }
         }
-        if (lane == 0) s_first_bad = first_bad;
+        if (is_k && lane == 0) s_first_bad = first_bad;
+        __syncwarp();
+        // The ring's first pages need no free stage: one per lane, four lanes
+        // issuing a group's four pages together.
+        prod_next = lane;
+        if (lane < kUmmaGroupPages) {
+            const CUtensorMap* map = is_k ? &kmap : &vmap;
+            const uint32_t ring = is_k ? k_ring : v_ring;
+            for (; prod_next < first_bad && prod_next < NS; prod_next += kUmmaGroupPages) {
+                const int j = prod_next;
+                const uint32_t bar = smem_addr(&full[j]);
+                mbar_arrive_expect_tx(bar, Shape::kTileBytes);
+                if (is_k) {
+                    const uint32_t slot = ring + (j / kUmmaGroupPages) * Shape::kKSlotBytes + (j % kUmmaGroupPages) * 2048;
+#pragma unroll
+                    for (int a = 0; a < D / 64; ++a) tma_load_5d(slot + a * 8192, map, 0, 0, a, h, ids[j], bar);
+                } else {
+                    tma_load_5d(ring + j * Shape::kTileBytes, map, 0, 0, 0, h, ids[j], bar);
+                }
+            }
+        }
     }
     // Q rows into shared memory in the MMA's K-major 128-byte-swizzled layout:
     // element (row, d) at [d / 64][row][16-byte chunk ((d % 64) / 8) ^ (row % 8)].
@@ -270,11 +298,13 @@ paged_chunk_umma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
         uint64_t* empty = is_k ? k_empty : v_empty;
         const CUtensorMap* map = is_k ? &kmap : &vmap;
         const uint32_t ring = is_k ? k_ring : v_ring;
+        const int* ids = is_k ? s_ids : s_vids;
         // Four lanes issue the four pages of a group together (one TMA
-        // instruction for all four), each waiting for its own stage.
+        // instruction for all four), each waiting for its own stage; the
+        // ring's first pages went out before the CTA barrier.
         if (lane < kUmmaGroupPages) {
-            int last = -1;   // this lane's last page issued
-            for (int j = lane; j < n_use; j += kUmmaGroupPages) {
+            int last = prod_next - kUmmaGroupPages;   // this lane's last page issued
+            for (int j = prod_next; j < n_use; j += kUmmaGroupPages) {
                 const int st = j % NS;
                 if (j >= NS && !mbar_wait_bounded(smem_addr(&empty[st]), ((j / NS) - 1) & 1)) {
                     s_failed = 1;
@@ -288,9 +318,9 @@ paged_chunk_umma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
                     // Each 64-dim half of the page at rows 16 (j % 4) of its group slot.
                     const uint32_t slot = ring + (st / kUmmaGroupPages) * Shape::kKSlotBytes + (st % kUmmaGroupPages) * 2048;
 #pragma unroll
-                    for (int a = 0; a < D / 64; ++a) tma_load_5d(slot + a * 8192, map, 0, 0, a, h, s_ids[j], bar);
+                    for (int a = 0; a < D / 64; ++a) tma_load_5d(slot + a * 8192, map, 0, 0, a, h, ids[j], bar);
                 } else {
-                    tma_load_5d(ring + st * Shape::kTileBytes, map, 0, 0, 0, h, s_ids[j], bar);
+                    tma_load_5d(ring + st * Shape::kTileBytes, map, 0, 0, 0, h, ids[j], bar);
                 }
                 last = j;
             }
