@@ -369,6 +369,16 @@ MV_API int mv_paged_decode_noalloc(const void* q, int64_t q_stride_seq, int64_t 
 MV_API int mv_device_status(int32_t device, uint32_t* status);
 MV_API int mv_clear_device_status(int32_t device);
 
+/*
+ * Self-test of the failure path (no reference counterpart: the reference's
+ * kernels have no bounded waits): launches one CTA on `stream` (current
+ * device) that waits on a barrier phase nothing completes, with the kernels'
+ * bounded wait shortened to limit_ns (at most 100 ms). The wait gives up, the
+ * kernel raises MV_DEVICE_STATUS_WAIT_TIMEOUT exactly as a decode kernel
+ * whose load never landed would, and returns; the context stays usable.
+ */
+MV_API int mv_selftest_wait_timeout(uint64_t limit_ns, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

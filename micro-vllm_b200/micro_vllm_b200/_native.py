@@ -42,7 +42,7 @@ EXPORTED_SYMBOLS = (
     'mv_paged_decode_plan', 'mv_paged_decode', 'mv_write_paged_kv',
     'mv_device_status', 'mv_clear_device_status', 'mv_paged_decode_append', 'mv_apply_rope',
     'mv_rms_norm', 'mv_silu_mul', 'mv_contiguous_decode_plan', 'mv_contiguous_decode',
-    'mv_paged_chunk_workspace_size', 'mv_paged_chunk_attention',
+    'mv_paged_chunk_workspace_size', 'mv_paged_chunk_attention', 'mv_selftest_wait_timeout',
 )
 
 _i32, _i64, _u32, _vp, _sz, _f32 = (ctypes.c_int32, ctypes.c_int64, ctypes.c_uint32,
@@ -124,6 +124,7 @@ _SIGNATURES = {
     'mv_silu_mul': (ctypes.c_int, [_vp, _i64, _vp, _i64, _i64, _i32, _i32, _vp]),
     'mv_device_status': (ctypes.c_int, [_i32, ctypes.POINTER(_u32)]),
     'mv_clear_device_status': (ctypes.c_int, [_i32]),
+    'mv_selftest_wait_timeout': (ctypes.c_int, [ctypes.c_uint64, _vp]),
 }
 
 

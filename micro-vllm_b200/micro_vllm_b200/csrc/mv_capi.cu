@@ -1592,6 +1592,29 @@ int mv_clear_device_status(int32_t device) {
     return err == cudaSuccess ? MV_OK : cuda_fail(err, "clearing device status");
 }
 
+// Self-test of the failure path: one CTA waits on an mbarrier phase that
+// nothing completes, with the kernels' bounded wait shortened to limit_ns;
+// giving up raises the same sticky status bit a real wait would.
+namespace mv {
+__global__ void wait_timeout_selftest_kernel(unsigned long long limit_ns) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) mbar_init(smem_addr(&bar), 1);
+    fence_mbar_init();
+    __syncthreads();
+    const bool ok = mbar_wait_bounded_ns(smem_addr(&bar), 0, limit_ns);
+    if (threadIdx.x == 0 && !ok) atomicOr(&g_device_status, kStatusWaitTimeout);
+}
+}  // namespace mv
+
+int mv_selftest_wait_timeout(uint64_t limit_ns, void* stream) {
+    if (limit_ns == 0 || limit_ns > 100000000ull)
+        return fail(MV_ERR_INVALID_ARGUMENT, "limit_ns must be in (0, 100 ms]");
+    mv::wait_timeout_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+        static_cast<unsigned long long>(limit_ns));
+    const cudaError_t err = cudaGetLastError();
+    return err == cudaSuccess ? MV_OK : cuda_fail(err, "self-test kernel launch");
+}
+
 // ------------------------------------------------- allocation-free decode
 
 // Split-KV scratch of mv_paged_decode_noalloc: a file-scope device array, so

@@ -397,14 +397,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     return done != 0;
 }
 
-// Wait for the barrier phase with the given parity; give up after kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+// Wait for the barrier phase with the given parity; give up after limit_ns.
+__device__ __forceinline__ bool mbar_wait_bounded_ns(uint32_t bar, uint32_t parity, unsigned long long limit_ns) {
     if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long start = global_timer_ns();
     while (true) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (global_timer_ns() - start > kWaitLimitNs) return false;
+        if (global_timer_ns() - start > limit_ns) return false;
     }
+}
+
+// The kernels' waits: give up after kWaitLimitNs.
+__device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity) {
+    return mbar_wait_bounded_ns(bar, parity, kWaitLimitNs);
 }
 
 // --------------------------------------------------------------------- TMA

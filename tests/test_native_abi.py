@@ -35,7 +35,7 @@ def test_header_declares_the_expected_entry_points():
         'mv_device_status', 'mv_clear_device_status', 'mv_paged_decode_noalloc',
         'mv_paged_decode_append', 'mv_apply_rope', 'mv_rms_norm', 'mv_silu_mul',
         'mv_contiguous_decode_plan', 'mv_contiguous_decode', 'mv_paged_chunk_workspace_size',
-        'mv_paged_chunk_attention'}
+        'mv_paged_chunk_attention', 'mv_selftest_wait_timeout'}
 
 
 def test_library_loads_and_exports_every_declared_symbol():
