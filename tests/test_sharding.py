@@ -69,3 +69,60 @@ def test_gather_full_heads_over_two_gloo_ranks(q_heads, kv_heads, batch):
         proc.join(timeout=60)
         assert proc.exitcode == 0
     assert results == {0: True, 1: True}
+
+
+def _failure_worker(rank, world, port, mode, result_queue):
+    """Rank 1 fails before the full-head gather (dies, or stalls and never
+    joins); rank 0 reports how its gather ended."""
+    os.environ['MASTER_ADDR'] = '127.0.0.1'
+    os.environ['MASTER_PORT'] = str(port)
+    import datetime
+    import time
+    try:
+        # A generous timeout for the rendezvous (process start-up is slow on a
+        # busy host), a short one for the group the gather runs on.
+        dist.init_process_group('gloo', rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=120))
+        group = dist.new_group(ranks=list(range(world)), timeout=datetime.timedelta(seconds=5))
+    except Exception as exc:  # noqa: BLE001 - reported, the test fails on it
+        result_queue.put(('setup failed: ' + type(exc).__name__, 0.0))
+        os._exit(1)
+    full = torch.arange(4 * 28 * 3, dtype=torch.float32).reshape(4, 28, 3)
+    s = kv_head_shard(rank, world, q_heads=28, kv_heads=4, batch=4)
+    local = full[s.batch[0]:s.batch[1], s.q_heads[0]:s.q_heads[1]].clone()
+    if rank == 1:
+        if mode == 'dies':
+            os._exit(3)
+        time.sleep(120)          # stalls: the test ends this process
+        os._exit(0)
+    start = time.monotonic()
+    try:
+        gather_full_heads(local, q_heads=28, kv_heads=4, batch=4, group=group)
+        result_queue.put(('completed', time.monotonic() - start))
+    except Exception as exc:  # noqa: BLE001 - any error is the expected outcome
+        result_queue.put((type(exc).__name__, time.monotonic() - start))
+    os._exit(0)
+
+
+@pytest.mark.parametrize('mode', ['dies', 'stalls'])
+def test_a_failed_rank_ends_the_full_head_gather_with_an_error_not_a_hang(mode):
+    """Host-side failure detection: a peer that exits or never joins makes the
+    surviving rank's gather raise within the process group's timeout."""
+    import socket
+    with socket.socket() as sock:
+        sock.bind(('127.0.0.1', 0))
+        port = sock.getsockname()[1]
+    ctx = mp.get_context('spawn')
+    queue = ctx.Queue()
+    procs = [ctx.Process(target=_failure_worker, args=(r, 2, port, mode, queue)) for r in range(2)]
+    for proc in procs:
+        proc.start()
+    try:
+        outcome, elapsed = queue.get(timeout=180)
+    finally:
+        for proc in procs:
+            if proc.is_alive():
+                proc.terminate()
+            proc.join(timeout=30)
+    assert outcome != 'completed' and not outcome.startswith('setup failed'), outcome
+    assert elapsed < 60
