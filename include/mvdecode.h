@@ -65,6 +65,7 @@ extern "C" {
 
 /* Device status bits (sticky, per device; see mv_device_status). */
 #define MV_DEVICE_STATUS_WAIT_TIMEOUT 1u
+#define MV_DEVICE_STATUS_BAD_PAGE_ID 2u /* a used block-table entry was outside [0, num_blocks): its rows are NaN, its write skipped */
 
 /* Kernel paths reported by mv_paged_decode_plan. */
 #define MV_PATH_SIMT 0            /* CUDA cores, one CTA per (split, KV head, sequence) */
@@ -364,7 +365,7 @@ MV_API int mv_paged_decode_noalloc(const void* q, int64_t q_stride_seq, int64_t 
 
 /*
  * Sticky MV_DEVICE_STATUS_* bits kernels have raised on `device` (a bounded
- * wait that gave up). Reading synchronises with the device's legacy stream.
+ * wait that gave up; a used page ID outside the pool). Reading synchronises with the device's legacy stream.
  */
 MV_API int mv_device_status(int32_t device, uint32_t* status);
 MV_API int mv_clear_device_status(int32_t device);

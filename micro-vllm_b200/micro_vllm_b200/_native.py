@@ -28,6 +28,7 @@ FLAG_CUDA_CORE_MATH = 128
 PATH_SIMT, PATH_TMA_MMA, PATH_TMA_MMA_PERSISTENT, PATH_TMA_MMA_CLUSTER = 0, 1, 2, 3
 PATH_NAMES = {0: 'simt', 1: 'tma_mma', 2: 'tma_mma_persistent', 3: 'tma_mma_cluster'}
 DEVICE_STATUS_WAIT_TIMEOUT = 1
+DEVICE_STATUS_BAD_PAGE_ID = 2
 
 MV_OK = 0
 STATUS_NAMES = {

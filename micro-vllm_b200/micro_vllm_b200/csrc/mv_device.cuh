@@ -18,6 +18,11 @@ namespace mv {
 __device__ unsigned int g_device_status;
 
 constexpr unsigned kStatusWaitTimeout = 1u;
+constexpr unsigned kStatusBadPageId = 2u;
+
+// A used block-table entry outside the pool: its rows become NaN (or its
+// write is skipped); the sticky status records that it happened.
+__device__ __forceinline__ void report_bad_page_id() { atomicOr(&g_device_status, kStatusBadPageId); }
 // A bounded wait gives up after this long; nothing legitimate takes it.
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 
@@ -256,7 +261,10 @@ __device__ inline void append_row_direct(const DecodeParams& p, int b, int h, in
     const int64_t logical = pos / p.block_size;
     if (logical >= p.blocks_per_seq) return;
     const int64_t id = load_index(p.block_table, p.table_i64, b * p.table_stride + logical);
-    if (id < 0 || id >= p.num_blocks) return;
+    if (id < 0 || id >= p.num_blocks) {
+        if (threadIdx.x == 0) report_bad_page_id();
+        return;
+    }
     const int chunks = p.head_dim / 8;  // 16-byte chunks of a 2-byte row
     const int64_t slot = pos - logical * p.block_size;
     for (int c = threadIdx.x; c < 2 * chunks; c += blockDim.x) {
@@ -293,7 +301,10 @@ __device__ inline void append_row_elements(const DecodeParams& p, int b, int h, 
     const int64_t logical = pos / p.block_size;
     if (logical >= p.blocks_per_seq) return;
     const int64_t id = load_index(p.block_table, p.table_i64, b * p.table_stride + logical);
-    if (id < 0 || id >= p.num_blocks) return;
+    if (id < 0 || id >= p.num_blocks) {
+        if (threadIdx.x == 0) report_bad_page_id();
+        return;
+    }
     const int64_t dst = ((id * p.kv_heads + h) * p.block_size + (pos - logical * p.block_size)) * p.head_dim;
     const Raw* krow = static_cast<const Raw*>(p.new_key) + b * p.new_key_stride[0] + h * p.new_key_stride[1];
     const Raw* vrow = static_cast<const Raw*>(p.new_value) + b * p.new_value_stride[0] + h * p.new_value_stride[1];

@@ -52,7 +52,10 @@ __global__ void __launch_bounds__(kAppendThreads) write_paged_kv_kernel(const Ap
         const int64_t logical = pos / a.block_size;
         if (logical >= a.blocks_per_seq) continue;
         const int64_t phys = load_index(a.block_table, a.table_i64, b * a.table_stride + logical);
-        if (phys < 0 || phys >= a.num_blocks) continue;
+        if (phys < 0 || phys >= a.num_blocks) {
+            report_bad_page_id();
+            continue;
+        }
 
         const int64_t* sstr = which ? a.value_stride : a.key_stride;
         const uint8_t* src = static_cast<const uint8_t*>(which ? a.value : a.key) +

@@ -140,6 +140,7 @@ paged_chunk_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMap
             }
             const unsigned mask = __ballot_sync(0xffffffffu, bad);
             if (mask) {
+                if (lane == 0) report_bad_page_id();
                 first_bad = i0 + __ffs(mask) - 1;
                 break;
             }

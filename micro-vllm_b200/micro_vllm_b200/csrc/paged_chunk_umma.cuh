@@ -223,6 +223,7 @@ paged_chunk_umma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
             }
             const unsigned mask = __ballot_sync(0xffffffffu, bad);
             if (mask) {
+                if (is_k && lane == 0) report_bad_page_id();
                 first_bad = i0 + __ffs(mask) - 1;
                 break;
             }

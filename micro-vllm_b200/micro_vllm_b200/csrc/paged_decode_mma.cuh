@@ -573,7 +573,9 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
                              : load_index(p.block_table, p.table_i64, row_seq(p, b) * p.table_stride + page);
         bad = !p.contiguous && (my_id < 0 || my_id >= p.num_blocks);
     }
-    const bool warp_has_bad = __any_sync(0xffffffffu, bad) || rope_missing;
+    const bool any_bad_id = __any_sync(0xffffffffu, bad);
+    if (any_bad_id && lane == 0) report_bad_page_id();
+    const bool warp_has_bad = any_bad_id || rope_missing;
     const uint32_t bar0 = smem_addr(&bars[warp][0]);
     if (lane == 0) {
 #pragma unroll
@@ -871,6 +873,7 @@ __device__ __forceinline__ PageRef locate_page(const DecodeParams& p, const int6
     ref.page = static_cast<int>(page);
     const int64_t id = load_index(p.block_table, p.table_i64, b * p.table_stride + page);
     ref.id = (id < 0 || id >= p.num_blocks) ? -1 : static_cast<int>(id);
+    if (ref.id < 0) report_bad_page_id();
     const int64_t len = p.context_lens ? load_index(p.context_lens, p.lens_i64, b) : p.uniform_len;
     const int64_t left = len - page * kPageTokens;
     ref.meta = static_cast<int>(left < kPageTokens ? left : kPageTokens) |
@@ -1257,6 +1260,7 @@ paged_decode_cluster_kernel(const DecodeParams p, const __grid_constant__ CUtens
         for (int j = i; j < last; ++j) mbar_wait_bounded(bar0 + 8 * (j % STAGES), (j / STAGES) & 1);
         if (lane == 0) atomicOr(&g_device_status, kStatusWaitTimeout);
     }
+    if (lane == 0 && warp_bad) report_bad_page_id();
     if (lane == 0) warp_flags[warp] = (failed ? 2 : 0) | (warp_bad ? 1 : 0);
     w.reduce_l();
 

@@ -79,7 +79,10 @@ __global__ void __launch_bounds__(kSimtThreads) paged_decode_simt_kernel(const D
     const int64_t seq_row = row_seq(p, b);  // the sequence this query row belongs to
     for (int64_t pg = page_begin + tid; !p.contiguous && pg < page_end; pg += blockDim.x) {
         const int64_t id = load_index(p.block_table, p.table_i64, seq_row * p.table_stride + pg);
-        if (id < 0 || id >= p.num_blocks) atomicOr(&cta_bad, 1);
+        if (id < 0 || id >= p.num_blocks) {
+            atomicOr(&cta_bad, 1);
+            report_bad_page_id();
+        }
     }
     __syncthreads();
     if (cta_bad) {

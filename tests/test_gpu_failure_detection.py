@@ -81,3 +81,51 @@ def test_the_self_test_rejects_limits_outside_its_range_without_launching():
         assert b'limit_ns' in lib.mv_last_error()
     torch.cuda.synchronize()
     assert _status(lib, device) == 0
+
+
+@pytest.mark.parametrize('mode', ['auto', 'simt', 'persistent', 'cluster', 'chunk_tiles', 'append'])
+def test_a_page_id_outside_the_pool_raises_its_status_bit(mode):
+    """Bounds violations are recorded, not trapped: a used block-table entry
+    outside the pool gives NaN rows (or a skipped write) and raises
+    MV_DEVICE_STATUS_BAD_PAGE_ID; clean calls raise nothing."""
+    from micro_vllm_b200 import _native, cuda_attention, cuda_paged_cache
+    lib = _native.library()
+    device = torch.cuda.current_device()
+    inputs = make_inputs('qwen7b_bf16_small')
+    t = workload_tensors(inputs)
+    kw = {'simt': dict(force_simt=True), 'persistent': dict(persistent=True),
+          'cluster': dict(cluster=True)}.get(mode, {})
+
+    def run(table):
+        if mode == 'append':
+            cuda_paged_cache.write_paged_kv(t['key_new'], t['value_new'], t['key_pool'].clone(),
+                                            t['value_pool'].clone(), table, positions=t['context_lens'],
+                                            positions_are_end=True)
+            return None
+        if mode == 'chunk_tiles':
+            q = torch.randn(t['q'].shape[0], t['q'].shape[1], 16, t['q'].shape[2], device=t['q'].device,
+                            dtype=t['q'].dtype)
+            return cuda_attention.paged_chunk_attention(q, t['key_pool'], t['value_pool'], table,
+                                                        t['context_lens'].clamp(min=16))
+        return cuda_attention.paged_decode_attention(t['q'], t['key_pool'], t['value_pool'], table,
+                                                     t['context_lens'], **kw)
+
+    _native.check(lib.mv_clear_device_status(device))
+    run(t['block_table'])
+    torch.cuda.synchronize()
+    assert _status(lib, device) == 0
+    lens = inputs['context_lens']
+    victim = int(np.argmax(lens))
+    table = t['block_table'].clone()
+    last = (int(lens[victim]) + 15) // 16 - 1
+    table[victim, last] = t['key_pool'].shape[0]           # one past the pool
+    out = run(table)
+    torch.cuda.synchronize()
+    assert _status(lib, device) & _native.DEVICE_STATUS_BAD_PAGE_ID
+    if out is not None and mode != 'chunk_tiles':
+        values = as_float(out)
+        assert np.isnan(values[victim]).all()
+        others = [b for b in range(values.shape[0]) if b != victim and lens[b] > 0]
+        assert np.isfinite(values[others]).all()
+    _native.check(lib.mv_clear_device_status(device))
+    assert _status(lib, device) == 0

@@ -78,6 +78,7 @@ def test_python_binding_constants_match_the_header():
     assert constants['MV_FLAG_CHUNK_MMA_SYNC'] == _native.FLAG_CHUNK_MMA_SYNC
     assert constants['MV_FLAG_CUDA_CORE_MATH'] == _native.FLAG_CUDA_CORE_MATH
     assert constants['MV_DEVICE_STATUS_WAIT_TIMEOUT'] == _native.DEVICE_STATUS_WAIT_TIMEOUT
+    assert constants['MV_DEVICE_STATUS_BAD_PAGE_ID'] == _native.DEVICE_STATUS_BAD_PAGE_ID
     assert constants['MV_ABI_VERSION'] == _native.MV_ABI_VERSION
 
 
