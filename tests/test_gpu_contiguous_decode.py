@@ -237,3 +237,30 @@ def test_unaligned_cache_views_take_the_cuda_core_kernel():
     for b in range(2):
         assert_close(out[b], decode_fp64_per_head(query[b].double().cpu().numpy(), key[b].double().cpu().numpy(),
                                                   value[b].double().cpu().numpy()), torch.bfloat16)
+
+
+def test_multi_wave_grid_with_a_first_split_matches_the_oracle():
+    """A batch big enough for more than one wave of CTAs takes the first-split
+    schedule (split 0 twice the split size, split-major order) on contiguous
+    caches too; checked against the fp64 oracle on a sample of sequences, and
+    against the uniform-split plan of the same size on all of them."""
+    api = _api()
+    gen = torch.Generator(device='cuda').manual_seed(21)
+    batch, hq, hkv, dim, cap = 128, 28, 4, 128, 704
+    key = randn((batch, hkv, cap, dim), torch.bfloat16, gen)
+    value = randn((batch, hkv, cap, dim), torch.bfloat16, gen)
+    query = randn((batch, hq, dim), torch.bfloat16, gen)
+    lens = torch.randint(1, cap + 1, (batch,), generator=torch.Generator().manual_seed(22)).to(torch.int32).cuda()
+    path, pps, splits = api.contiguous_decode_plan(key, value, hq)
+    max_pages = cap // 16
+    assert path == 'tma_mma' and 2 * pps < max_pages
+    assert splits == 1 + -(-(max_pages - 2 * pps) // pps)      # a first split of 2 x pps runs
+    out = api.contiguous_decode_attention(query, key, value, lens)
+    uniform = api.contiguous_decode_attention(query, key, value, lens, pages_per_split=pps)
+    np.testing.assert_allclose(out.float().cpu().numpy(), uniform.float().cpu().numpy(), rtol=2e-2, atol=2e-2)
+    for b in range(0, batch, 9):
+        length = int(lens[b])
+        expected = decode_fp64_per_head(query[b].double().cpu().numpy(),
+                                        key[b, :, :length].double().cpu().numpy(),
+                                        value[b, :, :length].double().cpu().numpy())
+        assert_close(out[b], expected, torch.bfloat16)
