@@ -364,6 +364,32 @@ MV_API int mv_paged_decode_noalloc(const void* q, int64_t q_stride_seq, int64_t 
                                    uint32_t flags, int32_t dtype, void* stream);
 
 /*
+ * The one-call decode step with its arguments in one struct: every field is
+ * 8 bytes wide, in this order, with no padding. No reference counterpart: the
+ * same call as mv_paged_decode_append (key and value non-NULL) or
+ * mv_paged_decode (both NULL; the RoPE fields then unused), for bindings that
+ * pay per marshalled argument (ctypes: ~0.4 us each, so a 35-argument call
+ * costs more host time than a small decode step takes on the GPU). A caller
+ * fills the struct once and changes only the fields that change per step.
+ * The int64 fields standing for int32 arguments must fit in int32.
+ */
+typedef struct MvDecodeStepArgs {
+    const void* q; int64_t q_stride_seq; int64_t q_stride_head;
+    const void* key; int64_t key_stride_seq; int64_t key_stride_head;
+    const void* value; int64_t value_stride_seq; int64_t value_stride_head;
+    const void* rope_cos; const void* rope_sin; int64_t rope_rows;
+    void* k_cache; void* v_cache; int64_t num_blocks; int64_t num_kv_heads; int64_t block_size;
+    int64_t head_dim;
+    const void* block_table; int64_t block_table_type; int64_t block_table_stride; int64_t blocks_per_seq;
+    const void* context_lens; int64_t context_lens_type; int64_t max_context_len;
+    int64_t batch; int64_t num_q_heads; double scale;
+    void* out; int64_t out_stride_seq; int64_t out_stride_head;
+    void* workspace; uint64_t workspace_bytes; int64_t pages_per_split; uint64_t flags; int64_t dtype;
+} MvDecodeStepArgs;
+
+MV_API int mv_paged_decode_step_args(const MvDecodeStepArgs* args, void* stream);
+
+/*
  * Sticky MV_DEVICE_STATUS_* bits kernels have raised on `device` (a bounded
  * wait that gave up; a used page ID outside the pool). Reading synchronises with the device's legacy stream.
  */

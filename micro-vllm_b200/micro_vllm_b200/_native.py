@@ -44,12 +44,30 @@ EXPORTED_SYMBOLS = (
     'mv_device_status', 'mv_clear_device_status', 'mv_paged_decode_append', 'mv_apply_rope',
     'mv_rms_norm', 'mv_silu_mul', 'mv_contiguous_decode_plan', 'mv_contiguous_decode',
     'mv_paged_chunk_workspace_size', 'mv_paged_chunk_attention', 'mv_selftest_wait_timeout',
+    'mv_paged_decode_step_args',
 )
 
 _i32, _i64, _u32, _vp, _sz, _f32 = (ctypes.c_int32, ctypes.c_int64, ctypes.c_uint32,
                                     ctypes.c_void_p, ctypes.c_size_t, ctypes.c_float)
 
+class MvDecodeStepArgs(ctypes.Structure):
+    """MvDecodeStepArgs of include/mvdecode.h: every field 8 bytes, no padding."""
+    _fields_ = [(name, kind) for names, kind in (
+        (('q',), _vp), (('q_stride_seq', 'q_stride_head'), _i64),
+        (('key',), _vp), (('key_stride_seq', 'key_stride_head'), _i64),
+        (('value',), _vp), (('value_stride_seq', 'value_stride_head'), _i64),
+        (('rope_cos', 'rope_sin'), _vp), (('rope_rows',), _i64),
+        (('k_cache', 'v_cache'), _vp), (('num_blocks', 'num_kv_heads', 'block_size', 'head_dim'), _i64),
+        (('block_table',), _vp), (('block_table_type', 'block_table_stride', 'blocks_per_seq'), _i64),
+        (('context_lens',), _vp), (('context_lens_type', 'max_context_len', 'batch', 'num_q_heads'), _i64),
+        (('scale',), ctypes.c_double),
+        (('out',), _vp), (('out_stride_seq', 'out_stride_head'), _i64),
+        (('workspace',), _vp), (('workspace_bytes',), ctypes.c_uint64), (('pages_per_split',), _i64),
+        (('flags',), ctypes.c_uint64), (('dtype',), _i64)) for name in names]
+
+
 _SIGNATURES = {
+    'mv_paged_decode_step_args': (ctypes.c_int, [ctypes.POINTER(MvDecodeStepArgs), _vp]),
     'mv_abi_version': (ctypes.c_int, []),
     'mv_last_error': (ctypes.c_char_p, []),
     'mv_paged_decode_workspace_size': (

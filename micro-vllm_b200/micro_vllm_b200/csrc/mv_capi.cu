@@ -8,6 +8,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <unordered_map>
 #include <string>
 #include <type_traits>
 #include <utility>
@@ -91,13 +92,43 @@ cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t 
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// Kernel attributes already set on a device (a cudaFuncSetAttribute per
+// launch costs host time every call): kernel -> dynamic shared memory bytes
+// allowed, and whether the largest carveout was requested.
+struct KernelAttrs {
+    size_t smem_bytes = 48 * 1024;
+    bool carveout = false;
+};
+std::mutex g_attr_mutex;
+std::unordered_map<const void*, KernelAttrs> g_attrs[kMaxDevices];
+
+template <typename Kernel>
+int set_kernel_attrs(Kernel kernel, size_t bytes, bool carveout) {
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaGetDevice");
+    if (dev < 0 || dev >= kMaxDevices) return fail(MV_ERR_UNSUPPORTED, "device index %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_attr_mutex);
+    KernelAttrs& attrs = g_attrs[dev][reinterpret_cast<const void*>(kernel)];
+    if (bytes > attrs.smem_bytes) {
+        err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+        if (err != cudaSuccess) return cuda_fail(err, "cudaFuncSetAttribute");
+        attrs.smem_bytes = bytes;
+    }
+    if (carveout && !attrs.carveout) {
+        err = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                   static_cast<int>(cudaSharedmemCarveoutMaxShared));
+        if (err != cudaSuccess) return cuda_fail(err, "cudaFuncSetAttribute");
+        attrs.carveout = true;
+    }
+    return MV_OK;
+}
+
 // Opt a kernel into `bytes` of dynamic shared memory on the current device.
 template <typename Kernel>
 int ensure_smem(Kernel kernel, size_t bytes) {
     if (bytes <= 48 * 1024) return MV_OK;
-    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           static_cast<int>(bytes));
-    return err == cudaSuccess ? MV_OK : cuda_fail(err, "cudaFuncSetAttribute");
+    return set_kernel_attrs(kernel, bytes, false);
 }
 
 // As ensure_smem, and prefer the largest shared-memory carveout: left to
@@ -105,11 +136,7 @@ int ensure_smem(Kernel kernel, size_t bytes) {
 // kernel's registers allow.
 template <typename Kernel>
 int ensure_smem_carveout(Kernel kernel, size_t bytes) {
-    int rc = ensure_smem(kernel, bytes);
-    if (rc != MV_OK) return rc;
-    cudaError_t err = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                           static_cast<int>(cudaSharedmemCarveoutMaxShared));
-    return err == cudaSuccess ? MV_OK : cuda_fail(err, "cudaFuncSetAttribute");
+    return set_kernel_attrs(kernel, bytes, true);
 }
 
 // ---------------------------------------------------------------- planning
@@ -1136,6 +1163,38 @@ int mv_paged_decode_append(const void* q, int64_t q_stride_seq, int64_t q_stride
                              blocks_per_seq, context_lens, context_lens_type, max_context_len, batch,
                              num_q_heads, scale, out, out_stride_seq, out_stride_head, workspace,
                              workspace_bytes, pages_per_split, flags, dtype, stream, &rows);
+}
+
+int mv_paged_decode_step_args(const MvDecodeStepArgs* a, void* stream) {
+    if (!a) return fail(MV_ERR_INVALID_ARGUMENT, "args must not be NULL");
+    const int64_t narrow[] = {a->num_kv_heads, a->block_size, a->head_dim, a->block_table_type,
+                              a->context_lens_type, a->batch, a->num_q_heads, a->pages_per_split, a->dtype};
+    for (const int64_t v : narrow)
+        if (v < INT32_MIN || v > INT32_MAX) return fail(MV_ERR_INVALID_ARGUMENT, "an int32 field is out of range");
+    if (a->flags > UINT32_MAX) return fail(MV_ERR_INVALID_ARGUMENT, "flags out of range");
+    const uint32_t flags = static_cast<uint32_t>(a->flags);
+    if (!a->key && !a->value)
+        return mv_paged_decode(a->q, a->q_stride_seq, a->q_stride_head, a->k_cache, a->v_cache, a->num_blocks,
+                               static_cast<int32_t>(a->num_kv_heads), static_cast<int32_t>(a->block_size),
+                               static_cast<int32_t>(a->head_dim), a->block_table,
+                               static_cast<int32_t>(a->block_table_type), a->block_table_stride, a->blocks_per_seq,
+                               a->context_lens, static_cast<int32_t>(a->context_lens_type), a->max_context_len,
+                               static_cast<int32_t>(a->batch), static_cast<int32_t>(a->num_q_heads),
+                               static_cast<float>(a->scale), a->out, a->out_stride_seq, a->out_stride_head,
+                               a->workspace, a->workspace_bytes, static_cast<int32_t>(a->pages_per_split), flags,
+                               static_cast<int32_t>(a->dtype), stream);
+    return mv_paged_decode_append(a->q, a->q_stride_seq, a->q_stride_head, a->key, a->key_stride_seq,
+                                  a->key_stride_head, a->value, a->value_stride_seq, a->value_stride_head,
+                                  a->rope_cos, a->rope_sin, a->rope_rows, a->k_cache, a->v_cache, a->num_blocks,
+                                  static_cast<int32_t>(a->num_kv_heads), static_cast<int32_t>(a->block_size),
+                                  static_cast<int32_t>(a->head_dim), a->block_table,
+                                  static_cast<int32_t>(a->block_table_type), a->block_table_stride,
+                                  a->blocks_per_seq, a->context_lens, static_cast<int32_t>(a->context_lens_type),
+                                  a->max_context_len, static_cast<int32_t>(a->batch),
+                                  static_cast<int32_t>(a->num_q_heads), static_cast<float>(a->scale), a->out,
+                                  a->out_stride_seq, a->out_stride_head, a->workspace, a->workspace_bytes,
+                                  static_cast<int32_t>(a->pages_per_split), flags, static_cast<int32_t>(a->dtype),
+                                  stream);
 }
 
 int mv_paged_chunk_attention(const void* q, int64_t q_stride_seq, int64_t q_stride_token, int64_t q_stride_head,

@@ -493,6 +493,10 @@ def _aligned16(*tensors):
     return True
 
 
+def _data_ptrs(*tensors):
+    return tuple(t.data_ptr() if t is not None else 0 for t in tensors)
+
+
 class PagedDecodeStep:
     """A decode step bound to one page pool, validated once and called per step.
 
@@ -502,8 +506,12 @@ class PagedDecodeStep:
     lengths (device data) and the output. Binding them once moves every check
     that ``paged_decode_attention`` / ``paged_decode_with_append`` repeat per
     call to construction, so a call costs a few attribute comparisons and one
-    C-ABI call (``mv_paged_decode`` or ``mv_paged_decode_append``). Results are
-    identical to those functions on the same arguments.
+    C-ABI call (``mv_paged_decode_step_args``: the arguments of
+    ``mv_paged_decode`` / ``mv_paged_decode_append`` in one struct, filled at
+    construction and on each validated call). A call repeating the last one
+    with the same tensor objects over the same storage, on the same stream,
+    skips even those comparisons. Results are identical to those functions on
+    the same arguments.
 
     ``step(query, context_lens, out=None, key=None, value=None)``: query
     [B, Hq, D] or [B, Hq, 1, D]; context_lens [B] int32/int64 on the pool's
@@ -549,12 +557,23 @@ class PagedDecodeStep:
                 batch, num_q_heads, kv_heads, dim, block_size, self._bound, self._pps, self._flags, dtype,
                 ctypes.byref(size)))
         self._workspace_bytes = size.value
-        # Arguments after the query/new-row pointers, with the per-call ones left as None.
-        self._pool_args = (key_cache.data_ptr(), value_cache.data_ptr(), num_blocks, kv_heads, block_size, dim,
-                           block_table.data_ptr(), INDEX_CODES[block_table.dtype], block_table.stride(0),
-                           block_table.shape[1])
         self._scale = float(scale)
         self._dtype_code = dtype
+        # The call's arguments in one struct (mv_paged_decode_step_args): the
+        # bound fields are set once, the per-call ones on each validated call.
+        self._args = _native.MvDecodeStepArgs(
+            k_cache=key_cache.data_ptr(), v_cache=value_cache.data_ptr(), num_blocks=num_blocks,
+            num_kv_heads=kv_heads, block_size=block_size, head_dim=dim, block_table=block_table.data_ptr(),
+            block_table_type=INDEX_CODES[block_table.dtype], block_table_stride=block_table.stride(0),
+            blocks_per_seq=block_table.shape[1], max_context_len=self._bound, batch=batch,
+            num_q_heads=num_q_heads, scale=self._scale, workspace_bytes=self._workspace_bytes,
+            pages_per_split=self._pps, flags=self._flags, dtype=dtype)
+        self._args_ref = ctypes.byref(self._args)
+        # Validated calls a repeat may skip the checks for (a serving loop
+        # cycles through a few static buffer sets): object ids -> (the
+        # objects, their data pointers, stream, workspace, packed arguments).
+        # Holding the objects keeps them, and so their ids, alive.
+        self._fast = {}
         self._rope = None
         self._rope_in_kernel = False
         if rope is not None:
@@ -590,6 +609,21 @@ class PagedDecodeStep:
 
     def __call__(self, query: torch.Tensor, context_lens: torch.Tensor, out: torch.Tensor | None = None,
                  key: torch.Tensor | None = None, value: torch.Tensor | None = None) -> torch.Tensor:
+        # A repeat of the last call -- the same tensor objects over the same
+        # storage, on the same stream (a serving loop's static buffers) -- was
+        # validated then: only the C call remains (a few us of host time
+        # instead of ~45 for the checks and a 35-argument ctypes call).
+        ids = (id(query), id(context_lens), id(out), id(key), id(value))
+        entry = self._fast.get(ids)
+        if entry is not None and torch.cuda.current_device() == self._device_index:
+            objects, ptrs, stream0, _, args_ref = entry
+            stream = current_stream_raw(self._device_index)
+            if (stream == stream0 and objects[0] is query and objects[2] is out
+                    and ptrs == _data_ptrs(query, context_lens, out, key, value)):
+                _native.check(self._lib.mv_paged_decode_step_args(args_ref, stream))
+                return out
+        self._fast.pop(ids, None)
+        out_given = out is not None
         q = query[:, :, 0] if query.dim() == 4 and query.shape[2] == 1 else query
         _check(tuple(q.shape) == self._q_shape and q.dtype == self._dtype and q.device == self._device,
                'query must be [B, Hq, D] (or [B, Hq, 1, D]) of the bound shape, dtype and device')
@@ -607,31 +641,44 @@ class PagedDecodeStep:
         _check((key is None) == (value is None), 'pass both new K and V rows, or neither')
         if torch.cuda.current_device() != self._device_index:
             with torch.cuda.device(self._device):
-                return self(query, context_lens, out, key, value)
+                return self(query, context_lens, out if out_given else None, key, value)
         stream = current_stream_raw(self._device_index)
         workspace = _workspace(self._device, stream, self._workspace_bytes) if self._workspace_bytes else None
-        tail = (context_lens.data_ptr(), lens_code, self._bound, self._q_shape[0], self._q_shape[1], self._scale,
-                out.data_ptr(), out.stride(0), out.stride(1),
-                workspace.data_ptr() if workspace is not None else None, self._workspace_bytes,
-                self._pps, self._flags, self._dtype_code, stream)
+        a = self._args
+        a.q, a.q_stride_seq, a.q_stride_head = q.data_ptr(), q.stride(0), q.stride(1)
+        a.context_lens, a.context_lens_type = context_lens.data_ptr(), lens_code
+        a.out, a.out_stride_seq, a.out_stride_head = out.data_ptr(), out.stride(0), out.stride(1)
+        a.workspace = workspace.data_ptr() if workspace is not None else None
+        rotated_here = False
         if key is None:
             _check(self._rope is None, 'a step bound with RoPE tables needs the new K/V rows')
-            _native.check(self._lib.mv_paged_decode(q.data_ptr(), q.stride(0), q.stride(1), *self._pool_args,
-                                                    *tail))
-            return out
-        key, value = self._check_rows(key), self._check_rows(value)
-        tables = (None, None, 0)
-        if self._rope is not None:
-            cos, sin = self._rope
-            if self._rope_in_kernel and (self._rope_kernel_path == 'simt' or _aligned16(key, value)):
-                tables = (cos.data_ptr(), sin.data_ptr(), cos.shape[0])
-            else:
-                from . import rope as rope_ops
-                q = rope_ops.apply_rope(q, cos, sin, positions=context_lens, positions_are_end=True)
-                key = rope_ops.apply_rope(key, cos, sin, positions=context_lens, positions_are_end=True)
-        _native.check(self._lib.mv_paged_decode_append(
-            q.data_ptr(), q.stride(0), q.stride(1), key.data_ptr(), key.stride(0), key.stride(1),
-            value.data_ptr(), value.stride(0), value.stride(1), *tables, *self._pool_args, *tail))
+            a.key = a.value = a.rope_cos = a.rope_sin = None
+            a.key_stride_seq = a.key_stride_head = a.value_stride_seq = a.value_stride_head = a.rope_rows = 0
+        else:
+            rows_k, rows_v = self._check_rows(key), self._check_rows(value)
+            a.rope_cos = a.rope_sin = None
+            a.rope_rows = 0
+            if self._rope is not None:
+                cos, sin = self._rope
+                if self._rope_in_kernel and (self._rope_kernel_path == 'simt' or _aligned16(rows_k, rows_v)):
+                    a.rope_cos, a.rope_sin, a.rope_rows = cos.data_ptr(), sin.data_ptr(), cos.shape[0]
+                else:
+                    from . import rope as rope_ops
+                    q = rope_ops.apply_rope(q, cos, sin, positions=context_lens, positions_are_end=True)
+                    rows_k = rope_ops.apply_rope(rows_k, cos, sin, positions=context_lens, positions_are_end=True)
+                    a.q, a.q_stride_seq, a.q_stride_head = q.data_ptr(), q.stride(0), q.stride(1)
+                    rotated_here = True
+            a.key, a.key_stride_seq, a.key_stride_head = rows_k.data_ptr(), rows_k.stride(0), rows_k.stride(1)
+            a.value, a.value_stride_seq, a.value_stride_head = rows_v.data_ptr(), rows_v.stride(0), rows_v.stride(1)
+        _native.check(self._lib.mv_paged_decode_step_args(self._args_ref, stream))
+        if out_given and not rotated_here and not torch.cuda.is_current_stream_capturing():
+            if len(self._fast) >= 8:
+                self._fast.pop(next(iter(self._fast)))
+            args = _native.MvDecodeStepArgs()
+            ctypes.pointer(args)[0] = a
+            self._fast[ids] = ((query, context_lens, out, key, value),
+                               _data_ptrs(query, context_lens, out, key, value), stream, workspace,
+                               ctypes.byref(args))
         return out
 
 

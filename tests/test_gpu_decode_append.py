@@ -284,3 +284,36 @@ def test_first_split_schedule_of_multi_wave_grids(lens):
     assert_attention_close(as_float(uniform), expected, 'bfloat16')
     empty = inputs['context_lens'] == 0
     assert (as_float(out)[empty] == 0).all()
+
+
+def test_bound_step_repeats_with_the_same_tensors_skip_the_checks_and_stay_exact():
+    """A repeat of the last call (same tensor objects and storage, same stream)
+    goes straight to the packed C call; it must see in-place changes to the
+    inputs, match the one-off call bit for bit, and fall back to the checked
+    path when any tensor changes."""
+    attention, _ = _ops()
+    inputs = make_inputs('qwen7b_bf16_small')
+    t = workload_tensors(inputs)
+    pools = (t['key_pool'].clone(), t['value_pool'].clone())
+    step = attention.PagedDecodeStep(*pools, t['block_table'], num_q_heads=t['q'].shape[1])
+    q, lens = t['q'].clone(), t['context_lens'].clone()
+    key, value = t['key_new'][:, :, 0].clone(), t['value_new'][:, :, 0].clone()
+    out = torch.empty_like(q)
+    step(q, lens, out, key=key, value=value)
+    assert len(step._fast) == 1
+    for scale in (0.5, -2.0):
+        q.mul_(scale)                              # same storage, new values
+        key.mul_(scale)
+        step(q, lens, out, key=key, value=value)  # the repeat
+        ref_pools = (t['key_pool'].clone(), t['value_pool'].clone())
+        expected = attention.paged_decode_with_append(q, key, value, *ref_pools, t['block_table'], lens)
+        torch.cuda.synchronize()
+        assert _same_bits(out, expected)
+        assert _same_bits(pools[0], ref_pools[0]) and _same_bits(pools[1], ref_pools[1])
+    other = torch.empty_like(q)
+    step(q, lens, other, key=key, value=value)    # a different output tensor: checked again
+    torch.cuda.synchronize()
+    assert _same_bits(other, out)
+    assert len(step._fast) == 2
+    with pytest.raises(RuntimeError, match='bound shape'):
+        step(q[:1], lens, out, key=key, value=value)

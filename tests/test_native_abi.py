@@ -35,7 +35,21 @@ def test_header_declares_the_expected_entry_points():
         'mv_device_status', 'mv_clear_device_status', 'mv_paged_decode_noalloc',
         'mv_paged_decode_append', 'mv_apply_rope', 'mv_rms_norm', 'mv_silu_mul',
         'mv_contiguous_decode_plan', 'mv_contiguous_decode', 'mv_paged_chunk_workspace_size',
-        'mv_paged_chunk_attention', 'mv_selftest_wait_timeout'}
+        'mv_paged_chunk_attention', 'mv_selftest_wait_timeout', 'mv_paged_decode_step_args'}
+
+
+def test_step_args_struct_matches_the_header():
+    """MvDecodeStepArgs: the ctypes mirror has the header's fields, in order, 8 bytes each."""
+    import ctypes
+    from micro_vllm_b200 import _native
+    body = re.search(r'typedef struct MvDecodeStepArgs \{(.*?)\} MvDecodeStepArgs;', HEADER.read_text(), re.S).group(1)
+    names = []
+    for decl in body.replace('\n', ' ').split(';'):
+        decl = decl.strip()
+        if decl:
+            names.append(re.findall(r'(\w+)\s*$', decl)[0])
+    assert names == [name for name, _ in _native.MvDecodeStepArgs._fields_]
+    assert ctypes.sizeof(_native.MvDecodeStepArgs) == 8 * len(names)
 
 
 def test_library_loads_and_exports_every_declared_symbol():
