@@ -508,10 +508,12 @@ class PagedDecodeStep:
     call to construction, so a call costs a few attribute comparisons and one
     C-ABI call (``mv_paged_decode_step_args``: the arguments of
     ``mv_paged_decode`` / ``mv_paged_decode_append`` in one struct, filled at
-    construction and on each validated call). A call repeating the last one
-    with the same tensor objects over the same storage, on the same stream,
-    skips even those comparisons. Results are identical to those functions on
-    the same arguments.
+    construction and on each validated call). A call repeating one of the
+    last eight validated ones -- the same tensor objects over the same
+    storage, on the same stream, with a caller-given output -- skips even
+    those comparisons; the step keeps references to those tensors until they
+    are evicted. Results are identical to those functions on the same
+    arguments.
 
     ``step(query, context_lens, out=None, key=None, value=None)``: query
     [B, Hq, D] or [B, Hq, 1, D]; context_lens [B] int32/int64 on the pool's
