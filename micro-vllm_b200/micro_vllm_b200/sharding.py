@@ -62,12 +62,16 @@ def kv_head_shard(rank, world, *, q_heads, kv_heads, batch):
     raise ValueError('world size must divide, or be a multiple of, the KV head count')
 
 
-def gather_full_heads(local_out, *, q_heads, kv_heads, batch, group=None):
+def gather_full_heads(local_out, *, q_heads, kv_heads, batch, group=None, timeout=None):
     """All-gather per-rank outputs [num_seqs, num_q_heads, D] into [batch, q_heads, D].
 
     Every rank calls this with its own shard's output (one collective, the
     same on every rank). NCCL uses ``all_gather_into_tensor``; other backends
     ``all_gather``. Ragged shards are padded to a common size for the exchange.
+    timeout (a ``datetime.timedelta``): the longest this call waits for the
+    exchange; past it (a peer that died or never joins) it raises
+    RuntimeError instead of waiting on the backend, which does not always
+    honour its own timeout when a peer's process is gone.
     """
     import torch.distributed as dist
 
@@ -81,11 +85,15 @@ def gather_full_heads(local_out, *, q_heads, kv_heads, batch, group=None):
     padded[:local_out.shape[0], :local_out.shape[1]] = local_out
     if dist.get_backend(group) == 'nccl':
         stacked = local_out.new_empty((world, rows, cols, dim))
-        dist.all_gather_into_tensor(stacked, padded, group=group)
+        work = dist.all_gather_into_tensor(stacked, padded, group=group, async_op=True)
         pieces = list(stacked.unbind(0))
     else:
         pieces = [torch.empty_like(padded) for _ in range(world)]
-        dist.all_gather(pieces, padded, group=group)
+        work = dist.all_gather(pieces, padded, group=group, async_op=True)
+    if timeout is None:
+        work.wait()
+    elif not work.wait(timeout):
+        raise RuntimeError(f'full-head gather did not complete within {timeout}')
     full = local_out.new_empty((batch, q_heads, dim))
     for shard, piece in zip(shards, pieces):
         full[shard.batch[0]:shard.batch[1], shard.q_heads[0]:shard.q_heads[1]] = \

@@ -378,3 +378,36 @@ def test_inputs_unchanged_and_repeatable():
     for key, tensor in t.items():
         assert torch.equal(tensor.view(torch.uint8) if tensor.dtype.is_floating_point else tensor,
                            before[key].view(torch.uint8) if tensor.dtype.is_floating_point else before[key])
+
+
+def test_repeated_calls_are_bit_identical_on_every_default_path():
+    """The same inputs give the same bits on every call: each split walks its
+    pages in a fixed order and the merge sums the splits in a fixed order, on
+    a multi-wave grid (first-split schedule), the one-call step, contiguous
+    caches and chunk query tiles alike."""
+    attention, cache = _native()
+    spec = dict(batch=128, q_heads=28, kv_heads=4, head_dim=128, block_size=16, pool=('factor', 1.25),
+                lens=('uniform', 100, 700), dtype='bfloat16', value_scale=0.5, seed=777)
+    inputs = make_inputs(spec)
+    t = workload_tensors(inputs)
+
+    def same(fn):
+        first = fn().clone()
+        for _ in range(3):
+            again = fn()
+            torch.cuda.synchronize()
+            assert torch.equal(first.view(torch.int16), again.view(torch.int16))
+
+    same(lambda: attention.paged_decode_attention(t['q'], t['key_pool'], t['value_pool'], t['block_table'],
+                                                  t['context_lens']))
+    same(lambda: attention.paged_decode_with_append(t['q'], t['key_new'], t['value_new'], t['key_pool'],
+                                                    t['value_pool'], t['block_table'], t['context_lens']))
+    gen = torch.Generator(device='cuda').manual_seed(5)
+    kc = torch.randn((64, 4, 512, 128), generator=gen, device='cuda').to(torch.bfloat16)
+    vc = torch.randn((64, 4, 512, 128), generator=gen, device='cuda').to(torch.bfloat16)
+    qc = torch.randn((64, 28, 128), generator=gen, device='cuda').to(torch.bfloat16)
+    lc = torch.randint(1, 513, (64,), generator=torch.Generator().manual_seed(6)).to(torch.int32).cuda()
+    same(lambda: attention.contiguous_decode_attention(qc, kc, vc, lc))
+    qt = torch.randn((8, 28, 32, 128), generator=gen, device='cuda').to(torch.bfloat16)
+    lens = t['context_lens'][:8].clamp(min=32)
+    same(lambda: attention.paged_chunk_attention(qt, t['key_pool'], t['value_pool'], t['block_table'][:8], lens))

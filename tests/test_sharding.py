@@ -71,6 +71,15 @@ def test_gather_full_heads_over_two_gloo_ranks(q_heads, kv_heads, batch):
     assert results == {0: True, 1: True}
 
 
+def _report(result_queue, item, code):
+    # Queue.put hands the item to a feeder thread; flush it to the pipe before
+    # os._exit, which would otherwise end the process with the item unsent.
+    result_queue.put(item)
+    result_queue.close()
+    result_queue.join_thread()
+    os._exit(code)
+
+
 def _failure_worker(rank, world, port, mode, result_queue):
     """Rank 1 fails before the full-head gather (dies, or stalls and never
     joins); rank 0 reports how its gather ended."""
@@ -84,9 +93,9 @@ def _failure_worker(rank, world, port, mode, result_queue):
         dist.init_process_group('gloo', rank=rank, world_size=world,
                                 timeout=datetime.timedelta(seconds=120))
         group = dist.new_group(ranks=list(range(world)), timeout=datetime.timedelta(seconds=5))
+        dist.barrier()   # both ranks are set up before rank 1 fails
     except Exception as exc:  # noqa: BLE001 - reported, the test fails on it
-        result_queue.put(('setup failed: ' + type(exc).__name__, 0.0))
-        os._exit(1)
+        _report(result_queue, ('setup failed: ' + type(exc).__name__, 0.0), 1)
     full = torch.arange(4 * 28 * 3, dtype=torch.float32).reshape(4, 28, 3)
     s = kv_head_shard(rank, world, q_heads=28, kv_heads=4, batch=4)
     local = full[s.batch[0]:s.batch[1], s.q_heads[0]:s.q_heads[1]].clone()
@@ -97,11 +106,12 @@ def _failure_worker(rank, world, port, mode, result_queue):
         os._exit(0)
     start = time.monotonic()
     try:
-        gather_full_heads(local, q_heads=28, kv_heads=4, batch=4, group=group)
-        result_queue.put(('completed', time.monotonic() - start))
+        gather_full_heads(local, q_heads=28, kv_heads=4, batch=4, group=group,
+                          timeout=datetime.timedelta(seconds=10))
+        outcome = 'completed'
     except Exception as exc:  # noqa: BLE001 - any error is the expected outcome
-        result_queue.put((type(exc).__name__, time.monotonic() - start))
-    os._exit(0)
+        outcome = type(exc).__name__
+    _report(result_queue, (outcome, time.monotonic() - start), 0)
 
 
 @pytest.mark.parametrize('mode', ['dies', 'stalls'])
