@@ -36,7 +36,7 @@ def test_rejects_bad_ranks_and_head_counts():
         kv_head_shard(0, 2, q_heads=27, kv_heads=4, batch=64)
 
 
-def _gather_worker(rank, world, port, q_heads, kv_heads, batch, result_queue):
+def _gather_worker(rank, world, port, q_heads, kv_heads, batch, timeout_s, result_queue):
     os.environ['MASTER_ADDR'] = '127.0.0.1'
     os.environ['MASTER_PORT'] = str(port)
     import datetime
@@ -46,21 +46,24 @@ def _gather_worker(rank, world, port, q_heads, kv_heads, batch, result_queue):
         full = torch.arange(batch * q_heads * 3, dtype=torch.float32).reshape(batch, q_heads, 3)
         s = kv_head_shard(rank, world, q_heads=q_heads, kv_heads=kv_heads, batch=batch)
         local = full[s.batch[0]:s.batch[1], s.q_heads[0]:s.q_heads[1]].clone()
-        gathered = gather_full_heads(local, q_heads=q_heads, kv_heads=kv_heads, batch=batch)
+        timeout = None if timeout_s is None else datetime.timedelta(seconds=timeout_s)
+        gathered = gather_full_heads(local, q_heads=q_heads, kv_heads=kv_heads, batch=batch,
+                                     timeout=timeout)
         result_queue.put((rank, bool(torch.equal(gathered, full))))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize('q_heads, kv_heads, batch', [(28, 4, 6), (14, 1, 5)])
-def test_gather_full_heads_over_two_gloo_ranks(q_heads, kv_heads, batch):
+@pytest.mark.parametrize('q_heads, kv_heads, batch, timeout_s',
+                         [(28, 4, 6, None), (14, 1, 5, None), (28, 4, 6, 60)])
+def test_gather_full_heads_over_two_gloo_ranks(q_heads, kv_heads, batch, timeout_s):
     import socket
     with socket.socket() as sock:
         sock.bind(('127.0.0.1', 0))
         port = sock.getsockname()[1]
     ctx = mp.get_context('spawn')
     queue = ctx.Queue()
-    procs = [ctx.Process(target=_gather_worker, args=(r, 2, port, q_heads, kv_heads, batch, queue))
+    procs = [ctx.Process(target=_gather_worker, args=(r, 2, port, q_heads, kv_heads, batch, timeout_s, queue))
              for r in range(2)]
     for proc in procs:
         proc.start()
