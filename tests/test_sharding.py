@@ -3,6 +3,8 @@ import os
 
 import pytest
 import torch
+from hypothesis import given, settings
+from hypothesis import strategies as st
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
@@ -25,6 +27,33 @@ def test_shards_cover_every_head_and_sequence_once(world, q_heads, kv_heads, bat
         assert s.q_heads == (s.kv_heads[0] * group, s.kv_heads[1] * group)
         owner[s.batch[0]:s.batch[1], s.q_heads[0]:s.q_heads[1]] += 1
     assert (owner == 1).all()
+
+
+@settings(max_examples=300, deadline=None)
+@given(world=st.integers(1, 16), kv_heads=st.integers(1, 16), group=st.integers(1, 8),
+       batch=st.integers(1, 300))
+def test_shards_partition_any_valid_layout_in_balanced_slices(world, kv_heads, group, batch):
+    q_heads = kv_heads * group
+    if kv_heads % world and world % kv_heads:
+        with pytest.raises(ValueError):
+            kv_head_shard(0, world, q_heads=q_heads, kv_heads=kv_heads, batch=batch)
+        return
+    if kv_heads % world and batch < world // kv_heads:
+        with pytest.raises(ValueError, match='batch too small'):
+            kv_head_shard(0, world, q_heads=q_heads, kv_heads=kv_heads, batch=batch)
+        return
+    shards = [kv_head_shard(r, world, q_heads=q_heads, kv_heads=kv_heads, batch=batch)
+              for r in range(world)]
+    owner = torch.zeros(batch, q_heads, dtype=torch.int64)
+    for s in shards:
+        assert s.q_heads == (s.kv_heads[0] * group, s.kv_heads[1] * group)
+        owner[s.batch[0]:s.batch[1], s.q_heads[0]:s.q_heads[1]] += 1
+    assert (owner == 1).all()
+    # Balanced: per-rank work differs by at most one KV head or one sequence.
+    units = [s.num_kv_heads * s.num_seqs for s in shards]
+    assert max(s.num_kv_heads for s in shards) - min(s.num_kv_heads for s in shards) <= 1
+    assert max(s.num_seqs for s in shards) - min(s.num_seqs for s in shards) <= 1
+    assert sum(units) == kv_heads * batch
 
 
 def test_rejects_bad_ranks_and_head_counts():
