@@ -1,4 +1,4 @@
-"""KV-head sharding: layout math, and the full-head all-gather over 2 gloo ranks on CPU."""
+"""KV-head sharding: layout math, and the full-head all-gather over 2 and 4 gloo ranks on CPU."""
 import os
 
 import pytest
@@ -83,24 +83,25 @@ def _gather_worker(rank, world, port, q_heads, kv_heads, batch, timeout_s, resul
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize('q_heads, kv_heads, batch, timeout_s',
-                         [(28, 4, 6, None), (14, 1, 5, None), (28, 4, 6, 60)])
-def test_gather_full_heads_over_two_gloo_ranks(q_heads, kv_heads, batch, timeout_s):
+@pytest.mark.parametrize('world, q_heads, kv_heads, batch, timeout_s',
+                         [(2, 28, 4, 6, None), (2, 14, 1, 5, None), (2, 28, 4, 6, 60),
+                          (4, 12, 2, 7, None)])
+def test_gather_full_heads_over_gloo_ranks(world, q_heads, kv_heads, batch, timeout_s):
     import socket
     with socket.socket() as sock:
         sock.bind(('127.0.0.1', 0))
         port = sock.getsockname()[1]
     ctx = mp.get_context('spawn')
     queue = ctx.Queue()
-    procs = [ctx.Process(target=_gather_worker, args=(r, 2, port, q_heads, kv_heads, batch, timeout_s, queue))
-             for r in range(2)]
+    procs = [ctx.Process(target=_gather_worker, args=(r, world, port, q_heads, kv_heads, batch, timeout_s, queue))
+             for r in range(world)]
     for proc in procs:
         proc.start()
     results = dict(queue.get(timeout=120) for _ in procs)
     for proc in procs:
         proc.join(timeout=60)
         assert proc.exitcode == 0
-    assert results == {0: True, 1: True}
+    assert results == {r: True for r in range(world)}
 
 
 def _report(result_queue, item, code):
