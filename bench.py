@@ -100,6 +100,22 @@ def init_distributed(args):
     return rank, world, local_rank
 
 
+def per_rank_values(value, rank, world, device):
+    """Every rank's `value` (a float) in rank order, on every rank.
+
+    One all-reduce (a sum over slots that only their own rank fills); every
+    rank calls it at the same point, as with any collective.
+    """
+    import torch
+    import torch.distributed as dist
+
+    slots = torch.zeros(world, dtype=torch.float64, device=device)
+    slots[rank] = value
+    if world > 1:
+        dist.all_reduce(slots, op=dist.ReduceOp.SUM)
+    return slots.tolist()
+
+
 def peak_hbm():
     path = ROOT / 'MEASURED_PEAKS.json'
     try:
@@ -490,6 +506,7 @@ def run_ours(args):
     times = torch.tensor([elapsed_ms, attn_ms, e2e['ms'], other_ms, rope_ms, cuda_core_ms], dtype=torch.float64,
                          device=device)
     totals = torch.tensor([float(step_total), float(attn_bytes)], dtype=torch.float64, device=device)
+    rank_ms_per_step = per_rank_values(elapsed_ms / args.steps, rank, world, device)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
         dist.all_reduce(totals, op=dist.ReduceOp.SUM)
@@ -573,6 +590,9 @@ def run_ours(args):
             'clocks': clock_summary,
             'gpu_launches': launches_per_step * args.steps,
         }
+        if world > 1:
+            # ms_per_step is the slowest of these.
+            result['per_rank_ms_per_step'] = [round(t, 6) for t in rank_ms_per_step]
         if world == 1 and not args.no_cpu_baseline:
             result['cpu_baseline'] = cpu_baseline(spec, data, q_heads, kv_heads, args.cpu_seconds)
     del step_graph, kernel_graph, other_graph, rope_graph, cuda_core_graph
