@@ -47,6 +47,8 @@ for _path in (ROOT, ROOT / 'micro-vllm_b200'):
     if str(_path) not in sys.path:
         sys.path.insert(0, str(_path))
 
+from tests.golden.workloads import WORKLOADS, make_workload  # noqa: E402
+
 METRIC = 'paged decode attn achieved HBM GB/s (% of B200 peak); decode tokens/s'
 DEFAULT_WORKLOAD = 'qwen7b_bf16'
 FALLBACK_HBM_GBS = 6650.0
@@ -135,66 +137,6 @@ def local_geometry(spec, rank, world, scaling):
     return shard.num_q_heads, shard.num_kv_heads, shard.batch
 
 
-def draw_lengths(spec, generator):
-    import torch
-    batch = spec['batch']
-    kind = spec['lens'][0]
-    if kind == 'uniform':
-        _, lo, hi = spec['lens']
-        return torch.randint(lo, hi + 1, (batch,), generator=generator, dtype=torch.int64)
-    if kind == 'lognormal':
-        _, median, sigma, lo, hi = spec['lens']
-        raw = torch.empty(batch, dtype=torch.float64).log_normal_(math.log(median), sigma,
-                                                                   generator=generator)
-        return raw.round().clamp(lo, hi).to(torch.int64)
-    return torch.tensor(spec['lens'][1], dtype=torch.int64)
-
-
-def make_workload(spec, q_heads, kv_heads, batch_slice, seed, device):
-    """Seeded synthetic inputs of the workload's shapes, built on the device."""
-    import torch
-    dtype = {'bfloat16': torch.bfloat16, 'float16': torch.float16, 'float32': torch.float32}[spec['dtype']]
-    cpu = torch.Generator().manual_seed(seed)
-    lens = draw_lengths(spec, cpu)[batch_slice[0]:batch_slice[1]]
-    bs, dim = spec['block_size'], spec['head_dim']
-    pages = (lens + bs - 1) // bs
-    total = int(pages.sum())
-    kind, amount = spec['pool']
-    num_pages = max(total, int(amount) if kind == 'fixed_pages' else int(math.ceil(total * amount)))
-    perm = torch.randperm(num_pages, generator=cpu).to(torch.int32)
-    table = torch.full((len(lens), int(pages.max())), -1, dtype=torch.int32)
-    offset = 0
-    for b, n in enumerate(pages.tolist()):
-        table[b, :n] = perm[offset:offset + n]
-        offset += n
-    gen = torch.Generator(device=device).manual_seed(seed + 1)
-    scale = spec['value_scale']
-
-    def normal(shape):
-        out = torch.empty(shape, dtype=dtype, device=device)
-        chunk = 1 << 26
-        flat = out.view(-1)
-        for start in range(0, flat.numel(), chunk):
-            piece = torch.randn(min(chunk, flat.numel() - start), generator=gen, device=device)
-            flat[start:start + piece.numel()] = piece.mul_(scale)
-        return out
-
-    pool_shape = (num_pages, kv_heads, bs, dim)
-    k_pool = normal(pool_shape)
-    v_pool = normal(pool_shape)
-    if 'k_outlier' in spec:
-        frac, factor = spec['k_outlier']
-        mask = torch.rand((num_pages, kv_heads, bs), generator=gen, device=device) < frac
-        k_pool[mask] *= factor
-    return dict(
-        q=normal((len(lens), q_heads, dim)),
-        k_pool=k_pool, v_pool=v_pool,
-        k_new=normal((len(lens), kv_heads, 1, dim)),
-        v_new=normal((len(lens), kv_heads, 1, dim)),
-        block_table=table.to(device), context_lens=lens.to(torch.int32).to(device),
-        host_lens=lens.clone(), host_table=table.clone(), dtype=dtype)
-
-
 def step_bytes(spec, lens, q_heads, kv_heads):
     """Algorithmic bytes of one step (decode + append) for this rank's slice."""
     elem = 4 if spec['dtype'] == 'float32' else 2
@@ -276,73 +218,185 @@ class ClockSampler:
 
 # ------------------------------------------------------------ CPU baseline
 
-def prepare_cpu_sample(spec, data, sequences):
+REFERENCE_DIR = ROOT / 'baseline' / '_ref'
+CPU_SAMPLE_BYTES = 1 << 30      # fp32 K/V pages of a host sample, at most
+
+
+def reference_modules():
+    """micro-vllm's own ``PagedKVCache`` and ``causal_attention`` from baseline/_ref, or None."""
+    if not (REFERENCE_DIR / 'micro_vllm' / '__init__.py').is_file():
+        return None
+    if str(REFERENCE_DIR) not in sys.path:
+        sys.path.append(str(REFERENCE_DIR))
+    from micro_vllm.attention import causal_attention
+    from micro_vllm.paged_kv_cache import PagedKVCache
+    return PagedKVCache, causal_attention
+
+
+def host_threads():
+    """Use every host thread this process may run on; returns the count."""
+    import torch
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, 'sched_getaffinity') else os.cpu_count()
+    torch.set_num_threads(threads)
+    return torch.get_num_threads()
+
+
+def cpu_model():
+    try:
+        for line in Path('/proc/cpuinfo').read_text().splitlines():
+            if line.startswith('model name'):
+                return line.split(':', 1)[1].strip()
+    except OSError:
+        pass
+    return 'unknown'
+
+
+def sample_size(spec, lens, wanted):
+    """How many leading sequences fit ``CPU_SAMPLE_BYTES`` of fp32 K/V pages (at least 1)."""
+    bs, hkv, dim = spec['block_size'], spec['kv_heads'], spec['head_dim']
+    total, count = 0, 0
+    for length in lens[:wanted]:
+        total += 2 * (-(-int(length) // bs)) * hkv * bs * dim * 4
+        if count and total > CPU_SAMPLE_BYTES:
+            break
+        count += 1
+    return count
+
+
+def host_sample(spec, data, sequences):
     """Host copy of the first ``sequences`` sequences of the workload (their pages only).
 
-    bf16 inputs are widened to fp32: the reference's CPU path is timed in fp32.
+    One compact fp32 pool per K and V holds just those sequences' pages (bf16
+    widened: the reference's CPU path is timed in fp32), with the block table
+    remapped onto it; q and the new K/V rows in fp32. torch CPU tensors.
     """
-    import numpy as np
     import torch
 
     sample = min(sequences, data['q'].shape[0])
-    lens = data['host_lens'][:sample].numpy()
-    table = data['host_table'][:sample].numpy()
+    lens = [int(x) for x in data['host_lens'][:sample].tolist()]
+    table = data['host_table'][:sample]
     bs = spec['block_size']
-    used = sorted({int(p) for b in range(sample) for p in table[b, :-(-int(lens[b]) // bs)]})
+    used = sorted({int(p) for b in range(sample) for p in table[b, :-(-lens[b] // bs)].tolist()})
     remap = {p: i for i, p in enumerate(used)}
-    local_table = np.full_like(table, -1)
+    local_table = torch.full_like(table, -1)
     for b in range(sample):
-        for j in range(-(-int(lens[b]) // bs)):
+        for j in range(-(-lens[b] // bs)):
             local_table[b, j] = remap[int(table[b, j])]
     idx = torch.tensor(used, device=data['k_pool'].device)
     return dict(
         lens=lens, table=local_table, batch=data['q'].shape[0],
-        k_pool=data['k_pool'].index_select(0, idx).float().cpu().numpy(),
-        v_pool=data['v_pool'].index_select(0, idx).float().cpu().numpy(),
-        q=data['q'][:sample].float().cpu().numpy(),
-        k_new=data['k_new'][:sample].float().cpu().numpy(),
-        v_new=data['v_new'][:sample].float().cpu().numpy())
+        k_pool=data['k_pool'].index_select(0, idx).float().cpu(),
+        v_pool=data['v_pool'].index_select(0, idx).float().cpu(),
+        q=data['q'][:sample].float().cpu(),
+        k_new=data['k_new'][:sample].float().cpu(),
+        v_new=data['v_new'][:sample].float().cpu())
 
 
-def run_cpu_sample(spec, sample):
-    """One pass of the oracle (append, then gather + causal attention per sequence)."""
-    import numpy as np
+class ReferenceCPUStep:
+    """One decode step of micro-vllm's own CPU path over a host sample of the workload.
 
-    from oracle import append_tokens, decode_float
+    Every sequence gets the reference's ``PagedKVCache`` over the sample's one
+    shared pool per K and V (its dataclass constructor accepts external pools)
+    with its own table row, built once. A step is, per sequence, the per-layer
+    work of micro-vllm's model for a paged cache on the CPU (model.py:215-216,
+    180-182): ``PagedKVCache.append(0, k_new, v_new)`` (its ``_append_cpu``,
+    paged_kv_cache.py:151-176), ``gather(0)`` (:178-193), then
+    ``causal_attention(q, k, v, past_length=L-1)`` (attention.py:57-94). Each
+    step first rewinds every cache's length to L-1, so the step rewrites the
+    same slot with the same row, as a decode step at that position would.
+    """
 
-    append_tokens(sample['k_pool'], sample['v_pool'], sample['k_new'], sample['v_new'],
-                  sample['table'], sample['lens'] - 1)
-    decode_float(sample['q'], sample['k_pool'], sample['v_pool'], sample['table'], sample['lens'],
-                 spec['head_dim'] ** -0.5, 'float32', accum=np.float32)
+    kind = 'reference'
+
+    def __init__(self, spec, sample, modules):
+        import torch
+
+        PagedKVCache, self.causal_attention = modules
+        bs = spec['block_size']
+        self.sample = sample
+        self.caches = []
+        for b, length in enumerate(sample['lens']):
+            ids = tuple(int(p) for p in sample['table'][b, :-(-length // bs)].tolist())
+            self.caches.append(PagedKVCache((sample['k_pool'],), (sample['v_pool'],), [length - 1], ids,
+                                            torch.tensor(ids, dtype=torch.int64)))
+        hq, dim = sample['q'].shape[1:]
+        self.queries = [sample['q'][b].view(1, hq, 1, dim) for b in range(len(sample['lens']))]
+        self.keys = [sample['k_new'][b:b + 1] for b in range(len(sample['lens']))]
+        self.values = [sample['v_new'][b:b + 1] for b in range(len(sample['lens']))]
+
+    def __call__(self):
+        for cache, length, q, key, value in zip(self.caches, self.sample['lens'], self.queries, self.keys,
+                                                self.values):
+            cache._lengths[0] = length - 1
+            cache.append(0, key, value)
+            k, v = cache.gather(0)
+            self.causal_attention(q, k, v, past_length=length - 1)
+
+    def describe(self, runs, elapsed):
+        lens = self.sample['lens']
+        return (f'{len(lens)} of {self.sample["batch"]} sequences (lens {min(lens)}..{max(lens)}): micro-vllm\'s '
+                f'own PagedKVCache.append (_append_cpu) + gather + causal_attention per sequence, torch fp32 '
+                f'(bf16 inputs widened), {runs} steps in {elapsed:.1f} s')
 
 
-def blas_threads():
-    from threadpoolctl import threadpool_info
-    return int(max((info.get('num_threads', 1) for info in threadpool_info()), default=1))
+class PortCPUStep:
+    """Fallback when micro-vllm is not installed: the oracle's numpy restatement of the same path."""
+
+    kind = 'port'
+
+    def __init__(self, spec, sample):
+        self.spec = spec
+        self.sample = dict(sample)
+        for key in ('k_pool', 'v_pool', 'q', 'k_new', 'v_new', 'table'):
+            self.sample[key] = sample[key].numpy()
+        self.sample['lens'] = __import__('numpy').asarray(sample['lens'])
+
+    def __call__(self):
+        import numpy as np
+
+        from oracle import append_tokens, decode_float
+
+        s = self.sample
+        append_tokens(s['k_pool'], s['v_pool'], s['k_new'], s['v_new'], s['table'], s['lens'] - 1)
+        decode_float(s['q'], s['k_pool'], s['v_pool'], s['table'], s['lens'], self.spec['head_dim'] ** -0.5,
+                     'float32', accum=np.float32)
+
+    def describe(self, runs, elapsed):
+        lens = self.sample['lens'].tolist()
+        return (f'{len(lens)} of {self.sample["batch"]} sequences (lens {min(lens)}..{max(lens)}): the oracle\'s '
+                f'numpy fp32 restatement of micro-vllm\'s CPU path (micro-vllm not installed in baseline/_ref), '
+                f'{runs} steps in {elapsed:.1f} s')
 
 
-def describe_sample(sample, runs, elapsed):
-    return (f'{len(sample["lens"])} of {sample["batch"]} sequences (lens {sample["lens"].tolist()}): '
-            f'append + gather + causal attention per sequence, fp32 numpy oracle of the '
-            f'reference CPU path, {runs} runs in {elapsed:.1f} s; host has {os.cpu_count()} CPUs')
+def cpu_step(spec, data, sequences):
+    """The reference's CPU step over the first ``sequences`` sequences (port if not installed)."""
+    sample = host_sample(spec, data, sequences)
+    modules = reference_modules()
+    return ReferenceCPUStep(spec, sample, modules) if modules else PortCPUStep(spec, sample)
+
+
+def cpu_record(step, value, runs, elapsed, threads):
+    return {'value': value, 'unit': 'GB/s', 'cores': threads, 'kind': step.kind,
+            'sample': step.describe(runs, elapsed),
+            'host': f'{cpu_model()}, os.cpu_count() {os.cpu_count()}, torch threads {threads}'}
 
 
 def cpu_baseline(spec, data, q_heads, kv_heads, seconds):
-    """Time the oracle on a sample of this workload for ``seconds``; GB/s on the
-    same algorithmic-bytes basis as the GPU number."""
-    sample = prepare_cpu_sample(spec, data, 4)
-    step, _ = step_bytes(spec, sample['lens'], q_heads, kv_heads)
+    """Time the reference's CPU path on a sample of this workload for about ``seconds``;
+    GB/s on the same algorithmic-bytes basis as the GPU number."""
+    threads = host_threads()
+    step = cpu_step(spec, data, sample_size(spec, data['host_lens'].tolist(), data['q'].shape[0]))
+    nbytes, _ = step_bytes(spec, step.sample['lens'], q_heads, kv_heads)
+    step()                                  # first touch of the sample's pages
     runs = 0
     start = time.perf_counter()
     while True:
-        run_cpu_sample(spec, sample)
+        step()
         runs += 1
         elapsed = time.perf_counter() - start
         if elapsed >= seconds:
             break
-    return {'value': round(step * runs / elapsed / 1e9, 3), 'unit': 'GB/s',
-            'cores': blas_threads(), 'kind': 'port',
-            'sample': describe_sample(sample, runs, elapsed)}
+    return cpu_record(step, round(nbytes * runs / elapsed / 1e9, 3), runs, elapsed, threads)
 
 
 # ------------------------------------------------------------------- ours
@@ -352,7 +406,6 @@ def run_ours(args):
     import torch.distributed as dist
 
     from micro_vllm_b200 import cuda_attention, cuda_paged_cache
-    from tests.golden.cases import WORKLOADS
 
     rank, world, local_rank = init_distributed(args)
     device = torch.device('cuda', local_rank)
@@ -688,47 +741,43 @@ def run_e2e(args, data, max_len, pps, stream, device, barrier):
 # -------------------------------------------------------------- reference
 
 def run_reference(args):
-    """The reference CPU path (oracle restatement) on this host's cores.
+    """The reference's CPU path (micro-vllm's own code from baseline/_ref) on this host's cores.
 
-    Each step is one pass over a bounded sample of the workload (the first
-    sequences; fewer when K + W steps would take more than ~2 minutes), timed
+    Each step is one pass of ``ReferenceCPUStep`` over a bounded sample of the
+    workload: all sequences, or the leading ones when K + W steps would take
+    more than ~2 minutes (or their pages more than ``CPU_SAMPLE_BYTES``), timed
     with the wall clock; value is the median GB/s over the K timed steps.
     """
     rank = int(os.environ.get('RANK', '0'))
     if rank != 0:
         return None
-    import torch
-
-    from tests.golden.cases import WORKLOADS
 
     spec = WORKLOADS[args.workload]
-    torch.manual_seed(0)
-    # Only the sampled sequences are built; their lengths match the GPU run's first four.
-    data = make_workload(spec, spec['q_heads'], spec['kv_heads'], (0, 4), spec['seed'], 'cpu')
-    sample = prepare_cpu_sample(spec, data, 4)
-    sample['batch'] = spec['batch']
-    start = time.perf_counter()
-    run_cpu_sample(spec, sample)
-    one = time.perf_counter() - start
+    threads = host_threads()
+    data = make_workload(spec, spec['q_heads'], spec['kv_heads'], (0, spec['batch']), spec['seed'], 'cpu')
+    sequences = sample_size(spec, data['host_lens'].tolist(), spec['batch'])
     budget = 120.0
-    while len(sample['lens']) > 1 and one * (args.steps + args.warmup) > budget:
-        sample = prepare_cpu_sample(spec, data, len(sample['lens']) // 2)
-        sample['batch'] = spec['batch']
+    while True:
+        step = cpu_step(spec, data, sequences)
+        step()
         start = time.perf_counter()
-        run_cpu_sample(spec, sample)
+        step()
         one = time.perf_counter() - start
-    step, _ = step_bytes(spec, sample['lens'], spec['q_heads'], spec['kv_heads'])
+        if sequences == 1 or one * (args.steps + args.warmup) <= budget:
+            break
+        sequences = max(1, int(sequences * budget / (one * (args.steps + args.warmup)) * 0.9))
+    nbytes, _ = step_bytes(spec, step.sample['lens'], spec['q_heads'], spec['kv_heads'])
     values = []
     total_elapsed = 0.0
     for i in range(args.warmup + args.steps):
         start = time.perf_counter()
-        run_cpu_sample(spec, sample)
+        step()
         elapsed = time.perf_counter() - start
         if i >= args.warmup:
-            values.append(step / elapsed / 1e9)
+            values.append(nbytes / elapsed / 1e9)
             total_elapsed += elapsed
     value = round(statistics.median(values), 3)
-    description = describe_sample(sample, args.steps, total_elapsed)
+    record = cpu_record(step, value, args.steps, total_elapsed, threads)
     line = {
         'impl': 'reference',
         'metric': METRIC, 'value': value, 'unit': 'GB/s', 'n_gpus': args.gpus,
@@ -736,9 +785,8 @@ def run_reference(args):
         'ms_per_step': round(total_elapsed / args.steps * 1e3, 6),
         'higher_is_better': True, 'scaling': args.scaling, 'vs_baseline': None,
         'dtype': 'fp32 (bf16 inputs widened)', 'data': 'synthetic (seeded)',
-        'config': {'workload': args.workload, 'sample': description},
-        'cpu_baseline': {'value': value, 'unit': 'GB/s', 'cores': blas_threads(), 'kind': 'port',
-                         'sample': description},
+        'config': {'workload': args.workload, 'sample': record['sample']},
+        'cpu_baseline': record,
         'e2e': {'value': value, 'unit': 'GB/s', 'h2d_bytes_per_step': 0, 'd2h_bytes_per_step': 0},
     }
     gpu = reference_gpu_kernels(spec)

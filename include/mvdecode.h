@@ -336,17 +336,20 @@ MV_API int mv_silu_mul(const void* gate_up, int64_t stride_row, void* out, int64
  * counterpart in the reference (its kernel allocates its own output-sized
  * buffer). Some callers of a decode kernel may not call cudaMalloc: a plugin
  * whose host owns every device allocation (a serving engine that reserves all
- * memory up front and hands the plugin only inputs and outputs), or code that
- * runs while a stream is being captured into a CUDA graph, where allocation is
- * not allowed. This entry point takes the same arguments as mv_paged_decode
- * minus the workspace and allocates nothing: its split-KV scratch is a
- * file-scope device array of MV_NOALLOC_SCRATCH_BYTES that every GPU loading
- * the library holds until the process exits.
- *   - Calls whose split plan needs more scratch than that are rejected with
- *     MV_ERR_UNSUPPORTED and a message naming the sizes; MV_FLAG_FUSED_MERGE
- *     is rejected too (its counters would have to start at zero).
+ * memory up front and hands the plugin only inputs and outputs) has no
+ * workspace to give and no right to take one. This entry point takes the same
+ * arguments as mv_paged_decode minus the workspace and allocates nothing: its
+ * split-KV scratch is a file-scope device array of MV_NOALLOC_SCRATCH_BYTES
+ * that every GPU loading the library holds until the process exits.
+ *   - Calls whose split plan needs more scratch than that (planned as the
+ *     call itself would run, including the caches' alignment) are rejected
+ *     with MV_ERR_UNSUPPORTED and a message naming the sizes;
+ *     MV_FLAG_FUSED_MERGE is rejected too (its counters would have to start
+ *     at zero).
  *   - The first call on a device looks up the array's device address (with
- *     that device current); make that first call before any stream capture.
+ *     that device current) and keeps it; make that first call before any
+ *     stream capture, and do not call this entry point on a device after a
+ *     cudaDeviceReset of it (the kept address would be stale).
  *   - Every call shares the one array and leaves its partial results in it:
  *     calls that overlap on the GPU (other streams, other threads) race.
  */

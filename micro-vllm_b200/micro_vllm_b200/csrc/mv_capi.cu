@@ -1694,10 +1694,14 @@ int mv_paged_decode_noalloc(const void* q, int64_t q_stride_seq, int64_t q_strid
     if (flags & MV_FLAG_FUSED_MERGE)
         return fail(MV_ERR_UNSUPPORTED,
                     "mv_paged_decode_noalloc does not take MV_FLAG_FUSED_MERGE (its counters must start at zero)");
-    size_t needed = 0;
-    int rc = mv_paged_decode_workspace_size(batch, num_q_heads, num_kv_heads, head_dim, block_size,
-                                            max_context_len, pages_per_split, flags, dtype, &needed);
+    // The scratch the call's own plan needs: planned with the caches' real
+    // alignment, as mv_paged_decode plans it (unaligned caches take the
+    // CUDA-core kernel, whose split sizes differ).
+    const Geometry g{batch, num_q_heads, num_kv_heads, head_dim, block_size, max_context_len, dtype};
+    Plan plan;
+    int rc = make_plan(g, pages_per_split, flags, tma_aligned(k_cache, v_cache), &plan);
     if (rc != MV_OK) return rc;
+    const size_t needed = plan.workspace;
     if (needed > MV_NOALLOC_SCRATCH_BYTES)
         return fail(MV_ERR_UNSUPPORTED,
                     "mv_paged_decode_noalloc: this call needs %zu bytes of split-KV scratch, the "
@@ -1705,7 +1709,10 @@ int mv_paged_decode_noalloc(const void* q, int64_t q_stride_seq, int64_t q_strid
                     "pages_per_split",
                     needed, static_cast<size_t>(MV_NOALLOC_SCRATCH_BYTES));
     // Set-up, once per device, with that device current: the array's name is a
-    // host-side stand-in, so look up its device address.
+    // host-side stand-in, so look up its device address. The address is kept
+    // for the life of the process; a cudaDeviceReset of the device unloads the
+    // module and leaves it stale, so this entry point must not be called on a
+    // device after it was reset.
     static void* scratch[kMaxDevices] = {nullptr};
     static std::mutex scratch_mutex;
     int device = 0;

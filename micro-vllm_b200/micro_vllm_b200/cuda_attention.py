@@ -4,8 +4,8 @@ Reference-shaped API (same names, arguments, error types and messages):
 
 * ``decode_attention_paged(query, cache, *, layer_idx)`` --
   src/micro_vllm/cuda_attention.py:116-135 with ``_checked_paged_query``
-  (:86-113). Accepts the reference's ``PagedKVCache`` (or this package's
-  mirror of it) and reads its pages in place.
+  (:86-113). Accepts the reference's own ``PagedKVCache`` and reads its
+  pages in place.
 * ``_load_extension()._decode_attention_paged(query, key_pages, value_pages,
   table, length)`` -- the native entry point and its metadata checks
   (src/micro_vllm/csrc/decode_attention.cpp:17-124, 147-152).
@@ -242,14 +242,15 @@ def _load_extension() -> _DecodeAttentionExtension:
 
 
 def _is_paged_cache(cache) -> bool:
-    """The reference's PagedKVCache, this package's mirror, or the same shape of object."""
-    from .paged_kv_cache import PagedKVCache
+    """micro-vllm's ``PagedKVCache`` (src/micro_vllm/paged_kv_cache.py:43-199).
 
-    if isinstance(cache, PagedKVCache):
-        return True
-    return all(hasattr(cache, name) for name in
-               ('_keys', '_values', '_device_page_table', 'length', 'num_kv_heads', 'head_dim',
-                'dtype', 'device')) and type(cache).__name__ == 'PagedKVCache'
+    Checked by class name and the attributes read here, so this package needs
+    no import of micro-vllm: the reference's call site has already checked
+    ``isinstance(cache, PagedKVCache)`` before calling (model.py:175-177).
+    """
+    return type(cache).__name__ == 'PagedKVCache' and all(
+        hasattr(cache, name) for name in ('_keys', '_values', '_device_page_table', 'length',
+                                          'num_kv_heads', 'head_dim', 'dtype', 'device'))
 
 
 def _checked_paged_query(query, cache, layer_idx):

@@ -17,7 +17,7 @@ travel with the repository to the GPU machine, where the reference tree is
 absent). Test infrastructure: only GPU tests load these modules, to compare
 this library's kernels with the reference's own on the same inputs.
 
-Usage: python oracle/build_ref.py [reference_root]
+Usage: python oracle/build_ref.py REFERENCE_ROOT  (or set MICRO_VLLM_REFERENCE_ROOT)
 """
 import os
 import shutil
@@ -27,7 +27,6 @@ import sysconfig
 from pathlib import Path
 
 OUT_DIR = Path(__file__).resolve().parent / '_ref'
-DEFAULT_ROOT = Path('/root/reference')
 
 EXTENSIONS = {
     '_micro_vllm_decode_attention': ('decode_attention.cpp', 'decode_attention.cu',
@@ -50,7 +49,7 @@ def _run(cmd):
     subprocess.run(cmd, check=True)
 
 
-def build(reference_root=DEFAULT_ROOT, force=False):
+def build(reference_root, force=False):
     """Build both extensions into oracle/_ref; returns the module paths built.
 
     Skips (returns []) when the reference tree is absent, as on the GPU
@@ -114,6 +113,8 @@ def load(name):
 
 
 if __name__ == '__main__':
-    root = Path(sys.argv[1]) if len(sys.argv) > 1 else DEFAULT_ROOT
-    for path in build(root, force=True):
+    source = sys.argv[1] if len(sys.argv) > 1 else os.environ.get('MICRO_VLLM_REFERENCE_ROOT')
+    if not source:
+        raise SystemExit('usage: python oracle/build_ref.py REFERENCE_ROOT')
+    for path in build(Path(source), force=True):
         print(path)

@@ -1,18 +1,10 @@
-"""Seeded paged-decode workloads shared by the golden fixtures, tests and bench.
+"""Host-side (numpy) inputs of the paged-decode workloads, for the fixtures and tests.
 
-Every workload is one decode step of one attention layer over a shared,
-randomly permuted page pool: each sequence appends one new K/V token at
-logical position ``L_i - 1`` and then attends over ``L_i`` cached tokens.
-
-The named workloads follow the shapes, sizes and value distributions of the
-benchmark configurations this path is measured on (seeded synthetic data; no
-dataset is involved). The small ``edge_*`` and ``*_small`` cases keep the
-same head geometry at sizes the CPU oracle and the committed fixtures handle
-in milliseconds.
-
-Inputs are generated with numpy's PCG64 ``default_rng``; the fixtures store a
-SHA-256 of the generated arrays so that a change in the generator is caught
-instead of silently comparing different data.
+The workload specs live in ``tests/golden/workloads.py`` (re-exported here as
+``WORKLOADS``). ``make_inputs`` draws a workload's inputs with numpy's PCG64
+``default_rng``, for the committed golden fixtures and the CPU-sized parity
+tests; the fixtures store a SHA-256 of the generated arrays so that a change
+in the generator is caught instead of silently comparing different data.
 """
 import hashlib
 import math
@@ -20,53 +12,7 @@ import math
 import numpy as np
 
 from oracle.dtypes import from_float32
-
-# name -> spec. lens: ('uniform', lo, hi) | ('lognormal', median, sigma, lo, hi) | ('fixed', [..])
-WORKLOADS = {
-    # Qwen2.5-0.5B head geometry, fp32, 256-page pool.
-    'qwen05b_fp32': dict(batch=4, q_heads=14, kv_heads=2, head_dim=64, block_size=16,
-                         pool=('fixed_pages', 256), lens=('uniform', 1, 512),
-                         dtype='float32', value_scale=1.0, seed=1001),
-    'qwen05b_fp16': dict(batch=4, q_heads=14, kv_heads=2, head_dim=64, block_size=16,
-                         pool=('fixed_pages', 256), lens=('uniform', 1, 512),
-                         dtype='float16', value_scale=1.0, seed=1002),
-    'qwen05b_bf16': dict(batch=4, q_heads=14, kv_heads=2, head_dim=64, block_size=16,
-                         pool=('fixed_pages', 256), lens=('uniform', 1, 512),
-                         dtype='bfloat16', value_scale=1.0, seed=1003),
-    # Qwen2.5-7B geometry, bf16, pool 1.25x the pages in use.
-    'qwen7b_bf16': dict(batch=64, q_heads=28, kv_heads=4, head_dim=128, block_size=16,
-                        pool=('factor', 1.25), lens=('uniform', 1024, 4096),
-                        dtype='bfloat16', value_scale=0.5, seed=2001),
-    'qwen7b_bf16_small': dict(batch=3, q_heads=28, kv_heads=4, head_dim=128, block_size=16,
-                              pool=('factor', 1.25), lens=('fixed', [1, 17, 300]),
-                              dtype='bfloat16', value_scale=0.5, seed=2002),
-    # Qwen3-8B long context, bf16, 1% of K rows scaled x8.
-    'qwen3_8b_long_bf16': dict(batch=8, q_heads=32, kv_heads=8, head_dim=128, block_size=16,
-                               pool=('factor', 1.0), lens=('uniform', 32768, 131072),
-                               dtype='bfloat16', value_scale=1.0, k_outlier=(0.01, 8.0),
-                               seed=3001),
-    'qwen3_8b_bf16_small': dict(batch=2, q_heads=32, kv_heads=8, head_dim=128, block_size=16,
-                                pool=('factor', 1.0), lens=('fixed', [700, 1029]),
-                                dtype='bfloat16', value_scale=1.0, k_outlier=(0.01, 8.0),
-                                seed=3002),
-    # Qwen2.5-72B TP layer geometry, lognormal lengths.
-    'qwen72b_bf16': dict(batch=256, q_heads=64, kv_heads=8, head_dim=128, block_size=16,
-                         pool=('factor', 1.0), lens=('lognormal', 2048, 1.0, 16, 32768),
-                         dtype='bfloat16', value_scale=1.0, seed=5001),
-    'qwen72b_bf16_small': dict(batch=4, q_heads=64, kv_heads=8, head_dim=128, block_size=16,
-                               pool=('factor', 1.0), lens=('fixed', [16, 33, 250, 64]),
-                               dtype='bfloat16', value_scale=1.0, seed=5002),
-    # Odd geometry from the reference's CUDA tests: page size 3/4, D 33/257, G 3/14.
-    'edge_bs3_d33_fp32': dict(batch=3, q_heads=6, kv_heads=2, head_dim=33, block_size=3,
-                              pool=('factor', 1.5), lens=('fixed', [2, 3, 65]),
-                              dtype='float32', value_scale=1.0, seed=7001),
-    'edge_bs4_d257_fp16': dict(batch=2, q_heads=14, kv_heads=1, head_dim=257, block_size=4,
-                               pool=('factor', 1.5), lens=('fixed', [5, 33]),
-                               dtype='float16', value_scale=1.0, seed=7002),
-    'edge_bs64_d64_bf16': dict(batch=2, q_heads=4, kv_heads=4, head_dim=64, block_size=64,
-                               pool=('factor', 2.0), lens=('fixed', [63, 129]),
-                               dtype='bfloat16', value_scale=1.0, seed=7003),
-}
+from tests.golden.workloads import WORKLOADS  # re-exported
 
 
 def _draw_lengths(rng, spec):

@@ -2,7 +2,7 @@
 
 Run in a container where the reference checkout is present:
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py REFERENCE_ROOT
 
 For each workload in ``GOLDEN_CASES`` this builds, per sequence, a reference
 ``PagedKVCache`` over ONE shared page pool (its dataclass constructor accepts
@@ -96,4 +96,7 @@ def main(reference_root):
 
 
 if __name__ == '__main__':
-    main(sys.argv[1] if len(sys.argv) > 1 else '/root/reference')
+    source = sys.argv[1] if len(sys.argv) > 1 else os.environ.get('MICRO_VLLM_REFERENCE_ROOT')
+    if not source:
+        raise SystemExit('usage: python tests/golden/make_golden.py REFERENCE_ROOT')
+    main(source)

@@ -2,7 +2,7 @@
 
 Run in a container where the reference checkout is present:
 
-    python tests/golden/make_golden_generate.py /root/reference
+    python tests/golden/make_golden_generate.py REFERENCE_ROOT
 
 For each model case, every prompt is decoded on its own (the reference is
 batch 1) by the reference's greedy loop over a paged KV cache
@@ -69,4 +69,7 @@ def main(reference_root):
 
 
 if __name__ == '__main__':
-    main(sys.argv[1] if len(sys.argv) > 1 else '/root/reference')
+    source = sys.argv[1] if len(sys.argv) > 1 else os.environ.get('MICRO_VLLM_REFERENCE_ROOT')
+    if not source:
+        raise SystemExit('usage: python tests/golden/make_golden_generate.py REFERENCE_ROOT')
+    main(source)

@@ -2,7 +2,7 @@
 
 Run in a container where the reference checkout is present:
 
-    python tests/golden/make_golden_rope.py /root/reference
+    python tests/golden/make_golden_rope.py REFERENCE_ROOT
 
 For each (dtype, head_dim) case this calls the reference's ``rope_cos_sin``
 (src/micro_vllm/model.py:79-98) on a set of positions with theta 1e6 (Qwen2)
@@ -75,4 +75,7 @@ def main(reference_root):
 
 
 if __name__ == '__main__':
-    main(sys.argv[1] if len(sys.argv) > 1 else '/root/reference')
+    source = sys.argv[1] if len(sys.argv) > 1 else os.environ.get('MICRO_VLLM_REFERENCE_ROOT')
+    if not source:
+        raise SystemExit('usage: python tests/golden/make_golden_rope.py REFERENCE_ROOT')
+    main(source)

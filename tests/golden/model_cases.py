@@ -29,9 +29,22 @@ MODEL_CASES = {
 }
 
 
+# The accelerated tiny Qwen2 of micro-vllm's paged-forward GPU test
+# (test/test_accelerated_generation.py:17-28): 2 layers, 14 query / 2 KV heads of
+# 64, intermediate 128, vocabulary 128, tied embeddings. Weights here are seeded
+# numpy draws rather than the Hugging Face initialisation.
+CALL_SITE_CONFIG = dict(num_hidden_layers=2, hidden_size=896, intermediate_size=128, num_attention_heads=14,
+                        num_key_value_heads=2, vocab_size=128, max_position_embeddings=128,
+                        rope_theta=10000.0, rms_norm_eps=1e-6, tie_word_embeddings=True)
+
 def model_config(name):
     """The case's configuration as an attribute object (no transformers needed)."""
-    c = dict(MODEL_CASES[name]['config'])
+    return config_object(MODEL_CASES[name]['config'])
+
+
+def config_object(config):
+    """A Qwen2 configuration dict as the attribute object micro-vllm's forward reads."""
+    c = dict(config)
     return SimpleNamespace(model_type='qwen2', hidden_act='silu', rope_scaling=None, use_sliding_window=False,
                            layer_types=['full_attention'] * c['num_hidden_layers'], head_dim=None,
                            partial_rotary_factor=1.0, **c)
@@ -40,9 +53,13 @@ def model_config(name):
 def make_weights(name):
     """name -> fp32 numpy array, in the checkpoint naming micro-vllm reads."""
     case = MODEL_CASES[name]
-    c = case['config']
-    rng = np.random.default_rng(case['weight_seed'])
-    std = np.float32(case['weight_std'])
+    return weights_for(case['config'], case['weight_seed'], case['weight_std'])
+
+
+def weights_for(c, seed, std):
+    """Seeded N(0, std^2) weights (RMSNorm scales 1 + N(0, std^2)) of a Qwen2 config dict."""
+    rng = np.random.default_rng(seed)
+    std = np.float32(std)
     hidden, inter = c['hidden_size'], c['intermediate_size']
     dim = hidden // c['num_attention_heads']
     kv = c['num_key_value_heads'] * dim

@@ -3,9 +3,11 @@
 Restated from micro-vllm's test/test_cuda_paged_attention.py,
 test/test_cuda_paged_cache.py and test/test_paged_attention.py (the
 integration part): same inputs, tolerances and error-message patterns, with
-``micro_vllm_b200`` in place of ``micro_vllm``. Where the reference compares
-against its contiguous-cache kernel (not part of this path), the fp64
-per-head oracle is used instead.
+``micro_vllm_b200`` in place of ``micro_vllm``. The cache-level tests use the
+reference's own ``PagedKVCache`` (installed in baseline/_ref), whose CUDA
+append reaches this package through ``integration.install()``. Where the
+reference compares against its contiguous-cache kernel (not part of this
+path), the fp64 per-head oracle is used instead.
 """
 import subprocess
 import sys
@@ -15,11 +17,19 @@ from unittest.mock import patch
 import pytest
 import torch
 
-from micro_vllm_b200 import cuda_attention, cuda_paged_cache
-from micro_vllm_b200.paged_kv_cache import PagedKVCache
+from micro_vllm_b200 import cuda_attention, cuda_paged_cache, integration
+from tests.reference_pkg import REF_DIR, reference
 
 pytestmark = pytest.mark.gpu
 ROOT = Path(__file__).resolve().parents[1]
+PagedKVCache = reference('micro_vllm.paged_kv_cache').PagedKVCache
+
+
+@pytest.fixture(autouse=True)
+def reference_routed_here():
+    """micro-vllm's native names bound to this package for every test, then restored."""
+    with integration.installed():
+        yield
 
 
 def fp64_reference(query, key, value):
@@ -240,9 +250,12 @@ def test_only_this_librarys_kernels_run_in_a_clean_process():
     script = f'''
 import sys
 sys.path.insert(0, {str(ROOT / 'micro-vllm_b200')!r})
+sys.path.append({str(REF_DIR)!r})
 import torch
+from micro_vllm_b200 import integration
 from micro_vllm_b200.cuda_attention import decode_attention_paged
-from micro_vllm_b200.paged_kv_cache import PagedKVCache
+from micro_vllm.paged_kv_cache import PagedKVCache
+integration.install()
 cache = PagedKVCache.allocate(
     num_layers=1,num_kv_heads=2,num_pages=5,page_size=32,head_dim=64,
     dtype=torch.float16,device='cuda',page_table=[3,0,2])

@@ -3,7 +3,9 @@
 Restates the reference's CPU tests for the public paged decode entry point
 (test/test_paged_attention.py:14-89): foreign caches, bad layers, empty
 layers, malformed queries and non-CUDA caches are rejected with ValueError
-before the extension is loaded, and nothing is gathered.
+before the extension is loaded, and nothing is gathered. The caches are the
+reference's own ``PagedKVCache`` (installed in baseline/_ref), the object the
+drop-in receives from micro-vllm's model code.
 """
 from unittest.mock import patch
 
@@ -11,11 +13,12 @@ import pytest
 import torch
 
 from micro_vllm_b200 import cuda_attention, cuda_paged_cache
-from micro_vllm_b200.paged_kv_cache import PagedKVCache
+from tests.reference_pkg import reference
 
 
 def cpu_cache(dtype=torch.float32):
-    """A cache over CPU tensors built through the dataclass constructor."""
+    """The reference's cache over CPU tensors, built through its dataclass constructor."""
+    PagedKVCache = reference('micro_vllm.paged_kv_cache').PagedKVCache
     keys = tuple(torch.zeros(7, 2, 4, 8, dtype=dtype) for _ in range(2))
     values = tuple(torch.zeros(7, 2, 4, 8, dtype=dtype) for _ in range(2))
     return PagedKVCache(keys, values, [5, 0], (4, 1, 5), torch.tensor([4, 1, 5]))
@@ -87,18 +90,6 @@ def test_bfloat16_is_rejected_like_the_reference():
     with pytest.raises(ValueError, match='float16 or float32'):
         cuda_attention.decode_attention_paged(torch.zeros(1, 4, 1, 8, dtype=torch.bfloat16), cache,
                                               layer_idx=0)
-
-
-def test_allocate_requires_cuda_and_validates_tables():
-    with pytest.raises(ValueError, match='CUDA'):
-        PagedKVCache.allocate(num_layers=1, num_kv_heads=1, num_pages=2, page_size=4, head_dim=8,
-                              dtype=torch.float32, device='cpu')
-    with pytest.raises(ValueError, match='positive'):
-        PagedKVCache.allocate(num_layers=0, num_kv_heads=1, num_pages=2, page_size=4, head_dim=8,
-                              dtype=torch.float32, device='cuda')
-    with pytest.raises(ValueError, match='dtype'):
-        PagedKVCache.allocate(num_layers=1, num_kv_heads=1, num_pages=2, page_size=4, head_dim=8,
-                              dtype=torch.float64, device='cuda')
 
 
 def test_native_write_checks_name_cuda_first():
