@@ -412,8 +412,10 @@ def run_ours(args):
     torch.cuda.set_device(device)
     spec = WORKLOADS[args.workload]
     q_heads, kv_heads, batch_slice = local_geometry(spec, rank, world, args.scaling)
-    seed = spec['seed'] + (rank * 7919 if args.scaling == 'weak' else 0)
-    data = make_workload(spec, q_heads, kv_heads, batch_slice, seed, device)
+    # Every rank draws the same lengths and page tables (the same shape of work);
+    # weak-scaled ranks fill them with their own values.
+    value_seed = spec['seed'] + 1 + (rank * 7919 if args.scaling == 'weak' else 0)
+    data = make_workload(spec, q_heads, kv_heads, batch_slice, spec['seed'], device, value_seed=value_seed)
     lens_host = data['host_lens'].tolist()
     max_len = max(lens_host)
     step_total, attn_bytes = step_bytes(spec, lens_host, q_heads, kv_heads)
@@ -555,6 +557,12 @@ def run_ours(args):
         # End to end through the public API: pinned host inputs in, output back out.
         e2e = run_e2e(args, data, max_len, pps, stream, device, barrier)
     clock_summary = clocks.summary()
+    del step_graph, kernel_graph, other_graph, rope_graph, cuda_core_graph
+    rank_us_per_launch = per_rank_values(attn_ms * 1e3, rank, world, device)
+    rank_separate_us = per_rank_values(other_ms / args.steps * 1e3, rank, world, device)
+    strong = None
+    if args.workload == DEFAULT_WORKLOAD and not args.pages_per_split:
+        strong = strong_scaling(rank, world, device, barrier)
 
     times = torch.tensor([elapsed_ms, attn_ms, e2e['ms'], other_ms, rope_ms, cuda_core_ms], dtype=torch.float64,
                          device=device)
@@ -644,15 +652,112 @@ def run_ours(args):
             'gpu_launches': launches_per_step * args.steps,
         }
         if world > 1:
-            # ms_per_step is the slowest of these.
+            # ms_per_step is the slowest of these; the kernels' own times per rank beside them.
             result['per_rank_ms_per_step'] = [round(t, 6) for t in rank_ms_per_step]
+            result['per_rank_us_per_launch'] = [round(t, 3) for t in rank_us_per_launch]
+            result['per_rank_separate_step_us'] = [round(t, 3) for t in rank_separate_us]
+        if strong is not None:
+            result['strong_scaling'] = strong
         if world == 1 and not args.no_cpu_baseline:
             result['cpu_baseline'] = cpu_baseline(spec, data, q_heads, kv_heads, args.cpu_seconds)
-    del step_graph, kernel_graph, other_graph, rope_graph, cuda_core_graph
     if world > 1:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
     return result
+
+
+STRONG_WORKLOADS = ('qwen3_8b_long_bf16', 'qwen72b_bf16')
+STRONG_REPLAYS = 40
+
+
+def time_one_call_step(data, stream, device, replays):
+    """Device time (ms) of one replay of a CUDA graph holding the one-call step on ``data``."""
+    import torch
+
+    from micro_vllm_b200 import cuda_attention
+
+    max_len = int(data['host_lens'].max())
+    out = torch.empty_like(data['q'])
+
+    def step():
+        cuda_attention.paged_decode_with_append(data['q'], data['k_new'][:, :, 0], data['v_new'][:, :, 0],
+                                                data['k_pool'], data['v_pool'], data['block_table'],
+                                                data['context_lens'], max_context_len=max_len, out=out)
+
+    stream.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            step()
+    torch.cuda.synchronize(device)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            graph.replay()
+    torch.cuda.synchronize(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        start.record(stream)
+        for _ in range(replays):
+            graph.replay()
+        end.record(stream)
+    torch.cuda.synchronize(device)
+    del graph
+    return start.elapsed_time(end) / replays
+
+
+def strong_scaling(rank, world, device, barrier):
+    """The long-context (Qwen3-8B geometry) and batch-256 (Qwen2.5-72B geometry)
+    layers split over the ranks by KV head -- one KV head per GPU at 8 -- each rank
+    timing the one-call step on its shard (CUDA-graph replays, max over ranks),
+    plus the whole layer on rank 0's GPU alone in the same run for comparison.
+    Every rank takes the same collective steps in the same order."""
+    import torch
+
+    from micro_vllm_b200 import cuda_attention
+
+    stream = torch.cuda.Stream(device)
+    records = {}
+    for name in STRONG_WORKLOADS:
+        spec = WORKLOADS[name]
+        q_heads, kv_heads, batch_slice = local_geometry(spec, rank, world, 'strong')
+        data = make_workload(spec, q_heads, kv_heads, batch_slice, spec['seed'], device)
+        lens = data['host_lens'].tolist()
+        plan = cuda_attention.paged_decode_plan(q_heads, data['k_pool'], max(lens), batch=len(lens))
+        nbytes, _ = step_bytes(spec, lens, q_heads, kv_heads)
+        barrier()
+        ms = time_one_call_step(data, stream, device, STRONG_REPLAYS)
+        barrier()
+        del data
+        per_rank_us = per_rank_values(ms * 1e3, rank, world, device)
+        per_rank_bytes = per_rank_values(float(nbytes), rank, world, device)
+        one_gpu_us = per_rank_us[0]
+        if world > 1:
+            if rank == 0:
+                whole = make_workload(spec, spec['q_heads'], spec['kv_heads'], (0, spec['batch']), spec['seed'],
+                                      device)
+                one_gpu_us = time_one_call_step(whole, stream, device, STRONG_REPLAYS) * 1e3
+                del whole
+            barrier()
+        torch.cuda.empty_cache()
+        slowest = max(per_rank_us)
+        total = sum(per_rank_bytes)
+        records[name] = {
+            'workload': (f'{name}: batch {spec["batch"]}, {spec["q_heads"]} q / {spec["kv_heads"]} kv heads, '
+                         f'head_dim {spec["head_dim"]}, lens {spec["lens"]}'),
+            'per_rank': {'batch': len(lens), 'q_heads': q_heads, 'kv_heads': kv_heads, 'plan': list(plan)},
+            'us_per_layer': round(slowest, 3),
+            'per_rank_us': [round(t, 3) for t in per_rank_us],
+            'aggregate_gbs': round(total / (slowest * 1e3), 1),
+            'per_gpu_gbs': round(total / (slowest * 1e3) / world, 1),
+            'us_per_layer_one_gpu': round(one_gpu_us, 3),
+            'speedup_vs_one_gpu': round(one_gpu_us / slowest, 3),
+            'strong_efficiency': round(one_gpu_us / (slowest * world), 3),
+            'timing': (f'one-call step (append + decode), CUDA events around {STRONG_REPLAYS} graph replays per '
+                       'rank, max over ranks; one-GPU time: the whole layer on rank 0 in the same run'),
+        }
+    return records
 
 
 def run_e2e(args, data, max_len, pps, stream, device, barrier):

@@ -82,11 +82,14 @@ def draw_lengths(spec, generator):
     return torch.tensor(spec['lens'][1], dtype=torch.int64)
 
 
-def make_workload(spec, q_heads, kv_heads, batch_slice, seed, device):
+def make_workload(spec, q_heads, kv_heads, batch_slice, seed, device, value_seed=None):
     """Seeded synthetic inputs of the workload's shapes, built on ``device``.
 
     ``q_heads``/``kv_heads``/``batch_slice`` select a KV-head shard (the whole
-    layer on one GPU: the spec's head counts and ``(0, batch)``). Returns q
+    layer on one GPU: the spec's head counts and ``(0, batch)``). ``seed``
+    draws the lengths and the page tables; ``value_seed`` (default ``seed +
+    1``) draws q, K and V, so ranks can share one shape of work with their own
+    values. Returns q
     [B, Hq, D], k_pool/v_pool [P, Hkv, bs, D] (before the append), k_new/v_new
     [B, Hkv, 1, D], block_table int32 [B, max_pages] (unused entries -1) and
     context_lens int32 [B] (after the append) on the device, plus host copies
@@ -107,7 +110,7 @@ def make_workload(spec, q_heads, kv_heads, batch_slice, seed, device):
     for b, n in enumerate(pages.tolist()):
         table[b, :n] = perm[offset:offset + n]
         offset += n
-    gen = torch.Generator(device=device).manual_seed(seed + 1)
+    gen = torch.Generator(device=device).manual_seed(seed + 1 if value_seed is None else value_seed)
     scale = spec['value_scale']
 
     def normal(shape):
