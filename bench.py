@@ -56,7 +56,17 @@ FALLBACK_HBM_GBS = 6650.0
 # one ncu capture: paged_decode_mma_kernel with the append fused (329.73 MB + 5.03 MB,
 # profiles/paged_decode_mma_qwen7b_bf16.md) + paged_decode_merge_warp_kernel (1.53 MB read with
 # ncu's cold caches, profiles/paged_decode_merge_warp_qwen7b_bf16.md).
-NCU_TRAFFIC_BYTES = {'qwen7b_bf16': 329_734_144 + 5_028_096 + 1_525_760}
+NCU_TRAFFIC_BYTES = {('qwen7b_bf16', 'tma_mma'): 329_734_144 + 5_028_096 + 1_525_760}
+# Kernels of one one-call step by plan path (the roofline's dominant kernel and the merge pass).
+STEP_KERNELS = {
+    'tma_mma': 'paged_decode_mma_kernel (append fused) + paged_decode_merge_warp_kernel',
+    'tma_mma_stream': 'paged_decode_stream_kernel (append fused) + paged_decode_merge_warp_kernel',
+}
+TRAFFIC_SOURCES = {
+    'tma_mma': ('ncu dram__bytes_read.sum + dram__bytes_write.sum of one step: paged_decode_mma_kernel (append '
+                'fused) + paged_decode_merge_warp_kernel (profiles/paged_decode_mma_qwen7b_bf16.md, '
+                'profiles/paged_decode_merge_warp_qwen7b_bf16.md)'),
+}
 L2_BYTES = 126 * 1024 * 1024
 KERNEL_CALLS = 8
 
@@ -457,10 +467,27 @@ def run_ours(args):
                                                 data['context_lens'], max_context_len=max_len, out=out,
                                                 pages_per_split=pps, cuda_core_math=True)
 
+    # The same one-call step on the per-warp stream schedule (one CTA per SM,
+    # every warp streaming work items from a queue): the comparison behind
+    # keeping the split grid as the default.
+    def stream_step():
+        cuda_attention.paged_decode_with_append(data['q'], data['k_new'][:, :, 0], data['v_new'][:, :, 0],
+                                                data['k_pool'], data['v_pool'], data['block_table'],
+                                                data['context_lens'], max_context_len=max_len, out=out,
+                                                pages_per_split=pps, schedule='stream')
+
+    try:
+        cuda_attention.paged_decode_plan(q_heads, data['k_pool'], max_len, batch=len(lens_host),
+                                         pages_per_split=pps, schedule='stream')
+        stream_ok = True
+    except RuntimeError:
+        stream_ok = False
+
     path, chosen_pps, splits = cuda_attention.paged_decode_plan(
         q_heads, data['k_pool'], max_len, batch=len(lens_host), pages_per_split=pps)
     # The fused step is one decode launch (+ merge); the separate one adds the append kernel.
-    launches_per_step = (1 if args.step == 'fused' and path == 'tma_mma' else 2) + (1 if splits > 1 else 0)
+    launches_per_step = (1 if args.step == 'fused' and path in ('tma_mma', 'tma_mma_stream') else 2) + \
+        (1 if splits > 1 else 0)
 
     stream = torch.cuda.Stream(device)
     stream.wait_stream(torch.cuda.current_stream(device))
@@ -470,6 +497,8 @@ def run_ours(args):
             other_step()
             rope_step()
             cuda_core_step()
+            if stream_ok:
+                stream_step()
     torch.cuda.synchronize(device)
     step_graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(step_graph, stream=stream):
@@ -483,6 +512,10 @@ def run_ours(args):
     cuda_core_graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(cuda_core_graph, stream=stream):
         cuda_core_step()
+    stream_graph = torch.cuda.CUDAGraph() if stream_ok else None
+    if stream_ok:
+        with torch.cuda.graph(stream_graph, stream=stream):
+            stream_step()
     # The step's kernels back to back, KERNEL_CALLS per graph, so their average
     # launch duration excludes the per-replay graph launch gap (roofline).
     kernel_graph = torch.cuda.CUDAGraph()
@@ -553,25 +586,26 @@ def run_ours(args):
         other_ms = time_form(other_graph)
         rope_ms = time_form(rope_graph)
         cuda_core_ms = time_form(cuda_core_graph)
+        stream_ms = time_form(stream_graph) if stream_ok else 0.0
 
         # End to end through the public API: pinned host inputs in, output back out.
         e2e = run_e2e(args, data, max_len, pps, stream, device, barrier)
     clock_summary = clocks.summary()
-    del step_graph, kernel_graph, other_graph, rope_graph, cuda_core_graph
+    del step_graph, kernel_graph, other_graph, rope_graph, cuda_core_graph, stream_graph
     rank_us_per_launch = per_rank_values(attn_ms * 1e3, rank, world, device)
     rank_separate_us = per_rank_values(other_ms / args.steps * 1e3, rank, world, device)
     strong = None
     if args.workload == DEFAULT_WORKLOAD and not args.pages_per_split:
         strong = strong_scaling(rank, world, device, barrier)
 
-    times = torch.tensor([elapsed_ms, attn_ms, e2e['ms'], other_ms, rope_ms, cuda_core_ms], dtype=torch.float64,
-                         device=device)
+    times = torch.tensor([elapsed_ms, attn_ms, e2e['ms'], other_ms, rope_ms, cuda_core_ms, stream_ms],
+                         dtype=torch.float64, device=device)
     totals = torch.tensor([float(step_total), float(attn_bytes)], dtype=torch.float64, device=device)
     rank_ms_per_step = per_rank_values(elapsed_ms / args.steps, rank, world, device)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
         dist.all_reduce(totals, op=dist.ReduceOp.SUM)
-    elapsed_ms, attn_ms, e2e_ms, other_ms, rope_ms, cuda_core_ms = times.tolist()
+    elapsed_ms, attn_ms, e2e_ms, other_ms, rope_ms, cuda_core_ms, stream_ms = times.tolist()
     job_step_bytes, job_attn_bytes = totals.tolist()
     ms_per_step = elapsed_ms / args.steps
     value = job_step_bytes * args.steps / (elapsed_ms / 1e3) / 1e9
@@ -582,7 +616,7 @@ def run_ours(args):
         peak, peak_kind = peak_hbm()
         achieved = step_total / (attn_ms / 1e3) / 1e9
         # The capture is of the default step form on one GPU's config-sized slice.
-        traffic = (NCU_TRAFFIC_BYTES.get(args.workload)
+        traffic = (NCU_TRAFFIC_BYTES.get((args.workload, path))
                    if args.step == 'fused' and not args.pages_per_split
                    and (world == 1 or args.scaling == 'weak') else None)
         batch = len(lens_host)
@@ -617,9 +651,8 @@ def run_ours(args):
             'pct_of_hbm_peak': round(100 * value / world / peak, 2),
             'roofline': {
                 'bound': 'hbm',
-                'kernel': ('paged_decode_mma_kernel (append fused) + paged_decode_merge_warp_kernel'
-                           if args.step == 'fused' else
-                           'write_paged_kv_kernel + paged_decode_mma_kernel + paged_decode_merge_warp_kernel'),
+                'kernel': (STEP_KERNELS.get(path, path) if args.step == 'fused' else
+                           'write_paged_kv_kernel + ' + STEP_KERNELS.get(path, path).replace(' (append fused)', '')),
                 'timing': (f'CUDA events around graphs of {KERNEL_CALLS} back-to-back steps: '
                            'average launch duration without the per-replay graph launch gap'),
                 'achieved': round(achieved, 1),
@@ -631,11 +664,7 @@ def run_ours(args):
                 'us_per_launch': round(attn_ms * 1e3, 3),
                 'algorithmic_bytes_per_launch': step_total,
                 'traffic': traffic,
-                'traffic_source': ('ncu dram__bytes_read.sum + dram__bytes_write.sum of one step: '
-                                   'paged_decode_mma_kernel (append fused) + paged_decode_merge_warp_kernel '
-                                   '(profiles/paged_decode_mma_qwen7b_bf16.md, '
-                                   'profiles/paged_decode_merge_warp_qwen7b_bf16.md)'
-                                   if traffic and args.step == 'fused' else None),
+                'traffic_source': TRAFFIC_SOURCES.get(path) if traffic else None,
             },
             'e2e': {'value': round(e2e_value, 1), 'unit': 'GB/s',
                     'h2d_bytes_per_step': e2e['h2d'], 'd2h_bytes_per_step': e2e['d2h'],
@@ -647,7 +676,8 @@ def run_ours(args):
                               ('separate' if args.step == 'fused' else 'fused'):
                                   round(other_ms / args.steps * 1e3, 3),
                               'fused_with_rope': round(rope_ms / args.steps * 1e3, 3),
-                              'fused_cuda_core_math': round(cuda_core_ms / args.steps * 1e3, 3)},
+                              'fused_cuda_core_math': round(cuda_core_ms / args.steps * 1e3, 3),
+                              'fused_stream_schedule': round(stream_ms / args.steps * 1e3, 3) if stream_ok else None},
             'clocks': clock_summary,
             'gpu_launches': launches_per_step * args.steps,
         }

@@ -55,6 +55,10 @@ extern "C" {
 #define MV_FLAG_CHUNK_MMA_SYNC 64u /* mv_paged_chunk_attention: 64-row mma.sync tiles, not tcgen05 tiles */
 #define MV_FLAG_CUDA_CORE_MATH 128u /* split grid (default shape, GQA group <= 8, head_dim 64/128): the same TMA
                                       pipeline with fp32 FMA math instead of the tensor-core tile (for comparison) */
+#define MV_FLAG_STREAM 256u /* tensor-core kernel on the per-warp stream schedule wherever its shape allows
+                              (bf16/fp16, page 16, head_dim 64/128, GQA group <= 8, at most 1024 sequences,
+                              pages_per_split <= 64 or 0 for automatic); MV_ERR_UNSUPPORTED elsewhere */
+#define MV_FLAG_SPLIT_GRID 512u /* never pick the stream schedule automatically (keep the split grid) */
 
 /* Status codes. */
 #define MV_OK 0
@@ -72,6 +76,8 @@ extern "C" {
 #define MV_PATH_TMA_MMA 1         /* TMA + tensor cores, one CTA per (split, KV head, sequence) */
 #define MV_PATH_TMA_MMA_PERSISTENT 2 /* TMA + tensor cores, persistent, equal page ranges per warp */
 #define MV_PATH_TMA_MMA_CLUSTER 3 /* TMA + tensor cores, one CTA cluster per (sequence, KV head) */
+#define MV_PATH_TMA_MMA_STREAM 4  /* TMA + tensor cores, one CTA per SM, every warp an independent page stream over
+                                     a queue of (sequence, KV head, run of pages) items; the split merge after */
 
 MV_API int mv_abi_version(void);
 
@@ -346,10 +352,10 @@ MV_API int mv_silu_mul(const void* gate_up, int64_t stride_row, void* out, int64
  *     with MV_ERR_UNSUPPORTED and a message naming the sizes;
  *     MV_FLAG_FUSED_MERGE is rejected too (its counters would have to start
  *     at zero).
- *   - The first call on a device looks up the array's device address (with
- *     that device current) and keeps it; make that first call before any
- *     stream capture, and do not call this entry point on a device after a
- *     cudaDeviceReset of it (the kept address would be stale).
+ *   - A call outside stream capture looks up the array's device address
+ *     (with the call's device current) and keeps it; a call inside a capture
+ *     uses the kept one. So the first call on a device, and the first after
+ *     a cudaDeviceReset of it, must come before any stream capture.
  *   - Every call shares the one array and leaves its partial results in it:
  *     calls that overlap on the GPU (other streams, other threads) race.
  */

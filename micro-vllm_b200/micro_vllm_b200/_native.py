@@ -25,8 +25,10 @@ FLAG_WIDE = 16
 FLAG_CHUNK_ROWS = 32
 FLAG_CHUNK_MMA_SYNC = 64
 FLAG_CUDA_CORE_MATH = 128
-PATH_SIMT, PATH_TMA_MMA, PATH_TMA_MMA_PERSISTENT, PATH_TMA_MMA_CLUSTER = 0, 1, 2, 3
-PATH_NAMES = {0: 'simt', 1: 'tma_mma', 2: 'tma_mma_persistent', 3: 'tma_mma_cluster'}
+FLAG_STREAM = 256
+FLAG_SPLIT_GRID = 512
+PATH_SIMT, PATH_TMA_MMA, PATH_TMA_MMA_PERSISTENT, PATH_TMA_MMA_CLUSTER, PATH_TMA_MMA_STREAM = 0, 1, 2, 3, 4
+PATH_NAMES = {0: 'simt', 1: 'tma_mma', 2: 'tma_mma_persistent', 3: 'tma_mma_cluster', 4: 'tma_mma_stream'}
 DEVICE_STATUS_WAIT_TIMEOUT = 1
 DEVICE_STATUS_BAD_PAGE_ID = 2
 

@@ -20,6 +20,7 @@
 #include "paged_decode_merge.cuh"
 #include "paged_decode_mma.cuh"
 #include "paged_decode_simt.cuh"
+#include "paged_decode_stream.cuh"
 #include "rope.cuh"
 #include "row_ops.cuh"
 
@@ -141,6 +142,12 @@ int ensure_smem_carveout(Kernel kernel, size_t bytes) {
 
 // ---------------------------------------------------------------- planning
 
+// Split grid's graded schedule: splits after the second hold pages_per_split /
+// MV_LATER_SPLIT_DIV pages (1: all splits after the first alike).
+#ifndef MV_LATER_SPLIT_DIV
+#define MV_LATER_SPLIT_DIV 1
+#endif
+
 // Tensor-core kernel shape: warps per CTA and TMA stages per warp by head_dim
 // (overridable at build time for tuning sweeps).
 #ifndef MV_MMA_WARPS
@@ -194,6 +201,7 @@ struct Plan {
     int pages_per_split;
     int max_splits;
     int first_pages; // split grid: pages of split 0 when longer than pages_per_split (split-major order), else 0
+    int later_pages = 0; // split grid with first_pages: pages of splits 2.. (0: pages_per_split)
     int cluster;     // cluster kernel: CTAs per (sequence, KV head)
     int nt;          // mma n-tiles (8 query heads each)
     int ctas;        // persistent grid size
@@ -208,6 +216,10 @@ struct Plan {
     bool cuda_core;  // split grid with CUDA-core math (MV_FLAG_CUDA_CORE_MATH)
 };
 
+// Where a plan may take the per-warp stream schedule: paged decode with one
+// query row per sequence (not chunks, not contiguous caches).
+enum class StreamUse { kNo, kAllowed };
+
 bool mma_shape_ok(const Geometry& g) {
     const int group = g.q_heads / g.kv_heads;
     return (g.dtype == MV_DTYPE_BF16 || g.dtype == MV_DTYPE_F16) && g.block_size == 16 &&
@@ -221,6 +233,7 @@ size_t round256(size_t bytes) { return (bytes + 255) / 256 * 256; }
 // workspace is zero-filled its counters stay zero between completed calls.
 constexpr size_t kCounterRegion = 256 * 1024;
 constexpr int64_t kMaxCounters = kCounterRegion / sizeof(unsigned);
+static_assert(kMaxCounters == mv::kCounterRegionSlots, "device and host agree on the counter region");
 
 // Persistent kernel: stages per warp for each head_dim (~96 KiB of stages per CTA
 // so two CTAs share an SM; one at head_dim 256), and the batch its prefix array fits.
@@ -280,8 +293,55 @@ size_t grid_stage_bytes(int dim, bool wide) {
     return static_cast<size_t>(wide ? kWideWarps : kMmaWarps) * stages * 2 * (16 * static_cast<size_t>(dim) * 2);
 }
 
+// The per-warp stream schedule (paged_decode_stream_kernel), on request
+// (MV_FLAG_STREAM): items of 8..64 pages, about four per warp. Measured on
+// B200 it loses to the split grid (Qwen2.5-7B geometry, batch 64: 68.7 us per
+// step with 32-page items, 77.6 us with 8-page ones, against 61.5 us; Qwen2.5-72B
+// geometry, batch 256: 620-635 against 598 us): a warp streams only its own
+// two stages, so items must be small for the queue to balance, and every item
+// switch costs the warp ~2 us (claim, page IDs, q) that its ring cannot hide.
+bool stream_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, const DeviceInfo& dev, Plan* plan) {
+    if (!(flags & MV_FLAG_STREAM)) return false;
+    const int64_t max_pages = (g.max_context_len + g.block_size - 1) / g.block_size;
+    const bool shape = plan->path == MV_PATH_TMA_MMA && !plan->wide && !plan->cuda_core && plan->nt == 1 &&
+                       (g.head_dim == 64 || g.head_dim == 128) && g.batch <= mv::kStreamMaxBatch &&
+                       g.max_context_len < (int64_t(1) << 30) &&
+                       !(flags & (MV_FLAG_FUSED_MERGE | MV_FLAG_CLUSTER | MV_FLAG_PERSISTENT | MV_FLAG_WIDE |
+                                  MV_FLAG_CUDA_CORE_MATH | MV_FLAG_SPLIT_GRID));
+    if (!shape) return false;
+    const int64_t warps = static_cast<int64_t>(dev.sms) * mv::kStreamWarps;
+    const int64_t est_pages = static_cast<int64_t>(g.batch) * g.kv_heads * std::max<int64_t>(max_pages, 1) / 2;
+    int64_t items = pages_per_split;
+    if (items == 0) {
+        // About four items per warp, and at most 32 per segment (one round of
+        // loads in the warp merge; partials bounded by 32 rows per query row).
+        const int64_t want = est_pages / (4 * warps);
+        items = 8;
+        while ((items * 2 <= want || items * 32 < max_pages) && items < mv::kStreamMaxItemPages) items *= 2;
+    }
+    if (items < 1 || items > mv::kStreamMaxItemPages) return false;
+    const int64_t splits = std::max<int64_t>(1, (max_pages + items - 1) / items);
+    if (splits > 8192) return false;
+    plan->path = MV_PATH_TMA_MMA_STREAM;
+    plan->pages_per_split = static_cast<int>(items);
+    plan->first_pages = 0;
+    plan->max_splits = static_cast<int>(splits);
+    plan->ctas = dev.sms;
+    plan->warps = dev.sms * mv::kStreamWarps;
+    plan->fused_merge = false;
+    plan->counter_bytes = kCounterRegion;  // the item queue's counters
+    plan->part_o_bytes = plan->part_lse_bytes = 0;
+    if (splits > 1) {
+        const size_t rows = static_cast<size_t>(g.batch) * g.q_heads * splits;
+        plan->part_o_bytes = round256(rows * g.head_dim * sizeof(float));
+        plan->part_lse_bytes = round256(rows * sizeof(float));
+    }
+    plan->workspace = plan->counter_bytes + plan->part_o_bytes + plan->part_lse_bytes;
+    return true;
+}
+
 int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool aligned_for_tma,
-              Plan* plan) {
+              Plan* plan, StreamUse stream_use = StreamUse::kNo) {
     int rc = check_geometry(g);
     if (rc != MV_OK) return rc;
     DeviceInfo dev;
@@ -304,6 +364,7 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
     plan->wide = false;
     plan->chunk_umma = false;
     plan->first_pages = 0;
+    plan->later_pages = 0;
     plan->cuda_core = false;
     const int64_t max_pages = (g.max_context_len + g.block_size - 1) / g.block_size;
 
@@ -347,7 +408,7 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
     // 12.7 us; 4 x 8 of 1024: 51 vs 56 us) and loses with many segments (the
     // default grid packs three CTAs per SM) or very few (more, smaller CTAs win).
     const int64_t segments = static_cast<int64_t>(g.batch) * g.kv_heads;
-    const bool auto_wide = pages_per_split == 0 && !(flags & (MV_FLAG_FUSED_MERGE | MV_FLAG_CLUSTER)) &&
+    const bool auto_wide = pages_per_split == 0 && !(flags & (MV_FLAG_FUSED_MERGE | MV_FLAG_CLUSTER | MV_FLAG_STREAM)) &&
                            segments >= 16 && segments <= dev.sms / 2 && max_pages <= 1024;
     plan->wide = plan->path == MV_PATH_TMA_MMA && ((flags & MV_FLAG_WIDE) || auto_wide) && g.head_dim != 256;
     // The CUDA-core variant runs the default shape only (it is a comparison point).
@@ -403,10 +464,15 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
         const int64_t first = std::min<int64_t>(2 * pps, kMaxPagesPerSplit);
         const int64_t est_ctas = static_cast<int64_t>(g.batch) * g.kv_heads *
                                  ((std::max<int64_t>(max_pages, 1) / 2 + pps - 1) / pps);
-        if (first > pps && est_ctas > static_cast<int64_t>(dev.sms) * 3) plan->first_pages = static_cast<int>(first);
+        if (first > pps && est_ctas > static_cast<int64_t>(dev.sms) * 3) {
+            plan->first_pages = static_cast<int>(first);
+            if (MV_LATER_SPLIT_DIV > 1) plan->later_pages = static_cast<int>(std::max<int64_t>(16, pps / MV_LATER_SPLIT_DIV));
+        }
     }
     const int64_t first = plan->first_pages;
-    const int64_t splits = first > 0 ? (max_pages <= first ? 1 : 1 + (max_pages - first + pps - 1) / pps)
+    const int64_t later = plan->later_pages > 0 ? plan->later_pages : pps;
+    const int64_t splits = first > 0 ? (max_pages <= first ? 1 : max_pages <= first + pps ? 2
+                                                               : 2 + (max_pages - first - pps + later - 1) / later)
                                      : std::max<int64_t>(1, (max_pages + pps - 1) / pps);
     if (splits > 8192) return fail(MV_ERR_UNSUPPORTED, "more than 8192 splits: raise pages_per_split");
     plan->pages_per_split = static_cast<int>(pps);
@@ -422,10 +488,16 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
         // separate merge pass (launched early with PDL), so it is opt-in.
         plan->fused_merge = (flags & MV_FLAG_FUSED_MERGE) && plan->path == MV_PATH_TMA_MMA &&
                             static_cast<size_t>(group) * splits * sizeof(float) <= grid_stage_bytes(g.head_dim, plan->wide) &&
-                            static_cast<int64_t>(g.batch) * g.kv_heads <= kMaxCounters;
+                            static_cast<int64_t>(g.batch) * g.kv_heads <= kMaxCounters - mv::kStreamCounterSlots;
         plan->counter_bytes = kCounterRegion;
     }
     plan->workspace = plan->counter_bytes + plan->part_o_bytes + plan->part_lse_bytes;
+    if (stream_use == StreamUse::kAllowed && stream_plan(g, pages_per_split, flags, dev, plan)) return MV_OK;
+    if ((flags & MV_FLAG_STREAM) && stream_use == StreamUse::kAllowed)
+        return fail(MV_ERR_UNSUPPORTED,
+                    "MV_FLAG_STREAM needs the tensor-core kernel (bf16/fp16, page 16, head_dim 64/128, GQA "
+                    "group <= 8, TMA-aligned caches), at most %d sequences, pages_per_split <= %d and no other "
+                    "schedule flag", mv::kStreamMaxBatch, mv::kStreamMaxItemPages);
     if (plan->path == MV_PATH_SIMT) {
         const size_t smem = mv::simt_smem_bytes(group, g.head_dim);
         if (smem > static_cast<size_t>(dev.smem_optin))
@@ -687,6 +759,18 @@ int launch_persistent(const mv::DecodeParams& p, const CUtensorMap& kmap, const 
     return err == cudaSuccess ? MV_OK : cuda_fail(err, "merge kernel launch");
 }
 
+// The per-warp stream schedule: one CTA per SM.
+template <typename T, int D>
+int launch_stream(const mv::DecodeParams& p, const CUtensorMap& kmap, const CUtensorMap& vmap, int ctas,
+                  cudaStream_t stream) {
+    auto kernel = mv::paged_decode_stream_kernel<T, D>;
+    int rc = ensure_smem(kernel, mv::StreamShape<D>::kSmemBytes);
+    if (rc != MV_OK) return rc;
+    cudaError_t err = launch_pdl(kernel, dim3(ctas), dim3(mv::kStreamWarps * 32), mv::StreamShape<D>::kSmemBytes,
+                                 stream, p, kmap, vmap);
+    return err == cudaSuccess ? MV_OK : cuda_fail(err, "stream decode kernel launch");
+}
+
 template <typename T>
 int launch_persistent_dispatch(const mv::DecodeParams& p, const CUtensorMap& kmap,
                                const CUtensorMap& vmap, int ctas, int nt, cudaStream_t stream) {
@@ -756,6 +840,20 @@ int launch_decode(const mv::DecodeParams& p, const Plan& plan, const CUtensorMap
             return fail(MV_ERR_UNSUPPORTED, "tensor-core kernel takes fp16/bf16 only");
         } else {
             return launch_persistent_dispatch<T>(p, *kmap, *vmap, plan.ctas, plan.nt, stream);
+        }
+    }
+    if (plan.path == MV_PATH_TMA_MMA_STREAM) {
+        if constexpr (std::is_same<T, float>::value) {
+            return fail(MV_ERR_UNSUPPORTED, "tensor-core kernel takes fp16/bf16 only");
+        } else {
+            int rc = p.head_dim == 64 ? launch_stream<T, 64>(p, *kmap, *vmap, plan.ctas, stream)
+                                      : launch_stream<T, 128>(p, *kmap, *vmap, plan.ctas, stream);
+            if (rc != MV_OK) return rc;
+            if (plan.max_splits > 1) {
+                cudaError_t err = launch_split_merge<T>(p, stream);
+                if (err != cudaSuccess) return cuda_fail(err, "merge kernel launch");
+            }
+            return MV_OK;
         }
     }
     const dim3 grid(plan.max_splits, p.kv_heads, p.batch);
@@ -906,7 +1004,7 @@ int mv_paged_decode_workspace_size(int32_t batch, int32_t num_q_heads, int32_t n
     const Geometry g{batch, num_q_heads, num_kv_heads, head_dim, block_size, max_context_len, dtype};
     Plan plan;
     // Alignment never changes the split shape, so plan as if aligned.
-    int rc = make_plan(g, pages_per_split, flags, true, &plan);
+    int rc = make_plan(g, pages_per_split, flags, true, &plan, StreamUse::kAllowed);
     if (rc != MV_OK) return rc;
     *bytes = plan.workspace;
     return MV_OK;
@@ -934,7 +1032,7 @@ int mv_paged_decode_plan(int32_t batch, int32_t num_q_heads, int32_t num_kv_head
                          int32_t* path, int32_t* chosen_pages_per_split, int32_t* max_splits) {
     const Geometry g{batch, num_q_heads, num_kv_heads, head_dim, block_size, max_context_len, dtype};
     Plan plan;
-    int rc = make_plan(g, pages_per_split, flags, tma_aligned(k_cache, v_cache), &plan);
+    int rc = make_plan(g, pages_per_split, flags, tma_aligned(k_cache, v_cache), &plan, StreamUse::kAllowed);
     if (rc != MV_OK) return rc;
     if (path) *path = plan.path;
     if (chosen_pages_per_split) *chosen_pages_per_split = plan.pages_per_split;
@@ -995,7 +1093,7 @@ static int paged_decode_impl(const void* q, int64_t q_stride_seq, int64_t q_stri
     Plan plan;
     bool tiles = false;
     rc = chunk ? make_chunk_plan(g, tokens, pages_per_split, flags, tma_aligned(k_cache, v_cache), &plan, &tiles)
-               : make_plan(g, pages_per_split, flags, tma_aligned(k_cache, v_cache), &plan);
+               : make_plan(g, pages_per_split, flags, tma_aligned(k_cache, v_cache), &plan, StreamUse::kAllowed);
     if (rc != MV_OK) return rc;
     if (plan.workspace > 0 && (!workspace || workspace_bytes < plan.workspace))
         return fail(MV_ERR_WORKSPACE_TOO_SMALL, "workspace of %zu bytes needed, %zu given", plan.workspace,
@@ -1003,7 +1101,7 @@ static int paged_decode_impl(const void* q, int64_t q_stride_seq, int64_t q_stri
     if (plan.workspace > 0 && reinterpret_cast<uintptr_t>(workspace) % 16)
         return fail(MV_ERR_INVALID_ARGUMENT, "workspace must be 16-byte aligned");
 
-    mv::DecodeParams p;
+    mv::DecodeParams p{};
     p.q = q;
     p.q_stride_seq = q_stride_seq;
     p.q_stride_head = q_stride_head;
@@ -1031,6 +1129,7 @@ static int paged_decode_impl(const void* q, int64_t q_stride_seq, int64_t q_stri
     p.pages_per_split = plan.pages_per_split;
     p.max_splits = plan.max_splits;
     p.first_pages = plan.first_pages;
+    p.later_pages = plan.later_pages;
     p.part_o = nullptr;
     p.part_lse = nullptr;
     p.prefix_out = nullptr;
@@ -1039,7 +1138,7 @@ static int paged_decode_impl(const void* q, int64_t q_stride_seq, int64_t q_stri
     p.fused_merge = plan.fused_merge ? 1 : 0;
     if (plan.workspace > 0) {
         uint8_t* base = static_cast<uint8_t*>(workspace);
-        if (plan.fused_merge) p.counters = reinterpret_cast<unsigned*>(base);
+        if (plan.counter_bytes > 0) p.counters = reinterpret_cast<unsigned*>(base);
         base += plan.counter_bytes;
         p.part_o = reinterpret_cast<float*>(base);
         p.part_lse = reinterpret_cast<float*>(base + plan.part_o_bytes);
@@ -1067,7 +1166,8 @@ static int paged_decode_impl(const void* q, int64_t q_stride_seq, int64_t q_stri
         const uintptr_t bits = reinterpret_cast<uintptr_t>(rows->key) | reinterpret_cast<uintptr_t>(rows->value) |
                                static_cast<uintptr_t>((rows->key_stride_seq | rows->key_stride_head |
                                                        rows->value_stride_seq | rows->value_stride_head) * 2);
-        const bool fusable = (plan.path == MV_PATH_TMA_MMA && bits % 16 == 0) || plan.path == MV_PATH_SIMT;
+        const bool fusable = ((plan.path == MV_PATH_TMA_MMA || plan.path == MV_PATH_TMA_MMA_STREAM) && bits % 16 == 0) ||
+                             plan.path == MV_PATH_SIMT;
         if (rows->rope_cos) {
             const bool tables_ok = plan.path == MV_PATH_SIMT ||
                                    (reinterpret_cast<uintptr_t>(rows->rope_cos) |
@@ -1101,7 +1201,7 @@ static int paged_decode_impl(const void* q, int64_t q_stride_seq, int64_t q_stri
 
     CUtensorMap kmap, vmap;
     if (plan.path == MV_PATH_TMA_MMA || plan.path == MV_PATH_TMA_MMA_PERSISTENT ||
-        plan.path == MV_PATH_TMA_MMA_CLUSTER) {
+        plan.path == MV_PATH_TMA_MMA_CLUSTER || plan.path == MV_PATH_TMA_MMA_STREAM) {
         rc = page_tensor_map(k_cache, num_blocks, num_kv_heads, head_dim, dtype, &kmap);
         if (rc == MV_OK) rc = page_tensor_map(v_cache, num_blocks, num_kv_heads, head_dim, dtype, &vmap);
         if (rc != MV_OK) return rc;
@@ -1271,7 +1371,7 @@ int mv_contiguous_decode(const void* q, int64_t q_stride_seq, int64_t q_stride_h
 
     const int64_t bound = std::min(max_context_len, cache_len);
     const int64_t runs = (cache_len + 15) / 16;  // 16-token runs stand in for pages
-    mv::DecodeParams p;
+    mv::DecodeParams p{};
     std::memset(&p, 0, sizeof(p));
     p.q = q;
     p.q_stride_seq = q_stride_seq;
@@ -1298,6 +1398,7 @@ int mv_contiguous_decode(const void* q, int64_t q_stride_seq, int64_t q_stride_h
     p.pages_per_split = plan.pages_per_split;
     p.max_splits = plan.max_splits;
     p.first_pages = plan.first_pages;
+    p.later_pages = plan.later_pages;
     p.fused_merge = plan.fused_merge ? 1 : 0;
     p.contiguous = 1;
     for (int i = 0; i < 3; ++i) {
@@ -1306,7 +1407,7 @@ int mv_contiguous_decode(const void* q, int64_t q_stride_seq, int64_t q_stride_h
     }
     if (plan.workspace > 0) {
         uint8_t* base = static_cast<uint8_t*>(workspace);
-        if (plan.fused_merge) p.counters = reinterpret_cast<unsigned*>(base);
+        if (plan.fused_merge || plan.path == MV_PATH_TMA_MMA_STREAM) p.counters = reinterpret_cast<unsigned*>(base);
         base += plan.counter_bytes;
         p.part_o = reinterpret_cast<float*>(base);
         p.part_lse = reinterpret_cast<float*>(base + plan.part_o_bytes);
@@ -1699,7 +1800,7 @@ int mv_paged_decode_noalloc(const void* q, int64_t q_stride_seq, int64_t q_strid
     // CUDA-core kernel, whose split sizes differ).
     const Geometry g{batch, num_q_heads, num_kv_heads, head_dim, block_size, max_context_len, dtype};
     Plan plan;
-    int rc = make_plan(g, pages_per_split, flags, tma_aligned(k_cache, v_cache), &plan);
+    int rc = make_plan(g, pages_per_split, flags, tma_aligned(k_cache, v_cache), &plan, StreamUse::kAllowed);
     if (rc != MV_OK) return rc;
     const size_t needed = plan.workspace;
     if (needed > MV_NOALLOC_SCRATCH_BYTES)
@@ -1708,21 +1809,24 @@ int mv_paged_decode_noalloc(const void* q, int64_t q_stride_seq, int64_t q_strid
                     "built-in array holds %zu; use mv_paged_decode with a workspace, or a larger "
                     "pages_per_split",
                     needed, static_cast<size_t>(MV_NOALLOC_SCRATCH_BYTES));
-    // Set-up, once per device, with that device current: the array's name is a
-    // host-side stand-in, so look up its device address. The address is kept
-    // for the life of the process; a cudaDeviceReset of the device unloads the
-    // module and leaves it stale, so this entry point must not be called on a
-    // device after it was reset.
+    // The array's name is a host-side stand-in: look up its device address,
+    // with the call's device current. Outside stream capture every call looks
+    // it up again (cheap), so a module reloaded after a cudaDeviceReset is
+    // found at its new address; inside a capture the call uses the address its
+    // device's last call outside capture found.
     static void* scratch[kMaxDevices] = {nullptr};
     static std::mutex scratch_mutex;
     int device = 0;
     cudaError_t err = cudaGetDevice(&device);
     if (err != cudaSuccess) return cuda_fail(err, "cudaGetDevice");
     if (device < 0 || device >= kMaxDevices) return fail(MV_ERR_UNSUPPORTED, "device index %d out of range", device);
+    cudaStreamCaptureStatus capture = cudaStreamCaptureStatusNone;
+    err = cudaStreamIsCapturing(static_cast<cudaStream_t>(stream), &capture);
+    if (err != cudaSuccess) return cuda_fail(err, "cudaStreamIsCapturing");
     void* ptr = nullptr;
     {
         std::lock_guard<std::mutex> lock(scratch_mutex);
-        if (!scratch[device]) {
+        if (!scratch[device] || capture == cudaStreamCaptureStatusNone) {
             err = cudaGetSymbolAddress(&scratch[device], g_noalloc_scratch);
             if (err != cudaSuccess) {
                 scratch[device] = nullptr;

@@ -26,6 +26,10 @@ __device__ __forceinline__ void report_bad_page_id() { atomicOr(&g_device_status
 // A bounded wait gives up after this long; nothing legitimate takes it.
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 
+// Every non-empty workspace starts with this many zero-initialised unsigned
+// counters (256 KiB); the kernels that use them leave them zero when they end.
+constexpr int kCounterRegionSlots = 65536;
+
 struct DecodeParams {
     const void* q;
     int64_t q_stride_seq;
@@ -93,6 +97,9 @@ struct DecodeParams {
     int q_tokens;
     int64_t q_stride_token;
     int64_t out_stride_token;
+    // Split grid with first_pages: splits from the third on hold later_pages
+    // pages (0: pages_per_split), so the splits dispatched last are shorter.
+    int later_pages;
 };
 
 struct AppendParams {
@@ -166,10 +173,12 @@ __device__ __forceinline__ SeqSplit seq_split(const DecodeParams& p, int b) {
     s.pages = s.state == 0 ? (s.len + p.block_size - 1) / p.block_size : 0;
     // The last split is partial. Measured on B200, evening out the splits'
     // sizes was slower: the small last splits fill the tail of the grid.
+    const int64_t later = p.later_pages > 0 ? p.later_pages : p.pages_per_split;
+    const int64_t two = static_cast<int64_t>(p.first_pages) + p.pages_per_split;
     const int64_t splits = p.first_pages > 0
-                               ? (s.pages <= p.first_pages
-                                      ? 1
-                                      : 1 + (s.pages - p.first_pages + p.pages_per_split - 1) / p.pages_per_split)
+                               ? (s.pages <= p.first_pages ? 1
+                                  : s.pages <= two        ? 2
+                                                          : 2 + (s.pages - two + later - 1) / later)
                                : (s.pages + p.pages_per_split - 1) / p.pages_per_split;
     s.splits = splits < 1 ? 1 : static_cast<int>(splits);
     return s;
@@ -177,14 +186,19 @@ __device__ __forceinline__ SeqSplit seq_split(const DecodeParams& p, int b) {
 
 // First page of split `split`; it does not depend on the sequence's length.
 __device__ __forceinline__ int64_t split_begin(const DecodeParams& p, int split) {
-    if (p.first_pages > 0)
-        return split == 0 ? 0 : p.first_pages + static_cast<int64_t>(split - 1) * p.pages_per_split;
+    if (p.first_pages > 0) {
+        if (split <= 1) return split == 0 ? 0 : p.first_pages;
+        const int64_t later = p.later_pages > 0 ? p.later_pages : p.pages_per_split;
+        return p.first_pages + p.pages_per_split + static_cast<int64_t>(split - 2) * later;
+    }
     return static_cast<int64_t>(split) * p.pages_per_split;
 }
 
 // Pages a full split `split` holds.
 __device__ __forceinline__ int split_pages(const DecodeParams& p, int split) {
-    return p.first_pages > 0 && split == 0 ? p.first_pages : p.pages_per_split;
+    if (p.first_pages <= 0 || split == 1) return p.pages_per_split;
+    if (split == 0) return p.first_pages;
+    return p.later_pages > 0 ? p.later_pages : p.pages_per_split;
 }
 
 // Pages [begin, end) of split `split` of a sequence.

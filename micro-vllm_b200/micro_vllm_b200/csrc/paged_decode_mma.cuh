@@ -76,6 +76,13 @@ struct WarpPageAttention {
 
     // Lane holds q[g][16 ks + 2(lane%4) + {0,1,8,9}] for g = nt*8 + lane/4 (0 beyond the group).
     __device__ __forceinline__ void load_q(const DecodeParams& p, int b, int h, int lane) {
+        load_q_frags(p, b, h, lane, qf);
+    }
+
+    // The same into any fragment array (the loads are only issued: nothing
+    // waits for them until the fragments are read).
+    __device__ __forceinline__ static void load_q_frags(const DecodeParams& p, int b, int h, int lane,
+                                                        uint32_t (&qf)[KS][NT][2]) {
         const uint16_t* qbase = static_cast<const uint16_t*>(p.q) + row_q_offset(p, b);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
@@ -182,8 +189,50 @@ struct WarpPageAttention {
 
     // Online-softmax update with one page held in registers.
     __device__ __forceinline__ void attend(const PageFrags& f, int valid, float scale_log2, int lane) {
-        // Two accumulator chains (even and odd k-steps) halve the dependent mma chain.
         float sc[NT][2][4];
+        scores(f.k, sc);
+        update(sc, f.v, valid, scale_log2, lane);
+    }
+
+    // The page's K tile as A fragments (lane layout of load_page).
+    __device__ __forceinline__ static void load_k(uint32_t (&k)[KS][4], uint32_t kt, int lane) {
+        const int k_slot = (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int k_chunk = lane >> 4;
+#pragma unroll
+        for (int ks = 0; ks < KS; ++ks) {
+            const int r = (ks >> 2) * 16 + k_slot;
+            const int c = ((ks & 3) << 1) + k_chunk;
+            ldmatrix_x4(k[ks], kt + r * 128 + ((c ^ (r & 7)) << 4));
+        }
+    }
+
+    // The page's V tile as transposed A fragments; slots past `valid` cleared first.
+    __device__ __forceinline__ static void load_v(uint32_t (&v)[KS][4], uint32_t vt, uint8_t* vgen, int valid,
+                                                  int lane) {
+        if (valid < kPageTokens) {
+            const int rows = kPageTokens - valid;
+            for (int idx = lane; idx < (D / 64) * rows * 8; idx += 32) {
+                const int chunk = idx & 7;
+                const int rr = idx >> 3;
+                const int half = rr / rows;
+                const int slot = valid + (rr - half * rows);
+                *reinterpret_cast<uint4*>(vgen + (half * 16 + slot) * 128 + chunk * 16) = make_uint4(0u, 0u, 0u, 0u);
+            }
+            __syncwarp();
+        }
+        const int v_tok = (lane & 7) + ((lane >> 4) & 1) * 8;
+        const int v_chunk = (lane >> 3) & 1;
+#pragma unroll
+        for (int mt = 0; mt < KS; ++mt) {
+            const int r = (mt >> 2) * 16 + v_tok;
+            const int c = ((mt & 3) << 1) + v_chunk;
+            ldmatrix_x4_trans(v[mt], vt + r * 128 + ((c ^ (r & 7)) << 4));
+        }
+    }
+
+    // S^T = K Q^T for one page (two accumulator chains: even and odd k-steps
+    // halve the dependent mma chain).
+    __device__ __forceinline__ void scores(const uint32_t (&k)[KS][4], float (&sc)[NT][2][4]) const {
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -191,8 +240,13 @@ struct WarpPageAttention {
 #pragma unroll
         for (int ks = 0; ks < KS; ++ks) {
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) Op::run(sc[nt][ks & 1], f.k[ks], qf[ks][nt][0], qf[ks][nt][1]);
+            for (int nt = 0; nt < NT; ++nt) Op::run(sc[nt][ks & 1], k[ks], qf[ks][nt][0], qf[ks][nt][1]);
         }
+    }
+
+    // Online-softmax update from one page's scores and its V fragments.
+    __device__ __forceinline__ void update(const float (&sc)[NT][2][4], const uint32_t (&v)[KS][4], int valid,
+                                           float scale_log2, int lane) {
         const int row0 = lane >> 2;  // token of accumulator rows c0/c1 (+8 for c2/c3)
         const bool v0 = row0 < valid;
         const bool v1 = row0 + 8 < valid;
@@ -235,7 +289,7 @@ struct WarpPageAttention {
 #pragma unroll
         for (int mt = 0; mt < KS; ++mt) {
 #pragma unroll
-            for (int nt = 0; nt < NT; ++nt) Op::run(o[mt][nt], f.v[mt], pb[nt][0], pb[nt][1]);
+            for (int nt = 0; nt < NT; ++nt) Op::run(o[mt][nt], v[mt], pb[nt][0], pb[nt][1]);
         }
     }
 
@@ -289,6 +343,29 @@ struct WarpPageAttention {
                     row[d + 8] = o[mt][nt][j + 2] * inv;
                 }
                 if ((lane >> 2) == 0) plse[q] = m[nt][j] + log2f(l[nt][j]);
+            }
+        }
+    }
+
+    // The same into rows `row_stride` floats apart (log2-sum-exps `lse_stride`
+    // apart): query row q of one split of the split-KV partial layout.
+    __device__ __forceinline__ void store_partial_strided(float* po, float* plse, int64_t row_stride,
+                                                          int64_t lse_stride, int group, int lane) const {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+                const int q = nt * 8 + 2 * (lane & 3) + j;
+                if (q >= group) continue;
+                const float inv = 1.0f / l[nt][j];
+                float* row = po + q * row_stride;
+#pragma unroll
+                for (int mt = 0; mt < KS; ++mt) {
+                    const int d = mt * 16 + (lane >> 2);
+                    row[d] = o[mt][nt][j] * inv;
+                    row[d + 8] = o[mt][nt][j + 2] * inv;
+                }
+                if ((lane >> 2) == 0) plse[q * lse_stride] = m[nt][j] + log2f(l[nt][j]);
             }
         }
     }

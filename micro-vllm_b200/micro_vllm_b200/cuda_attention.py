@@ -297,22 +297,44 @@ def decode_attention_paged(query: torch.Tensor, cache, *, layer_idx: int) -> tor
         cache._device_page_table, length)
 
 
-def _flags(force_simt, persistent, fused_merge=False, cluster=False, wide=False, cuda_core_math=False):
+# schedule keyword -> flag: the library's choice, the per-warp stream schedule
+# wherever its shape allows, or never the stream schedule.
+_SCHEDULES = {'auto': 0, 'stream': _native.FLAG_STREAM, 'split': _native.FLAG_SPLIT_GRID}
+
+
+def _flags(force_simt, persistent, fused_merge=False, cluster=False, wide=False, cuda_core_math=False,
+           schedule='auto'):
+    _check(schedule in _SCHEDULES, "schedule must be 'auto', 'stream' or 'split'")
     return ((_native.FLAG_FORCE_SIMT if force_simt else 0) | (_native.FLAG_PERSISTENT if persistent else 0)
             | (_native.FLAG_FUSED_MERGE if fused_merge else 0) | (_native.FLAG_CLUSTER if cluster else 0)
-            | (_native.FLAG_WIDE if wide else 0) | (_native.FLAG_CUDA_CORE_MATH if cuda_core_math else 0))
+            | (_native.FLAG_WIDE if wide else 0) | (_native.FLAG_CUDA_CORE_MATH if cuda_core_math else 0)
+            | _SCHEDULES[schedule])
+
+
+def _schedule_of(flags):
+    for name, bit in _SCHEDULES.items():
+        if bit and flags & bit:
+            return name
+    return 'auto'
+
+
+# Plans whose tensor-core kernel rotates q and the new K rows itself (fused RoPE).
+_ROPE_FUSED_TMA_PATHS = ('tma_mma', 'tma_mma_stream')
 
 
 def paged_decode_plan(query_heads, key_cache, context_bound, *, batch, pages_per_split=0,
-                      force_simt=False, persistent=False, cluster=False, wide=False, cuda_core_math=False):
+                      force_simt=False, persistent=False, cluster=False, wide=False, cuda_core_math=False,
+                      schedule='auto'):
     """(path, pages_per_split, max_splits) that ``paged_decode_attention`` would use.
 
-    path is 'tma_mma_cluster' (TMA + tensor cores, the splits of each
-    sequence/head in one thread-block cluster, combined through distributed
-    shared memory), 'tma_mma' (TMA + tensor cores, one CTA per split of pages,
-    merge pass), 'tma_mma_persistent' (TMA + tensor cores, a resident grid with
-    equal page ranges per warp, merge pass) or 'simt' (CUDA cores, one CTA per
-    split, merge pass).
+    path is 'tma_mma_stream' (TMA + tensor cores, one CTA per SM whose warps
+    each stream pages of work items -- runs of pages_per_split pages of one
+    sequence and KV head -- taken from a queue, merge pass), 'tma_mma_cluster'
+    (TMA + tensor cores, the splits of each sequence/head in one thread-block
+    cluster, combined through distributed shared memory), 'tma_mma' (TMA +
+    tensor cores, one CTA per split of pages, merge pass), 'tma_mma_persistent'
+    (TMA + tensor cores, a resident grid with equal page ranges per warp, merge
+    pass) or 'simt' (CUDA cores, one CTA per split, merge pass).
     """
     lib = _native.library()
     num_blocks, kv_heads, block_size, dim = key_cache.shape
@@ -320,7 +342,8 @@ def paged_decode_plan(query_heads, key_cache, context_bound, *, batch, pages_per
     with torch.cuda.device(key_cache.device):
         _native.check(lib.mv_paged_decode_plan(
             batch, query_heads, kv_heads, dim, block_size, context_bound, pages_per_split,
-            _flags(force_simt, persistent, cluster=cluster, wide=wide, cuda_core_math=cuda_core_math),
+            _flags(force_simt, persistent, cluster=cluster, wide=wide, cuda_core_math=cuda_core_math,
+                   schedule=schedule),
             DTYPE_CODES[key_cache.dtype],
             key_cache.data_ptr(), key_cache.data_ptr(), ctypes.byref(path), ctypes.byref(pps),
             ctypes.byref(splits)))
@@ -333,7 +356,7 @@ def paged_decode_attention(query: torch.Tensor, key_cache: torch.Tensor, value_c
                            out: torch.Tensor | None = None, pages_per_split: int = 0,
                            force_simt: bool = False, persistent: bool = False,
                            fused_merge: bool = False, cluster: bool = False, wide: bool = False,
-                           cuda_core_math: bool = False) -> torch.Tensor:
+                           cuda_core_math: bool = False, schedule: str = 'auto') -> torch.Tensor:
     """Batched paged GQA decode over one shared page pool.
 
     query: [B, Hq, D] (or [B, Hq, 1, D]) CUDA fp32/fp16/bf16, feature stride 1.
@@ -352,7 +375,11 @@ def paged_decode_attention(query: torch.Tensor, key_cache: torch.Tensor, value_c
     the last split CTA; the split grid's wide shape of 8 warps with deeper
     rings; the CUDA-core kernel). cuda_core_math: the split grid's TMA pipeline
     with fp32 FMA math instead of the tensor-core tile (GQA group <= 8,
-    head_dim 64/128; a comparison point). By default the library picks the
+    head_dim 64/128; a comparison point). schedule: 'auto' (the library's
+    choice), 'stream' (the per-warp stream schedule -- one CTA per SM, each
+    warp streaming pages of work items from a queue; measured slower than the
+    split grid, kept for comparison -- wherever its shape allows, else an
+    error) or 'split' (the same as 'auto'). By default the library picks the
     tensor-core split grid with a merge pass, and the CUDA-core kernel for
     shapes the tensor-core kernels do not take.
     Returns out, or a fresh [B, Hq, D] tensor of the query's dtype.
@@ -360,7 +387,8 @@ def paged_decode_attention(query: torch.Tensor, key_cache: torch.Tensor, value_c
     q, max_context_len, scale, out = _checked_batched(query, key_cache, value_cache, block_table,
                                                       context_lens, scale, max_context_len, out)
     _launch_batched(q, key_cache, value_cache, block_table, context_lens, max_context_len, scale, out,
-                    pages_per_split, _flags(force_simt, persistent, fused_merge, cluster, wide, cuda_core_math))
+                    pages_per_split, _flags(force_simt, persistent, fused_merge, cluster, wide, cuda_core_math,
+                                            schedule))
     return out
 
 
@@ -430,7 +458,7 @@ def paged_decode_with_append(query: torch.Tensor, key: torch.Tensor, value: torc
                              force_simt: bool = False, persistent: bool = False,
                              fused_merge: bool = False, cluster: bool = False, wide: bool = False,
                              rope: tuple[torch.Tensor, torch.Tensor] | None = None,
-                             cuda_core_math: bool = False) -> torch.Tensor:
+                             cuda_core_math: bool = False, schedule: str = 'auto') -> torch.Tensor:
     """One decode step of a layer: append this step's K/V row of every sequence, then attend.
 
     The result, in the pools and in the output, is that of
@@ -439,10 +467,10 @@ def paged_decode_with_append(query: torch.Tensor, key: torch.Tensor, value: torc
     ``paged_decode_attention(query, key_cache, value_cache, block_table,
     context_lens, scale)`` -- the append-before-attend order of the
     reference's decode layer (src/micro_vllm/model.py:215-216) -- but where
-    the split-grid tensor-core kernel or the CUDA-core kernel runs, the CTA
-    attending each sequence's last page writes the new row itself, so the step
-    is one kernel (plus the split merge) instead of two. The persistent and
-    cluster schedules run the append kernel first.
+    the stream schedule, the split-grid tensor-core kernel or the CUDA-core
+    kernel runs, the warp or CTA attending each sequence's last page writes the
+    new row itself, so the step is one kernel (plus the split merge) instead
+    of two. The persistent and cluster schedules run the append kernel first.
 
     key/value: [B, Hkv, D] or [B, Hkv, 1, D] CUDA tensors of the pool dtype,
     feature stride 1. context_lens count the new token. The page receiving a
@@ -466,7 +494,7 @@ def paged_decode_with_append(query: torch.Tensor, key: torch.Tensor, value: torc
            'new K/V must have shape [B, Hkv, D] or [B, Hkv, 1, D]')
     cache_ops._validate_pages(key4, key_cache, value_cache)
     cache_ops._validate_aliases(key4, value4, key_cache, value_cache, block_table)
-    flags = _flags(force_simt, persistent, fused_merge, cluster, wide, cuda_core_math)
+    flags = _flags(force_simt, persistent, fused_merge, cluster, wide, cuda_core_math, schedule)
     key3, value3 = key4[:, :, 0, :], value4[:, :, 0, :]
     tables = None
     if rope is not None:
@@ -475,8 +503,9 @@ def paged_decode_with_append(query: torch.Tensor, key: torch.Tensor, value: torc
         rope_ops.check_tables(cos, sin, q.shape[2], q.dtype, q.device)
         path = paged_decode_plan(q.shape[1], key_cache, max_context_len, batch=q.shape[0],
                                  pages_per_split=pages_per_split, force_simt=force_simt,
-                                 persistent=persistent, cluster=cluster, wide=wide)[0]
-        if (path == 'tma_mma' and _aligned16(key3, value3, cos, sin)) or path == 'simt':
+                                 persistent=persistent, cluster=cluster, wide=wide,
+                                 cuda_core_math=cuda_core_math, schedule=schedule)[0]
+        if (path in _ROPE_FUSED_TMA_PATHS and _aligned16(key3, value3, cos, sin)) or path == 'simt':
             tables = (cos, sin)
         else:
             q = rope_ops.apply_rope(q, cos, sin, positions=context_lens, positions_are_end=True)
@@ -495,7 +524,8 @@ def _aligned16(*tensors):
 
 
 def _data_ptrs(*tensors):
-    return tuple(t.data_ptr() if t is not None else 0 for t in tensors)
+    """Storage addresses and strides: a repeat must see the same views, not only the same memory."""
+    return tuple((t.data_ptr(), t.stride()) if t is not None else (0, ()) for t in tensors)
 
 
 class PagedDecodeStep:
@@ -511,7 +541,8 @@ class PagedDecodeStep:
     ``mv_paged_decode`` / ``mv_paged_decode_append`` in one struct, filled at
     construction and on each validated call). A call repeating one of the
     last eight validated ones -- the same tensor objects over the same
-    storage, on the same stream, with a caller-given output -- skips even
+    storage with the same strides, on the same stream, with a caller-given
+    output -- skips even
     those comparisons; the step keeps references to those tensors until they
     are evicted. Results are identical to those functions on the same
     arguments.
@@ -530,7 +561,7 @@ class PagedDecodeStep:
                  num_q_heads: int, max_context_len: int | None = None, scale: float | None = None,
                  pages_per_split: int = 0, force_simt: bool = False, persistent: bool = False,
                  fused_merge: bool = False, cluster: bool = False, wide: bool = False,
-                 rope: tuple[torch.Tensor, torch.Tensor] | None = None):
+                 rope: tuple[torch.Tensor, torch.Tensor] | None = None, schedule: str = 'auto'):
         batch = block_table.shape[0] if block_table.dim() == 2 else 0
         dim = key_cache.shape[-1] if key_cache.dim() == 4 else 0
         probe = torch.empty((max(batch, 1), num_q_heads, max(dim, 1)), dtype=key_cache.dtype,
@@ -545,7 +576,7 @@ class PagedDecodeStep:
         num_blocks, kv_heads, block_size, _ = key_cache.shape
         self._q_shape = (batch, num_q_heads, dim)
         self._row_shape = (batch, kv_heads, dim)
-        self._flags = _flags(force_simt, persistent, fused_merge, cluster, wide)
+        self._flags = _flags(force_simt, persistent, fused_merge, cluster, wide, schedule=schedule)
         self._pps = int(pages_per_split)
         self._bound = int(bound)
         self._pools = (key_cache, value_cache)
@@ -585,7 +616,7 @@ class PagedDecodeStep:
             self._rope = (rope[0], rope[1])
             path = self.plan[0]
             self._rope_kernel_path = path
-            self._rope_in_kernel = (path == 'tma_mma' and _aligned16(*rope)) or path == 'simt'
+            self._rope_in_kernel = (path in _ROPE_FUSED_TMA_PATHS and _aligned16(*rope)) or path == 'simt'
 
     @property
     def plan(self):
@@ -595,7 +626,8 @@ class PagedDecodeStep:
                                  force_simt=bool(self._flags & _native.FLAG_FORCE_SIMT),
                                  persistent=bool(self._flags & _native.FLAG_PERSISTENT),
                                  cluster=bool(self._flags & _native.FLAG_CLUSTER),
-                                 wide=bool(self._flags & _native.FLAG_WIDE))
+                                 wide=bool(self._flags & _native.FLAG_WIDE),
+                                 schedule=_schedule_of(self._flags))
 
     def _check_rows(self, rows):
         if rows.dim() == 4:

@@ -71,7 +71,12 @@ def gather_full_heads(local_out, *, q_heads, kv_heads, batch, group=None, timeou
     timeout (a ``datetime.timedelta``): the longest this call waits for the
     exchange; past it (a peer that died or never joins) it raises
     RuntimeError instead of waiting on the backend, which does not always
-    honour its own timeout when a peer's process is gone.
+    honour its own timeout when a peer's process is gone. Some backends
+    (NCCL) raise from the wait, others (gloo) return False; both give the same
+    RuntimeError here. After it the gather may still be queued on the
+    communicator and may still write its receive buffer: the caller must
+    abort or destroy the process group and discard this call's output before
+    any further collective.
     """
     import torch.distributed as dist
 
@@ -92,8 +97,13 @@ def gather_full_heads(local_out, *, q_heads, kv_heads, batch, group=None, timeou
         work = dist.all_gather(pieces, padded, group=group, async_op=True)
     if timeout is None:
         work.wait()
-    elif not work.wait(timeout):
-        raise RuntimeError(f'full-head gather did not complete within {timeout}')
+    else:
+        try:
+            done = work.wait(timeout)
+        except Exception as exc:  # the backend's own timeout or abort error
+            raise RuntimeError(f'full-head gather did not complete within {timeout}: {exc}') from exc
+        if not done:
+            raise RuntimeError(f'full-head gather did not complete within {timeout}')
     full = local_out.new_empty((batch, q_heads, dim))
     for shard, piece in zip(shards, pieces):
         full[shard.batch[0]:shard.batch[1], shard.q_heads[0]:shard.q_heads[1]] = \

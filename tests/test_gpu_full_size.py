@@ -8,7 +8,7 @@ those same inputs (same seeds, same KV-head shard geometry as ``bench.py
 --scaling strong`` gives a rank) and check it against the oracle:
 
 * the launch plan ``paged_decode_plan`` reports for the call is the one the
-  bench line reports (asserted exactly for the Qwen2.5-7B headline);
+  bench line reports (asserted exactly for each workload);
 * the append: the page each sequence wrote equals, bit for bit, the oracle's
   append of that row into the page's pre-step contents, and every other page
   of both pools is unchanged;
