@@ -143,9 +143,12 @@ int ensure_smem_carveout(Kernel kernel, size_t bytes) {
 // ---------------------------------------------------------------- planning
 
 // Split grid's graded schedule: splits after the second hold pages_per_split /
-// MV_LATER_SPLIT_DIV pages (1: all splits after the first alike).
+// MV_LATER_SPLIT_DIV pages (at least 16; 1: all splits after the first alike).
+// Measured on B200 (Qwen2.5-7B geometry, batch 64; graph of 8 steps): 128/64/64
+// pages 60.65 us, 128/64/32 60.44 us, 128/64/16 60.25 us; the batch-256 layer
+// unchanged (589.7-590.0 us).
 #ifndef MV_LATER_SPLIT_DIV
-#define MV_LATER_SPLIT_DIV 1
+#define MV_LATER_SPLIT_DIV 4
 #endif
 
 // Tensor-core kernel shape: warps per CTA and TMA stages per warp by head_dim
@@ -457,6 +460,8 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
     // to 2 x pps pages need no merge. Measured on B200 (Qwen2.5-7B geometry,
     // batch 64, 1k-4k tokens): 62.1 us per step against 65.0 us with uniform
     // 64-page splits and 62.8 us with uniform 128-page splits.
+    // Splits after the second are shorter again (MV_LATER_SPLIT_DIV), so the
+    // CTAs dispatched last are the smallest.
     // Only where the grid is more than one wave: with every CTA resident at
     // once the longest split sets the time (batch 1 x 4096 tokens: 13.8 us
     // with a 32-page first split, 10.3 us without).

@@ -261,7 +261,8 @@ def test_bound_step_rejects_changed_shapes_and_aliases():
                                   ('fixed', [700] * 120 + [0, 1, 15, 16, 17, 511, 512, 513])])
 def test_first_split_schedule_of_multi_wave_grids(lens):
     """Grids of more than one wave of CTAs take a first split twice the split
-    size, dispatched split-major. Check the shape the plan reports, then the
+    size, a second of the split size and later ones of a quarter of it (at
+    least 16 pages), dispatched split-major. Check the shape the plan reports, then the
     one-call step and the two-call path against each other, the uniform-split
     plan of the same size, and the oracle, with empty and page-edge lengths."""
     spec = dict(batch=128, q_heads=28, kv_heads=4, head_dim=128, block_size=16, pool=('factor', 1.25),
@@ -272,7 +273,9 @@ def test_first_split_schedule_of_multi_wave_grids(lens):
     max_pages = t['block_table'].shape[1]
     path, pps, splits = attention.paged_decode_plan(28, t['key_pool'], max_pages * 16, batch=128)
     assert path == 'tma_mma' and 2 * pps < max_pages
-    assert splits == 1 + -(-(max_pages - 2 * pps) // pps)   # a first split of 2 x pps pages
+    later = max(16, pps // 4)
+    expected = 1 if max_pages <= 2 * pps else 2 if max_pages <= 3 * pps else 2 + -(-(max_pages - 3 * pps) // later)
+    assert splits == expected   # splits of 2 x pps, pps, then `later` pages
     key_pool, value_pool, out = _one_call(t)
     ref_k, ref_v, ref_out = _two_calls(t)
     assert _same_bits(key_pool, ref_k) and _same_bits(value_pool, ref_v)

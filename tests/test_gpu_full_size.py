@@ -122,9 +122,10 @@ def test_qwen7b_headline_step_full_size_with_the_bench_plan():
     spec, data, lens, plan, pre_k, pre_v, out = _run_bench_step('qwen7b_bf16', 1, 0)
     max_pages = -(-max(lens) // 16)
     assert max_pages > 128
-    # The bench's plan: a first split of 128 pages, then 64-page splits (3 splits at up to 256 pages).
-    assert plan == ('tma_mma', 64, 1 + -(-(max_pages - 128) // 64))
-    assert plan[2] == 3
+    # The bench's plan: a first split of 128 pages, a second of 64, then 16-page splits
+    # (6 splits at up to 256 pages).
+    assert plan == ('tma_mma', 64, 2 + -(-(max_pages - 192) // 16))
+    assert plan[2] == 6
     _check_append(spec, data, lens, pre_k, pre_v)
     worst = _check_attention(spec, data, lens, out, range(len(lens)))
     print(f'qwen7b_bf16 full size: plan {plan}, max abs err {worst:.3e}')
