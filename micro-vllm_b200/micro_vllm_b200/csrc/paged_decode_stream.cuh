@@ -14,12 +14,13 @@
 // same partial layout and the same merge pass combines them. Items are
 // numbered in this order:
 //   1. every full item (C pages), sequence by sequence, KV head, split;
-//   2. each segment's ragged last item, in descending size;
+//   2. each segment's ragged last item, in sequence order;
 //   3. one item per KV head of each sequence the decode does not attend
 //      (empty: zeros; length out of range: NaN).
 // Warps take items in that order from a global counter, so the last items
-// taken are the smallest and the SMs finish within a small item of each
-// other. An item is a fixed run of pages walked in a fixed order by one warp
+// taken are the shorter ragged ones. Every CTA derives the numbering from the
+// lengths alone (prefix sums), so an index names one item grid-wide. An item
+// is a fixed run of pages walked in a fixed order by one warp
 // and written to a fixed partial slot, so the result does not depend on
 // which warp takes which item: repeated calls are bit-identical.
 //
@@ -89,7 +90,7 @@ struct StreamItem {
 struct StreamTables {
     const int* len;     // per sequence: context length (clamped to int32)
     const int* fprefix; // kv_heads x full items of the sequences before b; [B] = all full items
-    const int* ragged;  // sequences with a ragged last item, largest first
+    const int* ragged;  // sequences with a ragged last item, in sequence order
     const int* unused;  // sequences the decode does not attend
     int n_full, n_ragged_items, total;
 };
@@ -275,9 +276,8 @@ paged_decode_stream_kernel(const DecodeParams p, const __grid_constant__ CUtenso
 
     extern __shared__ uint8_t smem_raw[];
     __shared__ __align__(8) uint64_t bars[kStreamWarps][S];
-    __shared__ int hist[kStreamMaxItemPages + 1];
     __shared__ int counts[2];  // ragged sequences, unattended sequences
-    __shared__ int warp_sums[kStreamWarps];
+    __shared__ int warp_sums[3][kStreamWarps];
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -296,21 +296,22 @@ paged_decode_stream_kernel(const DecodeParams p, const __grid_constant__ CUtenso
         for (int st = 0; st < S; ++st) mbar_init(bar0 + 8 * st, 1);
     }
     fence_mbar_init();
-    for (int i = tid; i <= kStreamMaxItemPages; i += blockDim.x) hist[i] = 0;
-    if (tid < 2) counts[tid] = 0;
     wait_for_prior_grid();
     __syncthreads();
 
-    // ---- tables: every sequence's length, full items per sequence (prefix
-    // sums), ragged last items by size (counting sort), unattended sequences.
+    // ---- tables: every sequence's length, full items per sequence and the
+    // lists of sequences with a ragged last item and of sequences not attended,
+    // all by prefix sums in sequence order. Every CTA builds the same tables
+    // from the same lengths, so an item index names the same item in every CTA
+    // (no shared-memory atomics here: their order differs from CTA to CTA).
     constexpr int kPerThread = (kStreamMaxBatch + kStreamWarps * 32 - 1) / (kStreamWarps * 32);
-    int local_full = 0;
     int my_full[kPerThread];
-    int my_ragged[kPerThread];
+    unsigned my_bits = 0;  // bit r: sequence r has a ragged item; bit 8 + r: not attended
+    int c_full = 0, c_ragged = 0, c_unused = 0;
 #pragma unroll
     for (int r = 0; r < kPerThread; ++r) {
         const int b = tid * kPerThread + r;
-        my_full[r] = my_ragged[r] = 0;
+        my_full[r] = 0;
         if (b < p.batch) {
             const SeqSplit s = seq_split(p, b);
             // The raw length (an unattended sequence's append position needs it).
@@ -318,55 +319,55 @@ paged_decode_stream_kernel(const DecodeParams p, const __grid_constant__ CUtenso
             if (s.state == 0) {
                 const int pages = static_cast<int>(s.pages);
                 my_full[r] = pages / C;
-                my_ragged[r] = pages % C;
-                local_full += my_full[r];
-                if (my_ragged[r]) atomicAdd(&hist[C - my_ragged[r]], 1);
+                if (pages % C) {
+                    my_bits |= 1u << r;
+                    ++c_ragged;
+                }
             } else {
-                s_unused[atomicAdd(&counts[1], 1)] = b;
+                my_bits |= 1u << (8 + r);
+                ++c_unused;
             }
+            c_full += my_full[r];
         }
     }
-    int incl = local_full;
+    int in_full = c_full, in_ragged = c_ragged, in_unused = c_unused;
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
-        const int v = __shfl_up_sync(0xffffffffu, incl, off);
-        if (lane >= off) incl += v;
+        const int vf = __shfl_up_sync(0xffffffffu, in_full, off);
+        const int vr = __shfl_up_sync(0xffffffffu, in_ragged, off);
+        const int vu = __shfl_up_sync(0xffffffffu, in_unused, off);
+        if (lane >= off) {
+            in_full += vf;
+            in_ragged += vr;
+            in_unused += vu;
+        }
     }
-    if (lane == 31) warp_sums[warp] = incl;
+    if (lane == 31) {
+        warp_sums[0][warp] = in_full;
+        warp_sums[1][warp] = in_ragged;
+        warp_sums[2][warp] = in_unused;
+    }
     __syncthreads();
-    int run = incl - local_full;
-    for (int v = 0; v < warp; ++v) run += warp_sums[v];
+    int run_full = in_full - c_full, run_ragged = in_ragged - c_ragged, run_unused = in_unused - c_unused;
+    for (int v = 0; v < warp; ++v) {
+        run_full += warp_sums[0][v];
+        run_ragged += warp_sums[1][v];
+        run_unused += warp_sums[2][v];
+    }
 #pragma unroll
     for (int r = 0; r < kPerThread; ++r) {
         const int b = tid * kPerThread + r;
         if (b < p.batch) {
-            s_fprefix[b] = run * p.kv_heads;
-            run += my_full[r];
+            s_fprefix[b] = run_full * p.kv_heads;
+            run_full += my_full[r];
+            if (my_bits & (1u << r)) s_ragged[run_ragged++] = b;
+            if (my_bits & (1u << (8 + r))) s_unused[run_unused++] = b;
         }
     }
-    if (tid == blockDim.x - 1) s_fprefix[p.batch] = run * p.kv_heads;
-    if (warp == 0) {
-        // Exclusive offsets of the size buckets (bucket C - r holds ragged size r).
-        int carry = 0;
-        for (int base = 0; base <= kStreamMaxItemPages; base += 32) {
-            const int i = base + lane;
-            const int c = i <= kStreamMaxItemPages ? hist[i] : 0;
-            int x = c;
-#pragma unroll
-            for (int off = 1; off < 32; off <<= 1) {
-                const int v = __shfl_up_sync(0xffffffffu, x, off);
-                if (lane >= off) x += v;
-            }
-            if (i <= kStreamMaxItemPages) hist[i] = carry + x - c;
-            carry += __shfl_sync(0xffffffffu, x, 31);
-        }
-        if (lane == 0) counts[0] = carry;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int r = 0; r < kPerThread; ++r) {
-        const int b = tid * kPerThread + r;
-        if (b < p.batch && my_ragged[r]) s_ragged[atomicAdd(&hist[C - my_ragged[r]], 1)] = b;
+    if (tid == blockDim.x - 1) {
+        s_fprefix[p.batch] = run_full * p.kv_heads;
+        counts[0] = run_ragged;
+        counts[1] = run_unused;
     }
     __syncthreads();
     allow_next_grid();

@@ -121,6 +121,25 @@ def test_stream_length_mixes(lens, pps):
     assert_attention_close(as_float(out), as_float(split_out), 'bfloat16')
 
 
+@pytest.mark.parametrize('pps', [3, 8])
+def test_many_sequences_share_item_sizes(pps):
+    """500 sequences whose ragged last items share sizes many times over, and
+    some not attended: every CTA of the grid must number the items the same
+    way, or some items run twice and others never (the append of a skipped
+    last item would be missing)."""
+    lens = [1 + (b * 37) % 400 for b in range(500)]
+    lens[7] = lens[123] = 0
+    spec = dict(batch=len(lens), q_heads=28, kv_heads=4, head_dim=128, block_size=16,
+                pool=('factor', 1.1), lens=('fixed', lens), dtype='bfloat16', value_scale=0.5, seed=515 + pps)
+    inputs = make_inputs(spec)
+    t = workload_tensors(inputs)
+    mode = dict(schedule='stream', pages_per_split=pps)
+    key_pool, value_pool, out = _one_call(t, **mode)
+    k2, v2, o2 = _two_calls(t, **mode)
+    assert _same_bits(key_pool, k2) and _same_bits(value_pool, v2) and _same_bits(out, o2)
+    assert_attention_close(as_float(out), _oracle(inputs, key_pool, value_pool), 'bfloat16')
+
+
 def test_unattended_and_out_of_range_lengths_append_like_the_append_kernel():
     """Length 0 (zeros, no write), above the table (NaN, no write), negative
     (NaN, no write), above the caller's bound (NaN, row still written)."""
