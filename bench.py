@@ -588,6 +588,25 @@ def run_ours(args):
         cuda_core_ms = time_form(cuda_core_graph)
         stream_ms = time_form(stream_graph) if stream_ok else 0.0
 
+        # Rank 0's step alone on the same machine (the other ranks wait at a
+        # barrier): separates what running N GPUs at once costs each GPU from
+        # differences between machines.
+        solo_ms = 0.0
+        if world > 1:
+            if rank == 0:
+                reps = min(args.steps, 1000)
+                s_start, s_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                with torch.cuda.stream(stream):
+                    for _ in range(args.warmup):
+                        step_graph.replay()
+                    s_start.record(stream)
+                    for _ in range(reps):
+                        step_graph.replay()
+                    s_end.record(stream)
+                torch.cuda.synchronize(device)
+                solo_ms = s_start.elapsed_time(s_end) / reps
+            barrier()
+
         # End to end through the public API: pinned host inputs in, output back out.
         e2e = run_e2e(args, data, max_len, pps, stream, device, barrier)
     clock_summary = clocks.summary()
@@ -686,6 +705,7 @@ def run_ours(args):
             result['per_rank_ms_per_step'] = [round(t, 6) for t in rank_ms_per_step]
             result['per_rank_us_per_launch'] = [round(t, 3) for t in rank_us_per_launch]
             result['per_rank_separate_step_us'] = [round(t, 3) for t in rank_separate_us]
+            result['rank0_alone_ms_per_step'] = round(solo_ms, 6)
         if strong is not None:
             result['strong_scaling'] = strong
         if world == 1 and not args.no_cpu_baseline:
