@@ -471,7 +471,12 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
                                  ((std::max<int64_t>(max_pages, 1) / 2 + pps - 1) / pps);
         if (first > pps && est_ctas > static_cast<int64_t>(dev.sms) * 3) {
             plan->first_pages = static_cast<int>(first);
-            if (MV_LATER_SPLIT_DIV > 1) plan->later_pages = static_cast<int>(std::max<int64_t>(16, pps / MV_LATER_SPLIT_DIV));
+            // Graded only while the plan stays at 8 splits or fewer: long contexts
+            // would otherwise get dozens of small splits (more CTAs, partials and
+            // merge work for no gain).
+            const int64_t later = std::max<int64_t>(16, pps / MV_LATER_SPLIT_DIV);
+            const int64_t graded = max_pages <= first + pps ? 2 : 2 + (max_pages - first - pps + later - 1) / later;
+            if (MV_LATER_SPLIT_DIV > 1 && later < pps && graded <= 8) plan->later_pages = static_cast<int>(later);
         }
     }
     const int64_t first = plan->first_pages;
