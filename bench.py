@@ -54,9 +54,9 @@ DEFAULT_WORKLOAD = 'qwen7b_bf16'
 FALLBACK_HBM_GBS = 6650.0
 # dram__bytes_read.sum + dram__bytes_write.sum of one step's kernels on this workload, from
 # one ncu capture each: paged_decode_mma_kernel with the append fused (329.85 MB + 5.37 MB,
-# profiles/paged_decode_mma_qwen7b_bf16.md) + paged_decode_merge_warp_kernel (1.53 MB read with
+# profiles/paged_decode_mma_qwen7b_bf16.md) + paged_decode_merge_warp_kernel (2.07 MB read with
 # ncu's cold caches, profiles/paged_decode_merge_warp_qwen7b_bf16.md).
-NCU_TRAFFIC_BYTES = {('qwen7b_bf16', 'tma_mma'): 329_853_440 + 5_367_296 + 1_525_760}
+NCU_TRAFFIC_BYTES = {('qwen7b_bf16', 'tma_mma'): 329_853_440 + 5_367_296 + 2_069_248}
 # Kernels of one one-call step by plan path (the roofline's dominant kernel and the merge pass).
 STEP_KERNELS = {
     'tma_mma': 'paged_decode_mma_kernel (append fused) + paged_decode_merge_warp_kernel',
