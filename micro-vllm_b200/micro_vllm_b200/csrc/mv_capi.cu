@@ -448,6 +448,12 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
         pps = plan->path == MV_PATH_SIMT ? std::max<int64_t>(1, (mv::kSimtTile + g.block_size - 1) / g.block_size)
                                          : 16;
         while (pps * 2 <= want && pps < kMaxPagesPerSplit) pps *= 2;
+        // Tensor cores: at most 64 splits per sequence. Measured on B200 (Qwen3-8B
+        // geometry, one KV head of 8 sequences of 32k-131k tokens -- a rank's
+        // shard at 8 GPUs): 64-page splits (126 per sequence) 71.9 us, 128-page
+        // ones 63.8 us -- half the CTAs, and half the pieces for the merge.
+        if (plan->path == MV_PATH_TMA_MMA)
+            while (pps * 64 < max_pages && pps < kMaxPagesPerSplit) pps *= 2;
         pps = std::min<int64_t>(pps, kMaxPagesPerSplit);
     }
     if (plan->path == MV_PATH_TMA_MMA && pps > max_pps)
@@ -744,14 +750,19 @@ int launch_mma_dispatch(const mv::DecodeParams& p, const CUtensorMap& kmap, cons
 dim3 merge_grid(const mv::DecodeParams& p) { return dim3(p.q_heads, p.batch); }
 
 // The split grid's merge pass: a warp per output row where head_dim <= 128 is a
-// multiple of 4 and rows have at most 32 pieces, else a CTA per row.
+// multiple of 4 and rows have at most 32 pieces; a CTA per row whose warps
+// share the pieces for up to 128; else a CTA per row looping over them.
 template <typename T>
 cudaError_t launch_split_merge(const mv::DecodeParams& p, cudaStream_t stream) {
-    if (p.head_dim % 4 == 0 && p.head_dim <= 128 && p.max_splits <= 32) {
+    const bool columns = p.head_dim % 4 == 0 && p.head_dim <= 128;
+    if (columns && p.max_splits <= 32) {
         const int64_t rows = static_cast<int64_t>(p.batch) * p.q_heads;
         const dim3 grid(static_cast<unsigned>((rows + mv::kWarpMergeRows - 1) / mv::kWarpMergeRows));
         return launch_pdl(mv::paged_decode_merge_warp_kernel<T>, grid, dim3(mv::kWarpMergeRows * 32), 0, stream, p);
     }
+    if (columns && p.max_splits <= mv::kManyMergeMax)
+        return launch_pdl(mv::paged_decode_merge_many_kernel<T>, merge_grid(p), dim3(mv::kManyMergeWarps * 32), 0,
+                          stream, p);
     return launch_pdl(mv::paged_decode_merge_kernel<T>, merge_grid(p), dim3(mv::kMergeThreads), 0, stream, p);
 }
 

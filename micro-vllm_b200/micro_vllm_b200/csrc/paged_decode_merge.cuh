@@ -247,6 +247,101 @@ __global__ void __launch_bounds__(kWarpMergeRows * 32) paged_decode_merge_warp_k
     out[3] = from_float<T>(nan ? q : acc.w);
 }
 
+// The split grid's merge for rows of 33..kManyMergeMax pieces (long contexts),
+// head_dim <= 128 and a multiple of 4: one CTA per row, its warps splitting the
+// pieces (warp w: pieces w, w + 4, ...). Lane k of a warp loads the
+// log-sum-exp of the warp's k-th piece and every lane a float4 column of up to
+// kManyBatch of the warp's partial rows in the same round; the weights come
+// from a CTA-wide max and sum, and the warps' column sums meet in shared
+// memory in a fixed order. 64 pieces: one dependent round of loads (the
+// CTA-per-row merge above takes one for the log-sum-exps and then eight
+// rounds of 8 partial columns).
+constexpr int kManyMergeWarps = 4;
+constexpr int kManyBatch = 16;                                   // pieces per warp in flight at once
+constexpr int kManyMergeMax = kManyMergeWarps * 2 * kManyBatch;  // 128
+
+template <typename T>
+__global__ void __launch_bounds__(kManyMergeWarps * 32) paged_decode_merge_many_kernel(const DecodeParams p) {
+    __shared__ float red[2][kManyMergeWarps];
+    __shared__ float4 sums[kManyMergeWarps][32];
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int hq = blockIdx.x;
+    const int b = blockIdx.y;
+    allow_next_grid();
+    const int n = seq_split(p, b).splits;  // reads only the caller's lengths
+    wait_for_prior_grid();
+    if (n <= 1) return;
+    const int c4n = p.head_dim >> 2;
+    const bool col = lane < c4n;
+    const int64_t base = (static_cast<int64_t>(b) * p.q_heads + hq) * p.max_splits;
+    const int mine = n > warp ? (n - warp + kManyMergeWarps - 1) / kManyMergeWarps : 0;  // <= 32
+    const float4* src = reinterpret_cast<const float4*>(p.part_o + base * p.head_dim) + lane;
+    const float lse = lane < mine ? __ldcg(p.part_lse + base + warp + kManyMergeWarps * lane) : -INFINITY;
+    float4 v[kManyBatch];
+#pragma unroll
+    for (int k = 0; k < kManyBatch; ++k)
+        v[k] = col && k < mine ? __ldcg(src + static_cast<int64_t>(warp + kManyMergeWarps * k) * c4n)
+                               : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    const bool nan_here = __any_sync(0xffffffffu, isnan(lse));
+    const float wmax = warp_max(lse);
+    if (lane == 0) red[0][warp] = nan_here ? __int_as_float(0x7fffffff) : wmax;
+    __syncthreads();
+    float mx = -INFINITY;
+    bool nan = false;
+#pragma unroll
+    for (int w = 0; w < kManyMergeWarps; ++w) {
+        nan |= isnan(red[0][w]);
+        mx = fmaxf(mx, red[0][w]);
+    }
+    const float e = lane < mine ? fast_exp2(lse - mx) : 0.0f;
+    const float wsum = warp_sum(e);
+    if (lane == 0) red[1][warp] = wsum;
+    __syncthreads();
+    float total = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kManyMergeWarps; ++w) total += red[1][w];
+    const float wgt = e * (1.0f / total);
+    float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int k0 = 0; k0 < mine; k0 += kManyBatch) {
+        if (k0 > 0) {
+#pragma unroll
+            for (int k = 0; k < kManyBatch; ++k)
+                v[k] = col && k0 + k < mine
+                           ? __ldcg(src + static_cast<int64_t>(warp + kManyMergeWarps * (k0 + k)) * c4n)
+                           : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+#pragma unroll
+        for (int k = 0; k < kManyBatch; ++k) {
+            const float wk = __shfl_sync(0xffffffffu, wgt, (k0 + k) & 31);
+            if (k0 + k < mine) {
+                acc.x = fmaf(wk, v[k].x, acc.x);
+                acc.y = fmaf(wk, v[k].y, acc.y);
+                acc.z = fmaf(wk, v[k].z, acc.z);
+                acc.w = fmaf(wk, v[k].w, acc.w);
+            }
+        }
+    }
+    sums[warp][lane] = acc;
+    __syncthreads();
+    if (warp != 0 || !col) return;
+    float4 r = sums[0][lane];
+#pragma unroll
+    for (int w = 1; w < kManyMergeWarps; ++w) {
+        const float4 s = sums[w][lane];
+        r.x += s.x;
+        r.y += s.y;
+        r.z += s.z;
+        r.w += s.w;
+    }
+    const float q = __int_as_float(0x7fffffff);
+    T* out = static_cast<T*>(p.out) + row_out_offset(p, b) + static_cast<int64_t>(hq) * p.out_stride_head + lane * 4;
+    out[0] = from_float<T>(nan ? q : r.x);
+    out[1] = from_float<T>(nan ? q : r.y);
+    out[2] = from_float<T>(nan ? q : r.z);
+    out[3] = from_float<T>(nan ? q : r.w);
+}
+
 // Merge of the persistent schedule. Row (b, hq) belongs to segment (b, h =
 // hq / G). It writes the constant result of sequences with no pages (zeros or
 // NaN), and for a segment cut across warps w0..w1 combines their partials.

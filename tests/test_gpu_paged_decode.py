@@ -411,3 +411,30 @@ def test_repeated_calls_are_bit_identical_on_every_default_path():
     qt = torch.randn((8, 28, 32, 128), generator=gen, device='cuda').to(torch.bfloat16)
     lens = t['context_lens'][:8].clamp(min=32)
     same(lambda: attention.paged_chunk_attention(qt, t['key_pool'], t['value_pool'], t['block_table'][:8], lens))
+
+
+@pytest.mark.parametrize('pps', [32, 4, 2, 1])
+def test_merge_paths_for_many_splits(pps):
+    """Rows of up to 8 pieces (warp per row), 64 and 128 pieces (a CTA per row whose
+    warps share the pieces) and 256 (a CTA per row looping over them): the
+    same output within the parity bar, and a corrupted page in one split
+    poisons exactly its sequence."""
+    attention, _ = _native()
+    lens = [4096, 1000, 16, 2100, 1]
+    spec = dict(batch=len(lens), q_heads=28, kv_heads=4, head_dim=128, block_size=16,
+                pool=('factor', 1.2), lens=('fixed', lens), dtype='bfloat16', value_scale=0.5, seed=808 + pps)
+    inputs = make_inputs(spec)
+    t, out = _append_and_decode(inputs, pages_per_split=pps)
+    assert attention.paged_decode_plan(28, t['key_pool'], 4096, batch=len(lens), pages_per_split=pps)[2] == \
+        -(-256 // pps)
+    expected = _oracle(inputs, to_numpy(t['key_pool']), to_numpy(t['value_pool']))
+    assert_attention_close(as_float(out), expected, 'bfloat16')
+    table = t['block_table'].clone()
+    table[0, 200] = t['key_pool'].shape[0]          # a page in a middle split of the longest sequence
+    bad = attention.paged_decode_attention(t['q'], t['key_pool'], t['value_pool'], table, t['context_lens'],
+                                           pages_per_split=pps)
+    torch.cuda.synchronize()
+    values = as_float(bad)
+    assert np.isnan(values[0]).all() and np.isfinite(values[1:]).all()
+    from micro_vllm_b200 import _native as native
+    native.check(native.library().mv_clear_device_status(torch.cuda.current_device()))
