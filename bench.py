@@ -18,7 +18,9 @@ data; the KV pool (~0.42 GB per GPU) is larger than the 126 MB L2.
 Prints ONE JSON line on rank 0. ``value`` is whole-job achieved HBM GB/s by
 the path's algorithmic bytes (K and V read once, q and out, page indices,
 lengths, and the append's read+write), measured with CUDA events around K
-CUDA-graph replays of the step, max over ranks. ``e2e`` is the same metric
+steps run as replays of a CUDA graph of 8 back-to-back steps (a serving loop
+replays one graph per decode step of all its layers; ``ms_per_step_single_replay``
+gives the one-step-per-replay figure beside it), max over ranks. ``e2e`` is the same metric
 through the public Python API with this step's inputs copied from pinned host
 memory and the output copied back inside the timed region.
 
@@ -534,18 +536,36 @@ def run_ours(args):
         with torch.cuda.stream(stream):
             for _ in range(args.warmup):
                 step_graph.replay()
+            kernel_graph.replay()
         torch.cuda.synchronize(device)
         barrier()
         torch.cuda.synchronize(device)
+        # K steps as replays of the graph of KERNEL_CALLS back-to-back steps (the rest,
+        # K mod KERNEL_CALLS, as single-step replays): a serving loop replays one graph
+        # per decode step of all layers, not one per attention call.
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         with torch.cuda.stream(stream):
             start.record(stream)
-            for _ in range(args.steps):
+            for _ in range(args.steps // KERNEL_CALLS):
+                kernel_graph.replay()
+            for _ in range(args.steps % KERNEL_CALLS):
                 step_graph.replay()
             end.record(stream)
         torch.cuda.synchronize(device)
         barrier()
         elapsed_ms = start.elapsed_time(end)
+
+        # The same steps one graph replay each: every step then also pays a graph launch.
+        single_reps = min(args.steps, 1000)
+        s_start, s_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(stream):
+            s_start.record(stream)
+            for _ in range(single_reps):
+                step_graph.replay()
+            s_end.record(stream)
+        torch.cuda.synchronize(device)
+        barrier()
+        single_ms = s_start.elapsed_time(s_end) / single_reps
 
         # The step's kernels alone (decode + split merge, and the append kernel in the
         # separate form), average launch duration over back-to-back calls, for the roofline.
@@ -617,14 +637,14 @@ def run_ours(args):
     if args.workload == DEFAULT_WORKLOAD and not args.pages_per_split:
         strong = strong_scaling(rank, world, device, barrier)
 
-    times = torch.tensor([elapsed_ms, attn_ms, e2e['ms'], other_ms, rope_ms, cuda_core_ms, stream_ms],
+    times = torch.tensor([elapsed_ms, attn_ms, e2e['ms'], other_ms, rope_ms, cuda_core_ms, stream_ms, single_ms],
                          dtype=torch.float64, device=device)
     totals = torch.tensor([float(step_total), float(attn_bytes)], dtype=torch.float64, device=device)
     rank_ms_per_step = per_rank_values(elapsed_ms / args.steps, rank, world, device)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
         dist.all_reduce(totals, op=dist.ReduceOp.SUM)
-    elapsed_ms, attn_ms, e2e_ms, other_ms, rope_ms, cuda_core_ms, stream_ms = times.tolist()
+    elapsed_ms, attn_ms, e2e_ms, other_ms, rope_ms, cuda_core_ms, stream_ms, single_ms = times.tolist()
     job_step_bytes, job_attn_bytes = totals.tolist()
     ms_per_step = elapsed_ms / args.steps
     value = job_step_bytes * args.steps / (elapsed_ms / 1e3) / 1e9
@@ -662,10 +682,12 @@ def run_ours(args):
                             'two calls: write_paged_kv + paged_decode_attention')),
                 'l2': f'inputs larger than L2: KV pool {2 * data["k_pool"].numel() * data["k_pool"].element_size() / 1e9:.2f} GB per GPU',
                 'parallelism': f'kv-head sharded x{world}, {args.scaling}' if world > 1 else 'single GPU',
-                'timing': 'CUDA events around K CUDA-graph replays, max over ranks',
+                'timing': (f'CUDA events around K steps run as replays of a CUDA graph of {KERNEL_CALLS} back-to-back '
+                           'steps (a serving loop replays one graph per decode step of all layers), max over ranks'),
                 'kernel_path': path, 'pages_per_split': chosen_pps, 'max_splits': splits,
             },
             'us_per_layer': round(ms_per_step * 1e3, 3),
+            'ms_per_step_single_replay': round(single_ms, 6),
             'decode_tokens_per_s': round(spec['batch'] / (ms_per_step / 1e3), 1),
             'pct_of_hbm_peak': round(100 * value / world / peak, 2),
             'roofline': {
