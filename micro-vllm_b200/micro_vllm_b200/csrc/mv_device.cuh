@@ -100,6 +100,11 @@ struct DecodeParams {
     // Split grid with first_pages: splits from the third on hold later_pages
     // pages (0: pages_per_split), so the splits dispatched last are shorter.
     int later_pages;
+    // Split grid: CTAs whose dispatch index is below this (the first wave of
+    // resident CTAs) warm L2 with their first prewait_pages pages per warp
+    // before waiting for the previous grid (0: none).
+    int prewait_ctas;
+    int prewait_pages;
 };
 
 struct AppendParams {
@@ -129,6 +134,21 @@ struct AppendParams {
 __device__ __forceinline__ int64_t load_index(const void* base, int is64, int64_t i) {
     return is64 ? __ldg(static_cast<const long long*>(base) + i)
                 : static_cast<int64_t>(__ldg(static_cast<const int*>(base) + i));
+}
+
+// An index read through L2 only (ld.global.cg: no L1 line is filled), for reads
+// made before the grid-dependency wait: the value may predate the previous
+// grid's writes, so it may only steer prefetches, and no later load of this
+// kernel can hit a stale L1 copy of it.
+__device__ __forceinline__ int64_t load_index_l2_hint(const void* base, int is64, int64_t i) {
+    if (is64) {
+        long long v;
+        asm volatile("ld.global.cg.s64 %0, [%1];" : "=l"(v) : "l"(static_cast<const long long*>(base) + i));
+        return v;
+    }
+    int v;
+    asm volatile("ld.global.cg.s32 %0, [%1];" : "=r"(v) : "l"(static_cast<const int*>(base) + i));
+    return v;
 }
 
 __device__ __forceinline__ int64_t row_seq(const DecodeParams& p, int64_t z) {

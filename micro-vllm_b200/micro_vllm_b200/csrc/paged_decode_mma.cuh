@@ -580,6 +580,37 @@ struct MmaDecodeShape {
     static_assert(kRedBytes <= kWarpBytes, "warp merge buffer must fit the warp's stages");
 };
 
+// Before the grid-dependency wait, a CTA of the first wave can bring its first
+// pages into L2, so its first TMA loads after the wait hit L2 instead of
+// waiting on DRAM while the previous kernel (a merge pass, the previous
+// layer's step) finishes. The length and the page IDs may still be written by
+// that kernel, so they are read through L2 (load_index_l2_hint) and used only
+// as prefetch addresses: an L2 prefetch changes no data, an ID outside the pool
+// is skipped, and every value the kernel computes with is read again after the
+// wait.
+template <int NWARPS>
+__device__ __forceinline__ void prewait_page_prefetch(const DecodeParams& p, const CUtensorMap* kmap,
+                                                      const CUtensorMap* vmap, int split, int h, int b, int warp,
+                                                      int lane) {
+    if (!p.context_lens || p.contiguous || p.q_tokens != 1) return;
+    const int64_t len = load_index_l2_hint(p.context_lens, p.lens_i64, b);
+    if (len <= 0 || len > p.max_context_len || len > p.blocks_per_seq * p.block_size) return;
+    const int64_t pages = (len + kPageTokens - 1) / kPageTokens;
+    const int64_t begin = split_begin(p, split);
+    if (begin >= pages) return;
+    const int64_t raw_end = begin + split_pages(p, split);
+    const int n = static_cast<int>((raw_end < pages ? raw_end : pages) - begin);
+    const int n_my = warp < n ? (n - warp + NWARPS - 1) / NWARPS : 0;
+    if (lane < n_my && lane < p.prewait_pages) {
+        const int64_t id = load_index_l2_hint(p.block_table, p.table_i64,
+                                              b * p.table_stride + begin + warp + lane * NWARPS);
+        if (id >= 0 && id < p.num_blocks) {
+            tma_prefetch_l2_5d(kmap, 0, 0, 0, h, static_cast<int>(id));
+            tma_prefetch_l2_5d(vmap, 0, 0, 0, h, static_cast<int>(id));
+        }
+    }
+}
+
 // Shared memory the CUDA-core variant adds after the stages: q of the group
 // (fp32) and each warp's P buffer.
 template <typename T, int D, int NWARPS>
@@ -617,6 +648,10 @@ paged_decode_mma_kernel(const DecodeParams p, const __grid_constant__ CUtensorMa
         b = blockIdx.z;
     }
 
+    if (p.prewait_ctas > 0 &&
+        blockIdx.x + static_cast<int64_t>(gridDim.x) * (blockIdx.y + static_cast<int64_t>(gridDim.y) * blockIdx.z) <
+            p.prewait_ctas)
+        prewait_page_prefetch<NWARPS>(p, &kmap, &vmap, split, h, b, warp, lane);
     wait_for_prior_grid();
     allow_next_grid();
     const SeqSplit seq = seq_split(p, b);
