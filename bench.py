@@ -58,7 +58,7 @@ FALLBACK_HBM_GBS = 6650.0
 # one ncu capture each: paged_decode_mma_kernel with the append fused (329.85 MB + 5.37 MB,
 # profiles/paged_decode_mma_qwen7b_bf16.md) + paged_decode_merge_warp_kernel (2.07 MB read with
 # ncu's cold caches, profiles/paged_decode_merge_warp_qwen7b_bf16.md).
-NCU_TRAFFIC_BYTES = {('qwen7b_bf16', 'tma_mma'): 329_853_440 + 5_367_296 + 2_069_248}
+NCU_TRAFFIC_BYTES = {('qwen7b_bf16', 'tma_mma'): 330_413_056 + 4_460_800 + 2_069_248}
 # Kernels of one one-call step by plan path (the roofline's dominant kernel and the merge pass).
 STEP_KERNELS = {
     'tma_mma': 'paged_decode_mma_kernel (append fused) + paged_decode_merge_warp_kernel',
@@ -84,6 +84,8 @@ def parse_args(argv=None):
     parser.add_argument('--cpu-seconds', type=float, default=12.0,
                         help='wall-clock budget of the CPU baseline sample')
     parser.add_argument('--no-cpu-baseline', action='store_true')
+    parser.add_argument('--no-strong-scaling', action='store_true',
+                        help='skip the strong-scaling records (profiling runs: only the headline workload on the device)')
     parser.add_argument('--pages-per-split', type=int, default=0)
     parser.add_argument('--kernels', default='',
                         help='kernels_qwen15b workload: time only the entries whose names contain this text')
@@ -634,7 +636,7 @@ def run_ours(args):
     rank_us_per_launch = per_rank_values(attn_ms * 1e3, rank, world, device)
     rank_separate_us = per_rank_values(other_ms / args.steps * 1e3, rank, world, device)
     strong = None
-    if args.workload == DEFAULT_WORKLOAD and not args.pages_per_split:
+    if args.workload == DEFAULT_WORKLOAD and not args.pages_per_split and not args.no_strong_scaling:
         strong = strong_scaling(rank, world, device, barrier)
 
     times = torch.tensor([elapsed_ms, attn_ms, e2e['ms'], other_ms, rope_ms, cuda_core_ms, stream_ms, single_ms],
