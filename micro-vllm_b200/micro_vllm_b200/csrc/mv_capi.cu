@@ -507,7 +507,10 @@ int make_plan(const Geometry& g, int32_t pages_per_split, uint32_t flags, bool a
     // batch 64, 1k-4k tokens): 62.1 us per step against 65.0 us with uniform
     // 64-page splits and 62.8 us with uniform 128-page splits.
     // Splits after the second are shorter again (MV_LATER_SPLIT_DIV), so the
-    // CTAs dispatched last are the smallest.
+    // CTAs dispatched last are the smallest. Re-measured with the first wave's
+    // L2 warm-up (MV_PREWAIT_PAGES): first splits of 96 / 112 / 128 / 160 / 192 / 256
+    // pages 62.0 / 59.7 / 56.9 / 62.5 / 66.6 / 74.4 us; later splits of 16 /
+    // 32 / 64 pages 56.9 / 57.1 / 57.8 us.
     // Only where the grid is more than one wave: with every CTA resident at
     // once the longest split sets the time (batch 1 x 4096 tokens: 13.8 us
     // with a 32-page first split, 10.3 us without).

@@ -167,6 +167,67 @@ __device__ void merge_segment(const DecodeParams& p, int b, int h, int n, float*
     }
 }
 
+// Merge of one (sequence, KV head) segment's n <= kSegmentWarpBatch pieces
+// by the CTA that finished it last, a warp per output row: lane j loads piece
+// j's log-sum-exp and every lane its float4 column of every piece, for all the
+// warp's rows at once -- one dependent round of loads (merge_segment takes two
+// rounds, then one per few pieces). The arithmetic is the warp-per-row merge
+// pass's below, in the same order, so both give the same bits. Needs head_dim
+// 64 or 128 and at most two rows per warp.
+constexpr int kSegmentWarpBatch = 8;
+
+template <typename T>
+__device__ void merge_segment_warps(const DecodeParams& p, int b, int h, int n) {
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int nwarps = blockDim.x >> 5;
+    const int c4n = p.head_dim >> 2;
+    const bool col = lane < c4n;
+    float lse[2];
+    float4 v[2][kSegmentWarpBatch];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const int g = warp + r * nwarps;
+        const bool row = g < p.group;
+        const int64_t base = (static_cast<int64_t>(b) * p.q_heads + h * p.group + (row ? g : 0)) * p.max_splits;
+        const float4* src = reinterpret_cast<const float4*>(p.part_o + base * p.head_dim) + lane;
+        lse[r] = row && lane < n ? __ldcg(p.part_lse + base + lane) : -INFINITY;
+#pragma unroll
+        for (int j = 0; j < kSegmentWarpBatch; ++j)
+            v[r][j] = row && col && j < n ? __ldcg(src + static_cast<int64_t>(j) * c4n)
+                                          : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const int g = warp + r * nwarps;
+        if (g >= p.group) break;
+        const bool nan = __any_sync(0xffffffffu, isnan(lse[r]));
+        const float mx = warp_max(lse[r]);
+        const float e = lane < n ? fast_exp2(lse[r] - mx) : 0.0f;
+        const float w = e * (1.0f / warp_sum(e));
+        float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+        for (int j = 0; j < kSegmentWarpBatch; ++j) {
+            const float wj = __shfl_sync(0xffffffffu, w, j);
+            if (j < n) {
+                acc.x = fmaf(wj, v[r][j].x, acc.x);
+                acc.y = fmaf(wj, v[r][j].y, acc.y);
+                acc.z = fmaf(wj, v[r][j].z, acc.z);
+                acc.w = fmaf(wj, v[r][j].w, acc.w);
+            }
+        }
+        if (col) {
+            const float q = __int_as_float(0x7fffffff);
+            T* out = static_cast<T*>(p.out) + row_out_offset(p, b) +
+                     static_cast<int64_t>(h * p.group + g) * p.out_stride_head + lane * 4;
+            out[0] = from_float<T>(nan ? q : acc.x);
+            out[1] = from_float<T>(nan ? q : acc.y);
+            out[2] = from_float<T>(nan ? q : acc.z);
+            out[3] = from_float<T>(nan ? q : acc.w);
+        }
+    }
+}
+
 // Merge of the fixed split grid, one CTA per output row (b, hq). Row (b, hq)
 // has seq.splits pieces at part rows (b * q_heads + hq) * max_splits + j.
 // Sequences that fit one split were finished by the first pass.

@@ -563,7 +563,11 @@ __device__ void arrive_and_merge(const DecodeParams& p, int b, int h, int splits
     __syncthreads();
     if (*flag) {
         __threadfence();
-        merge_segment<T>(p, b, h, splits, weights);
+        if ((p.head_dim == 64 || p.head_dim == 128) && splits <= kSegmentWarpBatch &&
+            p.group <= 2 * static_cast<int>(blockDim.x >> 5))
+            merge_segment_warps<T>(p, b, h, splits);
+        else
+            merge_segment<T>(p, b, h, splits, weights);
     }
 }
 

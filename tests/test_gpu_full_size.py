@@ -169,3 +169,22 @@ def test_kv_head_shards_of_the_strong_scaling_runs(name, world, rank):
     worst = _check_attention(spec, data, lens, out, sequences)
     print(f'{name} shard {rank}/{world}: {data["q"].shape[1]}/{data["k_pool"].shape[1]} heads, '
           f'batch {len(lens)}, plan {plan}, {len(sequences)} sequences checked, max abs err {worst:.3e}')
+
+
+def test_qwen7b_fused_merge_matches_the_merge_pass_bit_for_bit():
+    """The opt-in fused merge (the last split CTA of each segment merges it, a
+    warp per output row) on the headline workload: the same bits as the
+    default merge pass. The append is idempotent (the same row to the same
+    slot), so the second call runs on the first call's pools."""
+    from micro_vllm_b200 import cuda_attention
+
+    spec, data, lens, plan, pre_k, pre_v, out = _run_bench_step('qwen7b_bf16', 1, 0)
+    k_after, v_after = data['k_pool'].clone(), data['v_pool'].clone()
+    fused = torch.empty_like(out)
+    cuda_attention.paged_decode_with_append(
+        data['q'], data['k_new'][:, :, 0], data['v_new'][:, :, 0], data['k_pool'], data['v_pool'],
+        data['block_table'], data['context_lens'], max_context_len=max(lens), out=fused, fused_merge=True)
+    torch.cuda.synchronize()
+    assert torch.equal(_bits(fused), _bits(out))
+    assert torch.equal(_bits(data['k_pool']), _bits(k_after))
+    assert torch.equal(_bits(data['v_pool']), _bits(v_after))
