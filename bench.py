@@ -611,22 +611,23 @@ def run_ours(args):
         stream_ms = time_form(stream_graph) if stream_ok else 0.0
 
         # Rank 0's step alone on the same machine (the other ranks wait at a
-        # barrier): separates what running N GPUs at once costs each GPU from
-        # differences between machines.
+        # barrier), timed as the headline is (graphs of KERNEL_CALLS steps):
+        # separates what running N GPUs at once costs each GPU from differences
+        # between machines.
         solo_ms = 0.0
         if world > 1:
             if rank == 0:
-                reps = min(args.steps, 1000)
+                reps = max(1, min(args.steps, 1000) // KERNEL_CALLS)
                 s_start, s_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
                 with torch.cuda.stream(stream):
-                    for _ in range(args.warmup):
-                        step_graph.replay()
+                    for _ in range(max(args.warmup // KERNEL_CALLS, 3)):
+                        kernel_graph.replay()
                     s_start.record(stream)
                     for _ in range(reps):
-                        step_graph.replay()
+                        kernel_graph.replay()
                     s_end.record(stream)
                 torch.cuda.synchronize(device)
-                solo_ms = s_start.elapsed_time(s_end) / reps
+                solo_ms = s_start.elapsed_time(s_end) / (reps * KERNEL_CALLS)
             barrier()
 
         # End to end through the public API: pinned host inputs in, output back out.
