@@ -110,6 +110,12 @@ def _validate_paged_inputs(query, key, value, table, length):
 # first use and every completed call leaves them zero, so buffers are zeroed once
 # and reused by the calls ordered on that stream.
 _WORKSPACES = {}
+# Buffers a larger one replaced. A CUDA graph that captured a call keeps that
+# call's workspace address, so a buffer once handed to the library is never
+# freed while the process runs: freeing it would leave the graph writing into
+# memory the allocator may give to others or release (torch.cuda.graph empties
+# the allocator's cache when a capture starts).
+_RETIRED_WORKSPACES = []
 
 
 def _workspace(device, stream, nbytes):
@@ -119,6 +125,8 @@ def _workspace(device, stream, nbytes):
         return cached
     buffer = torch.zeros(nbytes, dtype=torch.uint8, device=device)
     if not torch.cuda.is_current_stream_capturing():
+        if cached is not None:
+            _RETIRED_WORKSPACES.append(cached)
         _WORKSPACES[key] = buffer
     return buffer
 
