@@ -250,7 +250,14 @@ __global__ void __launch_bounds__(kMergeThreads) paged_decode_merge_kernel(const
 // together -- one dependent round of loads where the CTA-per-row merge takes
 // two (log-sum-exps, then partials). The row's piece count reads only the
 // caller's lengths, so it is computed before waiting for the first pass.
-constexpr int kWarpMergeRows = 4;    // rows (warps) per CTA
+// Rows (warps) per CTA. Measured on B200 (Qwen2.5-7B geometry, batch 64, graphs
+// of 8 steps): 1 / 2 / 4 / 8 / 16 / 32 rows 56.65-56.69 / 56.73-56.76 /
+// 56.84-56.96 / 57.99 / 58.50 / 58.53 us per step -- the next step's decode
+// launches once every merge CTA has started, and one-warp CTAs find room first.
+#ifndef MV_WARP_MERGE_ROWS
+#define MV_WARP_MERGE_ROWS 1
+#endif
+constexpr int kWarpMergeRows = MV_WARP_MERGE_ROWS;
 constexpr int kWarpMergeBatch = 8;   // pieces whose partials are in flight together
 
 template <typename T>
