@@ -58,7 +58,7 @@ FALLBACK_HBM_GBS = 6650.0
 # one ncu capture each: paged_decode_mma_kernel with the append fused (329.85 MB + 5.37 MB,
 # profiles/paged_decode_mma_qwen7b_bf16.md) + paged_decode_merge_warp_kernel (2.07 MB read with
 # ncu's cold caches, profiles/paged_decode_merge_warp_qwen7b_bf16.md).
-NCU_TRAFFIC_BYTES = {('qwen7b_bf16', 'tma_mma'): 330_413_056 + 4_460_800 + 2_069_248}
+NCU_TRAFFIC_BYTES = {('qwen7b_bf16', 'tma_mma'): 330_466_048 + 4_808_192 + 2_067_456}
 # Kernels of one one-call step by plan path (the roofline's dominant kernel and the merge pass).
 STEP_KERNELS = {
     'tma_mma': 'paged_decode_mma_kernel (append fused) + paged_decode_merge_warp_kernel',
