@@ -640,14 +640,15 @@ def run_ours(args):
     if args.workload == DEFAULT_WORKLOAD and not args.pages_per_split and not args.no_strong_scaling:
         strong = strong_scaling(rank, world, device, barrier)
 
-    times = torch.tensor([elapsed_ms, attn_ms, e2e['ms'], other_ms, rope_ms, cuda_core_ms, stream_ms, single_ms],
+    times = torch.tensor([elapsed_ms, attn_ms, e2e['ms'], other_ms, rope_ms, cuda_core_ms, stream_ms, single_ms,
+                          e2e['each_ms']],
                          dtype=torch.float64, device=device)
     totals = torch.tensor([float(step_total), float(attn_bytes)], dtype=torch.float64, device=device)
     rank_ms_per_step = per_rank_values(elapsed_ms / args.steps, rank, world, device)
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
         dist.all_reduce(totals, op=dist.ReduceOp.SUM)
-    elapsed_ms, attn_ms, e2e_ms, other_ms, rope_ms, cuda_core_ms, stream_ms, single_ms = times.tolist()
+    elapsed_ms, attn_ms, e2e_ms, other_ms, rope_ms, cuda_core_ms, stream_ms, single_ms, e2e_each_ms = times.tolist()
     job_step_bytes, job_attn_bytes = totals.tolist()
     ms_per_step = elapsed_ms / args.steps
     value = job_step_bytes * args.steps / (elapsed_ms / 1e3) / 1e9
@@ -713,9 +714,13 @@ def run_ours(args):
             'e2e': {'value': round(e2e_value, 1), 'unit': 'GB/s',
                     'h2d_bytes_per_step': e2e['h2d'], 'd2h_bytes_per_step': e2e['d2h'],
                     'us_per_step': round(e2e_ms / args.steps * 1e3, 3),
+                    'us_per_step_issued_one_by_one': round(e2e_each_ms * 1e3, 3),
                     'how': ('public API (PagedDecodeStep) per step: packed q/k/v + lengths uploaded from '
                             'pinned host memory and the output downloaded to pinned host memory, on '
-                            'their own streams, two buffer slots, overlapping neighbouring steps')},
+                            f'their own streams; issued in blocks of {KERNEL_CALLS} steps (the uploads of '
+                            'a block while the previous block computes, its calls back to back, then its '
+                            'downloads; 2 blocks of buffer slots). us_per_step_issued_one_by_one: each '
+                            'step waits for its own upload and two slots')},
             'step_forms_us': {args.step: round(ms_per_step * 1e3, 3),
                               ('separate' if args.step == 'fused' else 'fused'):
                                   round(other_ms / args.steps * 1e3, 3),
@@ -842,9 +847,13 @@ def run_e2e(args, data, max_len, pps, stream, device, barrier):
     the new K/V rows packed as one [B, Hq + 2 Hkv, D] block (the layout of a
     fused QKV projection) followed by the lengths -- runs the step through a bound
     ``PagedDecodeStep`` (or the two-call form), and downloads its output into
-    pinned host memory. Uploads and downloads run on their own streams with two
-    buffer slots, so step i+1's upload and step i-1's download overlap step i's
-    kernels, as a serving loop runs them.
+    pinned host memory. Uploads and downloads run on their own streams. The
+    reported figure issues the steps in blocks of KERNEL_CALLS (the block's
+    uploads while the previous block computes, its calls back to back, then its
+    downloads), so consecutive steps' kernels overlap as in the device timing;
+    the steps issued one by one (each waiting for its own upload, two buffer
+    slots) are timed too, since an event wait between two steps' kernels keeps
+    the next decode from launching early.
     """
     import torch
 
@@ -914,8 +923,73 @@ def run_e2e(args, data, max_len, pps, stream, device, barrier):
     end.record(stream)
     torch.cuda.synchronize(device)
     barrier()
+    each_ms = start.elapsed_time(end) / steps
+
+    # The same per-step copies and calls issued in blocks of KERNEL_CALLS steps
+    # (the grouping of the device timing): the block's uploads (one per step,
+    # 2 x KERNEL_CALLS buffer slots) on the upload stream while the previous
+    # block computes, its steps' calls back to back on the compute stream with
+    # no event between them (so each decode launches early and overlaps the
+    # previous merge), then one download per step.
+    block = KERNEL_CALLS
+    b_host_in = [staging.cpu().pin_memory() for _ in range(2 * block)]
+    b_dev_in = [torch.empty_like(staging) for _ in range(2 * block)]
+    b_qkv = [buf[:qkv_bytes].view(packed.dtype).view(packed.shape) for buf in b_dev_in]
+    b_lens = [buf[qkv_bytes:].view(data['context_lens'].dtype) for buf in b_dev_in]
+    b_views = [(qkv[:, :hq], qkv[:, hq:hq + hkv], qkv[:, hq + hkv:]) for qkv in b_qkv]
+    b_dev_out = [torch.empty_like(data['q']) for _ in range(2 * block)]
+    b_host_out = [torch.empty(data['q'].shape, dtype=data['q'].dtype).pin_memory() for _ in range(2 * block)]
+    b_loaded = [torch.cuda.Event() for _ in range(2)]
+    b_computed = [torch.cuda.Event() for _ in range(2)]
+    b_read = [torch.cuda.Event() for _ in range(2)]
+    for event in b_computed + b_read:
+        event.record(stream)
+
+    def run_block(j):
+        half = j % 2
+        slots_j = range(half * block, half * block + block)
+        up.wait_event(b_computed[half])      # block j-2 has consumed these input slots
+        with torch.cuda.stream(up):
+            for s in slots_j:
+                b_dev_in[s].copy_(b_host_in[s], non_blocking=True)
+        b_loaded[half].record(up)
+        stream.wait_event(b_loaded[half])
+        stream.wait_event(b_read[half])      # block j-2's outputs have been downloaded
+        with torch.cuda.stream(stream):
+            for s in slots_j:
+                q, key, value = b_views[s]
+                if args.step == 'fused':
+                    bound(q, b_lens[s], b_dev_out[s], key=key, value=value)
+                else:
+                    cuda_paged_cache.write_paged_kv(key.unsqueeze(2), value.unsqueeze(2), data['k_pool'],
+                                                    data['v_pool'], data['block_table'], positions=b_lens[s],
+                                                    positions_are_end=True)
+                    bound(q, b_lens[s], b_dev_out[s])
+        b_computed[half].record(stream)
+        down.wait_event(b_computed[half])
+        with torch.cuda.stream(down):
+            for s in slots_j:
+                b_host_out[s].copy_(b_dev_out[s], non_blocking=True)
+        b_read[half].record(down)
+
+    blocks = max(1, steps // block)
+    for j in range(3):
+        run_block(j)
+    torch.cuda.synchronize(device)
+    barrier()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(stream)
+    up.wait_event(start)
+    for j in range(blocks):
+        run_block(j)
+    stream.wait_stream(up)
+    stream.wait_stream(down)
+    end.record(stream)
+    torch.cuda.synchronize(device)
+    barrier()
+    block_ms = start.elapsed_time(end) / (blocks * block)
     # Scale to the main loop's step count so value and e2e share one unit basis.
-    return {'ms': start.elapsed_time(end) * args.steps / steps, 'h2d': h2d, 'd2h': d2h}
+    return {'ms': block_ms * args.steps, 'each_ms': each_ms, 'h2d': h2d, 'd2h': d2h}
 
 
 # -------------------------------------------------------------- reference
