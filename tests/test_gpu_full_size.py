@@ -188,3 +188,28 @@ def test_qwen7b_fused_merge_matches_the_merge_pass_bit_for_bit():
     assert torch.equal(_bits(fused), _bits(out))
     assert torch.equal(_bits(data['k_pool']), _bits(k_after))
     assert torch.equal(_bits(data['v_pool']), _bits(v_after))
+
+
+def test_qwen7b_two_call_step_matches_the_one_call_step_bit_for_bit():
+    """The two-call form of the headline step: the append kernel, then the decode.
+
+    The decode is launched with programmatic dependent launch while the append
+    kernel still runs, and its first CTAs prefetch pages into L2 -- among them
+    the last page of every sequence, which the append kernel is writing -- before
+    they wait for it. Pools and output must equal the one-call step's bit for bit.
+    """
+    from micro_vllm_b200 import cuda_attention, cuda_paged_cache
+
+    spec, data, lens, plan, pre_k, pre_v, out = _run_bench_step('qwen7b_bf16', 1, 0)
+    k_one, v_one = data['k_pool'].clone(), data['v_pool'].clone()
+    data['k_pool'].copy_(pre_k)
+    data['v_pool'].copy_(pre_v)
+    two = torch.empty_like(out)
+    cuda_paged_cache.write_paged_kv(data['k_new'], data['v_new'], data['k_pool'], data['v_pool'],
+                                    data['block_table'], positions=data['context_lens'], positions_are_end=True)
+    cuda_attention.paged_decode_attention(data['q'], data['k_pool'], data['v_pool'], data['block_table'],
+                                          data['context_lens'], max_context_len=max(lens), out=two)
+    torch.cuda.synchronize()
+    assert torch.equal(_bits(data['k_pool']), _bits(k_one))
+    assert torch.equal(_bits(data['v_pool']), _bits(v_one))
+    assert torch.equal(_bits(two), _bits(out))
